@@ -1,0 +1,133 @@
+/* spk.h — C-ABI of libspk, the B200 (sm_100a) decode hot path.
+ *
+ * Two families of entry points:
+ *
+ *  vqg_*  Drop-in for the reference's kernel ABI, tools/vq/gpu/decode-gpu.cu:765-1140,
+ *         same names, argument meaning and error convention: 0 = ok, -1 = error with
+ *         the message in vqg_decode_error(). `payload` is a DEVICE pointer to ONE stage
+ *         (starting at its 'DQV3'/'DQVQ' magic) followed by >= 8 zeroed slack bytes;
+ *         host code never dereferences it. y / out ACCUMULATE (+=). Default stream,
+ *         asynchronous; the *_launch* forms never synchronize, the timed forms do.
+ *         `variant` values are the reference's (0 auto, 1 generic warp, 2 dim-4 warp,
+ *         3 DQV3 block) with the reference's legality rules; they select between this
+ *         build's kernels, which all compute the same sum.
+ *
+ *  spk_*  New entry points for the rest of the path (multi-stage fused VQ GEMV,
+ *         Q6_K / Q8_0 dequant-GEMV, tied head with argmax, the decode step). Same
+ *         error convention; every one takes a cudaStream_t as `void *stream`
+ *         (NULL = legacy default stream). All data pointers are device pointers
+ *         unless a comment says otherwise.
+ *
+ * Errors are kept per host thread. Kernels never trap: a bounded wait that runs
+ * out records an error that spk_check_device_error() reports.
+ */
+#ifndef SPK_H
+#define SPK_H
+#include <stddef.h>
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------ errors, device */
+/* decode-gpu.cu:23 */
+const char *vqg_decode_error(void);
+/* Same string as vqg_decode_error, for the spk_* entry points. */
+const char *spk_last_error(void);
+/* 0, or -1 if a kernel recorded a device-side error (a wait that ran out). */
+int spk_check_device_error(void);
+/* decode-gpu.cu:769-776 (current device instead of device 0) */
+int vqg_device_name(char *out, int n);
+/* decode-gpu.cu:780-784 */
+int vqg_driver_version(void);
+
+/* ----------------------------------------------- reference kernel ABI (vqg_*) */
+/* decode-gpu.cu:789-798 */
+int vqg_gemv_ready(int dim, int nc, int rows, int cols, int v3, int variant);
+/* decode-gpu.cu:864-901 (timed: best of `iters` launches into *ms) */
+int vqg_gemv_t(const void *payload, int dim, int nc, int rows, int cols, int v3, const float *x, float *y,
+               int variant, int threads, int iters, double *ms);
+/* decode-gpu.cu:903-906 */
+int vqg_gemv(const void *payload, int dim, int nc, int rows, int cols, int v3, const float *x, float *y, int variant,
+             int iters, double *ms);
+/* decode-gpu.cu:911-916 (one launch, no sync) */
+int vqg_gemv_launch_t(const void *payload, int dim, int nc, int rows, int cols, int v3, const float *x, float *y,
+                      int variant, int threads);
+/* decode-gpu.cu:918-922 */
+int vqg_gemv_launch(const void *payload, int dim, int nc, int rows, int cols, int v3, const float *x, float *y,
+                    int variant);
+/* decode-gpu.cu:834-858 (bit-exact: out += decoded stage) */
+int vqg_dequant(const void *payload, int dim, int nc, int rows, int cols, int v3, float *out, int iters, double *ms);
+/* decode-gpu.cu:947-956 (bit-exact: out[cols] += decoded row) */
+int vqg_row_dequant(const void *payload, int dim, int nc, int rows, int cols, int v3, int row, float *out);
+/* decode-gpu.cu:1120-1138 (y += W x over an expanded f32 matrix) */
+int vqg_gemv_f32(const float *w, const float *x, float *y, int rows, int cols, int iters, double *ms);
+
+/* Prefill / verify (xT is [cols][ntok], y is [ntok][rows], y accumulates).
+ * decode-gpu.cu:998-1008 */
+int vqg_prefill_ready(int dim, int nc, int rows, int cols, int v3, int variant);
+/* decode-gpu.cu:1012 */
+int vqg_prefill_cfg_count(void);
+/* decode-gpu.cu:1014-1019 */
+int vqg_prefill_cfg(int idx, int *bn, int *bk);
+/* decode-gpu.cu:1024-1029 */
+int vqg_prefill_cfg_ready(int dim, int nc, int rows, int cols, int v3, int bn, int bk, int variant);
+/* decode-gpu.cu:1034-1048 */
+int vqg_prefill(const void *payload, int dim, int nc, int rows, int cols, int v3, const float *xT, int ntok, float *y,
+                int iters, double *ms, int variant);
+/* decode-gpu.cu:1051-1065 */
+int vqg_prefill_tile(const void *payload, int dim, int nc, int rows, int cols, int v3, const float *xT, int ntok,
+                     float *y, int iters, double *ms, int bn, int bk, int variant);
+/* decode-gpu.cu:1071-1094 */
+int vqg_prefill_launch(const void *payload, int dim, int nc, int rows, int cols, int v3, const float *xT, int ntok,
+                       float *y, int variant);
+/* decode-gpu.cu:1099-1118 */
+int vqg_prefill_launch_tile(const void *payload, int dim, int nc, int rows, int cols, int v3, const float *xT,
+                            int ntok, float *y, int bn, int bk, int variant);
+
+/* ------------------------------------------------------------- new (spk_*) */
+/* All stages of a VQ container in one pass (replaces the per-stage loop of
+ * vq-model-gpu.cu:651-660 `gemv()` plus its memset).
+ *   ngroups 1: y = (accumulate ? y : 0) + sum_s gain_s * W_s x
+ *   ngroups 2: y = gelu_erf(W_gate x) * (W_up x), stages = {gate stages..., up stages...}
+ *              (replaces the gate GEMV, up GEMV and gelu_mul_kernel, vq-model-gpu.cu:464-469, 822-826)
+ * norm_w (may be NULL) folds RMSNorm(x; norm_w, eps) into the load of x
+ * (replaces rmsnorm_kernel, vq-model-gpu.cu:364-377). */
+int spk_vq_gemv(const void *const *stages, int nstages, int ngroups, int dim, int nc, int rows, int cols, int v3,
+                const float *x, const float *norm_w, float eps, float *y, int accumulate, void *stream);
+/* 1 if spk_vq_gemv runs the persistent TMA kernel for this geometry, 0 if the generic one. */
+int spk_vq_gemv_fast_ok(int nstages, int ngroups, int dim, int nc, int rows, int cols, int v3);
+/* Bit-exact stage decode on a stream: out += decoded stage (vqg_dequant without timing). */
+int spk_vq_dequant(const void *payload, int dim, int nc, int rows, int cols, int v3, float *out, void *stream);
+
+/* Q6_K / Q8_0 dequant-GEMV over raw ggml blocks (row-major, cols a multiple of the
+ * block width). No reference GPU implementation: the reference serves these
+ * formats through llama.cpp (tools/runtime/build-runtime.sh:181-246); the block
+ * rules are ggml's, called at tools/vq/quant_err.c:35-42.
+ *   y = (accumulate ? y : 0) + W RMSNorm?(x) */
+int spk_q6k_gemv(const void *w, int rows, int cols, const float *x, const float *norm_w, float eps, float *y,
+                 int accumulate, void *stream);
+int spk_q80_gemv(const void *w, int rows, int cols, const float *x, const float *norm_w, float eps, float *y,
+                 int accumulate, void *stream);
+/* Tied Q8_0 head: logits = W RMSNorm(x) and the first index of the maximum into
+ * *argmax_out (replaces the head GEMV + argmax_kernel, vq-model-gpu.cu:471-488, 831-833;
+ * argmax rule model.rs:594-604). Allocates a small per-device workspace on first use. */
+int spk_q80_head(const void *w, int rows, int cols, const float *x, const float *norm_w, float eps, float *logits,
+                 int *argmax_out, void *stream);
+/* Bit-exact block decode (ggml dequantize_row_q6_K / dequantize_row_q8_0). */
+int spk_q6k_dequant(const void *w, size_t nblocks, float *out, void *stream);
+int spk_q80_dequant(const void *w, size_t nblocks, float *out, void *stream);
+/* One decoded Q8_0 row into out[cols]; row index from `row`, or from the device
+ * int *token when token != NULL (replaces the embedding row of vq-model-gpu.cu:783-788). */
+int spk_q80_row(const void *w, int rows, int cols, int row, const int *token, float *out, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+#endif

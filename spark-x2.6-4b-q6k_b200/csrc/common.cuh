@@ -1,0 +1,145 @@
+// common.cuh — shared host/device helpers for libspk (sm_100a only).
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <string.h>
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "libspk is built for sm_100a only"
+#endif
+
+namespace spk {
+
+// ---------------------------------------------------------------- errors ---
+// Thread-local last-error string. The reference keeps one process-global
+// buffer (decode-gpu.cu:21-28); a thread-local one gives the same answer to a
+// single-threaded caller and does not race for a multi-threaded one.
+const char *last_error();
+int set_error(const char *fmt, ...);
+int cuda_fail(const char *what, cudaError_t e);
+
+// Device-side error word. Kernels never trap: a bounded wait that runs out
+// sets a code here and the kernel returns; the host reads it with check_device_error().
+enum : int { DEV_OK = 0, DEV_WAIT_TIMEOUT = 1, DEV_BAD_INDEX = 2 };
+int check_device_error(const char *where);
+int *device_error_ptr();   // address of the word on the current device
+
+// ------------------------------------------------------- stage geometry ---
+// One stage payload as the host parses it; the payload itself is a device
+// pointer that host code never dereferences (decode-gpu.cu:30-56).
+struct Layout {
+    int dim, nc, rows, cols, nbit, v3;
+    uint32_t mask;
+    size_t cb_off, gain_off, stream_off, nidx, nidx_row, mrow, prow;
+};
+
+inline Layout make_layout(int dim, int nc, int rows, int cols, int v3) {
+    Layout L;
+    L.dim = dim;
+    L.nc = nc;
+    L.rows = rows;
+    L.cols = cols;
+    L.v3 = v3 ? 1 : 0;
+    L.nbit = 1;
+    while ((1u << L.nbit) < (unsigned)nc) L.nbit++;
+    L.mask = (1u << L.nbit) - 1u;
+    const size_t nidx_row = dim > 0 ? (size_t)cols / (size_t)dim : 0;
+    const int mb = L.nbit > 12 ? 12 : L.nbit;
+    L.cb_off = v3 ? 24 : 16;
+    L.gain_off = L.cb_off + (size_t)nc * dim * 2;
+    L.stream_off = L.gain_off + (size_t)rows * 2;
+    L.nidx = (size_t)rows * nidx_row;
+    L.nidx_row = nidx_row;
+    L.mrow = v3 ? (nidx_row * (size_t)mb + 7) / 8 : 0;
+    L.prow = (v3 && L.nbit > 12) ? (nidx_row + 7) / 8 : 0;
+    return L;
+}
+
+inline size_t stage_bytes(const Layout &L) {
+    if (L.v3) return L.stream_off + (size_t)L.rows * (L.mrow + L.prow);
+    const size_t idx = L.nbit == 8 ? L.nidx : (L.nidx * (size_t)L.nbit + 7) / 8 + 1;
+    return L.stream_off + idx;
+}
+
+// A DQV3 width above 13 bits would decode truncated indices silently
+// (decode-gpu.cu:66-80), so every entry point refuses it.
+inline bool v3_width_ok(int nc) {
+    int b = 1;
+    while ((1 << b) < nc) b++;
+    return b <= 13;
+}
+
+int sm_count();
+size_t smem_optin_max();
+
+// ------------------------------------------------------ device helpers ---
+#define SPK_WAIT_LIMIT (1u << 26)
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: returns false (and records DEV_WAIT_TIMEOUT) if the phase never
+// completes, so a lost copy ends the kernel with an error instead of a hang.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err) {
+    for (uint32_t i = 0; i < SPK_WAIT_LIMIT; i++)
+        if (mbar_try_wait(bar, parity)) return true;
+    if (err) atomicExch(err, DEV_WAIT_TIMEOUT);
+    return false;
+}
+
+// 1-D bulk copy global -> shared (TMA engine, no tensor map, no multicast).
+// dst, src 16-byte aligned; bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+}  // namespace spk

@@ -1,0 +1,340 @@
+// ggml.cu — Q6_K / Q8_0 block decode kernels for B200 (raw ggml block layout).
+//
+// Block formats (ggml, sizes as tools/kquant/stubs.c:23-52 price them):
+//   Q6_K: 256 weights in 210 bytes: ql[128] low 4 bits, qh[64] high 2 bits,
+//         int8 scales[16] (one per 16 weights), f16 d; w = (d * scale) * (q - 32).
+//         Weight n = 128h + 32j + l (h half, j quadrant, l lane 0..31):
+//         low nibble of ql[64h + l + 32(j&1)] (j<2) or its high nibble (j>=2),
+//         high bits (qh[32h + l] >> 2j) & 3, scale scales[8h + 2j + l/16].
+//   Q8_0: 32 weights in 34 bytes: f16 d, int8 qs[32]; w = q * d.
+//
+// The GEMVs accumulate sum (q - 32) * x per 16-weight sub-block and apply the
+// block scale once per sub-block. The integer-to-float step uses the bit
+// pattern 0x3F000000 | q << 16 == 0.5 + q/256 (q < 64), so a 6-bit value
+// becomes a float with one byte permute: sum (q-32) x = 256 (sum f x - 0.625 sum x).
+// Dequant kernels are bit-exact with ggml's CPU decode (one rounded f32 multiply
+// per operand, in ggml's order).
+#include "common.cuh"
+#include "spk.h"
+
+using namespace spk;
+
+namespace {
+
+__device__ __forceinline__ float h2f_bits(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+
+__device__ __forceinline__ uint32_t ld_u32_unaligned(const uint8_t *p) {
+    // p is at least 2-byte aligned (ggml blocks are 210 / 34 bytes); a 2-aligned
+    // word is read as two halves so no byte outside the field is touched.
+    if (((uintptr_t)p & 3) == 0) return __ldg((const uint32_t *)p);
+    const uint32_t lo = __ldg((const unsigned short *)p), hi = __ldg((const unsigned short *)(p + 2));
+    return lo | (hi << 16);
+}
+
+__device__ float block_rms_inv(const float *x, int n, float eps, double *red) {
+    double s = 0.0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) s += (double)x[i] * (double)x[i];
+    s = warp_sum_d(s);
+    const int w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+    if ((threadIdx.x & 31) == 0) red[w] = s;
+    __syncthreads();
+    double t = 0.0;
+    for (int k = 0; k < nw; k++) t += red[k];
+    __syncthreads();
+    return (float)(1.0 / sqrt(t / (double)n + (double)eps));
+}
+
+__device__ __forceinline__ float xval(const float *x, const float *nw, float inv, int c) {
+    float v = x[c];
+    if (nw) v = __fmul_rn(__fmul_rn(v, inv), nw[c]);
+    return v;
+}
+
+// One unit = 16 weights of one row: half h, lane-quad m (l = 4m..4m+3), all
+// four quadrants j. Returns sum over the unit of w * x.
+__device__ __forceinline__ float q6k_unit(const uint8_t *blk, int h, int m, const float *x, const float *nw,
+                                          float inv, int col0) {
+    const uint32_t qa = ld_u32_unaligned(blk + 64 * h + 4 * m);
+    const uint32_t qb = ld_u32_unaligned(blk + 64 * h + 32 + 4 * m);
+    const uint32_t qh = ld_u32_unaligned(blk + 128 + 32 * h + 4 * m);
+    const float d = h2f_bits(*(const uint16_t *)(blk + 208));
+    const int8_t *sc = (const int8_t *)(blk + 192 + 8 * h + (m >> 2));
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const uint32_t lo = ((j & 1) ? qb : qa) >> ((j & 2) ? 4 : 0);
+        const uint32_t q = (lo & 0x0F0F0F0Fu) | (((qh >> (2 * j)) & 0x03030303u) << 4);
+        float s = 0.f, xs = 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const float xv = xval(x, nw, inv, col0 + 128 * h + 32 * j + 4 * m + e);
+            const float f = __uint_as_float(__byte_perm(q, 0x3F000000u, 0x7044u | ((uint32_t)e << 8)));
+            s = fmaf(f, xv, s);
+            xs += xv;
+        }
+        s = fmaf(-0.625f, xs, s);
+        acc = fmaf(__fmul_rn(d, (float)sc[2 * j]) * 256.0f, s, acc);
+    }
+    return acc;
+}
+
+struct BlkArgs {
+    const uint8_t *w;   // row-major blocks
+    int rows, cols;
+    const float *x;
+    const float *norm_w;
+    float eps;
+    float *y;
+    int accumulate;
+};
+
+// Warp per row, lanes stride over the row's 16-weight units.
+__global__ void q6k_gemv_kernel(const BlkArgs a) {
+    __shared__ double red[32];
+    float inv = 1.0f;
+    if (a.norm_w) inv = block_rms_inv(a.x, a.cols, a.eps, red);
+    const int warp = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+    if (warp >= a.rows) return;
+    const int nb = a.cols / 256;
+    const uint8_t *row = a.w + (size_t)warp * nb * 210;
+    float acc = 0.f;
+    for (int u = lane; u < nb * 16; u += 32) {
+        const int b = u >> 4, h = (u >> 3) & 1, m = u & 7;
+        acc += q6k_unit(row + (size_t)b * 210, h, m, a.x, a.norm_w, inv, b * 256);
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) a.y[warp] = (a.accumulate ? a.y[warp] : 0.0f) + acc;
+}
+
+// 8 weights of a Q8_0 block (quarter k of block blk).
+__device__ __forceinline__ float q80_quarter(const uint8_t *blk, int k, const float *x, const float *nw, float inv,
+                                             int col0) {
+    const float d = h2f_bits(*(const uint16_t *)blk);
+    const uint32_t w0 = ld_u32_unaligned(blk + 2 + 8 * k) ^ 0x80808080u;
+    const uint32_t w1 = ld_u32_unaligned(blk + 6 + 8 * k) ^ 0x80808080u;
+    float s = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+        const uint32_t w = e < 4 ? w0 : w1;
+        // 0x4B0000bb = 2^23 + bb; bb = q + 128
+        const float f = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440u | (uint32_t)(e & 3))) - 8388736.0f;
+        s = fmaf(f, xval(x, nw, inv, col0 + 8 * k + e), s);
+    }
+    return d * s;
+}
+
+__global__ void q80_gemv_kernel(const BlkArgs a) {
+    __shared__ double red[32];
+    float inv = 1.0f;
+    if (a.norm_w) inv = block_rms_inv(a.x, a.cols, a.eps, red);
+    const int warp = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+    if (warp >= a.rows) return;
+    const int nb = a.cols / 32;
+    const uint8_t *row = a.w + (size_t)warp * nb * 34;
+    float acc = 0.f;
+    for (int u = lane; u < nb * 4; u += 32) acc += q80_quarter(row + (size_t)(u >> 2) * 34, u & 3, a.x, a.norm_w, inv, (u >> 2) * 32);
+    acc = warp_sum(acc);
+    if (lane == 0) a.y[warp] = (a.accumulate ? a.y[warp] : 0.0f) + acc;
+}
+
+// Q8_0 head: logits plus the first index of the maximum (model.rs:594-604),
+// reduced per block and then by the last block to finish (a counter that the
+// last block resets, so the kernel replays in a graph).
+struct HeadArgs {
+    BlkArgs b;
+    unsigned long long *partial;   // per block: (ordered value << 32) | ~index
+    unsigned int *counter;
+    int *argmax_out;
+};
+
+__device__ __forceinline__ unsigned long long pack_vi(float v, int i) {
+    // Larger value wins; for equal values the smaller index wins. NaN never wins.
+    uint32_t u = __float_as_uint(v);
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    if (v == 0.0f) u = 0x80000000u;   // -0 ties +0, as the CPU's strict > does
+    if (v != v) u = 0;
+    return ((unsigned long long)u << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)i);
+}
+
+__global__ void q80_head_kernel(const HeadArgs a) {
+    __shared__ double red[32];
+    __shared__ unsigned long long best_w[32];
+    __shared__ bool last;
+    const BlkArgs &b = a.b;
+    float inv = 1.0f;
+    if (b.norm_w) inv = block_rms_inv(b.x, b.cols, b.eps, red);
+    const int wib = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarp = blockDim.x >> 5;
+    const int nb = b.cols / 32;
+    unsigned long long best = pack_vi(-INFINITY, 0);
+    for (int r = blockIdx.x * nwarp + wib; r < b.rows; r += gridDim.x * nwarp) {
+        const uint8_t *row = b.w + (size_t)r * nb * 34;
+        float acc = 0.f;
+        for (int u = lane; u < nb * 4; u += 32) acc += q80_quarter(row + (size_t)(u >> 2) * 34, u & 3, b.x, b.norm_w, inv, (u >> 2) * 32);
+        acc = warp_sum(acc);
+        if (lane == 0) {
+            b.y[r] = acc;
+            const unsigned long long c = pack_vi(acc, r);
+            if (c > best) best = c;
+        }
+    }
+    if (lane == 0) best_w[wib] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned long long m = best_w[0];
+        for (int k = 1; k < nwarp; k++) m = best_w[k] > m ? best_w[k] : m;
+        a.partial[blockIdx.x] = m;
+        __threadfence();
+        last = atomicAdd(a.counter, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (last && threadIdx.x == 0) {
+        __threadfence();
+        unsigned long long m = 0;
+        for (int k = 0; k < (int)gridDim.x; k++) {
+            const unsigned long long v = ((volatile unsigned long long *)a.partial)[k];
+            m = v > m ? v : m;
+        }
+        *a.argmax_out = (int)(0xFFFFFFFFu - (uint32_t)(m & 0xFFFFFFFFull));
+        *a.counter = 0;
+    }
+}
+
+// ggml dequantize_row_q6_K, bit-exact: (d * (float)sc) * (float)(q - 32).
+__global__ void q6k_dequant_kernel(const uint8_t *w, size_t nblk, float *out) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;   // weight index
+    if (i >= nblk * 256) return;
+    const size_t b = i >> 8;
+    const int n = (int)(i & 255), h = n >> 7, j = (n >> 5) & 3, l = n & 31;
+    const uint8_t *blk = w + b * 210;
+    const uint8_t qlb = blk[64 * h + l + 32 * (j & 1)];
+    const int lo = (j & 2) ? (qlb >> 4) : (qlb & 0xF);
+    const int hi = (blk[128 + 32 * h + l] >> (2 * j)) & 3;
+    const int q = (lo | (hi << 4)) - 32;
+    const int8_t sc = (int8_t)blk[192 + 8 * h + 2 * j + l / 16];
+    const float d = h2f_bits((uint16_t)(blk[208] | (blk[209] << 8)));
+    out[i] = __fmul_rn(__fmul_rn(d, (float)sc), (float)q);
+}
+
+// ggml dequantize_row_q8_0, bit-exact: (float)q * d.
+__global__ void q80_dequant_kernel(const uint8_t *w, size_t nblk, float *out) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= nblk * 32) return;
+    const uint8_t *blk = w + (i >> 5) * 34;
+    const float d = h2f_bits((uint16_t)(blk[0] | (blk[1] << 8)));
+    out[i] = __fmul_rn((float)(int8_t)blk[2 + (i & 31)], d);
+}
+
+// One row of a Q8_0 matrix (the token embedding of the tied head).
+__global__ void q80_row_kernel(const uint8_t *w, int rows, int cols, const int *tok, int row, float *out, int *err) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= cols) return;
+    int r = tok ? *tok : row;
+    if (r < 0 || r >= rows) {   // a device-side token id out of range: report, read row 0
+        if (c == 0) atomicExch(err, DEV_BAD_INDEX);
+        r = 0;
+    }
+    const uint8_t *blk = w + ((size_t)r * (cols / 32) + (c >> 5)) * 34;
+    const float d = h2f_bits((uint16_t)(blk[0] | (blk[1] << 8)));
+    out[c] = __fmul_rn((float)(int8_t)blk[2 + (c & 31)], d);
+}
+
+int check_blocks(const void *w, int rows, int cols, int wpb) {
+    if (!w) return set_error("weight pointer is null");
+    if (rows <= 0 || cols <= 0) return set_error("gemv needs a non-empty matrix");
+    if (cols % wpb) return set_error("cols %d is not a multiple of the %d-weight block", cols, wpb);
+    if ((uintptr_t)w & 1) return set_error("block pointer must be 2-byte aligned");
+    return 0;
+}
+
+int launch_blk(bool q6k, const BlkArgs &a, cudaStream_t s) {
+    const int threads = 256;
+    const int blocks = (int)(((size_t)a.rows * 32 + threads - 1) / threads);
+    if (q6k)
+        q6k_gemv_kernel<<<blocks, threads, 0, s>>>(a);
+    else
+        q80_gemv_kernel<<<blocks, threads, 0, s>>>(a);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_fail(q6k ? "q6_k gemv launch" : "q8_0 gemv launch", e);
+}
+
+unsigned int *g_head_counter[64];
+unsigned long long *g_head_partial[64];
+
+}  // namespace
+
+extern "C" {
+
+/* Q6_K dequant-GEMV over raw ggml blocks: y = (accumulate ? y : 0) + W x, with
+ * an optional RMSNorm(x; norm_w, eps) prologue. All pointers are device pointers. */
+int spk_q6k_gemv(const void *w, int rows, int cols, const float *x, const float *norm_w, float eps, float *y,
+                 int accumulate, void *stream) {
+    if (check_blocks(w, rows, cols, 256)) return -1;
+    BlkArgs a = {(const uint8_t *)w, rows, cols, x, norm_w, eps, y, accumulate};
+    return launch_blk(true, a, (cudaStream_t)stream);
+}
+
+/* Q8_0 dequant-GEMV over raw ggml blocks (same contract as spk_q6k_gemv). */
+int spk_q80_gemv(const void *w, int rows, int cols, const float *x, const float *norm_w, float eps, float *y,
+                 int accumulate, void *stream) {
+    if (check_blocks(w, rows, cols, 32)) return -1;
+    BlkArgs a = {(const uint8_t *)w, rows, cols, x, norm_w, eps, y, accumulate};
+    return launch_blk(false, a, (cudaStream_t)stream);
+}
+
+/* Tied Q8_0 head: logits = W RMSNorm(x) and the first index of the maximum
+ * logit into *argmax_out (device int). Logits are written, not accumulated. */
+int spk_q80_head(const void *w, int rows, int cols, const float *x, const float *norm_w, float eps, float *logits,
+                 int *argmax_out, void *stream) {
+    if (check_blocks(w, rows, cols, 32)) return -1;
+    if (!argmax_out) return set_error("argmax output pointer is null");
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int grid = 2 * sm_count();
+    if (!g_head_counter[dev & 63]) {
+        void *c = nullptr, *p = nullptr;
+        cudaError_t e = cudaMalloc(&c, sizeof(unsigned int));
+        if (e == cudaSuccess) e = cudaMalloc(&p, sizeof(unsigned long long) * 1024);
+        if (e == cudaSuccess) e = cudaMemset(c, 0, sizeof(unsigned int));
+        if (e != cudaSuccess) return cuda_fail("head scratch allocation", e);
+        g_head_counter[dev & 63] = (unsigned int *)c;
+        g_head_partial[dev & 63] = (unsigned long long *)p;
+    }
+    HeadArgs a;
+    a.b = {(const uint8_t *)w, rows, cols, x, norm_w, eps, logits, 0};
+    a.partial = g_head_partial[dev & 63];
+    a.counter = g_head_counter[dev & 63];
+    a.argmax_out = argmax_out;
+    q80_head_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(a);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_fail("q8_0 head launch", e);
+}
+
+/* Bit-exact block decode into f32 (nblocks * 256 or * 32 values). */
+int spk_q6k_dequant(const void *w, size_t nblocks, float *out, void *stream) {
+    if (!w || !out) return set_error("dequant needs input and output");
+    const size_t n = nblocks * 256;
+    q6k_dequant_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>((const uint8_t *)w, nblocks, out);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_fail("q6_k dequant launch", e);
+}
+
+int spk_q80_dequant(const void *w, size_t nblocks, float *out, void *stream) {
+    if (!w || !out) return set_error("dequant needs input and output");
+    const size_t n = nblocks * 32;
+    q80_dequant_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>((const uint8_t *)w, nblocks, out);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_fail("q8_0 dequant launch", e);
+}
+
+/* One decoded row of a Q8_0 matrix into out[cols]: row `row`, or *token when
+ * token (device int) is not null — the token-embedding gather of a tied head. */
+int spk_q80_row(const void *w, int rows, int cols, int row, const int *token, float *out, void *stream) {
+    if (check_blocks(w, rows, cols, 32)) return -1;
+    if (!token && (row < 0 || row >= rows)) return set_error("row %d is outside %d", row, rows);
+    q80_row_kernel<<<(cols + 255) / 256, 256, 0, (cudaStream_t)stream>>>((const uint8_t *)w, rows, cols, token, row, out,
+                                                                       device_error_ptr());
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_fail("q8_0 row launch", e);
+}
+
+}  // extern "C"

@@ -1,0 +1,726 @@
+// vq.cu — residual-VQ (DQV3 / DQVQ) decode kernels for B200, and the vqg_* C-ABI.
+//
+// What the reference computes (tools/vq-format/src/lib.rs:162-228,
+// tools/vq/gpu/decode-gpu.cu:103-301): for every stage s of a container,
+//   y[r] += gain_s[r] * sum_i sum_d cb_s[idx_s(r,i)][d] * x[i*dim + d]
+// with idx_s read from the stage's packed stream.
+//
+// The B200 design (fast path, DQV3 dim 4 with a 12-bit main stream):
+//   * persistent CTAs, one per SM, each owning a contiguous row range;
+//   * every stage's f16 codebook staged once per CTA in shared memory;
+//   * the row index streams of a tile of rows pulled by the TMA engine
+//     (cp.async.bulk, 1-D, no tensor map, no multicast) into a 3-deep ring of
+//     shared-memory slots completed by mbarriers, so HBM reads run ahead of the math;
+//   * every lane owns a fixed contiguous run of F indices of the row, so its
+//     4F activations live in registers for the whole kernel and only the
+//     codebook gathers touch shared memory;
+//   * all stages (and, for the FFN, the gate and up matrices) of a row are
+//     reduced in one pass, with an optional RMSNorm prologue and either a
+//     store / residual-accumulate or an erf-GELU(gate)*up epilogue.
+// Every other legal geometry (any dim, DQVQ v2 global streams, narrow or
+// unaligned streams) runs a generic warp-per-row kernel with the reference's
+// exact index semantics. Dequant kernels are bit-exact: one f32 multiply and
+// one f32 add per element, no contraction.
+#include "common.cuh"
+#include "spk.h"
+
+using namespace spk;
+
+namespace {
+
+// ----------------------------------------------------------- index read ---
+// lib.rs:162-190 / decode-gpu.cu:82-121. Byte reads: a payload's row stream
+// need not be word aligned for the generic path. The 4-byte window may read
+// up to 3 bytes past the last index, inside the caller's 8 zeroed slack bytes.
+__device__ __forceinline__ uint32_t rd_idx(const uint8_t *st, const Layout &L, size_t r, size_t i) {
+    if (!L.v3) {
+        const size_t gi = r * L.nidx_row + i;
+        if (L.nbit == 8) return st[gi];
+        const size_t bit = gi * (size_t)L.nbit;
+        const uint8_t *q = st + (bit >> 3);
+        const uint32_t w = (uint32_t)q[0] | ((uint32_t)q[1] << 8) | ((uint32_t)q[2] << 16);
+        return (w >> (bit & 7)) & L.mask;
+    }
+    const uint32_t mb = L.nbit > 12 ? 12u : (uint32_t)L.nbit;
+    const size_t bit = i * mb;
+    const uint8_t *q = st + r * L.mrow + (bit >> 3);
+    const uint32_t w = (uint32_t)q[0] | ((uint32_t)q[1] << 8) | ((uint32_t)q[2] << 16) | ((uint32_t)q[3] << 24);
+    uint32_t v = (w >> (bit & 7)) & ((1u << mb) - 1u);
+    if (L.prow) {
+        const uint8_t *pl = st + L.mrow * (size_t)L.rows + r * L.prow;
+        v |= (uint32_t)((pl[i >> 3] >> (i & 7)) & 1u) << 12;
+    }
+    return v;
+}
+
+__device__ __forceinline__ float h2f_bits(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+
+__device__ __forceinline__ float gelu_erf(float g) {
+    // model.rs:253-258: 0.5*x*(1 + erf(x/sqrt2)) with erf evaluated in f64.
+    const double e = erf((double)g * 0.70710678118654752440);
+    return __fmul_rn(__fmul_rn(0.5f, g), __fadd_rn(1.0f, (float)e));
+}
+
+// Block-wide RMSNorm scale, sum of squares in f64 (model.rs:236-245). Every CTA
+// sums in the same order, so every CTA gets the same scale.
+__device__ float block_rms_inv(const float *x, int n, float eps, double *red) {
+    double s = 0.0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) s += (double)x[i] * (double)x[i];
+    s = warp_sum_d(s);
+    const int w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+    if ((threadIdx.x & 31) == 0) red[w] = s;
+    __syncthreads();
+    double t = 0.0;
+    for (int k = 0; k < nw; k++) t += red[k];
+    __syncthreads();
+    return (float)(1.0 / sqrt(t / (double)n + (double)eps));
+}
+
+// ============================================================ fast path ===
+constexpr int FAST_WARPS = 16;
+constexpr int FAST_THREADS = FAST_WARPS * 32;
+constexpr int FAST_NBUF = 3;
+constexpr int MAXQ = 4;   // streams: groups x stages
+
+struct FastArgs {
+    const uint8_t *st[MAXQ];   // stage payloads, group-major
+    Layout L;
+    const float *x;
+    const float *norm_w;       // optional RMSNorm weight (nullptr: none)
+    float eps;
+    float *y;                  // NG 1: y[rows]; NG 2: act[rows]
+    int accumulate;            // NG 1: y += result instead of y = result
+    int ks;                    // warps per row chunk split
+    int tr;                    // rows per tile
+    uint32_t main_slot, plane_slot, slot_bytes;
+    int *err;
+};
+
+template <int F>
+struct Chunk {
+    static constexpr int MAXSH = ((12 * F) % 32 == 0) ? 0 : 16;
+    static constexpr int NWR = (MAXSH + 12 * F + 31) / 32;   // words read
+    static constexpr int NWU = (12 * F + 31) / 32;           // words used after the shift
+};
+
+// One lane's partial dot over its F indices of one row of one stage.
+template <int F, int EXT>
+__device__ __forceinline__ float row_chunk(const uint8_t *row, const uint8_t *plane, const uint2 *cb,
+                                           const float (&xr)[4 * F], uint32_t bit0, uint32_t pbit0) {
+    using C = Chunk<F>;
+    const uint32_t *wp = reinterpret_cast<const uint32_t *>(row) + (bit0 >> 5);
+    const uint32_t sh = bit0 & 31u;
+    uint32_t w[C::NWR];
+#pragma unroll
+    for (int j = 0; j < C::NWR; j++) w[j] = wp[j];
+    uint32_t u[C::NWU];
+#pragma unroll
+    for (int j = 0; j < C::NWU; j++) u[j] = __funnelshift_r(w[j], (j + 1 < C::NWR) ? w[j + 1] : 0u, sh);
+    uint32_t pb = 0;
+    if (EXT) {
+        const uint32_t *pp = reinterpret_cast<const uint32_t *>(plane) + (pbit0 >> 5);
+        pb = __funnelshift_r(pp[0], pp[1], pbit0 & 31u);
+    }
+    float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < F; j++) {
+        const int b = 12 * j, wi = b >> 5, s = b & 31;
+        uint32_t v;
+        if (s + 12 <= 32)
+            v = (u[wi] >> s) & 0xFFFu;
+        else
+            v = __funnelshift_r(u[wi], u[wi + 1], s) & 0xFFFu;
+        if (EXT) v |= ((pb >> j) & 1u) << 12;
+        const uint2 c = cb[v];
+        const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&c.x));
+        const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&c.y));
+        a0 = fmaf(lo.x, xr[4 * j + 0], a0);
+        a1 = fmaf(lo.y, xr[4 * j + 1], a1);
+        a0 = fmaf(hi.x, xr[4 * j + 2], a0);
+        a1 = fmaf(hi.y, xr[4 * j + 3], a1);
+    }
+    return a0 + a1;
+}
+
+// Producer: thread 0 fills one ring slot with the index streams of rows
+// [r0, r0+nr) of every stream. The 16-byte-aligned interior goes by bulk copy,
+// a ragged tail (< 16 bytes) by plain loads, so nothing is read past the
+// stream beyond what the generic path reads.
+__device__ __forceinline__ void issue_tile(const FastArgs &a, int nq, int ext, uint8_t *slot, uint64_t *bar,
+                                           int r0, int nr) {
+    const Layout &L = a.L;
+    uint32_t tx = 0;
+    const uint8_t *src_al[2 * MAXQ];
+    uint32_t len[2 * MAXQ];
+    uint8_t *dst[2 * MAXQ];
+    int n = 0;
+    for (int q = 0; q < nq; q++) {
+        for (int part = 0; part < 1 + ext; part++) {
+            const uint8_t *base = a.st[q] + L.stream_off +
+                                  (part ? (size_t)L.rows * L.mrow + (size_t)r0 * L.prow : (size_t)r0 * L.mrow);
+            const size_t bytes = (size_t)nr * (part ? L.prow : L.mrow);
+            const uintptr_t A = (uintptr_t)base, B = A + bytes;
+            const uintptr_t Aal = A & ~(uintptr_t)15, Bfl = B & ~(uintptr_t)15;
+            uint8_t *d = slot + (part ? (nq * a.main_slot + q * a.plane_slot) : q * a.main_slot);
+            // ragged tail by plain loads
+            const uintptr_t t0 = Bfl > Aal ? Bfl : Aal;
+            for (uintptr_t b = t0; b < B; b++) d[b - Aal] = *(const uint8_t *)b;
+            if (Bfl > Aal) {
+                src_al[n] = (const uint8_t *)Aal;
+                len[n] = (uint32_t)(Bfl - Aal);
+                dst[n] = d;
+                tx += len[n];
+                n++;
+            }
+        }
+    }
+    mbar_arrive_expect_tx(bar, tx);
+    fence_proxy_async();
+    for (int k = 0; k < n; k++) bulk_g2s(dst[k], src_al[k], len[k], bar);
+}
+
+template <int NSTG, int NG, int F, int EXT>
+__global__ void __launch_bounds__(FAST_THREADS, 1) vq_fast_kernel(const FastArgs a) {
+    constexpr int NQ = NSTG * NG;
+    extern __shared__ __align__(16) uint8_t smem[];
+    const Layout &L = a.L;
+    const int nc = L.nc;
+    uint2 *cb = reinterpret_cast<uint2 *>(smem);
+    uint8_t *ring = smem + (((size_t)NQ * nc * 8 + 15) & ~(size_t)15);
+    uint64_t *full = reinterpret_cast<uint64_t *>(ring + (size_t)FAST_NBUF * a.slot_bytes);
+    float *part = reinterpret_cast<float *>(full + FAST_NBUF);   // [2][tr][NG][ks][NSTG]
+    double *red = reinterpret_cast<double *>(part + 2 * a.tr * NG * a.ks * NSTG);
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int ks_n = a.ks, tr = a.tr;
+    // warp -> (row in tile, group, k chunk)
+    const int ks = warp % ks_n, g = (warp / ks_n) % NG, rw = warp / (ks_n * NG);
+
+    const int G = gridDim.x;
+    const int rb = (int)(((long long)blockIdx.x * L.rows) / G), re = (int)(((long long)(blockIdx.x + 1) * L.rows) / G);
+    const int ntile = (re - rb + tr - 1) / tr;
+
+    if (tid == 0) {
+        for (int b = 0; b < FAST_NBUF; b++) mbar_init(&full[b], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (tid == 0) {
+        for (int t = 0; t < FAST_NBUF - 1 && t < ntile; t++) {
+            const int r0 = rb + t * tr;
+            issue_tile(a, NQ, EXT, ring + (size_t)t * a.slot_bytes, &full[t], r0, min(tr, re - r0));
+        }
+    }
+    // Codebooks: NQ x nc code words of 8 bytes (the payload keeps them 8-byte aligned).
+    for (int q = 0; q < NQ; q++) {
+        const uint2 *src = reinterpret_cast<const uint2 *>(a.st[q] + L.cb_off);
+        for (int v = tid; v < nc; v += FAST_THREADS) cb[q * nc + v] = __ldg(src + v);
+    }
+    // Activations of this lane's index run, with the optional RMSNorm folded in.
+    float inv = 1.0f;
+    if (a.norm_w) inv = block_rms_inv(a.x, L.cols, a.eps, red);
+    float xr[4 * F];
+    const int i0 = ks * 32 * F + lane * F;
+#pragma unroll
+    for (int j = 0; j < 4 * F; j++) {
+        const int c = 4 * i0 + j;
+        float v = a.x[c];
+        if (a.norm_w) v = __fmul_rn(__fmul_rn(v, inv), a.norm_w[c]);
+        xr[j] = v;
+    }
+    __syncthreads();
+
+    const uint32_t bit0 = 12u * (uint32_t)i0, pbit0 = (uint32_t)i0;
+    for (int t = 0; t < ntile; t++) {
+        const int slot = t % FAST_NBUF;
+        if (tid == 0 && t + FAST_NBUF - 1 < ntile) {
+            const int tn = t + FAST_NBUF - 1, r0 = rb + tn * tr;
+            issue_tile(a, NQ, EXT, ring + (size_t)(tn % FAST_NBUF) * a.slot_bytes, &full[tn % FAST_NBUF], r0,
+                       min(tr, re - r0));
+        }
+        const int r0 = rb + t * tr, nr = min(tr, re - r0);
+        const bool ok = mbar_wait(&full[slot], (uint32_t)((t / FAST_NBUF) & 1), a.err);
+        if (!ok) return;
+        float *pt = part + (size_t)(t & 1) * tr * NG * ks_n * NSTG;
+        if (rw < nr) {
+            const uint8_t *sb = ring + (size_t)slot * a.slot_bytes;
+            float acc[NSTG];
+#pragma unroll
+            for (int s = 0; s < NSTG; s++) {
+                const int q = g * NSTG + s;
+                const uintptr_t A = (uintptr_t)(a.st[q] + L.stream_off + (size_t)r0 * L.mrow);
+                const uint8_t *row = sb + q * a.main_slot + (A & 15) + (size_t)rw * L.mrow;
+                const uint8_t *pl = nullptr;
+                if (EXT) {
+                    const uintptr_t P = (uintptr_t)(a.st[q] + L.stream_off + (size_t)L.rows * L.mrow +
+                                                    (size_t)r0 * L.prow);
+                    pl = sb + NQ * a.main_slot + q * a.plane_slot + (P & 15) + (size_t)rw * L.prow;
+                }
+                acc[s] = warp_sum(row_chunk<F, EXT>(row, pl, cb + (size_t)q * nc, xr, bit0, pbit0));
+            }
+            if (lane == 0) {
+#pragma unroll
+                for (int s = 0; s < NSTG; s++) pt[((rw * NG + g) * ks_n + ks) * NSTG + s] = acc[s];
+            }
+        }
+        __syncthreads();
+        if (tid < nr) {
+            const int r = r0 + tid;
+            float outv[NG];
+#pragma unroll
+            for (int gg = 0; gg < NG; gg++) {
+                float o = (NG == 1 && a.accumulate) ? a.y[r] : 0.0f;
+#pragma unroll
+                for (int s = 0; s < NSTG; s++) {
+                    float v = 0.f;
+                    for (int k = 0; k < ks_n; k++) v += pt[((tid * NG + gg) * ks_n + k) * NSTG + s];
+                    const uint16_t gh = *reinterpret_cast<const uint16_t *>(a.st[gg * NSTG + s] + L.gain_off + 2 * (size_t)r);
+                    o = __fadd_rn(o, __fmul_rn(v, h2f_bits(gh)));
+                }
+                outv[gg] = o;
+            }
+            if (NG == 1)
+                a.y[r] = outv[0];
+            else
+                a.y[r] = __fmul_rn(gelu_erf(outv[0]), outv[NG - 1]);
+        }
+    }
+}
+
+// ========================================================= generic path ===
+// One warp per row, codebook read through L1. Any dim, DQVQ or DQV3, any width.
+struct GenArgs {
+    const uint8_t *st[MAXQ];
+    int nstg, ng;
+    Layout L;
+    const float *x;
+    const float *norm_w;
+    float eps;
+    float *y;
+    int accumulate;
+};
+
+__global__ void vq_generic_kernel(const GenArgs a) {
+    __shared__ double red[32];
+    const Layout &L = a.L;
+    float inv = 1.0f;
+    if (a.norm_w) inv = block_rms_inv(a.x, L.cols, a.eps, red);
+    const int warp = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+    if (warp >= L.rows) return;
+    const int r = warp;
+    float outv[2] = {0.f, 0.f};
+    for (int g = 0; g < a.ng; g++) {
+        float o = (a.ng == 1 && a.accumulate) ? a.y[r] : 0.0f;
+        for (int s = 0; s < a.nstg; s++) {
+            const uint8_t *p = a.st[g * a.nstg + s];
+            const __half *cb = reinterpret_cast<const __half *>(p + L.cb_off);
+            const uint8_t *st = p + L.stream_off;
+            float acc = 0.f;
+            for (size_t i = lane; i < L.nidx_row; i += 32) {
+                const uint32_t v = min(rd_idx(st, L, (size_t)r, i), (uint32_t)L.nc - 1u);   // malformed stream: stay in the codebook
+                const __half *c = cb + (size_t)v * L.dim;
+                for (int d = 0; d < L.dim; d++) {
+                    const size_t col = i * (size_t)L.dim + (size_t)d;
+                    float xv = a.x[col];
+                    if (a.norm_w) xv = __fmul_rn(__fmul_rn(xv, inv), a.norm_w[col]);
+                    acc = fmaf(__half2float(c[d]), xv, acc);
+                }
+            }
+            acc = warp_sum(acc);
+            const uint16_t gh = *reinterpret_cast<const uint16_t *>(p + L.gain_off + 2 * (size_t)r);
+            o = __fadd_rn(o, __fmul_rn(acc, h2f_bits(gh)));
+        }
+        outv[g] = o;
+    }
+    if (lane == 0) a.y[r] = a.ng == 1 ? outv[0] : __fmul_rn(gelu_erf(outv[0]), outv[1]);
+}
+
+// lib.rs:197-212 / decode-gpu.cu:124-150: out[r][i*dim+d] += cb[v][d] * gain[r],
+// one rounded multiply and one rounded add, bit-exact with the CPU decode.
+__global__ void vq_dequant_kernel(const uint8_t *p, const Layout L, float *out, int *err) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= L.nidx) return;
+    const size_t r = i / L.nidx_row, k = i - r * L.nidx_row;
+    const uint32_t v = rd_idx(p + L.stream_off, L, r, k);
+    if (v >= (uint32_t)L.nc) {
+        atomicExch(err, DEV_BAD_INDEX);
+        return;
+    }
+    const float g = h2f_bits(*reinterpret_cast<const uint16_t *>(p + L.gain_off + 2 * r));
+    const __half *c = reinterpret_cast<const __half *>(p + L.cb_off) + (size_t)v * L.dim;
+    float *o = out + i * (size_t)L.dim;
+    for (int d = 0; d < L.dim; d++) o[d] = __fadd_rn(o[d], __fmul_rn(__half2float(c[d]), g));
+}
+
+// decode-gpu.cu:934-945: one row of one stage accumulated into out (the
+// embedding row of a VQ embedding matrix).
+__global__ void vq_row_dequant_kernel(const uint8_t *p, const Layout L, int row, float *out) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= L.nidx_row) return;
+    const uint32_t v = min(rd_idx(p + L.stream_off, L, (size_t)row, i), (uint32_t)L.nc - 1u);
+    const float g = h2f_bits(*reinterpret_cast<const uint16_t *>(p + L.gain_off + 2 * (size_t)row));
+    const __half *c = reinterpret_cast<const __half *>(p + L.cb_off) + (size_t)v * L.dim;
+    float *o = out + i * (size_t)L.dim;
+    for (int d = 0; d < L.dim; d++) o[d] = __fadd_rn(o[d], __fmul_rn(__half2float(c[d]), g));
+}
+
+// Plain f32 GEMV, the "already expanded" bandwidth baseline (decode-gpu.cu:662-677).
+__global__ void gemv_f32_kernel(const float *w, const float *x, float *y, int rows, int cols) {
+    const int warp = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+    if (warp >= rows) return;
+    const float *wr = w + (size_t)warp * cols;
+    float acc = 0.f;
+    if ((cols & 3) == 0 && ((uintptr_t)wr & 15) == 0 && ((uintptr_t)x & 15) == 0) {
+        const float4 *w4 = reinterpret_cast<const float4 *>(wr), *x4 = reinterpret_cast<const float4 *>(x);
+        for (int c = lane; c < cols / 4; c += 32) {
+            const float4 a = __ldg(w4 + c), b = x4[c];
+            acc = fmaf(a.x, b.x, fmaf(a.y, b.y, fmaf(a.z, b.z, fmaf(a.w, b.w, acc))));
+        }
+    } else {
+        for (int c = lane; c < cols; c += 32) acc = fmaf(wr[c], x[c], acc);
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) y[warp] += acc;
+}
+
+// ----------------------------------------------------------- dispatch ---
+// Preconditions of the fast path (same contract as v3_blk_ok, decode-gpu.cu:62-64,
+// plus dim 4 and this kernel's lane split): a DQV3 payload with a 12-bit main
+// stream, whole 32-index groups, word-aligned row streams, an 8-byte aligned
+// codebook.
+bool blk_ok(const Layout &L) {
+    return L.v3 && L.nbit >= 12 && L.nidx_row % 32 == 0 && L.mrow % 4 == 0 && L.stream_off % 4 == 0;
+}
+
+int pick_split(const Layout &L, int *F) {
+    // smallest k (warps per row chunk) with nidx_row/(32k) in {20, 16, 8, 4}
+    for (int k = 1; k <= 8; k *= 2) {
+        if (L.nidx_row % (32 * (size_t)k)) continue;
+        const int f = (int)(L.nidx_row / (32 * (size_t)k));
+        if (f == 20 || f == 16 || f == 8 || f == 4) {
+            *F = f;
+            return k;
+        }
+    }
+    return 0;
+}
+
+struct FastPlan {
+    int ks, F, tr;
+    size_t smem;
+    FastArgs args;
+};
+
+bool fast_plan(const uint8_t *const *st, int nstg, int ng, const Layout &L, FastPlan *P) {
+    if (L.dim != 4 || !blk_ok(L) || nstg < 1 || nstg > 2 || ng < 1 || ng > 2) return false;
+    for (int q = 0; q < nstg * ng; q++)
+        if (((uintptr_t)st[q] & 7) != 0) return false;
+    int F = 0;
+    const int ks = pick_split(L, &F);
+    if (!ks || ks * ng > FAST_WARPS) return false;
+    const int tr = FAST_WARPS / (ks * ng);
+    const int nq = nstg * ng, ext = L.prow ? 1 : 0;
+    const uint32_t main_slot = (uint32_t)(((size_t)tr * L.mrow + 32 + 15) & ~(size_t)15);
+    const uint32_t plane_slot = ext ? (uint32_t)(((size_t)tr * L.prow + 32 + 15) & ~(size_t)15) : 0u;
+    const uint32_t slot = nq * (main_slot + plane_slot);
+    const size_t smem = (((size_t)nq * L.nc * 8 + 15) & ~(size_t)15) + (size_t)FAST_NBUF * slot + FAST_NBUF * 8 +
+                        (size_t)2 * tr * ng * ks * nstg * 4 + 32 * 8;
+    if (smem > smem_optin_max()) return false;
+    FastArgs &a = P->args;
+    memset(&a, 0, sizeof a);
+    for (int q = 0; q < nq; q++) a.st[q] = st[q];
+    a.L = L;
+    a.ks = ks;
+    a.tr = tr;
+    a.main_slot = main_slot;
+    a.plane_slot = plane_slot;
+    a.slot_bytes = slot;
+    P->ks = ks;
+    P->F = F;
+    P->tr = tr;
+    P->smem = smem;
+    return true;
+}
+
+template <int NSTG, int NG, int F, int EXT>
+int launch_fast_t(const FastPlan &P, cudaStream_t s) {
+    auto k = vq_fast_kernel<NSTG, NG, F, EXT>;
+    static size_t opted[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (P.smem > opted[dev & 63]) {
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P.smem);
+        if (e != cudaSuccess) return cuda_fail("vq fast kernel shared-memory opt-in", e);
+        opted[dev & 63] = P.smem;
+    }
+    const int ntr = (P.args.L.rows + P.tr - 1) / P.tr;
+    const int grid = ntr < sm_count() ? ntr : sm_count();
+    k<<<grid, FAST_THREADS, P.smem, s>>>(P.args);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_fail("vq fast kernel launch", e);
+}
+
+template <int NSTG, int NG, int F>
+int launch_fast_e(const FastPlan &P, cudaStream_t s) {
+    return P.args.L.prow ? launch_fast_t<NSTG, NG, F, 1>(P, s) : launch_fast_t<NSTG, NG, F, 0>(P, s);
+}
+
+template <int NSTG, int NG>
+int launch_fast_f(const FastPlan &P, cudaStream_t s) {
+    switch (P.F) {
+        case 20: return launch_fast_e<NSTG, NG, 20>(P, s);
+        case 16: return launch_fast_e<NSTG, NG, 16>(P, s);
+        case 8: return launch_fast_e<NSTG, NG, 8>(P, s);
+        case 4: return launch_fast_e<NSTG, NG, 4>(P, s);
+    }
+    return set_error("vq fast kernel: no instantiation for F=%d", P.F);
+}
+
+int launch_fast(const FastPlan &P, int nstg, int ng, cudaStream_t s) {
+    if (nstg == 1 && ng == 1) return launch_fast_f<1, 1>(P, s);
+    if (nstg == 2 && ng == 1) return launch_fast_f<2, 1>(P, s);
+    if (nstg == 1 && ng == 2) return launch_fast_f<1, 2>(P, s);
+    if (nstg == 2 && ng == 2) return launch_fast_f<2, 2>(P, s);
+    return set_error("vq fast kernel: %d stages x %d groups not instantiated", nstg, ng);
+}
+
+int launch_generic(const uint8_t *const *st, int nstg, int ng, const Layout &L, const float *x,
+                   const float *norm_w, float eps, float *y, int accumulate, int threads, cudaStream_t s) {
+    GenArgs a;
+    memset(&a, 0, sizeof a);
+    for (int q = 0; q < nstg * ng; q++) a.st[q] = st[q];
+    a.nstg = nstg;
+    a.ng = ng;
+    a.L = L;
+    a.x = x;
+    a.norm_w = norm_w;
+    a.eps = eps;
+    a.y = y;
+    a.accumulate = accumulate;
+    const int blocks = (int)(((size_t)L.rows * 32 + threads - 1) / threads);
+    vq_generic_kernel<<<blocks, threads, 0, s>>>(a);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_fail("vq generic kernel launch", e);
+}
+
+int check_geometry(int dim, int nc, int rows, int cols, int v3) {
+    if (v3 && !v3_width_ok(nc)) {
+        int b = 1;
+        while ((1 << b) < nc) b++;
+        return set_error("DQV3 carries 13 index bits, nc %d needs %d", nc, b);
+    }
+    if (rows <= 0 || cols <= 0) return set_error("gemv needs a non-empty matrix");
+    if (dim <= 0 || nc <= 0 || cols % dim) return set_error("geometry dim %d nc %d cols %d is inconsistent", dim, nc, cols);
+    if (nc > 65535) return set_error("nc %d does not fit the u16 header field", nc);
+    return 0;
+}
+
+// Multi-stage, optionally paired (gate/up) GEMV on a stream.
+int vq_gemv_impl(const void *const *stages, int nstg, int ng, const Layout &L, const float *x,
+                 const float *norm_w, float eps, float *y, int accumulate, int variant, int threads,
+                 cudaStream_t s) {
+    const uint8_t *st[MAXQ];
+    if (nstg < 1 || ng < 1 || nstg * ng > MAXQ) return set_error("%d stages x %d groups exceeds %d streams", nstg, ng, MAXQ);
+    for (int q = 0; q < nstg * ng; q++) {
+        if (!stages[q]) return set_error("stage %d payload pointer is null", q);
+        st[q] = (const uint8_t *)stages[q];
+    }
+    if (!x || !y) return set_error("gemv needs x and y");
+    FastPlan P;
+    if ((variant == 0 || variant == 3) && fast_plan(st, nstg, ng, L, &P)) {
+        P.args.x = x;
+        P.args.norm_w = norm_w;
+        P.args.eps = eps;
+        P.args.y = y;
+        P.args.accumulate = accumulate;
+        P.args.err = device_error_ptr();
+        return launch_fast(P, nstg, ng, s);
+    }
+    if (variant == 3) return set_error("the DQV3 block kernel does not take this geometry");
+    return launch_generic(st, nstg, ng, L, x, norm_w, eps, y, accumulate, threads, s);
+}
+
+int timed(int iters, double *ms, int (*fn)(void *), void *ctx) {
+    cudaEvent_t a, b;
+    if (cudaEventCreate(&a) != cudaSuccess || cudaEventCreate(&b) != cudaSuccess)
+        return cuda_fail("event create", cudaGetLastError());
+    float best = 1e30f;
+    int rc = 0;
+    for (int it = 0; it < iters && !rc; it++) {
+        cudaEventRecord(a);
+        rc = fn(ctx);
+        cudaEventRecord(b);
+        cudaError_t e = cudaEventSynchronize(b);
+        if (!rc && e != cudaSuccess) rc = cuda_fail("timed launch", e);
+        float t = 0;
+        cudaEventElapsedTime(&t, a, b);
+        if (t < best) best = t;
+    }
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    if (!rc) rc = check_device_error("timed launch");
+    if (ms) *ms = iters > 0 ? best : 0.0;
+    return rc;
+}
+
+}  // namespace
+
+// =================================================================== ABI ===
+extern "C" {
+
+/* decode-gpu.cu:789-798. Legality is the reference's, variant by variant; the
+ * variants are accepted aliases of this build's kernels. */
+int vqg_gemv_ready(int dim, int nc, int rows, int cols, int v3, int variant) {
+    const Layout L = make_layout(dim, nc, rows, cols, v3);
+    switch (variant) {
+        case 3: return blk_ok(L) ? 1 : 0;
+        case 2: return L.dim == 4;
+        case 1: return 1;
+        case 0: return (size_t)L.nc * L.dim * 2 <= smem_optin_max();
+        default: return 0;
+    }
+}
+
+struct GemvCtx {
+    const void *p;
+    Layout L;
+    const float *x;
+    float *y;
+    int variant, threads;
+};
+
+static int gemv_once(void *c) {
+    GemvCtx *g = (GemvCtx *)c;
+    const void *st[1] = {g->p};
+    return vq_gemv_impl(st, 1, 1, g->L, g->x, nullptr, 0.f, g->y, 1, g->variant == 0 ? 0 : g->variant, g->threads,
+                        0);
+}
+
+/* decode-gpu.cu:864-901: timed fused GEMV of one stage, y += W_s x (device pointers). */
+int vqg_gemv_t(const void *payload, int dim, int nc, int rows, int cols, int v3, const float *x, float *y,
+               int variant, int threads, int iters, double *ms) {
+    if (check_geometry(dim, nc, rows, cols, v3)) return -1;
+    if (variant < 0 || variant > 3) return set_error("unknown gemv variant %d", variant);
+    if (variant != 0 && (threads < 32 || threads > 1024 || threads % 32))
+        return set_error("gemv launch width %d is not a warp multiple up to 1024", threads);
+    const Layout L = make_layout(dim, nc, rows, cols, v3);
+    if (variant == 3 && !blk_ok(L)) return set_error("the DQV3 block kernel does not take this geometry");
+    GemvCtx c = {payload, L, x, y, variant, variant == 0 ? 256 : threads};
+    return timed(iters, ms, gemv_once, &c);
+}
+
+/* decode-gpu.cu:903-906 */
+int vqg_gemv(const void *payload, int dim, int nc, int rows, int cols, int v3, const float *x, float *y, int variant,
+             int iters, double *ms) {
+    return vqg_gemv_t(payload, dim, nc, rows, cols, v3, x, y, variant, 256, iters, ms);
+}
+
+/* decode-gpu.cu:911-916: one launch, no timing, no synchronization. */
+int vqg_gemv_launch_t(const void *payload, int dim, int nc, int rows, int cols, int v3, const float *x, float *y,
+                      int variant, int threads) {
+    if (check_geometry(dim, nc, rows, cols, v3)) return -1;
+    if (threads < 32 || threads > 1024 || threads % 32)
+        return set_error("gemv launch width %d is not a warp multiple up to 1024", threads);
+    if (variant < 0 || variant > 3) return set_error("unknown gemv variant %d", variant);
+    const Layout L = make_layout(dim, nc, rows, cols, v3);
+    const void *st[1] = {payload};
+    return vq_gemv_impl(st, 1, 1, L, x, nullptr, 0.f, y, 1, variant, threads, 0);
+}
+
+/* decode-gpu.cu:918-922 */
+int vqg_gemv_launch(const void *payload, int dim, int nc, int rows, int cols, int v3, const float *x, float *y,
+                    int variant) {
+    return vqg_gemv_launch_t(payload, dim, nc, rows, cols, v3, x, y, variant, 256);
+}
+
+struct DqCtx {
+    const void *p;
+    Layout L;
+    float *out;
+};
+
+static int dequant_once(void *c) {
+    DqCtx *d = (DqCtx *)c;
+    const int threads = 256;
+    const int blocks = (int)((d->L.nidx + threads - 1) / threads);
+    vq_dequant_kernel<<<blocks, threads>>>((const uint8_t *)d->p, d->L, d->out, device_error_ptr());
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_fail("dequant launch", e);
+}
+
+/* decode-gpu.cu:834-858: out += decoded stage (bit-exact), optionally timed. */
+int vqg_dequant(const void *payload, int dim, int nc, int rows, int cols, int v3, float *out, int iters, double *ms) {
+    if (check_geometry(dim, nc, rows, cols, v3)) return -1;
+    DqCtx c = {payload, make_layout(dim, nc, rows, cols, v3), out};
+    return timed(iters, ms, dequant_once, &c);
+}
+
+/* decode-gpu.cu:947-956 */
+int vqg_row_dequant(const void *payload, int dim, int nc, int rows, int cols, int v3, int row, float *out) {
+    if (check_geometry(dim, nc, rows, cols, v3)) return -1;
+    const Layout L = make_layout(dim, nc, rows, cols, v3);
+    if (row < 0 || row >= L.rows) return set_error("row %d is outside %d", row, L.rows);
+    const int threads = 256;
+    const int blocks = (int)((L.nidx_row + threads - 1) / threads);
+    vq_row_dequant_kernel<<<blocks, threads>>>((const uint8_t *)payload, L, row, out);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_fail("row dequant launch", e);
+}
+
+struct F32Ctx {
+    const float *w, *x;
+    float *y;
+    int rows, cols;
+};
+
+static int f32_once(void *c) {
+    F32Ctx *f = (F32Ctx *)c;
+    const int threads = 256;
+    gemv_f32_kernel<<<(f->rows * 32 + threads - 1) / threads, threads>>>(f->w, f->x, f->y, f->rows, f->cols);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_fail("gemv f32 launch", e);
+}
+
+/* decode-gpu.cu:1120-1138: y += W x for an expanded f32 matrix, timed. */
+int vqg_gemv_f32(const float *w, const float *x, float *y, int rows, int cols, int iters, double *ms) {
+    if (rows <= 0 || cols <= 0) return set_error("gemv f32 needs a non-empty matrix");
+    F32Ctx c = {w, x, y, rows, cols};
+    return timed(iters, ms, f32_once, &c);
+}
+
+/* New: all stages of a container (and optionally a second, paired container)
+ * in one pass, on a caller stream.
+ *   ng 1: y = (accumulate ? y : 0) + sum_s gain_s * W_s x
+ *   ng 2: y = gelu_erf(W_gate x) * (W_up x); stages = {gate_0..gate_n, up_0..up_n}
+ * norm_w (optional) folds RMSNorm(x) with eps into the load of x. */
+int spk_vq_gemv(const void *const *stages, int nstages, int ngroups, int dim, int nc, int rows, int cols, int v3,
+                const float *x, const float *norm_w, float eps, float *y, int accumulate, void *stream) {
+    if (check_geometry(dim, nc, rows, cols, v3)) return -1;
+    if (ngroups == 2 && accumulate) return set_error("the paired gate/up form writes its output, it cannot accumulate");
+    const Layout L = make_layout(dim, nc, rows, cols, v3);
+    return vq_gemv_impl(stages, nstages, ngroups, L, x, norm_w, eps, y, accumulate, 0, 256, (cudaStream_t)stream);
+}
+
+/* Which kernel spk_vq_gemv would run: 1 = the persistent TMA kernel, 0 = generic. */
+int spk_vq_gemv_fast_ok(int nstages, int ngroups, int dim, int nc, int rows, int cols, int v3) {
+    if (dim <= 0 || nc <= 0 || rows <= 0 || cols <= 0) return 0;
+    const Layout L = make_layout(dim, nc, rows, cols, v3);
+    const uint8_t *st[MAXQ] = {nullptr};
+    for (int q = 0; q < MAXQ; q++) st[q] = (const uint8_t *)(uintptr_t)256;
+    FastPlan P;
+    return fast_plan(st, nstages, ngroups, L, &P) ? 1 : 0;
+}
+
+/* Bit-exact stage decode on a stream: out += decoded stage. */
+int spk_vq_dequant(const void *payload, int dim, int nc, int rows, int cols, int v3, float *out, void *stream) {
+    if (check_geometry(dim, nc, rows, cols, v3)) return -1;
+    const Layout L = make_layout(dim, nc, rows, cols, v3);
+    const int threads = 256;
+    const int blocks = (int)((L.nidx + threads - 1) / threads);
+    vq_dequant_kernel<<<blocks, threads, 0, (cudaStream_t)stream>>>((const uint8_t *)payload, L, out,
+                                                                   device_error_ptr());
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_fail("dequant launch", e);
+}
+
+}  // extern "C"
