@@ -124,6 +124,58 @@ int spk_q80_dequant(const void *w, size_t nblocks, float *out, void *stream);
  * int *token when token != NULL (replaces the embedding row of vq-model-gpu.cu:783-788). */
 int spk_q80_row(const void *w, int rows, int cols, int row, const int *token, float *out, void *stream);
 
+/* --------------------------------------------------- decode step (model) ---
+ * The model-level ABI the Rust host side (tools/vq-runtime/src/model.rs Model)
+ * needs: forward(token, pos) -> logits / next id, rollback, reset. Weights are
+ * borrowed device pointers (the caller keeps them alive); the model owns its
+ * KV cache and scratch. */
+
+/* tools/vq-runtime/src/config.rs:16-30, plus the cache capacity and dtype. */
+typedef struct {
+    int hidden, layers, heads, kv_heads, head_dim, inter, vocab, window;
+    float eps;
+    float rope_theta_full, rope_partial_full, rope_theta_slide, rope_partial_slide;
+    const int *full;   /* host array [layers]: 1 = full attention, 0 = sliding window */
+    int max_ctx;       /* cache capacity in positions */
+    int kv_f16;        /* 0: f32 K/V (the reference runtimes' cache), 1: f16 K/V */
+} spk_model_config;
+
+/* One VQ matrix: the device pointers of its stage payloads (each with >= 8 zeroed
+ * slack bytes) and their geometry, as load_mat parses it (vq-model-gpu.cu:230-328). */
+typedef struct {
+    const void *stages[4];
+    int nstages, dim, nc, rows, cols, v3;
+} spk_vq_matrix;
+
+typedef struct spk_model spk_model;
+
+/* Model::new (model.rs:294-320). stream: the cudaStream_t every launch goes to. */
+spk_model *spk_model_create(const spk_model_config *cfg, void *stream);
+void spk_model_destroy(spk_model *m);
+/* Weights::load per layer (model.rs:130-187): q_k_v_proj, g_proj, out_proj,
+ * gate_proj, up_proj, down_proj and the two norms (device f32 [hidden]). */
+int spk_model_set_layer(spk_model *m, int layer, const spk_vq_matrix *qkv, const spk_vq_matrix *attn_gate,
+                        const spk_vq_matrix *out, const spk_vq_matrix *gate, const spk_vq_matrix *up,
+                        const spk_vq_matrix *down, const float *in_norm, const float *post_norm);
+/* Tied embedding / LM head as Q8_0 blocks [vocab][hidden] and model.norm.weight. */
+int spk_model_set_head(spk_model *m, const void *embed_q80, const float *final_norm);
+/* Model::forward (model.rs:442-591) + Model::argmax (594-604) through HOST buffers:
+ * logits_host (may be NULL) receives vocab f32, *next_host the greedy id. Synchronizes. */
+int spk_model_forward(spk_model *m, int token, int pos, float *logits_host, int *next_host);
+/* Device-resident greedy loop: set the start (token, pos) and a device int buffer
+ * for the generated ids; spk_model_run then replays the captured step `steps` times
+ * with no host round trip (asynchronous on the model's stream). */
+int spk_model_begin(spk_model *m, int token, int pos, int *ids_dev, int ids_cap);
+int spk_model_run(spk_model *m, int steps);
+/* Device pointer to the last step's logits [vocab]. */
+const float *spk_model_logits(spk_model *m);
+/* Model::rollback (model.rs:361-382) and Model::reset (384-396). */
+int spk_model_rollback(spk_model *m, int pos);
+int spk_model_reset(spk_model *m);
+/* Positions cached; and the host-side length bump after spk_model_run. */
+int spk_model_len(spk_model *m);
+int spk_model_advance_len(spk_model *m, int n);
+
 #ifdef __cplusplus
 }
 #endif

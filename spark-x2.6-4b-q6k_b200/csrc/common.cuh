@@ -74,6 +74,10 @@ inline bool v3_width_ok(int nc) {
 int sm_count();
 size_t smem_optin_max();
 
+// Q8_0 head (logits + argmax) with caller-owned scratch (ggml.cu).
+int q80_head_launch(const void *w, int rows, int cols, const float *x, const float *norm_w, float eps, float *logits,
+                    int *argmax_out, unsigned long long *partial, unsigned int *counter, cudaStream_t s);
+
 // ------------------------------------------------------ device helpers ---
 #define SPK_WAIT_LIMIT (1u << 26)
 
@@ -109,6 +113,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
         : "r"(smem_u32(bar)), "r"(parity)
         : "memory");
     return ok != 0;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 // Bounded wait: returns false (and records DEV_WAIT_TIMEOUT) if the phase never

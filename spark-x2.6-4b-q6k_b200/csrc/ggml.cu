@@ -16,6 +16,7 @@
 // per operand, in ggml's order).
 #include "common.cuh"
 #include "spk.h"
+#include "stream.cuh"
 
 using namespace spk;
 
@@ -238,6 +239,301 @@ __global__ void q80_row_kernel(const uint8_t *w, int rows, int cols, const int *
     out[c] = __fmul_rn((float)(int8_t)blk[2 + (c & 31)], d);
 }
 
+// ============================================================ fast path ===
+// Persistent CTAs (one per SM), each owning a contiguous row range. Tiles of
+// block rows arrive by TMA (stream.cuh) in a 3-deep ring. A unit is 16
+// weights (Q6_K: one half-block lane quad) or 8 weights (Q8_0: a quarter
+// block); lane l of a warp takes units chunk + l + 32k, so the 32 lanes of one
+// shared-memory load read neighbouring bytes, and every lane's columns are the
+// same for every row: its activations live in registers.
+constexpr int GF_WARPS = 16;
+constexpr int GF_THREADS = GF_WARPS * 32;
+constexpr int GF_NBUF = 3;
+
+template <int FMT>
+struct GFmt;
+template <>
+struct GFmt<0> {   // Q6_K
+    static constexpr int BB = 210, WPB = 256, UPB = 16, WPU = 16, UMAX = 5;
+};
+template <>
+struct GFmt<1> {   // Q8_0
+    static constexpr int BB = 34, WPB = 32, UPB = 4, WPU = 8, UMAX = 10;
+};
+
+struct GFArgs {
+    const uint8_t *w;
+    int rows, cols;
+    const float *x;
+    const float *norm_w;
+    float eps;
+    float *y;
+    int accumulate;
+    int ks, tr;
+    uint32_t rb_bytes, slot_bytes;
+    unsigned long long *partial;   // head only
+    unsigned int *counter;
+    int *argmax_out;
+    int *err;
+};
+
+// A 32-bit little-endian word at a 2-byte aligned shared-memory address.
+__device__ __forceinline__ uint32_t lds_a2(const uint8_t *p) {
+    const uint32_t *w = reinterpret_cast<const uint32_t *>((uintptr_t)p & ~(uintptr_t)3);
+    return __funnelshift_r(w[0], w[1], (uint32_t)((uintptr_t)p & 2) * 8u);
+}
+
+// Exact integer value of byte e of v minus `bias`, via 0x4B0000bb == 2^23 + bb.
+__device__ __forceinline__ float byte_val(uint32_t v, int e, float bias) {
+    return __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7440u | (uint32_t)e)) - bias;
+}
+
+template <int FMT>
+__device__ __forceinline__ int unit_col(int u, int i) {
+    if constexpr (FMT == 0) {
+        const int b = u >> 4, h = (u >> 3) & 1, m = u & 7, j = i >> 2, e = i & 3;
+        return 256 * b + 128 * h + 32 * j + 4 * m + e;
+    }
+    return 8 * u + i;
+}
+
+// Q6_K unit: half h, lane quad m (l = 4m..4m+3), quadrants j = 0..3.
+__device__ __forceinline__ float q6k_unit_s(const uint8_t *row, int u, const float (&xu)[16]) {
+    const int b = u >> 4, h = (u >> 3) & 1, m = u & 7;
+    const uint8_t *blk = row + 210 * b;
+    const uint32_t qa = lds_a2(blk + 64 * h + 4 * m);
+    const uint32_t qb = lds_a2(blk + 64 * h + 32 + 4 * m);
+    const uint32_t qh = lds_a2(blk + 128 + 32 * h + 4 * m);
+    const uint8_t *S = blk + 192 + 8 * h + (m >> 2);
+    const uint8_t *S2 = reinterpret_cast<const uint8_t *>((uintptr_t)S & ~(uintptr_t)1);
+    const int o = (int)((uintptr_t)S & 1);
+    const uint32_t slo = lds_a2(S2) ^ 0x80808080u, shi = lds_a2(S2 + 4) ^ 0x80808080u;
+    const float d = h2f_bits(*reinterpret_cast<const uint16_t *>(blk + 208));
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const uint32_t lo = ((j & 1) ? qb : qa) >> ((j & 2) ? 4 : 0);
+        const uint32_t q = (lo & 0x0F0F0F0Fu) | (((qh >> (2 * j)) & 0x03030303u) << 4);
+        float s = 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; e++) s = fmaf(byte_val(q, e, 8388640.0f), xu[4 * j + e], s);   // q - 32
+        const int sb = o + 2 * j;                                   // scale byte in the window
+        const uint32_t sw = sb < 4 ? slo : shi;
+        const float sc = __uint_as_float(__byte_perm(sw, 0x4B000000u, 0x7440u | (uint32_t)(sb & 3))) - 8388736.0f;
+        acc = fmaf(d * sc, s, acc);
+    }
+    return acc;
+}
+
+// Q8_0 unit: quarter k of block b.
+__device__ __forceinline__ float q80_unit_s(const uint8_t *row, int u, const float (&xu)[8]) {
+    const uint8_t *blk = row + 34 * (u >> 2);
+    const int k = u & 3;
+    const float d = h2f_bits(*reinterpret_cast<const uint16_t *>(blk));
+    const uint32_t w0 = lds_a2(blk + 2 + 8 * k) ^ 0x80808080u, w1 = lds_a2(blk + 6 + 8 * k) ^ 0x80808080u;
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        s0 = fmaf(byte_val(w0, e, 8388736.0f), xu[e], s0);
+        s1 = fmaf(byte_val(w1, e, 8388736.0f), xu[4 + e], s1);
+    }
+    return d * (s0 + s1);
+}
+
+__device__ __forceinline__ void gf_issue(const GFArgs &a, uint8_t *slot, uint64_t *bar, int r0, int nr) {
+    BulkList bl;
+    bl.n = 0;
+    bl.tx = 0;
+    const uintptr_t A = (uintptr_t)(a.w + (size_t)r0 * a.rb_bytes);
+    const uintptr_t limit = (uintptr_t)(a.w + (size_t)a.rows * a.rb_bytes);   // no slack promised
+    bulk_plan(bl, slot, A, A + (size_t)nr * a.rb_bytes, limit);
+    bulk_issue(bl, bar);
+}
+
+template <int FMT, int U, int HEAD>
+__global__ void __launch_bounds__(GF_THREADS, 1) blk_fast_kernel(const GFArgs a) {
+    using Fm = GFmt<FMT>;
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint8_t *ring = smem;
+    uint64_t *full = reinterpret_cast<uint64_t *>(ring + (size_t)GF_NBUF * a.slot_bytes);
+    float *part = reinterpret_cast<float *>(full + GF_NBUF);   // [2][tr][ks]
+    double *red = reinterpret_cast<double *>(part + 2 * a.tr * a.ks);
+    unsigned long long *bw = reinterpret_cast<unsigned long long *>(red + 32);
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int ks_n = a.ks, tr = a.tr, ks = warp % ks_n, rw = warp / ks_n;
+    const int G = gridDim.x;
+    const int rb = (int)(((long long)blockIdx.x * a.rows) / G), re = (int)(((long long)(blockIdx.x + 1) * a.rows) / G);
+    const int ntile = (re - rb + tr - 1) / tr;
+
+    if (tid == 0) {
+        for (int b = 0; b < GF_NBUF; b++) mbar_init(&full[b], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (tid == 0)
+        for (int t = 0; t < GF_NBUF - 1 && t < ntile; t++) {
+            const int r0 = rb + t * tr;
+            gf_issue(a, ring + (size_t)t * a.slot_bytes, &full[t], r0, min(tr, re - r0));
+        }
+    float inv = 1.0f;
+    if (a.norm_w) inv = block_rms_inv(a.x, a.cols, a.eps, red);
+    float xr[U][Fm::WPU];
+    const int u0 = ks * 32 * U + lane;
+#pragma unroll
+    for (int k = 0; k < U; k++)
+#pragma unroll
+        for (int i = 0; i < Fm::WPU; i++) {
+            const int c = unit_col<FMT>(u0 + 32 * k, i);
+            float v = a.x[c];
+            if (a.norm_w) v = __fmul_rn(__fmul_rn(v, inv), a.norm_w[c]);
+            xr[k][i] = v;
+        }
+    unsigned long long best = pack_vi(-INFINITY, 0);
+
+    for (int t = 0; t < ntile; t++) {
+        const int slot = t % GF_NBUF;
+        if (tid == 0 && t + GF_NBUF - 1 < ntile) {
+            const int tn = t + GF_NBUF - 1, r0n = rb + tn * tr;
+            gf_issue(a, ring + (size_t)(tn % GF_NBUF) * a.slot_bytes, &full[tn % GF_NBUF], r0n, min(tr, re - r0n));
+        }
+        const int r0 = rb + t * tr, nr = min(tr, re - r0);
+        if (!mbar_wait(&full[slot], (uint32_t)((t / GF_NBUF) & 1), a.err)) return;
+        float *pt = part + (size_t)(t & 1) * tr * ks_n;
+        if (rw < nr) {
+            const uintptr_t A = (uintptr_t)(a.w + (size_t)r0 * a.rb_bytes);
+            const uint8_t *row = ring + (size_t)slot * a.slot_bytes + (A & 15) + (size_t)rw * a.rb_bytes;
+            float acc = 0.f;
+#pragma unroll
+            for (int k = 0; k < U; k++) {
+                if constexpr (FMT == 0)
+                    acc += q6k_unit_s(row, u0 + 32 * k, reinterpret_cast<const float(&)[16]>(xr[k]));
+                else
+                    acc += q80_unit_s(row, u0 + 32 * k, reinterpret_cast<const float(&)[8]>(xr[k]));
+            }
+            acc = warp_sum(acc);
+            if (lane == 0) pt[rw * ks_n + ks] = acc;
+        }
+        __syncthreads();
+        if (tid < nr) {
+            const int r = r0 + tid;
+            float v = 0.f;
+            for (int k = 0; k < ks_n; k++) v += pt[tid * ks_n + k];
+            const float o = (a.accumulate ? a.y[r] : 0.0f) + v;
+            a.y[r] = o;
+            if (HEAD) {
+                const unsigned long long c = pack_vi(o, r);
+                best = c > best ? c : best;
+            }
+        }
+    }
+    if (HEAD) {
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const unsigned long long o = __shfl_xor_sync(0xffffffffu, best, off);
+            best = o > best ? o : best;
+        }
+        if (lane == 0) bw[warp] = best;
+        __syncthreads();
+        if (tid == 0) {
+            unsigned long long m = bw[0];
+            for (int k = 1; k < GF_WARPS; k++) m = bw[k] > m ? bw[k] : m;
+            a.partial[blockIdx.x] = m;
+            __threadfence();
+            const bool last = atomicAdd(a.counter, 1u) == gridDim.x - 1;
+            if (last) {
+                __threadfence();
+                unsigned long long mm = 0;
+                for (int k = 0; k < (int)gridDim.x; k++) {
+                    const unsigned long long v = ((volatile unsigned long long *)a.partial)[k];
+                    mm = v > mm ? v : mm;
+                }
+                *a.argmax_out = (int)(0xFFFFFFFFu - (uint32_t)(mm & 0xFFFFFFFFull));
+                *a.counter = 0;
+            }
+        }
+    }
+}
+
+struct GFPlan {
+    int U;
+    size_t smem;
+    GFArgs a;
+};
+
+// The fast path needs whole lane runs of units: units per row divisible by 32*ks
+// with U = units/(32 ks) one of the instantiated widths.
+bool gf_plan(int fmt, const void *w, int rows, int cols, GFPlan *P) {
+    const int wpb = fmt == 0 ? 256 : 32, upb = fmt == 0 ? 16 : 4, bb = fmt == 0 ? 210 : 34;
+    const int umax = fmt == 0 ? 5 : 10;
+    const long nu = (long)(cols / wpb) * upb;
+    int ks = 0, U = 0;
+    for (int k = 1; k <= 16; k *= 2) {
+        if (nu % (32 * k)) continue;
+        const int u = (int)(nu / (32 * k));
+        const bool ok = fmt == 0 ? (u == 1 || u == 2 || u == 4 || u == 5)
+                                 : (u == 1 || u == 2 || u == 4 || u == 5 || u == 8 || u == 10);
+        if (ok && u <= umax) {
+            ks = k;
+            U = u;
+            break;
+        }
+    }
+    if (!ks) return false;
+    GFArgs &a = P->a;
+    memset(&a, 0, sizeof a);
+    a.w = (const uint8_t *)w;
+    a.rows = rows;
+    a.cols = cols;
+    a.ks = ks;
+    a.tr = GF_WARPS / ks;
+    a.rb_bytes = (uint32_t)((cols / wpb) * bb);
+    a.slot_bytes = (uint32_t)(((size_t)a.tr * a.rb_bytes + 32 + 15) & ~(size_t)15);
+    P->U = U;
+    P->smem = (size_t)GF_NBUF * a.slot_bytes + GF_NBUF * 8 + (size_t)2 * a.tr * ks * 4 + 32 * 8 + GF_WARPS * 8;
+    return P->smem <= smem_optin_max();
+}
+
+template <int FMT, int U, int HEAD>
+int gf_launch_t(const GFPlan &P, cudaStream_t s) {
+    auto k = blk_fast_kernel<FMT, U, HEAD>;
+    static size_t opted[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (P.smem > opted[dev & 63]) {
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P.smem);
+        if (e != cudaSuccess) return cuda_fail("ggml fast kernel shared-memory opt-in", e);
+        opted[dev & 63] = P.smem;
+    }
+    const int ntr = (P.a.rows + P.a.tr - 1) / P.a.tr;
+    const int grid = ntr < sm_count() ? ntr : sm_count();
+    k<<<grid, GF_THREADS, P.smem, s>>>(P.a);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_fail("ggml fast kernel launch", e);
+}
+
+template <int HEAD>
+int gf_launch(int fmt, const GFPlan &P, cudaStream_t s) {
+    if (fmt == 0) {
+        switch (P.U) {
+            case 1: return gf_launch_t<0, 1, HEAD>(P, s);
+            case 2: return gf_launch_t<0, 2, HEAD>(P, s);
+            case 4: return gf_launch_t<0, 4, HEAD>(P, s);
+            case 5: return gf_launch_t<0, 5, HEAD>(P, s);
+        }
+    } else {
+        switch (P.U) {
+            case 1: return gf_launch_t<1, 1, HEAD>(P, s);
+            case 2: return gf_launch_t<1, 2, HEAD>(P, s);
+            case 4: return gf_launch_t<1, 4, HEAD>(P, s);
+            case 5: return gf_launch_t<1, 5, HEAD>(P, s);
+            case 8: return gf_launch_t<1, 8, HEAD>(P, s);
+            case 10: return gf_launch_t<1, 10, HEAD>(P, s);
+        }
+    }
+    return set_error("ggml fast kernel: no instantiation for U=%d", P.U);
+}
+
 int check_blocks(const void *w, int rows, int cols, int wpb) {
     if (!w) return set_error("weight pointer is null");
     if (rows <= 0 || cols <= 0) return set_error("gemv needs a non-empty matrix");
@@ -269,6 +565,16 @@ extern "C" {
 int spk_q6k_gemv(const void *w, int rows, int cols, const float *x, const float *norm_w, float eps, float *y,
                  int accumulate, void *stream) {
     if (check_blocks(w, rows, cols, 256)) return -1;
+    GFPlan P;
+    if (gf_plan(0, w, rows, cols, &P)) {
+        P.a.x = x;
+        P.a.norm_w = norm_w;
+        P.a.eps = eps;
+        P.a.y = y;
+        P.a.accumulate = accumulate;
+        P.a.err = device_error_ptr();
+        return gf_launch<0>(0, P, (cudaStream_t)stream);
+    }
     BlkArgs a = {(const uint8_t *)w, rows, cols, x, norm_w, eps, y, accumulate};
     return launch_blk(true, a, (cudaStream_t)stream);
 }
@@ -277,6 +583,16 @@ int spk_q6k_gemv(const void *w, int rows, int cols, const float *x, const float 
 int spk_q80_gemv(const void *w, int rows, int cols, const float *x, const float *norm_w, float eps, float *y,
                  int accumulate, void *stream) {
     if (check_blocks(w, rows, cols, 32)) return -1;
+    GFPlan P;
+    if (gf_plan(1, w, rows, cols, &P)) {
+        P.a.x = x;
+        P.a.norm_w = norm_w;
+        P.a.eps = eps;
+        P.a.y = y;
+        P.a.accumulate = accumulate;
+        P.a.err = device_error_ptr();
+        return gf_launch<0>(1, P, (cudaStream_t)stream);
+    }
     BlkArgs a = {(const uint8_t *)w, rows, cols, x, norm_w, eps, y, accumulate};
     return launch_blk(false, a, (cudaStream_t)stream);
 }
@@ -299,6 +615,19 @@ int spk_q80_head(const void *w, int rows, int cols, const float *x, const float 
         g_head_counter[dev & 63] = (unsigned int *)c;
         g_head_partial[dev & 63] = (unsigned long long *)p;
     }
+    GFPlan P;
+    if (gf_plan(1, w, rows, cols, &P)) {
+        P.a.x = x;
+        P.a.norm_w = norm_w;
+        P.a.eps = eps;
+        P.a.y = logits;
+        P.a.accumulate = 0;
+        P.a.partial = g_head_partial[dev & 63];
+        P.a.counter = g_head_counter[dev & 63];
+        P.a.argmax_out = argmax_out;
+        P.a.err = device_error_ptr();
+        return gf_launch<1>(1, P, (cudaStream_t)stream);
+    }
     HeadArgs a;
     a.b = {(const uint8_t *)w, rows, cols, x, norm_w, eps, logits, 0};
     a.partial = g_head_partial[dev & 63];
@@ -308,6 +637,40 @@ int spk_q80_head(const void *w, int rows, int cols, const float *x, const float 
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? 0 : cuda_fail("q8_0 head launch", e);
 }
+
+}  // extern "C"
+
+namespace spk {
+// The head with caller-owned scratch (partial: >= sm_count() entries, counter
+// zeroed once), for callers that capture it in a graph.
+int q80_head_launch(const void *w, int rows, int cols, const float *x, const float *norm_w, float eps, float *logits,
+                    int *argmax_out, unsigned long long *partial, unsigned int *counter, cudaStream_t s) {
+    if (check_blocks(w, rows, cols, 32)) return -1;
+    GFPlan P;
+    if (gf_plan(1, w, rows, cols, &P)) {
+        P.a.x = x;
+        P.a.norm_w = norm_w;
+        P.a.eps = eps;
+        P.a.y = logits;
+        P.a.accumulate = 0;
+        P.a.partial = partial;
+        P.a.counter = counter;
+        P.a.argmax_out = argmax_out;
+        P.a.err = device_error_ptr();
+        return gf_launch<1>(1, P, s);
+    }
+    HeadArgs a;
+    a.b = {(const uint8_t *)w, rows, cols, x, norm_w, eps, logits, 0};
+    a.partial = partial;
+    a.counter = counter;
+    a.argmax_out = argmax_out;
+    q80_head_kernel<<<2 * sm_count() < 1024 ? 2 * sm_count() : 1024, 256, 0, s>>>(a);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_fail("q8_0 head launch", e);
+}
+}  // namespace spk
+
+extern "C" {
 
 /* Bit-exact block decode into f32 (nblocks * 256 or * 32 values). */
 int spk_q6k_dequant(const void *w, size_t nblocks, float *out, void *stream) {

@@ -1,0 +1,587 @@
+// model.cu — the batch-1 decode step of the Spark2_5 decoder on B200, and its C-ABI.
+//
+// What it computes is tools/vq-runtime/src/model.rs:442-591 (Model::forward):
+//   h = embed[token]
+//   per layer:  xn = rmsnorm(h); qkv = W_qkv xn; g = W_g xn; rope(q, k); kv[pos] = (k, v)
+//               a_h = softmax(q_h K^T / sqrt(hd)) V * sigmoid(g_h)   (GQA, sliding or full)
+//               h += W_out a;  xn = rmsnorm(h);  h += W_down (gelu_erf(W_gate xn) * W_up xn)
+//   logits = W_embed rmsnorm(h); next = argmax(logits)
+// The launches per layer (the reference issues ~218 launches and one host sync
+// per token, vq-model-gpu.cu:776-835):
+//   1. QKV GEMV with the RMSNorm prologue              (vq.cu, persistent TMA kernel)
+//   2. g_proj GEMV with the RMSNorm prologue
+//   3. attention partials: rope, KV store, split-K flash-decode over the cache
+//   4. attention combine: merge the splits, sigmoid gate
+//   5. out_proj GEMV accumulating into h
+//   6. gate+up GEMV pair with RMSNorm prologue and erf-GELU(gate)*up epilogue
+//   7. down GEMV accumulating into h
+// then the tied Q8_0 head with fused argmax (ggml.cu) and a one-thread advance
+// kernel (pos += 1, token = argmax). Token and position live in device memory,
+// so the whole step is captured once in a CUDA graph and replayed per token.
+#include <math.h>
+#include <stdlib.h>
+
+#include <vector>
+
+#include "common.cuh"
+#include "spk.h"
+
+using namespace spk;
+
+namespace {
+
+constexpr int ATT_THREADS = 256;
+constexpr int ATT_WARPS = ATT_THREADS / 32;
+constexpr int MAX_GROUP = 4;   // q heads per kv head handled by one CTA
+
+struct AttnArgs {
+    const float *qkv;          // [q_dim + 2 kv_dim] this token's projections (pre-rope)
+    void *kc, *vc;             // this layer's caches: [kv_heads][slots][hd], f32 or f16
+    int kv_f16;
+    int slots;                 // ctx (full layer) or window (sliding layer, a ring)
+    int full, window;
+    const float *freq;         // [pdim/2] rope frequencies of this layer type (model.rs:416-429)
+    int pdim;
+    int heads, kv_heads, hd;
+    const int *pos;            // device position of this token
+    int nsplit;                // grid.y: sequence splits
+    float *part;               // [kv_heads][nsplit][group][hd + 2]: o, m, l
+};
+
+__device__ __forceinline__ float kv_load(const void *base, int kv_f16, size_t idx) {
+    return kv_f16 ? __half2float(reinterpret_cast<const __half *>(base)[idx]) : reinterpret_cast<const float *>(base)[idx];
+}
+
+// NeoX rotate-half on the first pdim elements of x (shared memory), model.rs:431-439:
+//   x[i] = a cos - b sin ; x[i+half] = b cos + a sin, each product rounded.
+__device__ void rope_smem(float *x, const float *freq, int pdim, int pos) {
+    const int half = pdim / 2;
+    for (int i = threadIdx.x; i < half; i += blockDim.x) {
+        const float ang = __fmul_rn((float)pos, freq[i]);
+        const float c = cosf(ang), s = sinf(ang);
+        const float a = x[i], b = x[i + half];
+        x[i] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+        x[i + half] = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
+    }
+}
+
+// One CTA = one kv head x one split of the visible positions, for all the q
+// heads of its GQA group (their K/V reads are shared). Per position a warp
+// reads one K row (lane d-slice), forms the group's scores with a butterfly
+// sum, and keeps an online softmax; warps are merged at the end.
+template <int HD>
+__global__ void __launch_bounds__(ATT_THREADS) attn_partial_kernel(const AttnArgs a) {
+    constexpr int DPL = HD / 32;   // dims per lane
+    __shared__ float qs[MAX_GROUP][HD];
+    __shared__ float kn[HD], vn[HD];
+    __shared__ float wm[ATT_WARPS][MAX_GROUP], wl[ATT_WARPS][MAX_GROUP];
+    __shared__ float wo[ATT_WARPS][MAX_GROUP][HD];
+    const int kvh = blockIdx.x, split = blockIdx.y;
+    const int G = a.heads / a.kv_heads;
+    const int qd = a.heads * HD, kvd = a.kv_heads * HD;
+    const int pos = *a.pos;
+    const int start = a.full ? 0 : max(0, pos + 1 - a.window);
+    const int n = pos + 1 - start;
+    const int csz = max((n + a.nsplit - 1) / a.nsplit, 16);
+    const int c0 = start + split * csz, c1 = min(pos + 1, c0 + csz);
+    float *out = a.part + ((size_t)kvh * a.nsplit + split) * G * (HD + 2);
+
+    for (int i = threadIdx.x; i < G * HD; i += blockDim.x) qs[i / HD][i % HD] = a.qkv[(size_t)(kvh * G + i / HD) * HD + i % HD];
+    for (int i = threadIdx.x; i < HD; i += blockDim.x) {
+        kn[i] = a.qkv[qd + (size_t)kvh * HD + i];
+        vn[i] = a.qkv[qd + kvd + (size_t)kvh * HD + i];
+    }
+    __syncthreads();
+    for (int h = 0; h < G; h++) rope_smem(qs[h], a.freq, a.pdim, pos);
+    rope_smem(kn, a.freq, a.pdim, pos);
+    __syncthreads();
+    // The split that owns `pos` writes the new row; nobody else reads that slot now.
+    const int wslot = a.full ? pos : pos % a.window;
+    if (c0 <= pos && pos < c1) {
+        for (int i = threadIdx.x; i < HD; i += blockDim.x) {
+            const size_t o = ((size_t)kvh * a.slots + wslot) * HD + i;
+            if (a.kv_f16) {
+                reinterpret_cast<__half *>(a.kc)[o] = __float2half_rn(kn[i]);
+                reinterpret_cast<__half *>(a.vc)[o] = __float2half_rn(vn[i]);
+            } else {
+                reinterpret_cast<float *>(a.kc)[o] = kn[i];
+                reinterpret_cast<float *>(a.vc)[o] = vn[i];
+            }
+        }
+    }
+    if (c0 >= c1) {   // an empty split: nothing to merge
+        if (threadIdx.x < G) {
+            out[threadIdx.x * (HD + 2) + HD] = -INFINITY;
+            out[threadIdx.x * (HD + 2) + HD + 1] = 0.f;
+        }
+        return;
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float q[MAX_GROUP][DPL], o[MAX_GROUP][DPL], m[MAX_GROUP], l[MAX_GROUP];
+    const float scale = 1.0f / sqrtf((float)HD);
+#pragma unroll
+    for (int h = 0; h < MAX_GROUP; h++) {
+        m[h] = -INFINITY;
+        l[h] = 0.f;
+#pragma unroll
+        for (int d = 0; d < DPL; d++) {
+            q[h][d] = h < G ? qs[h][lane * DPL + d] : 0.f;
+            o[h][d] = 0.f;
+        }
+    }
+    for (int j = c0 + warp; j < c1; j += ATT_WARPS) {
+        float kr[DPL], vr[DPL];
+        if (j == pos) {
+#pragma unroll
+            for (int d = 0; d < DPL; d++) {
+                kr[d] = kn[lane * DPL + d];
+                vr[d] = vn[lane * DPL + d];
+            }
+        } else {
+            const int slot = a.full ? j : j % a.window;
+            const size_t base = ((size_t)kvh * a.slots + slot) * HD + lane * DPL;
+#pragma unroll
+            for (int d = 0; d < DPL; d++) {
+                kr[d] = kv_load(a.kc, a.kv_f16, base + d);
+                vr[d] = kv_load(a.vc, a.kv_f16, base + d);
+            }
+        }
+        float s[MAX_GROUP];
+#pragma unroll
+        for (int h = 0; h < MAX_GROUP; h++) {
+            float t = 0.f;
+#pragma unroll
+            for (int d = 0; d < DPL; d++) t = fmaf(q[h][d], kr[d], t);
+            s[h] = t;
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+            for (int h = 0; h < MAX_GROUP; h++) s[h] += __shfl_xor_sync(0xffffffffu, s[h], off);
+#pragma unroll
+        for (int h = 0; h < MAX_GROUP; h++) {
+            if (h >= G) break;
+            const float sc = s[h] * scale;
+            const float mn = fmaxf(m[h], sc);
+            const float corr = expf(m[h] - mn), p = expf(sc - mn);
+            l[h] = l[h] * corr + p;
+#pragma unroll
+            for (int d = 0; d < DPL; d++) o[h][d] = fmaf(p, vr[d], o[h][d] * corr);
+            m[h] = mn;
+        }
+    }
+    // merge the warps
+    if (lane == 0)
+        for (int h = 0; h < G; h++) {
+            wm[warp][h] = m[h];
+            wl[warp][h] = l[h];
+        }
+    for (int h = 0; h < G; h++)
+#pragma unroll
+        for (int d = 0; d < DPL; d++) wo[warp][h][lane * DPL + d] = o[h][d];
+    __syncthreads();
+    for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
+        const int h = i / HD, d = i % HD;
+        float M = -INFINITY;
+        for (int w = 0; w < ATT_WARPS; w++) M = fmaxf(M, wm[w][h]);
+        float L = 0.f, O = 0.f;
+        for (int w = 0; w < ATT_WARPS; w++) {
+            if (wm[w][h] == -INFINITY) continue;
+            const float e = expf(wm[w][h] - M);
+            L += wl[w][h] * e;
+            O += wo[w][h][d] * e;
+        }
+        out[h * (HD + 2) + d] = O;
+        if (d == 0) {
+            out[h * (HD + 2) + HD] = M;
+            out[h * (HD + 2) + HD + 1] = L;
+        }
+    }
+}
+
+// Merge the splits of every q head and apply the per-head sigmoid gate
+// (model.rs:538-550): attn[h][d] = (sum_c o_c e^{m_c-M}) / (sum_c l_c e^{m_c-M}) * sigmoid(g_h).
+__global__ void attn_combine_kernel(const float *part, int nsplit, int heads, int kv_heads, int hd,
+                                    const float *gate, float *attn) {
+    const int h = blockIdx.x, G = heads / kv_heads, kvh = h / G, gi = h % G;
+    const float *p0 = part + (size_t)kvh * nsplit * G * (hd + 2) + (size_t)gi * (hd + 2);
+    const size_t stride = (size_t)G * (hd + 2);
+    float M = -INFINITY;
+    for (int c = 0; c < nsplit; c++) M = fmaxf(M, p0[c * stride + hd]);
+    float L = 0.f;
+    for (int c = 0; c < nsplit; c++) {
+        const float mc = p0[c * stride + hd];
+        if (mc != -INFINITY) L += p0[c * stride + hd + 1] * expf(mc - M);
+    }
+    const float gsig = 1.0f / (1.0f + expf(-gate[h]));
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+        float O = 0.f;
+        for (int c = 0; c < nsplit; c++) {
+            const float mc = p0[c * stride + hd];
+            if (mc != -INFINITY) O += p0[c * stride + d] * expf(mc - M);
+        }
+        attn[(size_t)h * hd + d] = (O / L) * gsig;
+    }
+}
+
+// End of a step: record the generated id, feed it back as the next token, advance.
+struct DevCtl {
+    int *ids;   // where spk_model_run records generated ids (may be null)
+    int cap;
+};
+
+__global__ void advance_kernel(int *pos, int *token, const int *argmax, const DevCtl *ctl, int *step) {
+    const int s = *step;
+    if (ctl->ids && s < ctl->cap) ctl->ids[s] = *argmax;
+    *token = *argmax;
+    *pos = *pos + 1;
+    *step = s + 1;
+}
+
+__global__ void set_state_kernel(int *pos, int *token, int p, int t) {
+    *pos = p;
+    *token = t;
+}
+
+}  // namespace
+
+// ================================================================ host ===
+struct spk_model {
+    spk_model_config cfg;
+    std::vector<int> full;
+    struct Layer {
+        spk_vq_matrix m[6];   // qkv, attn_gate, out, gate, up, down
+        const float *in_norm = nullptr, *post_norm = nullptr;
+        bool set = false;
+    };
+    std::vector<Layer> layers;
+    const void *embed = nullptr;
+    const float *final_norm = nullptr;
+    int q_dim = 0, kv_dim = 0, G = 0, pdim_full = 0, pdim_slide = 0, nsplit_full = 1, nsplit_slide = 1;
+    float *h = nullptr, *qkv = nullptr, *gate = nullptr, *attn = nullptr, *act = nullptr, *logits = nullptr,
+          *part = nullptr, *freq_full = nullptr, *freq_slide = nullptr;
+    void *kc = nullptr, *vc = nullptr;
+    std::vector<size_t> kv_off;   // per layer element offset into kc / vc
+    std::vector<int> kv_slots;
+    int *state = nullptr;         // device: pos, token, argmax, step
+    DevCtl *ctl = nullptr;        // device: id buffer of spk_model_run
+    DevCtl *host_ctl = nullptr;   // pinned staging for it
+    unsigned long long *head_partial = nullptr;
+    unsigned int *head_counter = nullptr;
+    int *host_io = nullptr;       // pinned: pos, token, argmax
+    cudaStream_t stream = nullptr;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    int eager_steps = 0;
+    int len = 0;                  // positions cached (host view, for rollback checks)
+};
+
+namespace {
+
+int vq_call(const spk_vq_matrix &M, int ngroups, const spk_vq_matrix *M2, const float *x, const float *norm_w,
+            float eps, float *y, int accumulate, cudaStream_t s) {
+    const void *st[8];
+    for (int i = 0; i < M.nstages; i++) st[i] = M.stages[i];
+    if (M2)
+        for (int i = 0; i < M2->nstages; i++) st[M.nstages + i] = M2->stages[i];
+    return spk_vq_gemv(st, M.nstages, ngroups, M.dim, M.nc, M.rows, M.cols, M.v3, x, norm_w, eps, y, accumulate, s);
+}
+
+template <int HD>
+int attn_launch(const AttnArgs &a, cudaStream_t s) {
+    attn_partial_kernel<HD><<<dim3(a.kv_heads, a.nsplit), ATT_THREADS, 0, s>>>(a);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_fail("attention launch", e);
+}
+
+// Enqueue one decode step on m->stream: reads pos/token from m->state.
+int enqueue_step(spk_model *m) {
+    const spk_model_config &c = m->cfg;
+    cudaStream_t s = m->stream;
+    int *pos = m->state, *token = m->state + 1, *amax = m->state + 2;
+    if (spk_q80_row(m->embed, c.vocab, c.hidden, 0, token, m->h, s)) return -1;
+    for (int li = 0; li < c.layers; li++) {
+        const spk_model::Layer &L = m->layers[li];
+        if (vq_call(L.m[0], 1, nullptr, m->h, L.in_norm, c.eps, m->qkv, 0, s)) return -1;
+        if (vq_call(L.m[1], 1, nullptr, m->h, L.in_norm, c.eps, m->gate, 0, s)) return -1;
+        AttnArgs a;
+        a.qkv = m->qkv;
+        const size_t esz = c.kv_f16 ? 2 : 4;
+        a.kc = (uint8_t *)m->kc + m->kv_off[li] * esz;
+        a.vc = (uint8_t *)m->vc + m->kv_off[li] * esz;
+        a.kv_f16 = c.kv_f16;
+        a.slots = m->kv_slots[li];
+        a.full = m->full[li];
+        a.window = c.window;
+        a.freq = a.full ? m->freq_full : m->freq_slide;
+        a.pdim = a.full ? m->pdim_full : m->pdim_slide;
+        a.heads = c.heads;
+        a.kv_heads = c.kv_heads;
+        a.hd = c.head_dim;
+        a.pos = pos;
+        a.nsplit = a.full ? m->nsplit_full : m->nsplit_slide;
+        a.part = m->part;
+        if ((c.head_dim == 256 ? attn_launch<256>(a, s) : attn_launch<128>(a, s))) return -1;
+        attn_combine_kernel<<<c.heads, 128, 0, s>>>(m->part, a.nsplit, c.heads, c.kv_heads, c.head_dim, m->gate,
+                                                    m->attn);
+        if (vq_call(L.m[2], 1, nullptr, m->attn, nullptr, 0.f, m->h, 1, s)) return -1;
+        if (vq_call(L.m[3], 2, &L.m[4], m->h, L.post_norm, c.eps, m->act, 0, s)) return -1;
+        if (vq_call(L.m[5], 1, nullptr, m->act, nullptr, 0.f, m->h, 1, s)) return -1;
+    }
+    if (q80_head_launch(m->embed, c.vocab, c.hidden, m->h, m->final_norm, c.eps, m->logits, amax, m->head_partial,
+                        m->head_counter, s))
+        return -1;
+    advance_kernel<<<1, 1, 0, s>>>(pos, token, amax, m->ctl, m->state + 3);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_fail("decode step launch", e);
+}
+
+bool ready(const spk_model *m) {
+    if (!m->embed || !m->final_norm) return false;
+    for (const auto &L : m->layers)
+        if (!L.set) return false;
+    return true;
+}
+
+// One step: eager for the first one (it also performs every one-time kernel
+// set-up), then from a CUDA graph captured once.
+int run_step(spk_model *m) {
+    if (!ready(m)) return set_error("model weights are not all set");
+    if (m->eager_steps == 0) {
+        m->eager_steps++;
+        return enqueue_step(m);
+    }
+    if (!m->exec) {
+        cudaError_t e = cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal);
+        if (e != cudaSuccess) return cuda_fail("begin step capture", e);
+        const int rc = enqueue_step(m);
+        cudaGraph_t g = nullptr;
+        e = cudaStreamEndCapture(m->stream, &g);
+        if (rc) {
+            if (g) cudaGraphDestroy(g);
+            return -1;
+        }
+        if (e != cudaSuccess) return cuda_fail("end step capture", e);
+        m->graph = g;
+        e = cudaGraphInstantiate(&m->exec, g, 0);
+        if (e != cudaSuccess) return cuda_fail("instantiate step graph", e);
+    }
+    cudaError_t e = cudaGraphLaunch(m->exec, m->stream);
+    return e == cudaSuccess ? 0 : cuda_fail("step graph launch", e);
+}
+
+int alloc(void **p, size_t bytes, const char *what) {
+    cudaError_t e = cudaMalloc(p, bytes ? bytes : 16);
+    if (e != cudaSuccess) return cuda_fail(what, e);
+    return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+/* vq_runtime::model::Model::new (model.rs:294-320) plus the device state the
+ * reference GPU runtime allocates in alloc_model (vq-model-gpu.cu:662-705). */
+spk_model *spk_model_create(const spk_model_config *cfg, void *stream) {
+    if (!cfg || !cfg->full) {
+        set_error("model config is missing");
+        return nullptr;
+    }
+    const spk_model_config &c = *cfg;
+    if (c.hidden <= 0 || c.layers <= 0 || c.heads <= 0 || c.kv_heads <= 0 || c.heads % c.kv_heads ||
+        c.heads / c.kv_heads > MAX_GROUP || (c.head_dim != 128 && c.head_dim != 256) || c.inter <= 0 ||
+        c.vocab <= 0 || c.window <= 0 || c.max_ctx <= 0 || c.hidden % 32 || c.hidden > 65536) {
+        set_error("unsupported model geometry (head_dim 128/256, GQA group <= 4, hidden a multiple of 32)");
+        return nullptr;
+    }
+    spk_model *m = new spk_model();
+    m->cfg = c;
+    m->full.assign(c.full, c.full + c.layers);
+    m->cfg.full = m->full.data();
+    m->layers.resize(c.layers);
+    m->stream = (cudaStream_t)stream;
+    m->q_dim = c.heads * c.head_dim;
+    m->kv_dim = c.kv_heads * c.head_dim;
+    m->G = c.heads / c.kv_heads;
+    auto pdim = [&](float partial) {
+        int d = (int)((float)c.head_dim * partial);
+        return d < c.head_dim ? d : c.head_dim;
+    };
+    m->pdim_full = pdim(c.rope_partial_full);
+    m->pdim_slide = pdim(c.rope_partial_slide);
+    const int per_head = sm_count() / c.kv_heads > 0 ? sm_count() / c.kv_heads : 1;
+    m->nsplit_full = std::max(1, std::min(per_head, (c.max_ctx + 15) / 16));
+    m->nsplit_slide = std::max(1, std::min(per_head, (std::min(c.window, c.max_ctx) + 15) / 16));
+    size_t kv_elems = 0;
+    for (int li = 0; li < c.layers; li++) {
+        const int slots = m->full[li] ? c.max_ctx : std::min(c.window, c.max_ctx);
+        m->kv_off.push_back(kv_elems);
+        m->kv_slots.push_back(slots);
+        kv_elems += (size_t)c.kv_heads * slots * c.head_dim;
+    }
+    const size_t esz = c.kv_f16 ? 2 : 4;
+    const int nsplit = std::max(m->nsplit_full, m->nsplit_slide);
+    bool ok = !alloc((void **)&m->h, c.hidden * 4, "alloc h") && !alloc((void **)&m->qkv, (m->q_dim + 2 * m->kv_dim) * 4, "alloc qkv") &&
+              !alloc((void **)&m->gate, c.heads * 4, "alloc gate") && !alloc((void **)&m->attn, m->q_dim * 4, "alloc attn") &&
+              !alloc((void **)&m->act, (size_t)c.inter * 4, "alloc act") && !alloc((void **)&m->logits, (size_t)c.vocab * 4, "alloc logits") &&
+              !alloc((void **)&m->part, (size_t)c.kv_heads * nsplit * m->G * (c.head_dim + 2) * 4, "alloc attention partials") &&
+              !alloc((void **)&m->freq_full, c.head_dim * 4, "alloc rope") && !alloc((void **)&m->freq_slide, c.head_dim * 4, "alloc rope") &&
+              !alloc(&m->kc, kv_elems * esz, "alloc K cache") && !alloc(&m->vc, kv_elems * esz, "alloc V cache") &&
+              !alloc((void **)&m->state, 4 * sizeof(int), "alloc state") &&
+              !alloc((void **)&m->ctl, sizeof(DevCtl), "alloc control") &&
+              !alloc((void **)&m->head_partial, 1024 * sizeof(unsigned long long), "alloc head partials") &&
+              !alloc((void **)&m->head_counter, sizeof(unsigned int), "alloc head counter");
+    if (ok && (cudaMallocHost((void **)&m->host_io, 4 * sizeof(int)) != cudaSuccess ||
+               cudaMallocHost((void **)&m->host_ctl, sizeof(DevCtl)) != cudaSuccess))
+        ok = !set_error("pinned staging allocation failed");
+    if (ok) {
+        // rope frequencies in f32 exactly as model.rs:416-429 forms them
+        std::vector<float> ff(c.head_dim, 0.f), fs(c.head_dim, 0.f);
+        for (int i = 0; i < m->pdim_full / 2; i++) ff[i] = 1.0f / powf(c.rope_theta_full, (float)(2 * i) / (float)m->pdim_full);
+        for (int i = 0; i < m->pdim_slide / 2; i++) fs[i] = 1.0f / powf(c.rope_theta_slide, (float)(2 * i) / (float)m->pdim_slide);
+        ok = cudaMemcpy(m->freq_full, ff.data(), c.head_dim * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+             cudaMemcpy(m->freq_slide, fs.data(), c.head_dim * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+             cudaMemset(m->kc, 0, kv_elems * esz) == cudaSuccess && cudaMemset(m->vc, 0, kv_elems * esz) == cudaSuccess &&
+             cudaMemset(m->state, 0, 4 * sizeof(int)) == cudaSuccess && cudaMemset(m->ctl, 0, sizeof(DevCtl)) == cudaSuccess &&
+             cudaMemset(m->head_counter, 0, sizeof(unsigned int)) == cudaSuccess;
+        if (!ok) set_error("model initialisation copies failed");
+    }
+    if (!ok) {
+        spk_model_destroy(m);
+        return nullptr;
+    }
+    return m;
+}
+
+void spk_model_destroy(spk_model *m) {
+    if (!m) return;
+    if (m->exec) cudaGraphExecDestroy(m->exec);
+    if (m->graph) cudaGraphDestroy(m->graph);
+    void *ps[] = {m->h, m->qkv, m->gate, m->attn, m->act, m->logits, m->part, m->freq_full, m->freq_slide,
+                  m->kc, m->vc, m->state, m->ctl, m->head_partial, m->head_counter};
+    for (void *p : ps)
+        if (p) cudaFree(p);
+    if (m->host_io) cudaFreeHost(m->host_io);
+    if (m->host_ctl) cudaFreeHost(m->host_ctl);
+    delete m;
+}
+
+static int check_mat(const spk_vq_matrix *M, int rows, int cols, const char *name) {
+    if (!M) return set_error("%s: matrix is missing", name);
+    if (M->rows != rows || M->cols != cols)
+        return set_error("%s: is %dx%d, the architecture needs %dx%d", name, M->rows, M->cols, rows, cols);
+    if (M->nstages < 1 || M->nstages > 4) return set_error("%s: %d stages (1..4 supported)", name, M->nstages);
+    for (int s = 0; s < M->nstages; s++)
+        if (!M->stages[s]) return set_error("%s: stage %d is null", name, s);
+    return 0;
+}
+
+/* Weights::load per layer (model.rs:130-187): shapes checked as the reference checks them. */
+int spk_model_set_layer(spk_model *m, int layer, const spk_vq_matrix *qkv, const spk_vq_matrix *attn_gate,
+                        const spk_vq_matrix *out, const spk_vq_matrix *gate, const spk_vq_matrix *up,
+                        const spk_vq_matrix *down, const float *in_norm, const float *post_norm) {
+    if (!m) return set_error("model is null");
+    if (layer < 0 || layer >= m->cfg.layers) return set_error("layer %d is outside the %d layers", layer, m->cfg.layers);
+    const spk_model_config &c = m->cfg;
+    if (check_mat(qkv, m->q_dim + 2 * m->kv_dim, c.hidden, "q_k_v_proj") || check_mat(attn_gate, c.heads, c.hidden, "g_proj") ||
+        check_mat(out, c.hidden, m->q_dim, "out_proj") || check_mat(gate, c.inter, c.hidden, "gate_proj") ||
+        check_mat(up, c.inter, c.hidden, "up_proj") || check_mat(down, c.hidden, c.inter, "down_proj"))
+        return -1;
+    if (gate->nstages != up->nstages || gate->dim != up->dim || gate->nc != up->nc || gate->v3 != up->v3)
+        return set_error("gate_proj and up_proj must share one encoding to run as a pair");
+    if (!in_norm || !post_norm) return set_error("layer %d: a norm is missing", layer);
+    spk_model::Layer &L = m->layers[layer];
+    L.m[0] = *qkv;
+    L.m[1] = *attn_gate;
+    L.m[2] = *out;
+    L.m[3] = *gate;
+    L.m[4] = *up;
+    L.m[5] = *down;
+    L.in_norm = in_norm;
+    L.post_norm = post_norm;
+    L.set = true;
+    return 0;
+}
+
+/* The tied embedding / LM head as Q8_0 blocks [vocab][hidden] and the final norm. */
+int spk_model_set_head(spk_model *m, const void *embed_q80, const float *final_norm) {
+    if (!m || !embed_q80 || !final_norm) return set_error("head weights are missing");
+    m->embed = embed_q80;
+    m->final_norm = final_norm;
+    return 0;
+}
+
+/* Model::forward(token, pos) (model.rs:442-591) through host buffers: the token
+ * goes up, the greedy next id (and, if logits_host is not NULL, the vocab-wide
+ * logits) come back; synchronizes the model's stream. */
+int spk_model_forward(spk_model *m, int token, int pos, float *logits_host, int *next_host) {
+    if (!m) return set_error("model is null");
+    if (token < 0 || token >= m->cfg.vocab) return set_error("token %d is outside the vocabulary", token);
+    if (pos < 0 || pos >= m->cfg.max_ctx) return set_error("position %d exceeds the %d-token cache", pos, m->cfg.max_ctx);
+    if (pos > m->len) return set_error("position %d skips cached positions (%d cached)", pos, m->len);
+    m->host_io[0] = pos;
+    m->host_io[1] = token;
+    cudaError_t e = cudaMemcpyAsync(m->state, m->host_io, 2 * sizeof(int), cudaMemcpyHostToDevice, m->stream);
+    if (e != cudaSuccess) return cuda_fail("state upload", e);
+    if (run_step(m)) return -1;
+    e = cudaMemcpyAsync(m->host_io + 2, m->state + 2, sizeof(int), cudaMemcpyDeviceToHost, m->stream);
+    if (e == cudaSuccess && logits_host)
+        e = cudaMemcpyAsync(logits_host, m->logits, (size_t)m->cfg.vocab * 4, cudaMemcpyDeviceToHost, m->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+    if (e != cudaSuccess) return cuda_fail("forward", e);
+    if (check_device_error("forward")) return -1;
+    if (next_host) *next_host = m->host_io[2];
+    m->len = pos + 1;
+    return 0;
+}
+
+/* Device-resident greedy decoding: set (pos, token) and the device id buffer
+ * that spk_model_run fills, one id per step. */
+int spk_model_begin(spk_model *m, int token, int pos, int *ids_dev, int ids_cap) {
+    if (!m) return set_error("model is null");
+    if (token < 0 || token >= m->cfg.vocab || pos < 0 || pos > m->len) return set_error("bad start token/position");
+    cudaError_t e = cudaStreamSynchronize(m->stream);   // the pinned staging may still be in flight
+    if (e != cudaSuccess) return cuda_fail("begin", e);
+    m->host_ctl->ids = ids_dev;
+    m->host_ctl->cap = ids_dev ? ids_cap : 0;
+    e = cudaMemcpyAsync(m->ctl, m->host_ctl, sizeof(DevCtl), cudaMemcpyHostToDevice, m->stream);
+    if (e != cudaSuccess) return cuda_fail("begin", e);
+    set_state_kernel<<<1, 1, 0, m->stream>>>(m->state, m->state + 1, pos, token);
+    e = cudaMemsetAsync(m->state + 3, 0, sizeof(int), m->stream);
+    return e == cudaSuccess ? 0 : cuda_fail("begin", e);
+}
+
+/* Run `steps` greedy decode steps from the device state, no host round trip. */
+int spk_model_run(spk_model *m, int steps) {
+    if (!m) return set_error("model is null");
+    for (int i = 0; i < steps; i++)
+        if (run_step(m)) return -1;
+    return 0;
+}
+
+/* Device pointer of the last step's logits [vocab]. */
+const float *spk_model_logits(spk_model *m) { return m ? m->logits : nullptr; }
+
+/* Model::rollback (model.rs:361-382): keep the first `pos` cached positions. */
+int spk_model_rollback(spk_model *m, int pos) {
+    if (!m) return set_error("model is null");
+    if (pos < 0 || pos > m->len) return set_error("rollback to %d exceeds the %d cached positions", pos, m->len);
+    m->len = pos;
+    return 0;
+}
+
+/* Model::reset (model.rs:384-396) */
+int spk_model_reset(spk_model *m) { return spk_model_rollback(m, 0); }
+
+/* Positions cached (Model::len). */
+int spk_model_len(spk_model *m) { return m ? m->len : -1; }
+
+/* Record that `n` device-run steps extended the cache (spk_model_run does not
+ * sync, so the host view is advanced explicitly). */
+int spk_model_advance_len(spk_model *m, int n) {
+    if (!m || n < 0 || m->len + n > m->cfg.max_ctx) return set_error("bad length advance");
+    m->len += n;
+    return 0;
+}
+
+}  // extern "C"

@@ -23,6 +23,7 @@
 // one f32 add per element, no contraction.
 #include "common.cuh"
 #include "spk.h"
+#include "stream.cuh"
 
 using namespace spk;
 
@@ -93,6 +94,7 @@ struct FastArgs {
     int ks;                    // warps per row chunk split
     int tr;                    // rows per tile
     uint32_t main_slot, plane_slot, slot_bytes;
+    int nbuf;                  // ring depth (2 or 3, whatever fits shared memory)
     int *err;
 };
 
@@ -143,70 +145,64 @@ __device__ __forceinline__ float row_chunk(const uint8_t *row, const uint8_t *pl
 }
 
 // Producer: thread 0 fills one ring slot with the index streams of rows
-// [r0, r0+nr) of every stream. The 16-byte-aligned interior goes by bulk copy,
-// a ragged tail (< 16 bytes) by plain loads, so nothing is read past the
-// stream beyond what the generic path reads.
+// [r0, r0+nr) of every stream (stream.cuh). The contract gives every stage
+// payload 8 zeroed slack bytes, so a copy may round up to at most 8 bytes past
+// the payload end.
 __device__ __forceinline__ void issue_tile(const FastArgs &a, int nq, int ext, uint8_t *slot, uint64_t *bar,
                                            int r0, int nr) {
     const Layout &L = a.L;
-    uint32_t tx = 0;
-    const uint8_t *src_al[2 * MAXQ];
-    uint32_t len[2 * MAXQ];
-    uint8_t *dst[2 * MAXQ];
-    int n = 0;
+    const size_t payload = L.stream_off + (size_t)L.rows * (L.mrow + L.prow);
+    BulkList bl;
+    bl.n = 0;
+    bl.tx = 0;
     for (int q = 0; q < nq; q++) {
+        const uintptr_t limit = (uintptr_t)(a.st[q] + payload + 8);
         for (int part = 0; part < 1 + ext; part++) {
             const uint8_t *base = a.st[q] + L.stream_off +
                                   (part ? (size_t)L.rows * L.mrow + (size_t)r0 * L.prow : (size_t)r0 * L.mrow);
             const size_t bytes = (size_t)nr * (part ? L.prow : L.mrow);
-            const uintptr_t A = (uintptr_t)base, B = A + bytes;
-            const uintptr_t Aal = A & ~(uintptr_t)15, Bfl = B & ~(uintptr_t)15;
             uint8_t *d = slot + (part ? (nq * a.main_slot + q * a.plane_slot) : q * a.main_slot);
-            // ragged tail by plain loads
-            const uintptr_t t0 = Bfl > Aal ? Bfl : Aal;
-            for (uintptr_t b = t0; b < B; b++) d[b - Aal] = *(const uint8_t *)b;
-            if (Bfl > Aal) {
-                src_al[n] = (const uint8_t *)Aal;
-                len[n] = (uint32_t)(Bfl - Aal);
-                dst[n] = d;
-                tx += len[n];
-                n++;
-            }
+            bulk_plan(bl, d, (uintptr_t)base, (uintptr_t)base + bytes, limit);
         }
     }
-    mbar_arrive_expect_tx(bar, tx);
-    fence_proxy_async();
-    for (int k = 0; k < n; k++) bulk_g2s(dst[k], src_al[k], len[k], bar);
+    bulk_issue(bl, bar);
 }
 
 template <int NSTG, int NG, int F, int EXT>
 __global__ void __launch_bounds__(FAST_THREADS, 1) vq_fast_kernel(const FastArgs a) {
     constexpr int NQ = NSTG * NG;
+    constexpr int XS = 4 * F + 4;   // padded per-lane stride of the staged activations (floats)
     extern __shared__ __align__(16) uint8_t smem[];
     const Layout &L = a.L;
     const int nc = L.nc;
+    const int ks_n = a.ks, tr = a.tr, NB = a.nbuf;
     uint2 *cb = reinterpret_cast<uint2 *>(smem);
-    uint8_t *ring = smem + (((size_t)NQ * nc * 8 + 15) & ~(size_t)15);
-    uint64_t *full = reinterpret_cast<uint64_t *>(ring + (size_t)FAST_NBUF * a.slot_bytes);
-    float *part = reinterpret_cast<float *>(full + FAST_NBUF);   // [2][tr][NG][ks][NSTG]
-    double *red = reinterpret_cast<double *>(part + 2 * a.tr * NG * a.ks * NSTG);
+    float *xs = reinterpret_cast<float *>(smem + (((size_t)NQ * nc * 8 + 15) & ~(size_t)15));
+    uint8_t *ring = reinterpret_cast<uint8_t *>(xs + (size_t)ks_n * 32 * XS);
+    uint64_t *full = reinterpret_cast<uint64_t *>(ring + (size_t)NB * a.slot_bytes);
+    uint64_t *empty = full + NB;
+    float *part = reinterpret_cast<float *>(empty + NB);   // [2][tr][NG][ks][NSTG]
+    double *red = reinterpret_cast<double *>(part + 2 * tr * NG * ks_n * NSTG);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int ks_n = a.ks, tr = a.tr;
     // warp -> (row in tile, group, k chunk)
     const int ks = warp % ks_n, g = (warp / ks_n) % NG, rw = warp / (ks_n * NG);
+    const bool direct = (NG == 1) && (ks_n == 1);   // the row's warp finishes the row itself
 
     const int G = gridDim.x;
     const int rb = (int)(((long long)blockIdx.x * L.rows) / G), re = (int)(((long long)(blockIdx.x + 1) * L.rows) / G);
     const int ntile = (re - rb + tr - 1) / tr;
 
     if (tid == 0) {
-        for (int b = 0; b < FAST_NBUF; b++) mbar_init(&full[b], 1);
+        for (int b = 0; b < NB; b++) {
+            mbar_init(&full[b], 1);
+            mbar_init(&empty[b], FAST_WARPS);
+        }
         fence_mbar_init();
     }
     __syncthreads();
     if (tid == 0) {
-        for (int t = 0; t < FAST_NBUF - 1 && t < ntile; t++) {
+        for (int t = 0; t < NB - 1 && t < ntile; t++) {
             const int r0 = rb + t * tr;
             issue_tile(a, NQ, EXT, ring + (size_t)t * a.slot_bytes, &full[t], r0, min(tr, re - r0));
         }
@@ -216,35 +212,55 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) vq_fast_kernel(const FastArgs
         const uint2 *src = reinterpret_cast<const uint2 *>(a.st[q] + L.cb_off);
         for (int v = tid; v < nc; v += FAST_THREADS) cb[q * nc + v] = __ldg(src + v);
     }
-    // Activations of this lane's index run, with the optional RMSNorm folded in.
+    // Activations: coalesced loads (with the optional RMSNorm folded in) into a
+    // per-lane padded layout, then each lane takes its 4F values with 16-byte
+    // shared loads that hit distinct banks.
     float inv = 1.0f;
     if (a.norm_w) inv = block_rms_inv(a.x, L.cols, a.eps, red);
-    float xr[4 * F];
-    const int i0 = ks * 32 * F + lane * F;
-#pragma unroll
-    for (int j = 0; j < 4 * F; j++) {
-        const int c = 4 * i0 + j;
+    for (int c = tid; c < L.cols; c += FAST_THREADS) {
         float v = a.x[c];
         if (a.norm_w) v = __fmul_rn(__fmul_rn(v, inv), a.norm_w[c]);
-        xr[j] = v;
+        const int ln = c / (4 * F);   // global lane index = ks * 32 + lane
+        xs[(size_t)ln * XS + (c - ln * 4 * F)] = v;
     }
     __syncthreads();
-
+    float xr[4 * F];
+    {
+        const float4 *xp = reinterpret_cast<const float4 *>(xs + (size_t)(ks * 32 + lane) * XS);
+#pragma unroll
+        for (int j = 0; j < F; j++) {
+            const float4 v = xp[j];
+            xr[4 * j] = v.x;
+            xr[4 * j + 1] = v.y;
+            xr[4 * j + 2] = v.z;
+            xr[4 * j + 3] = v.w;
+        }
+    }
+    const int i0 = ks * 32 * F + lane * F;
     const uint32_t bit0 = 12u * (uint32_t)i0, pbit0 = (uint32_t)i0;
+
     for (int t = 0; t < ntile; t++) {
-        const int slot = t % FAST_NBUF;
-        if (tid == 0 && t + FAST_NBUF - 1 < ntile) {
-            const int tn = t + FAST_NBUF - 1, r0 = rb + tn * tr;
-            issue_tile(a, NQ, EXT, ring + (size_t)(tn % FAST_NBUF) * a.slot_bytes, &full[tn % FAST_NBUF], r0,
-                       min(tr, re - r0));
+        const int slot = t % NB;
+        if (tid == 0 && t + NB - 1 < ntile) {
+            const int tn = t + NB - 1, r0n = rb + tn * tr, sn = tn % NB;
+            // the slot last held tile tn - NBUF: wait until every warp released it
+            if (tn >= NB && !mbar_wait(&empty[sn], (uint32_t)(((tn / NB) - 1) & 1), a.err)) return;
+            issue_tile(a, NQ, EXT, ring + (size_t)sn * a.slot_bytes, &full[sn], r0n, min(tr, re - r0n));
         }
         const int r0 = rb + t * tr, nr = min(tr, re - r0);
-        const bool ok = mbar_wait(&full[slot], (uint32_t)((t / FAST_NBUF) & 1), a.err);
-        if (!ok) return;
+        const int r = r0 + rw;
+        float gain[NSTG], yold = 0.f;
+        if (direct && lane == 0 && rw < nr) {   // issued before the gathers, consumed after
+#pragma unroll
+            for (int s = 0; s < NSTG; s++)
+                gain[s] = h2f_bits(*reinterpret_cast<const uint16_t *>(a.st[s] + L.gain_off + 2 * (size_t)r));
+            if (a.accumulate) yold = a.y[r];
+        }
+        if (!mbar_wait(&full[slot], (uint32_t)((t / NB) & 1), a.err)) return;
         float *pt = part + (size_t)(t & 1) * tr * NG * ks_n * NSTG;
+        float acc[NSTG];
         if (rw < nr) {
             const uint8_t *sb = ring + (size_t)slot * a.slot_bytes;
-            float acc[NSTG];
 #pragma unroll
             for (int s = 0; s < NSTG; s++) {
                 const int q = g * NSTG + s;
@@ -256,33 +272,48 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) vq_fast_kernel(const FastArgs
                                                     (size_t)r0 * L.prow);
                     pl = sb + NQ * a.main_slot + q * a.plane_slot + (P & 15) + (size_t)rw * L.prow;
                 }
-                acc[s] = warp_sum(row_chunk<F, EXT>(row, pl, cb + (size_t)q * nc, xr, bit0, pbit0));
-            }
-            if (lane == 0) {
-#pragma unroll
-                for (int s = 0; s < NSTG; s++) pt[((rw * NG + g) * ks_n + ks) * NSTG + s] = acc[s];
+                acc[s] = row_chunk<F, EXT>(row, pl, cb + (size_t)q * nc, xr, bit0, pbit0);
             }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);   // this warp is done reading the slot
+        if (rw < nr) {
+#pragma unroll
+            for (int s = 0; s < NSTG; s++) acc[s] = warp_sum(acc[s]);
+            if (lane == 0) {
+                if (direct) {
+                    float o = yold;
+#pragma unroll
+                    for (int s = 0; s < NSTG; s++) o = __fadd_rn(o, __fmul_rn(acc[s], gain[s]));
+                    a.y[r] = o;
+                } else {
+#pragma unroll
+                    for (int s = 0; s < NSTG; s++) pt[((rw * NG + g) * ks_n + ks) * NSTG + s] = acc[s];
+                }
+            }
+        }
+        if (direct) continue;
         __syncthreads();
         if (tid < nr) {
-            const int r = r0 + tid;
+            const int rr = r0 + tid;
             float outv[NG];
 #pragma unroll
             for (int gg = 0; gg < NG; gg++) {
-                float o = (NG == 1 && a.accumulate) ? a.y[r] : 0.0f;
+                float o = (NG == 1 && a.accumulate) ? a.y[rr] : 0.0f;
 #pragma unroll
                 for (int s = 0; s < NSTG; s++) {
                     float v = 0.f;
                     for (int k = 0; k < ks_n; k++) v += pt[((tid * NG + gg) * ks_n + k) * NSTG + s];
-                    const uint16_t gh = *reinterpret_cast<const uint16_t *>(a.st[gg * NSTG + s] + L.gain_off + 2 * (size_t)r);
+                    const uint16_t gh =
+                        *reinterpret_cast<const uint16_t *>(a.st[gg * NSTG + s] + L.gain_off + 2 * (size_t)rr);
                     o = __fadd_rn(o, __fmul_rn(v, h2f_bits(gh)));
                 }
                 outv[gg] = o;
             }
             if (NG == 1)
-                a.y[r] = outv[0];
+                a.y[rr] = outv[0];
             else
-                a.y[r] = __fmul_rn(gelu_erf(outv[0]), outv[NG - 1]);
+                a.y[rr] = __fmul_rn(gelu_erf(outv[0]), outv[NG - 1]);
         }
     }
 }
@@ -423,9 +454,14 @@ bool fast_plan(const uint8_t *const *st, int nstg, int ng, const Layout &L, Fast
     const uint32_t main_slot = (uint32_t)(((size_t)tr * L.mrow + 32 + 15) & ~(size_t)15);
     const uint32_t plane_slot = ext ? (uint32_t)(((size_t)tr * L.prow + 32 + 15) & ~(size_t)15) : 0u;
     const uint32_t slot = nq * (main_slot + plane_slot);
-    const size_t smem = (((size_t)nq * L.nc * 8 + 15) & ~(size_t)15) + (size_t)FAST_NBUF * slot + FAST_NBUF * 8 +
-                        (size_t)2 * tr * ng * ks * nstg * 4 + 32 * 8;
-    if (smem > smem_optin_max()) return false;
+    int nbuf = FAST_NBUF;
+    size_t smem = 0;
+    for (; nbuf >= 2; nbuf--) {
+        smem = (((size_t)nq * L.nc * 8 + 15) & ~(size_t)15) + (size_t)ks * 32 * (4 * F + 4) * 4 + (size_t)nbuf * slot +
+               2 * (size_t)nbuf * 8 + (size_t)2 * tr * ng * ks * nstg * 4 + 32 * 8;
+        if (smem <= smem_optin_max()) break;
+    }
+    if (nbuf < 2) return false;
     FastArgs &a = P->args;
     memset(&a, 0, sizeof a);
     for (int q = 0; q < nq; q++) a.st[q] = st[q];
@@ -435,6 +471,7 @@ bool fast_plan(const uint8_t *const *st, int nstg, int ng, const Layout &L, Fast
     a.main_slot = main_slot;
     a.plane_slot = plane_slot;
     a.slot_bytes = slot;
+    a.nbuf = nbuf;
     P->ks = ks;
     P->F = F;
     P->tr = tr;

@@ -60,6 +60,18 @@ _PROTOS = {
     "spk_q6k_dequant": ([_vp, C.c_size_t, _vp, _vp], _i),
     "spk_q80_dequant": ([_vp, C.c_size_t, _vp, _vp], _i),
     "spk_q80_row": ([_vp, _i, _i, _i, _vp, _vp, _vp], _i),
+    "spk_model_create": ([_vp, _vp], _vp),
+    "spk_model_destroy": ([_vp], None),
+    "spk_model_set_layer": ([_vp, _i] + [_vp] * 8, _i),
+    "spk_model_set_head": ([_vp, _vp, _vp], _i),
+    "spk_model_forward": ([_vp, _i, _i, _vp, _vp], _i),
+    "spk_model_begin": ([_vp, _i, _i, _vp, _i], _i),
+    "spk_model_run": ([_vp, _i], _i),
+    "spk_model_logits": ([_vp], _vp),
+    "spk_model_rollback": ([_vp, _i], _i),
+    "spk_model_reset": ([_vp], _i),
+    "spk_model_len": ([_vp], _i),
+    "spk_model_advance_len": ([_vp, _i], _i),
 }
 
 

@@ -211,6 +211,43 @@ def random_rvq(rows: int, cols: int, dim: int = 4, nc: int = 4096, stages: int =
     return rqvq(payloads, dim, nc, rows, cols)
 
 
+def random_rvq_fast(rows: int, cols: int, dim: int = 4, nc: int = 4096, stages: int = 2, seed: int = 0,
+                    scale: float = 0.02) -> bytes:
+    """random_rvq for a power-of-two codebook of 12 or 13 bits: every bit pattern of the row
+    streams is a valid index there, so the streams are drawn as random bytes (fast enough for a
+    whole 36-layer model). Codebooks N(0, s_k^2) per stage, gains 1.0."""
+    g = StageGeom(dim, nc, rows, cols, True)
+    if nc != (1 << g.nbit) or g.nbit not in (12, 13):
+        raise ValueError("random_rvq_fast needs nc = 4096 or 8192")
+    rng = np.random.default_rng(seed)
+    hdr = b"DQV3" + struct.pack("<HHIIII", dim, nc, rows, cols, 1 if g.nbit > 12 else 0, 0)
+    gains = _f16_bits(np.ones(rows)).astype("<u2").tobytes()
+    payloads = []
+    s_k = scale
+    for _ in range(stages):
+        cb = _f16_bits(rng.normal(0.0, s_k, size=nc * dim)).astype("<u2").tobytes()
+        payloads.append(hdr + cb + gains + rng.bytes(g.index_bytes))
+        s_k *= 0.125
+    return rqvq(payloads, dim, nc, rows, cols)
+
+
+def synth_q8_0(rows: int, cols: int, seed: int = 0, sigma: float = 0.02) -> bytes:
+    """Q8_0 blocks with the statistics of quantize_q8_0(N(0, sigma^2)) without materialising the
+    f32 matrix: q ~ round(N(0, (127/2.5)^2)) clipped to +-127, d ~ 2.5 sigma / 127 (the expected
+    max |w| of 32 Gaussian draws over 127), jittered per block."""
+    rng = np.random.default_rng(seed)
+    nblk = rows * cols // Q80_BLOCK_WEIGHTS
+    out = np.empty((nblk, Q80_BLOCK_BYTES), np.uint8)
+    d = (2.5 * sigma / 127.0) * rng.uniform(0.8, 1.25, nblk)
+    out[:, 0:2] = d.astype(np.float16).view(np.uint8).reshape(-1, 2)
+    step = 1 << 22
+    for i in range(0, nblk, step):
+        n = min(step, nblk - i)
+        q = np.clip(np.rint(rng.standard_normal((n, 32), dtype=np.float32) * (127.0 / 2.5)), -127, 127)
+        out[i:i + n, 2:] = q.astype(np.int8).view(np.uint8)
+    return out.tobytes()
+
+
 def encode_rvq(W: np.ndarray, dim: int = 4, nc: int = 4096, stages: int = 2, iters: int = 8,
                v3: bool = True) -> bytes:
     """Residual Lloyd encoder following build-vq-gpu.c:224-253: per stage a strided subsample of

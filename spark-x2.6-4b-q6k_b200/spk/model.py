@@ -1,0 +1,217 @@
+"""Host side of the decode step: the vq_runtime Model API over libspk.
+
+Mirrors tools/vq-runtime/src/{config.rs, model.rs}: ``ModelConfig`` is
+``Config`` (defaults are the Spark-X2.6-4B values), ``DeviceModel`` offers
+``forward(token, pos) -> logits``, ``argmax``, ``rollback``, ``reset``. The
+compute is libspk's (include/spk.h, spk_model_*); this module uploads weights
+and marshals pointers.
+
+``synth_weights`` builds a seeded random-init model in the reference's formats
+(DQV3 residual-VQ containers for every projection, a Q8_0 tied embedding/head,
+f32 norms), standing in for the absent real checkpoint.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from . import SpkError, check, dev_bytes, lib
+from . import formats as F
+
+
+@dataclass
+class ModelConfig:
+    """tools/vq-runtime/src/config.rs:16-30 (values from SURVEY §0.1 / models/quantize.log)."""
+
+    hidden: int = 2560
+    layers: int = 36
+    heads: int = 16
+    kv_heads: int = 4
+    head_dim: int = 256
+    inter: int = 10240
+    vocab: int = 131072
+    window: int = 512
+    eps: float = 1e-6
+    rope_theta_full: float = 5_000_000.0
+    rope_partial_full: float = 0.25
+    rope_theta_slide: float = 10_000.0
+    rope_partial_slide: float = 1.0
+    full: list = field(default_factory=lambda: [(i % 4) == 3 for i in range(36)])   # [T,T,T,F] pattern
+
+    @property
+    def q_dim(self) -> int:
+        return self.heads * self.head_dim
+
+    @property
+    def kv_dim(self) -> int:
+        return self.kv_heads * self.head_dim
+
+    def as_oracle(self) -> dict:
+        d = {k: getattr(self, k) for k in ("hidden", "layers", "heads", "kv_heads", "head_dim", "inter", "vocab",
+                                           "window", "eps", "rope_theta_full", "rope_partial_full",
+                                           "rope_theta_slide", "rope_partial_slide")}
+        d["full"] = [int(f) for f in self.full]
+        return d
+
+
+def small_config(layers: int = 4, hidden: int = 512, heads: int = 4, kv_heads: int = 1, head_dim: int = 128,
+                 inter: int = 1024, vocab: int = 4096, window: int = 16) -> ModelConfig:
+    """A reduced geometry with the same structure (GQA group 4, [T,T,T,F] layers), for
+    parity runs the CPU oracle finishes in seconds."""
+    return ModelConfig(hidden=hidden, layers=layers, heads=heads, kv_heads=kv_heads, head_dim=head_dim, inter=inter,
+                       vocab=vocab, window=window, full=[(i % 4) == 3 for i in range(layers)])
+
+
+MATS = ("qkv", "attn_gate", "out", "gate", "up", "down")
+
+
+def mat_shapes(cfg: ModelConfig) -> dict:
+    """model.rs:138-174: out x in of every projection."""
+    return {"qkv": (cfg.q_dim + 2 * cfg.kv_dim, cfg.hidden), "attn_gate": (cfg.heads, cfg.hidden),
+            "out": (cfg.hidden, cfg.q_dim), "gate": (cfg.inter, cfg.hidden), "up": (cfg.inter, cfg.hidden),
+            "down": (cfg.hidden, cfg.inter)}
+
+
+def synth_weights(cfg: ModelConfig, seed: int = 0, nc: int = 4096, stages: int = 2, exact_q80: bool = False) -> dict:
+    """Seeded random-init weights: per layer a DQV3 container per projection (codebooks
+    N(0, 0.02^2), residual stage scaled down, gains 1.0), norms N(1, 0.1^2); a Q8_0 tied
+    embedding. exact_q80 quantizes an explicit N(0, 0.02^2) matrix (small vocab only)."""
+    rng = np.random.default_rng(seed)
+    shapes = mat_shapes(cfg)
+    layers = []
+    for li in range(cfg.layers):
+        L = {}
+        for k, n in enumerate(MATS):
+            r, c = shapes[n]
+            s = seed * 1000 + li * 16 + k
+            L[n] = F.random_rvq_fast(r, c, 4, nc, stages, seed=s) if nc in (4096, 8192) else \
+                F.random_rvq(r, c, 4, nc, stages, seed=s)
+        L["in_norm"] = rng.normal(1.0, 0.1, cfg.hidden).astype(np.float32)
+        L["post_norm"] = rng.normal(1.0, 0.1, cfg.hidden).astype(np.float32)
+        layers.append(L)
+    if exact_q80:
+        embed = F.quantize_q8_0(rng.normal(0, 0.02, (cfg.vocab, cfg.hidden)).astype(np.float32))
+    else:
+        embed = F.synth_q8_0(cfg.vocab, cfg.hidden, seed=seed + 7)
+    norm = rng.normal(1.0, 0.1, cfg.hidden).astype(np.float32)
+    return {"layers": layers, "embed": embed, "norm": norm}
+
+
+class _Cfg(C.Structure):
+    _fields_ = [("hidden", C.c_int), ("layers", C.c_int), ("heads", C.c_int), ("kv_heads", C.c_int),
+                ("head_dim", C.c_int), ("inter", C.c_int), ("vocab", C.c_int), ("window", C.c_int),
+                ("eps", C.c_float), ("rope_theta_full", C.c_float), ("rope_partial_full", C.c_float),
+                ("rope_theta_slide", C.c_float), ("rope_partial_slide", C.c_float),
+                ("full", C.POINTER(C.c_int)), ("max_ctx", C.c_int), ("kv_f16", C.c_int)]
+
+
+class VqMatrix(C.Structure):
+    """spk_vq_matrix: stage device pointers + geometry."""
+
+    _fields_ = [("stages", C.c_void_p * 4), ("nstages", C.c_int), ("dim", C.c_int), ("nc", C.c_int),
+                ("rows", C.c_int), ("cols", C.c_int), ("v3", C.c_int)]
+
+
+def upload_container(buf: bytes, device) -> tuple[VqMatrix, list]:
+    """Every stage in its own device buffer with zeroed slack (vq-model-gpu.cu:278-288)."""
+    c = F.parse_container(buf)
+    keep = []
+    M = VqMatrix()
+    for s in range(c.nstages):
+        o = c.stage_offset(s)
+        t = dev_bytes(buf[o:o + c.stage_bytes], device)
+        keep.append(t)
+        M.stages[s] = t.data_ptr()
+    M.nstages, M.dim, M.nc, M.rows, M.cols, M.v3 = c.nstages, c.dim, c.nc, c.rows, c.cols, int(c.v3)
+    return M, keep
+
+
+class DeviceModel:
+    """vq_runtime::model::Model on the GPU (model.rs:260-615)."""
+
+    def __init__(self, cfg: ModelConfig, weights: dict, max_ctx: int, kv_f16: bool = False, device="cuda:0",
+                 stream=None):
+        import torch
+
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.stream = stream if stream is not None else torch.cuda.Stream(device=self.device)
+        self._keep = []
+        self._full = (C.c_int * cfg.layers)(*[int(f) for f in cfg.full])
+        c = _Cfg(cfg.hidden, cfg.layers, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.inter, cfg.vocab, cfg.window,
+                 cfg.eps, cfg.rope_theta_full, cfg.rope_partial_full, cfg.rope_theta_slide, cfg.rope_partial_slide,
+                 self._full, max_ctx, int(kv_f16))
+        L = lib()
+        L.spk_model_create.restype = C.c_void_p
+        self.h = L.spk_model_create(C.byref(c), C.c_void_p(self.stream.cuda_stream))
+        if not self.h:
+            raise SpkError(L.spk_last_error().decode())
+        self.max_ctx = max_ctx
+        self.weight_bytes = 0
+        for li, Lw in enumerate(weights["layers"]):
+            mats = []
+            for n in MATS:
+                M, keep = upload_container(Lw[n], self.device)
+                self._keep += keep
+                mats.append(M)
+                self.weight_bytes += len(Lw[n]) - 32
+            nin = torch.from_numpy(np.ascontiguousarray(Lw["in_norm"])).to(self.device)
+            npost = torch.from_numpy(np.ascontiguousarray(Lw["post_norm"])).to(self.device)
+            self._keep += [nin, npost, mats]
+            check(L.spk_model_set_layer(self.h, li, *[C.byref(M) for M in mats], nin.data_ptr(), npost.data_ptr()),
+                  f"layer {li}")
+        emb = dev_bytes(weights["embed"], self.device)
+        norm = torch.from_numpy(np.ascontiguousarray(weights["norm"])).to(self.device)
+        self._keep += [emb, norm]
+        self.weight_bytes += len(weights["embed"])
+        check(L.spk_model_set_head(self.h, emb.data_ptr(), norm.data_ptr()), "head")
+        self._logits = np.empty(cfg.vocab, np.float32)
+        torch.cuda.synchronize(self.device)   # uploads ran on torch's stream; the model runs on its own
+
+    def forward(self, token: int, pos: int, want_logits: bool = True):
+        """Model::forward: returns (next_id, logits or None) through host buffers."""
+        nxt = C.c_int()
+        lp = self._logits.ctypes.data_as(C.c_void_p) if want_logits else None
+        check(lib().spk_model_forward(self.h, token, pos, lp, C.byref(nxt)), f"forward({token}, {pos})")
+        return nxt.value, (self._logits.copy() if want_logits else None)
+
+    def begin(self, token: int, pos: int, ids_dev=None, cap: int = 0):
+        import torch
+
+        torch.cuda.synchronize(self.device)   # ids_dev may have been written on torch's stream
+        check(lib().spk_model_begin(self.h, token, pos, ids_dev.data_ptr() if ids_dev is not None else None, cap))
+
+    def run(self, steps: int):
+        check(lib().spk_model_run(self.h, steps), "run")
+
+    def rollback(self, pos: int):
+        check(lib().spk_model_rollback(self.h, pos), "rollback")
+
+    def reset(self):
+        check(lib().spk_model_reset(self.h), "reset")
+
+    def advance_len(self, n: int):
+        check(lib().spk_model_advance_len(self.h, n), "advance_len")
+
+    @property
+    def len(self) -> int:
+        return lib().spk_model_len(self.h)
+
+    @staticmethod
+    def argmax(logits: np.ndarray) -> int:
+        """Model::argmax (model.rs:594-604): first index of the maximum."""
+        return int(np.argmax(np.where(np.isnan(logits), -np.inf, logits)))
+
+    def close(self):
+        if self.h:
+            self.stream.synchronize()
+            lib().spk_model_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
