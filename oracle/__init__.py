@@ -56,6 +56,7 @@ def lib():
         L.orc_model_free.argtypes = [C.c_void_p]
         L.orc_model_forward.argtypes = [C.c_void_p, C.c_uint32, C.c_int, _f32p]
         L.orc_model_forward.restype = C.c_int
+        L.orc_model_fill_kv.argtypes = [C.c_void_p, C.c_int, C.c_uint64]
         _lib = L
     return _lib
 
@@ -209,6 +210,10 @@ class Model:
         if lib().orc_model_forward(self.h, token, pos, out):
             raise ValueError(f"forward({token}, {pos}) rejected")
         return out
+
+    def fill_kv(self, n: int, seed: int = 0):
+        """Seeded K/V for the first n positions (CPU-baseline samples at long context)."""
+        lib().orc_model_fill_kv(self.h, n, seed)
 
     def close(self):
         if self.h:

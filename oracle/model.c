@@ -191,3 +191,23 @@ int orc_model_rollback(orc_model *m, int pos) { return (pos < 0 || pos > m->max_
 
 /* The hidden state entering the final norm, for debugging parity. */
 const float *orc_model_hidden(const orc_model *m) { return m->h; }
+
+/* Fill the first n positions of every layer's K/V cache with seeded values
+ * (splitmix-style hash -> uniform [-1, 1)), so a CPU-baseline sample can time a
+ * step at a long context without first running the whole prompt on the CPU. */
+void orc_model_fill_kv(orc_model *m, int n, uint64_t seed) {
+    const orc_cfg *c = &m->c;
+    const size_t kvd = (size_t)c->kv_heads * c->head_dim;
+    if (n > m->max_ctx) n = m->max_ctx;
+    for (int li = 0; li < c->layers; li++) {
+        float *kc = m->kv_k + (size_t)li * m->max_ctx * kvd, *vc = m->kv_v + (size_t)li * m->max_ctx * kvd;
+        for (size_t i = 0; i < (size_t)n * kvd; i++) {
+            uint64_t z = seed + (uint64_t)li * 0x9E3779B97F4A7C15ull + i * 0xBF58476D1CE4E5B9ull;
+            z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+            z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+            z ^= z >> 31;
+            kc[i] = (float)((double)(z >> 11) * (1.0 / 4503599627370496.0)) - 1.0f;
+            vc[i] = (float)((double)((z * 0x2545F4914F6CDD1Dull) >> 11) * (1.0 / 4503599627370496.0)) - 1.0f;
+        }
+    }
+}

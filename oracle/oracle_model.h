@@ -32,6 +32,7 @@ int orc_model_forward(orc_model *m, uint32_t token, int pos, float *logits);
 int orc_model_rollback(orc_model *m, int pos);
 int orc_rope_dim(const orc_cfg *c, int layer);
 const float *orc_model_hidden(const orc_model *m);
+void orc_model_fill_kv(orc_model *m, int n, uint64_t seed);
 
 #ifdef __cplusplus
 }

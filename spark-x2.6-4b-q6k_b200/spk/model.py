@@ -150,6 +150,7 @@ class DeviceModel:
             raise SpkError(L.spk_last_error().decode())
         self.max_ctx = max_ctx
         self.weight_bytes = 0
+        self.mats, self.norms = [], []   # per layer: {name: VqMatrix}, (in_norm, post_norm) device tensors
         for li, Lw in enumerate(weights["layers"]):
             mats = []
             for n in MATS:
@@ -160,6 +161,8 @@ class DeviceModel:
             nin = torch.from_numpy(np.ascontiguousarray(Lw["in_norm"])).to(self.device)
             npost = torch.from_numpy(np.ascontiguousarray(Lw["post_norm"])).to(self.device)
             self._keep += [nin, npost, mats]
+            self.mats.append(dict(zip(MATS, mats)))
+            self.norms.append((nin, npost))
             check(L.spk_model_set_layer(self.h, li, *[C.byref(M) for M in mats], nin.data_ptr(), npost.data_ptr()),
                   f"layer {li}")
         emb = dev_bytes(weights["embed"], self.device)
