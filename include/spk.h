@@ -117,6 +117,15 @@ int spk_q80_gemv(const void *w, int rows, int cols, const float *x, const float 
  * argmax rule model.rs:594-604). Allocates a small per-device workspace on first use. */
 int spk_q80_head(const void *w, int rows, int cols, const float *x, const float *norm_w, float eps, float *logits,
                  int *argmax_out, void *stream);
+/* The same head without any allocation. No counterpart in the reference. For callers
+ * that cannot call cudaMalloc: code inside a CUDA-graph capture, real-time loops that
+ * must not stall on an allocation, and host frameworks that own all device memory.
+ * Its scratch is a fixed 8,448-byte array inside libspk (held by every GPU that loads
+ * the library until exit); a launch needing more than 1024 CTAs is rejected. The first
+ * call on a device looks up that array (make it before any stream capture); calls on a
+ * device share the array, so calls that overlap on the GPU race: serialize them. */
+int spk_q80_head_noalloc(const void *w, int rows, int cols, const float *x, const float *norm_w, float eps,
+                         float *logits, int *argmax_out, void *stream);
 /* Bit-exact block decode (ggml dequantize_row_q6_K / dequantize_row_q8_0). */
 int spk_q6k_dequant(const void *w, size_t nblocks, float *out, void *stream);
 int spk_q80_dequant(const void *w, size_t nblocks, float *out, void *stream);

@@ -701,3 +701,74 @@ int spk_q80_row(const void *w, int rows, int cols, int row, const int *token, fl
 }
 
 }  // extern "C"
+
+// ================================================ head with no allocation ===
+// spk_q80_head keeps its scratch (one 8-byte partial per CTA plus a finishing
+// counter) in memory it allocates with cudaMalloc on first use. Some callers
+// cannot allow that: code running while a stream is being captured into a CUDA
+// graph (cudaMalloc is not permitted there), real-time decode loops that must
+// not stall on the implicit device synchronization an allocation can cause,
+// and host frameworks that own every device byte through their own pool and
+// forbid a library from allocating behind them. For them the same head runs
+// with its scratch in the fixed array below, which lives in the library's
+// device image: every GPU that loads libspk holds these 8,448 bytes until the
+// process exits.
+namespace {
+constexpr int NOALLOC_HEAD_MAX_CTAS = 1024;   // partial slots: the largest grid this head may launch
+constexpr int NOALLOC_HEAD_PARTIAL0 = 32;     // the counter sits in slot 0; partials start 256 bytes in
+static __device__ __align__(256) unsigned long long g_head_noalloc_scratch[NOALLOC_HEAD_PARTIAL0 + NOALLOC_HEAD_MAX_CTAS];
+// Device address of the array per device. In host code the array's name is
+// only a host-side stand-in, never a device address, so it is looked up with
+// cudaGetSymbolAddress once per device, with that device current.
+static unsigned long long *g_head_noalloc_dev[64];
+}  // namespace
+
+extern "C" {
+
+/* Tied Q8_0 head without any allocation (no counterpart in the reference): the
+ * same contract as spk_q80_head — logits = W RMSNorm(x) and the first index of the
+ * maximum into *argmax_out — but its scratch is a fixed array inside libspk.
+ * Limits and rules:
+ *  - the launch may use at most 1024 CTAs (at most sm_count CTAs are used on the
+ *    fast path, 2 x sm_count capped at 1024 otherwise); a launch needing more is
+ *    rejected with an error;
+ *  - the first call on a device looks up the array's device address
+ *    (cudaGetSymbolAddress) — make that first call before any stream capture;
+ *  - every call on a device shares the one array and leaves its contents behind;
+ *    each call clears the counter it needs at zero (an asynchronous memset on
+ *    `stream`, not an allocation), and calls that overlap on the GPU (different
+ *    streams, or graphs replayed concurrently) race on it: serialize them. */
+int spk_q80_head_noalloc(const void *w, int rows, int cols, const float *x, const float *norm_w, float eps,
+                         float *logits, int *argmax_out, void *stream) {
+    if (check_blocks(w, rows, cols, 32)) return -1;
+    if (!argmax_out || !x || !logits) return set_error("head needs x, logits and argmax_out");
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail("no-alloc head: current device", e);
+    if (dev < 0 || dev >= 64) return set_error("no-alloc head: device %d is outside the 64 this build tracks", dev);
+    if (!g_head_noalloc_dev[dev]) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_head_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_fail("no-alloc head: scratch address", e);
+        g_head_noalloc_dev[dev] = (unsigned long long *)p;
+    }
+    GFPlan P;
+    int grid;
+    if (gf_plan(1, w, rows, cols, &P)) {
+        const int ntr = (rows + P.a.tr - 1) / P.a.tr;
+        grid = ntr < sm_count() ? ntr : sm_count();
+    } else {
+        grid = 2 * sm_count() < 1024 ? 2 * sm_count() : 1024;
+    }
+    if (grid > NOALLOC_HEAD_MAX_CTAS)
+        return set_error("no-alloc head: this launch needs %d CTAs, the built-in scratch holds %d", grid,
+                         NOALLOC_HEAD_MAX_CTAS);
+    unsigned long long *base = g_head_noalloc_dev[dev];
+    unsigned int *counter = reinterpret_cast<unsigned int *>(base);
+    e = cudaMemsetAsync(counter, 0, sizeof(unsigned int), (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail("no-alloc head: clear counter", e);
+    return q80_head_launch(w, rows, cols, x, norm_w, eps, logits, argmax_out, base + NOALLOC_HEAD_PARTIAL0, counter,
+                           (cudaStream_t)stream);
+}
+
+}  // extern "C"

@@ -57,6 +57,7 @@ _PROTOS = {
     "spk_q6k_gemv": ([_vp, _i, _i, _vp, _vp, _f, _vp, _i, _vp], _i),
     "spk_q80_gemv": ([_vp, _i, _i, _vp, _vp, _f, _vp, _i, _vp], _i),
     "spk_q80_head": ([_vp, _i, _i, _vp, _vp, _f, _vp, _vp, _vp], _i),
+    "spk_q80_head_noalloc": ([_vp, _i, _i, _vp, _vp, _f, _vp, _vp, _vp], _i),
     "spk_q6k_dequant": ([_vp, C.c_size_t, _vp, _vp], _i),
     "spk_q80_dequant": ([_vp, C.c_size_t, _vp, _vp], _i),
     "spk_q80_row": ([_vp, _i, _i, _i, _vp, _vp, _vp], _i),
