@@ -187,8 +187,11 @@ def run_ours(args) -> None:
     del W
     # the synthetic prompt, fed through the host API (teacher-forced)
     prompt = np.random.default_rng(7 + rank).integers(0, cfg.vocab, args.ctx)
-    for p, t in enumerate(prompt):
-        m.forward(int(t), p, want_logits=False)
+    if args.fill_kv:
+        m.advance_len(args.ctx)
+    else:
+        for p, t in enumerate(prompt):
+            m.forward(int(t), p, want_logits=False)
     ids = torch.zeros(args.warmup + args.steps, dtype=torch.int32, device=dev)
     m.begin(int(prompt[-1]), args.ctx, ids, args.warmup + args.steps)
     m.run(args.warmup)
@@ -269,7 +272,8 @@ def run_ours(args) -> None:
             "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded random-init weights in DQV3/Q8_0 formats, seeded prompt ids)",
-            "config": {"workload": f"config2: 36-layer VQ decoder batch-1 greedy decode at ctx {args.ctx}",
+            "config": {"workload": f"config2: 36-layer VQ decoder batch-1 greedy decode at ctx {args.ctx}"
+                                   + (" (zeroed KV, no prompt run)" if args.fill_kv else ""),
                        "model": "spark-x2.6-4b geometry, VQ 4x4096x2 trunk, Q8_0 tied head, f16 KV",
                        "global_batch": world, "seq_len": args.ctx,
                        "parallelism": "replicas" if world > 1 else "single", "l2": "weights 3.2 GB > L2, no flush",
@@ -291,6 +295,198 @@ def run_ours(args) -> None:
         pg.destroy_process_group()
 
 
+def _gemv_line(args, workload: str, value: float, alg: int, t_launch: float, kernel: str, traffic, extra: dict,
+               e2e: float, h2d: int, d2h: int, cb, clk, launches: int) -> dict:
+    peak, peak_kind = hbm_peak()
+    ach = alg / t_launch / 1e9
+    line = {"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": alg / value / 1e6, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic (seeded weights in the reference's formats, x ~ N(0,1))",
+            "config": {"workload": workload, **extra},
+            "roofline": {"bound": "hbm", "kernel": kernel, "achieved": ach, "peak": peak, "peak_kind": peak_kind,
+                         "unit": "GB/s", "frac": ach / peak, "traffic": traffic, "alg_bytes_per_launch": alg,
+                         "us_per_launch": t_launch * 1e6},
+            "e2e": {"value": e2e, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches, "clocks": clk.summary()}
+    if cb:
+        line["cpu_baseline"] = cb
+    return line
+
+
+def run_vq_gemv(args) -> None:
+    """Config 0: one VQ decode-GEMV, W 10240x2560 as DQV3 4x4096x2 (seeded codebooks and
+    indices), x ~ N(0,1) seed 1, y fp32 [10240]. A step is the whole GEMV (both stages, one
+    launch). Eight copies of the container (158 MB > L2) rotate, so every step reads HBM."""
+    import ctypes as C
+
+    import torch
+
+    import spk
+    from spk import formats as F
+
+    rows, cols, ncopy = 10240, 2560, 8
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    L = spk.lib()
+    buf = F.random_rvq_fast(rows, cols, 4, 4096, 2, seed=0)
+    c = F.parse_container(buf)
+    copies = []
+    for _ in range(ncopy):
+        ts = [spk.dev_bytes(buf[c.stage_offset(s):c.stage_offset(s) + c.stage_bytes], dev) for s in range(2)]
+        copies.append(((C.c_void_p * 2)(*[t.data_ptr() for t in ts]), ts))
+    x_host = np.random.default_rng(1).normal(0, 1, cols).astype(np.float32)
+    x = torch.from_numpy(x_host).to(dev)
+    y = torch.zeros(rows, device=dev)
+    s = torch.cuda.Stream(dev)
+    sp = C.c_void_p(s.cuda_stream)
+    alg = len(buf) + cols * 4 + rows * 4
+
+    def step(k):
+        spk.check(L.spk_vq_gemv(copies[k % ncopy][0], 2, 1, 4, 4096, rows, cols, 1, x.data_ptr(), None, 0.0,
+                                y.data_ptr(), 0, sp))
+
+    for k in range(args.warmup):
+        step(k)
+    s.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(0) as clk:
+        e0.record(s)
+        for k in range(args.steps):
+            step(k)
+        e1.record(s)
+        e1.synchronize()
+    t = e0.elapsed_time(e1) / 1e3 / args.steps
+    # end to end: x from pinned host memory up, the GEMV, y down, every step
+    xh = torch.from_numpy(x_host).pin_memory()
+    yh = torch.empty(rows, dtype=torch.float32).pin_memory()
+    n = min(args.steps, 64)
+    t0 = time.perf_counter()
+    with torch.cuda.stream(s):
+        for k in range(n):
+            x.copy_(xh, non_blocking=True)
+            step(k)
+            yh.copy_(y, non_blocking=True)
+            s.synchronize()
+    e2e = alg * n / (time.perf_counter() - t0) / 1e9
+    cb = None
+    if not args.no_cpu:
+        import oracle
+
+        thr = os.cpu_count() or 1
+        oracle.gemv_fused(buf, x_host, thr)
+        reps = 5
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            oracle.gemv_fused(buf, x_host, thr)
+        tc = (time.perf_counter() - t0) / reps
+        cb = {"value": alg / tc / 1e9, "unit": "GB/s", "cores": thr, "kind": "port",
+              "sample": f"Stage::dot_row fused GEMV restated in C (oracle/), the full config-0 matrix, {reps} reps, "
+                        f"{tc * 1e3:.1f} ms each"}
+    line = _gemv_line(args, "config0: VQ decode-GEMV 10240x2560, DQV3 dim 4, K 4096, 2 stages, batch 1",
+                      alg / t / 1e9, alg, t, "vq_fast_kernel<2,1,20,0> 10240x2560 x2 stages",
+                      traffic_from_profiles("vq_gemv_10240x2560x2"),
+                      {"rows": rows, "cols": cols, "container_bytes": len(buf), "l2": f"{ncopy} rotating copies, 158 MB > L2"},
+                      e2e, cols * 4, rows * 4, cb, clk, args.steps)
+    print(json.dumps(line), flush=True)
+
+
+GGML_SHAPES = [("q6k", "q", 4096, 2560), ("q6k", "k", 1024, 2560), ("q6k", "v", 1024, 2560),
+               ("q6k", "o", 2560, 4096), ("q6k", "gate", 10240, 2560), ("q6k", "up", 10240, 2560),
+               ("q6k", "down", 2560, 10240), ("q80", "head", 131072, 2560)]
+
+
+def run_ggml(args) -> None:
+    """Config 1: the Q6_K dequant-GEMV over every trunk shape and the Q8_0 GEMV over the
+    131072x2560 tied head, batch 1, W ~ N(0, 0.02^2) quantized with the block rules (Q6_K by
+    the package's encoder, Q8_0 by ggml's d = max|w|/127 statistics), x ~ N(0,1). A step is
+    one pass over the eight matrices (442 MB > L2, so each step reads HBM)."""
+    import ctypes as C
+
+    import torch
+
+    import spk
+    from spk import formats as F
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    L = spk.lib()
+    rng = np.random.default_rng(0)
+    mats = []
+    for fmt, name, rows, cols in GGML_SHAPES:
+        if fmt == "q6k":
+            blob = F.quantize_q6_k(rng.normal(0, 0.02, (rows, cols)).astype(np.float32))
+        else:
+            blob = F.synth_q8_0(rows, cols, seed=1)
+        x_host = rng.normal(0, 1, cols).astype(np.float32)
+        mats.append({"fmt": fmt, "name": name, "rows": rows, "cols": cols, "blob": blob,
+                     "w": spk.dev_bytes(blob, dev), "x_host": x_host, "x": torch.from_numpy(x_host).to(dev),
+                     "y": torch.zeros(rows, device=dev), "alg": len(blob) + 4 * cols + 4 * rows})
+    s = torch.cuda.Stream(dev)
+    sp = C.c_void_p(s.cuda_stream)
+
+    def launch(m):
+        fn = L.spk_q6k_gemv if m["fmt"] == "q6k" else L.spk_q80_gemv
+        spk.check(fn(m["w"].data_ptr(), m["rows"], m["cols"], m["x"].data_ptr(), None, 0.0, m["y"].data_ptr(), 0, sp))
+
+    for _ in range(args.warmup):
+        for m in mats:
+            launch(m)
+    s.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(mats) + 1)]
+    per = np.zeros(len(mats))
+    with Clocks(0) as clk:
+        for _ in range(args.steps):
+            ev[0].record(s)
+            for i, m in enumerate(mats):
+                launch(m)
+                ev[i + 1].record(s)
+            ev[-1].synchronize()
+            per += [ev[i].elapsed_time(ev[i + 1]) / 1e3 for i in range(len(mats))]
+    per /= args.steps
+    alg = sum(m["alg"] for m in mats)
+    t = float(per.sum())
+    xh = [torch.from_numpy(m["x_host"]).pin_memory() for m in mats]
+    yh = [torch.empty(m["rows"], dtype=torch.float32).pin_memory() for m in mats]
+    n = min(args.steps, 16)
+    t0 = time.perf_counter()
+    with torch.cuda.stream(s):
+        for _ in range(n):
+            for i, m in enumerate(mats):
+                m["x"].copy_(xh[i], non_blocking=True)
+                launch(m)
+                yh[i].copy_(m["y"], non_blocking=True)
+            s.synchronize()
+    e2e = alg * n / (time.perf_counter() - t0) / 1e9
+    cb = None
+    if not args.no_cpu:
+        import oracle
+
+        thr = os.cpu_count() or 1
+        tc = 0.0
+        for m in mats:
+            fn = oracle.q6k_gemv if m["fmt"] == "q6k" else oracle.q80_gemv
+            fn(m["blob"], m["rows"], m["cols"], m["x_host"], thr)
+            t0 = time.perf_counter()
+            fn(m["blob"], m["rows"], m["cols"], m["x_host"], thr)
+            tc += time.perf_counter() - t0
+        cb = {"value": alg / tc / 1e9, "unit": "GB/s", "cores": thr, "kind": "port",
+              "sample": f"ggml dequantize_row_q6_K / q8_0 order GEMV restated in C (oracle/), one pass over the "
+                        f"eight matrices, {tc * 1e3:.1f} ms"}
+    peak, _ = hbm_peak()
+    detail = {f"{m['fmt']}_{m['name']}_{m['rows']}x{m['cols']}": {"us": per[i] * 1e6,
+                                                                   "gbs": m["alg"] / per[i] / 1e9,
+                                                                   "frac": m["alg"] / per[i] / 1e9 / peak}
+              for i, m in enumerate(mats)}
+    head = len(mats) - 1
+    line = _gemv_line(args, "config1: Q6_K trunk shapes + Q8_0 131072x2560 head, batch 1", alg / t / 1e9,
+                      mats[head]["alg"], per[head], "blk_fast_kernel Q8_0 131072x2560",
+                      traffic_from_profiles("q80_gemv_131072x2560"),
+                      {"matrices": detail, "l2": "442 MB per pass > L2, no flush"},
+                      e2e, sum(4 * m["cols"] for m in mats), sum(4 * m["rows"] for m in mats), cb, clk,
+                      args.steps * len(mats))
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -298,12 +494,21 @@ def main():
     ap.add_argument("--warmup", type=int, default=16)
     ap.add_argument("--ctx", type=int, default=4096)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "vq", "ggml"],
+                    help="decode: config 2 (default); vq: config 0 GEMV; ggml: config 1 Q6_K/Q8_0 sweep")
+    ap.add_argument("--fill-kv", action="store_true",
+                    help="decode: start at ctx over a zeroed KV cache instead of running the prompt "
+                         "(the same attention bytes per step; for profiler captures)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("at least 3 warm-up steps")
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "vq":
+        run_vq_gemv(args)
+    elif args.workload == "ggml":
+        run_ggml(args)
     else:
         run_ours(args)
 

@@ -74,6 +74,10 @@ inline bool v3_width_ok(int nc) {
 int sm_count();
 size_t smem_optin_max();
 
+// Tensor-core VQ GEMV (vq_mma.cu): 1 launched, 0 geometry not taken, -1 error.
+int vq_mma_gemv(const void *const *stages, int nstg, const Layout &L, const float *x, const float *norm_w, float eps,
+                float *y, int accumulate, int mode, const float *aux, cudaStream_t s);
+
 // Q8_0 head (logits + argmax) with caller-owned scratch (ggml.cu).
 int q80_head_launch(const void *w, int rows, int cols, const float *x, const float *norm_w, float eps, float *logits,
                     int *argmax_out, unsigned long long *partial, unsigned int *counter, cudaStream_t s);

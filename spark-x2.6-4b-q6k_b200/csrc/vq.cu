@@ -78,8 +78,13 @@ __device__ float block_rms_inv(const float *x, int n, float eps, double *red) {
 }
 
 // ============================================================ fast path ===
-constexpr int FAST_WARPS = 16;
-constexpr int FAST_THREADS = FAST_WARPS * 32;
+// 16 warps per CTA at every F: a lane's 4F activations live in registers
+// (512 threads, up to 128 registers each). 24 warps at F <= 10 measured slower
+// on the model's shapes than 16 warps at F 16/20.
+template <int F>
+struct Warps {
+    static constexpr int W = 16;
+};
 constexpr int FAST_NBUF = 3;
 constexpr int MAXQ = 4;   // streams: groups x stages
 
@@ -100,7 +105,9 @@ struct FastArgs {
 
 template <int F>
 struct Chunk {
-    static constexpr int MAXSH = ((12 * F) % 32 == 0) ? 0 : 16;
+    // largest bit offset a lane's run can start at inside a 32-bit word
+    static constexpr int G = ((12 * F) % 32 == 0) ? 32 : ((12 * F) % 32 % 16 == 0 ? 16 : ((12 * F) % 32 % 8 == 0 ? 8 : 4));
+    static constexpr int MAXSH = 32 - G == 0 ? 0 : 32 - G;
     static constexpr int NWR = (MAXSH + 12 * F + 31) / 32;   // words read
     static constexpr int NWU = (12 * F + 31) / 32;           // words used after the shift
 };
@@ -169,9 +176,12 @@ __device__ __forceinline__ void issue_tile(const FastArgs &a, int nq, int ext, u
 }
 
 template <int NSTG, int NG, int F, int EXT>
-__global__ void __launch_bounds__(FAST_THREADS, 1) vq_fast_kernel(const FastArgs a) {
+__global__ void __launch_bounds__(Warps<F>::W * 32, 1) vq_fast_kernel(const FastArgs a) {
+    constexpr int FAST_WARPS = Warps<F>::W, FAST_THREADS = FAST_WARPS * 32;
     constexpr int NQ = NSTG * NG;
-    constexpr int XS = 4 * F + 4;   // padded per-lane stride of the staged activations (floats)
+    // padded per-lane stride of the staged activations (floats): an odd number of
+    // 16-byte chunks, so 8 lanes' float4 reads hit 8 distinct bank quads
+    constexpr int XS = 4 * (F + 1 + (F & 1));
     extern __shared__ __align__(16) uint8_t smem[];
     const Layout &L = a.L;
     const int nc = L.nc;
@@ -424,15 +434,18 @@ bool blk_ok(const Layout &L) {
 }
 
 int pick_split(const Layout &L, int *F) {
-    // smallest k (warps per row chunk) with nidx_row/(32k) in {20, 16, 8, 4}
-    for (int k = 1; k <= 8; k *= 2) {
-        if (L.nidx_row % (32 * (size_t)k)) continue;
-        const int f = (int)(L.nidx_row / (32 * (size_t)k));
-        if (f == 20 || f == 16 || f == 8 || f == 4) {
-            *F = f;
-            return k;
+    // smallest k (warps per row) giving F = nidx_row/(32k) of 20 or 16 (fewest
+    // warps per row, least partial-sum traffic); else the smallest k giving one
+    // of the other instantiated F
+    for (int pass = 0; pass < 2; pass++)
+        for (int k = 1; k <= 16; k *= 2) {
+            if (L.nidx_row % (32 * (size_t)k)) continue;
+            const int f = (int)(L.nidx_row / (32 * (size_t)k));
+            if ((pass == 0 && (f == 20 || f == 16)) || (pass == 1 && (f == 10 || f == 8 || f == 5 || f == 4))) {
+                *F = f;
+                return k;
+            }
         }
-    }
     return 0;
 }
 
@@ -448,8 +461,9 @@ bool fast_plan(const uint8_t *const *st, int nstg, int ng, const Layout &L, Fast
         if (((uintptr_t)st[q] & 7) != 0) return false;
     int F = 0;
     const int ks = pick_split(L, &F);
-    if (!ks || ks * ng > FAST_WARPS) return false;
-    const int tr = FAST_WARPS / (ks * ng);
+    const int W = Warps<20>::W;
+    if (!ks || ks * ng > W || W % (ks * ng)) return false;
+    const int tr = W / (ks * ng);
     const int nq = nstg * ng, ext = L.prow ? 1 : 0;
     const uint32_t main_slot = (uint32_t)(((size_t)tr * L.mrow + 32 + 15) & ~(size_t)15);
     const uint32_t plane_slot = ext ? (uint32_t)(((size_t)tr * L.prow + 32 + 15) & ~(size_t)15) : 0u;
@@ -457,7 +471,7 @@ bool fast_plan(const uint8_t *const *st, int nstg, int ng, const Layout &L, Fast
     int nbuf = FAST_NBUF;
     size_t smem = 0;
     for (; nbuf >= 2; nbuf--) {
-        smem = (((size_t)nq * L.nc * 8 + 15) & ~(size_t)15) + (size_t)ks * 32 * (4 * F + 4) * 4 + (size_t)nbuf * slot +
+        smem = (((size_t)nq * L.nc * 8 + 15) & ~(size_t)15) + (size_t)ks * 32 * (4 * (F + 1 + (F & 1))) * 4 + (size_t)nbuf * slot +
                2 * (size_t)nbuf * 8 + (size_t)2 * tr * ng * ks * nstg * 4 + 32 * 8;
         if (smem <= smem_optin_max()) break;
     }
@@ -492,7 +506,7 @@ int launch_fast_t(const FastPlan &P, cudaStream_t s) {
     }
     const int ntr = (P.args.L.rows + P.tr - 1) / P.tr;
     const int grid = ntr < sm_count() ? ntr : sm_count();
-    k<<<grid, FAST_THREADS, P.smem, s>>>(P.args);
+    k<<<grid, Warps<F>::W * 32, P.smem, s>>>(P.args);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? 0 : cuda_fail("vq fast kernel launch", e);
 }
@@ -507,7 +521,9 @@ int launch_fast_f(const FastPlan &P, cudaStream_t s) {
     switch (P.F) {
         case 20: return launch_fast_e<NSTG, NG, 20>(P, s);
         case 16: return launch_fast_e<NSTG, NG, 16>(P, s);
+        case 10: return launch_fast_e<NSTG, NG, 10>(P, s);
         case 8: return launch_fast_e<NSTG, NG, 8>(P, s);
+        case 5: return launch_fast_e<NSTG, NG, 5>(P, s);
         case 4: return launch_fast_e<NSTG, NG, 4>(P, s);
     }
     return set_error("vq fast kernel: no instantiation for F=%d", P.F);
