@@ -147,6 +147,13 @@ typedef struct {
     const int *full;   /* host array [layers]: 1 = full attention, 0 = sliding window */
     int max_ctx;       /* cache capacity in positions */
     int kv_f16;        /* 0: f32 K/V (the reference runtimes' cache), 1: f16 K/V */
+    /* Tensor parallelism (no counterpart in the reference, which runs one GPU): this
+     * model is rank tp_rank of tp_world (0 or 1: a single GPU). A rank holds q heads
+     * [r*heads/t, (r+1)*heads/t), the KV heads they read (KV heads are replicated when
+     * t > kv_heads), intermediate rows [r*inter/t, (r+1)*inter/t) of gate/up and the
+     * matching input columns of down, and vocabulary rows [r*vocab/t, (r+1)*vocab/t)
+     * of the head; the embedding table stays whole on every rank. */
+    int tp_rank, tp_world;
 } spk_model_config;
 
 /* One VQ matrix: the device pointers of its stage payloads (each with >= 8 zeroed
@@ -184,6 +191,22 @@ int spk_model_reset(spk_model *m);
 /* Positions cached; and the host-side length bump after spk_model_run. */
 int spk_model_len(spk_model *m);
 int spk_model_advance_len(spk_model *m, int n);
+
+/* Tensor-parallel wiring (no counterpart in the reference). Each rank's model owns a
+ * mailbox in device memory; the residual reductions and the head's argmax store rows
+ * into every rank's mailbox over NVLink and wait on release flags there, bounded by
+ * wait_ms (a wait that runs out sets a device error that spk_model_forward reports).
+ * spk_model_tp_handle writes the mailbox's cudaIpcMemHandle_t (n >= 64 bytes);
+ * spk_model_tp_attach takes every rank's handle in rank order (n = 64 * tp_world);
+ * spk_model_tp_attach_ptrs takes the mailboxes as pointers valid in this process (one
+ * process driving several GPUs with peer access enabled). Attach before the first step.
+ * With tp_world > 1, spk_model_logits is this rank's vocabulary shard; spk_model_forward
+ * gathers the whole vocabulary when logits_host is not NULL. */
+int spk_model_tp_handle(spk_model *m, void *handle_out, int n);
+int spk_model_tp_attach(spk_model *m, const void *handles, int n, int wait_ms);
+int spk_model_tp_attach_ptrs(spk_model *m, void *const *mailboxes, int world, int wait_ms);
+/* This rank's mailbox pointer (for spk_model_tp_attach_ptrs). */
+void *spk_model_tp_mailbox(spk_model *m);
 
 #ifdef __cplusplus
 }

@@ -45,7 +45,9 @@ int check_device_error(const char *where) {
         int z = 0;
         cudaMemcpyToSymbol(g_dev_err, &z, sizeof z);
         return set_error("%s: device reported %s", where,
-                         v == DEV_WAIT_TIMEOUT ? "a wait that ran out (copy never completed)" : "an out-of-range index");
+                         v == DEV_WAIT_TIMEOUT   ? "a wait that ran out (copy never completed)"
+                         : v == DEV_PEER_TIMEOUT ? "a peer that never reached an exchange (tensor-parallel rank missing or stalled)"
+                                                 : "an out-of-range index");
     }
     return 0;
 }

@@ -22,7 +22,7 @@ int cuda_fail(const char *what, cudaError_t e);
 
 // Device-side error word. Kernels never trap: a bounded wait that runs out
 // sets a code here and the kernel returns; the host reads it with check_device_error().
-enum : int { DEV_OK = 0, DEV_WAIT_TIMEOUT = 1, DEV_BAD_INDEX = 2 };
+enum : int { DEV_OK = 0, DEV_WAIT_TIMEOUT = 1, DEV_BAD_INDEX = 2, DEV_PEER_TIMEOUT = 3 };
 int check_device_error(const char *where);
 int *device_error_ptr();   // address of the word on the current device
 
@@ -77,6 +77,12 @@ size_t smem_optin_max();
 // Tensor-core VQ GEMV (vq_mma.cu): 1 launched, 0 geometry not taken, -1 error.
 int vq_mma_gemv(const void *const *stages, int nstg, const Layout &L, const float *x, const float *norm_w, float eps,
                 float *y, int accumulate, int mode, const float *aux, cudaStream_t s);
+
+// QKV and g_proj in one launch (vq.cu): y = W RMSNorm?(x), xy = X RMSNorm?(x).
+// 0 launched, 1 geometry not taken, -1 error.
+int vq_gemv_with_extra(const void *const *stages, int nstg, const Layout &L, const void *const *xstages,
+                       const Layout &XL, const float *x, const float *norm_w, float eps, float *y, float *xy,
+                       int accumulate, cudaStream_t s);
 
 // Q8_0 head (logits + argmax) with caller-owned scratch (ggml.cu).
 int q80_head_launch(const void *w, int rows, int cols, const float *x, const float *norm_w, float eps, float *logits,

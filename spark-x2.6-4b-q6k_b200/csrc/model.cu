@@ -18,6 +18,11 @@
 // then the tied Q8_0 head with fused argmax (ggml.cu) and a one-thread advance
 // kernel (pos += 1, token = argmax). Token and position live in device memory,
 // so the whole step is captured once in a CUDA graph and replayed per token.
+//
+// Tensor parallel (tp_world t > 1): a rank runs the same launches over its shards
+// (q heads / KV heads, intermediate rows, vocabulary rows); out_proj and down_proj
+// write a partial residual that tp_sum (tp.cu) reduces over all ranks into the
+// replicated h, and tp_argmax picks the greedy id over the vocabulary shards.
 #include <math.h>
 #include <stdlib.h>
 
@@ -25,6 +30,7 @@
 
 #include "common.cuh"
 #include "spk.h"
+#include "tp.cuh"
 
 using namespace spk;
 
@@ -109,10 +115,10 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_partial_kernel(const AttnArg
             }
         }
     }
-    if (c0 >= c1) {   // an empty split: nothing to merge
-        if (threadIdx.x < G) {
-            out[threadIdx.x * (HD + 2) + HD] = -INFINITY;
-            out[threadIdx.x * (HD + 2) + HD + 1] = 0.f;
+    if (c0 >= c1) {   // an empty split: weight 0 in the merge (o zeroed so 0 * o stays 0)
+        for (int i = threadIdx.x; i < G * (HD + 2); i += blockDim.x) {
+            const int d = i % (HD + 2);
+            out[i] = d == HD ? -INFINITY : 0.f;
         }
         return;
     }
@@ -201,25 +207,41 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_partial_kernel(const AttnArg
 
 // Merge the splits of every q head and apply the per-head sigmoid gate
 // (model.rs:538-550): attn[h][d] = (sum_c o_c e^{m_c-M}) / (sum_c l_c e^{m_c-M}) * sigmoid(g_h).
-__global__ void attn_combine_kernel(const float *part, int nsplit, int heads, int kv_heads, int hd,
-                                    const float *gate, float *attn) {
+// One CTA per q head: the split maxima and weights are formed once in shared
+// memory (one thread per split), then every thread sums its dims over the splits
+// with independent loads.
+constexpr int COMB_MAX_SPLIT = 256;
+__global__ void __launch_bounds__(128) attn_combine_kernel(const float *part, int nsplit, int heads, int kv_heads,
+                                                           int hd, const float *gate, float *attn) {
+    __shared__ float w[COMB_MAX_SPLIT];
+    __shared__ float red[4];
     const int h = blockIdx.x, G = heads / kv_heads, kvh = h / G, gi = h % G;
     const float *p0 = part + (size_t)kvh * nsplit * G * (hd + 2) + (size_t)gi * (hd + 2);
     const size_t stride = (size_t)G * (hd + 2);
-    float M = -INFINITY;
-    for (int c = 0; c < nsplit; c++) M = fmaxf(M, p0[c * stride + hd]);
-    float L = 0.f;
-    for (int c = 0; c < nsplit; c++) {
-        const float mc = p0[c * stride + hd];
-        if (mc != -INFINITY) L += p0[c * stride + hd + 1] * expf(mc - M);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float mc = -INFINITY;
+    for (int c = threadIdx.x; c < nsplit; c += blockDim.x) mc = fmaxf(mc, p0[c * stride + hd]);
+    for (int o = 16; o > 0; o >>= 1) mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, o));
+    if (lane == 0) red[warp] = mc;
+    __syncthreads();
+    const float M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    __syncthreads();
+    float lsum = 0.f;
+    for (int c = threadIdx.x; c < nsplit; c += blockDim.x) {
+        const float m = p0[c * stride + hd];
+        const float e = m == -INFINITY ? 0.f : expf(m - M);
+        w[c] = e;
+        lsum += p0[c * stride + hd + 1] * e;
     }
+    lsum = warp_sum(lsum);
+    if (lane == 0) red[warp] = lsum;
+    __syncthreads();
+    const float L = (red[0] + red[1]) + (red[2] + red[3]);
     const float gsig = 1.0f / (1.0f + expf(-gate[h]));
     for (int d = threadIdx.x; d < hd; d += blockDim.x) {
         float O = 0.f;
-        for (int c = 0; c < nsplit; c++) {
-            const float mc = p0[c * stride + hd];
-            if (mc != -INFINITY) O += p0[c * stride + d] * expf(mc - M);
-        }
+#pragma unroll 8
+        for (int c = 0; c < nsplit; c++) O += p0[c * stride + d] * w[c];
         attn[(size_t)h * hd + d] = (O / L) * gsig;
     }
 }
@@ -258,12 +280,23 @@ struct spk_model {
     const void *embed = nullptr;
     const float *final_norm = nullptr;
     int q_dim = 0, kv_dim = 0, G = 0, pdim_full = 0, pdim_slide = 0, nsplit_full = 1, nsplit_slide = 1;
+    // tensor parallel: local head counts, intermediate rows, vocabulary shard
+    int tp_rank = 0, tp_world = 1, hl = 0, kvl = 0, inter_l = 0, vocab_l = 0, row0 = 0;
+    void *mailbox = nullptr;      // this rank's exchange mailbox (+ flags + logits shard when t > 1)
+    size_t mail_flags_off = 0, mail_logits_off = 0;
+    int mail_stride = 0;
+    void *peer_open[TP_MAX] = {};   // IPC mappings to close
+    const float *peer_logits[TP_MAX] = {};
+    float *pbuf = nullptr, *logits_full = nullptr;
+    unsigned int *tp_seq = nullptr;
+    TpView tpv = {};
+    bool tp_ready = false;
     float *h = nullptr, *qkv = nullptr, *gate = nullptr, *attn = nullptr, *act = nullptr, *logits = nullptr,
           *part = nullptr, *freq_full = nullptr, *freq_slide = nullptr;
     void *kc = nullptr, *vc = nullptr;
     std::vector<size_t> kv_off;   // per layer element offset into kc / vc
     std::vector<int> kv_slots;
-    int *state = nullptr;         // device: pos, token, argmax, step
+    int *state = nullptr;         // device: pos, token, argmax, step, local argmax
     DevCtl *ctl = nullptr;        // device: id buffer of spk_model_run
     DevCtl *host_ctl = nullptr;   // pinned staging for it
     unsigned long long *head_partial = nullptr;
@@ -287,6 +320,19 @@ int vq_call(const spk_vq_matrix &M, int ngroups, const spk_vq_matrix *M2, const 
     return spk_vq_gemv(st, M.nstages, ngroups, M.dim, M.nc, M.rows, M.cols, M.v3, x, norm_w, eps, y, accumulate, s);
 }
 
+// q_k_v_proj and g_proj (same input, same encoding) as one launch when the
+// encodings agree, else two.
+int qkv_gate(const spk_model::Layer &L, const float *h, float eps, float *qkv, float *gate, cudaStream_t s) {
+    const spk_vq_matrix &Q = L.m[0], &G = L.m[1];
+    if (Q.nstages == G.nstages && Q.nstages <= 2) {
+        const Layout LQ = make_layout(Q.dim, Q.nc, Q.rows, Q.cols, Q.v3), LG = make_layout(G.dim, G.nc, G.rows, G.cols, G.v3);
+        const int rc = vq_gemv_with_extra(Q.stages, Q.nstages, LQ, G.stages, LG, h, L.in_norm, eps, qkv, gate, 0, s);
+        if (rc <= 0) return rc;
+    }
+    if (vq_call(Q, 1, nullptr, h, L.in_norm, eps, qkv, 0, s)) return -1;
+    return vq_call(G, 1, nullptr, h, L.in_norm, eps, gate, 0, s);
+}
+
 template <int HD>
 int attn_launch(const AttnArgs &a, cudaStream_t s) {
     attn_partial_kernel<HD><<<dim3(a.kv_heads, a.nsplit), ATT_THREADS, 0, s>>>(a);
@@ -298,12 +344,12 @@ int attn_launch(const AttnArgs &a, cudaStream_t s) {
 int enqueue_step(spk_model *m) {
     const spk_model_config &c = m->cfg;
     cudaStream_t s = m->stream;
-    int *pos = m->state, *token = m->state + 1, *amax = m->state + 2;
+    int *pos = m->state, *token = m->state + 1, *amax = m->state + 2, *amax_l = m->state + 4;
+    const bool tp = m->tp_world > 1;
     if (spk_q80_row(m->embed, c.vocab, c.hidden, 0, token, m->h, s)) return -1;
     for (int li = 0; li < c.layers; li++) {
         const spk_model::Layer &L = m->layers[li];
-        if (vq_call(L.m[0], 1, nullptr, m->h, L.in_norm, c.eps, m->qkv, 0, s)) return -1;
-        if (vq_call(L.m[1], 1, nullptr, m->h, L.in_norm, c.eps, m->gate, 0, s)) return -1;
+        if (qkv_gate(L, m->h, c.eps, m->qkv, m->gate, s)) return -1;
         AttnArgs a;
         a.qkv = m->qkv;
         const size_t esz = c.kv_f16 ? 2 : 4;
@@ -315,22 +361,33 @@ int enqueue_step(spk_model *m) {
         a.window = c.window;
         a.freq = a.full ? m->freq_full : m->freq_slide;
         a.pdim = a.full ? m->pdim_full : m->pdim_slide;
-        a.heads = c.heads;
-        a.kv_heads = c.kv_heads;
+        a.heads = m->hl;
+        a.kv_heads = m->kvl;
         a.hd = c.head_dim;
         a.pos = pos;
         a.nsplit = a.full ? m->nsplit_full : m->nsplit_slide;
         a.part = m->part;
         if ((c.head_dim == 256 ? attn_launch<256>(a, s) : attn_launch<128>(a, s))) return -1;
-        attn_combine_kernel<<<c.heads, 128, 0, s>>>(m->part, a.nsplit, c.heads, c.kv_heads, c.head_dim, m->gate,
-                                                    m->attn);
-        if (vq_call(L.m[2], 1, nullptr, m->attn, nullptr, 0.f, m->h, 1, s)) return -1;
+        attn_combine_kernel<<<m->hl, 128, 0, s>>>(m->part, a.nsplit, m->hl, m->kvl, c.head_dim, m->gate, m->attn);
+        if (tp) {
+            if (vq_call(L.m[2], 1, nullptr, m->attn, nullptr, 0.f, m->pbuf, 0, s)) return -1;
+            if (tp_sum(m->tpv, m->pbuf, m->h, c.hidden, s)) return -1;
+        } else if (vq_call(L.m[2], 1, nullptr, m->attn, nullptr, 0.f, m->h, 1, s)) {
+            return -1;
+        }
         if (vq_call(L.m[3], 2, &L.m[4], m->h, L.post_norm, c.eps, m->act, 0, s)) return -1;
-        if (vq_call(L.m[5], 1, nullptr, m->act, nullptr, 0.f, m->h, 1, s)) return -1;
+        if (tp) {
+            if (vq_call(L.m[5], 1, nullptr, m->act, nullptr, 0.f, m->pbuf, 0, s)) return -1;
+            if (tp_sum(m->tpv, m->pbuf, m->h, c.hidden, s)) return -1;
+        } else if (vq_call(L.m[5], 1, nullptr, m->act, nullptr, 0.f, m->h, 1, s)) {
+            return -1;
+        }
     }
-    if (q80_head_launch(m->embed, c.vocab, c.hidden, m->h, m->final_norm, c.eps, m->logits, amax, m->head_partial,
-                        m->head_counter, s))
+    const uint8_t *head_rows = (const uint8_t *)m->embed + (size_t)m->row0 * (c.hidden / 32) * 34;
+    if (q80_head_launch(head_rows, m->vocab_l, c.hidden, m->h, m->final_norm, c.eps, m->logits, tp ? amax_l : amax,
+                        m->head_partial, m->head_counter, s))
         return -1;
+    if (tp && tp_argmax(m->tpv, m->logits, amax_l, m->row0, amax, s)) return -1;
     advance_kernel<<<1, 1, 0, s>>>(pos, token, amax, m->ctl, m->state + 3);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? 0 : cuda_fail("decode step launch", e);
@@ -338,6 +395,7 @@ int enqueue_step(spk_model *m) {
 
 bool ready(const spk_model *m) {
     if (!m->embed || !m->final_norm) return false;
+    if (m->tp_world > 1 && !m->tp_ready) return false;
     for (const auto &L : m->layers)
         if (!L.set) return false;
     return true;
@@ -394,22 +452,36 @@ spk_model *spk_model_create(const spk_model_config *cfg, void *stream) {
         set_error("unsupported model geometry (head_dim 128/256, GQA group <= 4, hidden a multiple of 32)");
         return nullptr;
     }
+    const int t = c.tp_world > 1 ? c.tp_world : 1, r = t > 1 ? c.tp_rank : 0;
+    if (t > TP_MAX || r < 0 || r >= t || c.heads % t || (c.kv_heads % t && t % c.kv_heads) || c.inter % t ||
+        c.vocab % t) {
+        set_error("tensor parallel %d of %d: heads, inter and vocab must divide by the world size, and kv_heads "
+                  "must divide it or be divisible by it (at most %d ranks)", r, t, TP_MAX);
+        return nullptr;
+    }
     spk_model *m = new spk_model();
+    m->tp_rank = r;
+    m->tp_world = t;
+    m->hl = c.heads / t;
+    m->kvl = c.kv_heads >= t ? c.kv_heads / t : 1;
+    m->inter_l = c.inter / t;
+    m->vocab_l = c.vocab / t;
+    m->row0 = r * m->vocab_l;
     m->cfg = c;
     m->full.assign(c.full, c.full + c.layers);
     m->cfg.full = m->full.data();
     m->layers.resize(c.layers);
     m->stream = (cudaStream_t)stream;
-    m->q_dim = c.heads * c.head_dim;
-    m->kv_dim = c.kv_heads * c.head_dim;
-    m->G = c.heads / c.kv_heads;
+    m->q_dim = m->hl * c.head_dim;
+    m->kv_dim = m->kvl * c.head_dim;
+    m->G = m->hl / m->kvl;
     auto pdim = [&](float partial) {
         int d = (int)((float)c.head_dim * partial);
         return d < c.head_dim ? d : c.head_dim;
     };
     m->pdim_full = pdim(c.rope_partial_full);
     m->pdim_slide = pdim(c.rope_partial_slide);
-    const int per_head = sm_count() / c.kv_heads > 0 ? sm_count() / c.kv_heads : 1;
+    const int per_head = std::min(COMB_MAX_SPLIT, sm_count() / m->kvl > 0 ? sm_count() / m->kvl : 1);
     m->nsplit_full = std::max(1, std::min(per_head, (c.max_ctx + 15) / 16));
     m->nsplit_slide = std::max(1, std::min(per_head, (std::min(c.window, c.max_ctx) + 15) / 16));
     size_t kv_elems = 0;
@@ -417,20 +489,36 @@ spk_model *spk_model_create(const spk_model_config *cfg, void *stream) {
         const int slots = m->full[li] ? c.max_ctx : std::min(c.window, c.max_ctx);
         m->kv_off.push_back(kv_elems);
         m->kv_slots.push_back(slots);
-        kv_elems += (size_t)c.kv_heads * slots * c.head_dim;
+        kv_elems += (size_t)m->kvl * slots * c.head_dim;
     }
     const size_t esz = c.kv_f16 ? 2 : 4;
     const int nsplit = std::max(m->nsplit_full, m->nsplit_slide);
     bool ok = !alloc((void **)&m->h, c.hidden * 4, "alloc h") && !alloc((void **)&m->qkv, (m->q_dim + 2 * m->kv_dim) * 4, "alloc qkv") &&
-              !alloc((void **)&m->gate, c.heads * 4, "alloc gate") && !alloc((void **)&m->attn, m->q_dim * 4, "alloc attn") &&
-              !alloc((void **)&m->act, (size_t)c.inter * 4, "alloc act") && !alloc((void **)&m->logits, (size_t)c.vocab * 4, "alloc logits") &&
-              !alloc((void **)&m->part, (size_t)c.kv_heads * nsplit * m->G * (c.head_dim + 2) * 4, "alloc attention partials") &&
+              !alloc((void **)&m->gate, m->hl * 4, "alloc gate") && !alloc((void **)&m->attn, m->q_dim * 4, "alloc attn") &&
+              !alloc((void **)&m->act, (size_t)m->inter_l * 4, "alloc act") &&
+              !alloc((void **)&m->part, (size_t)m->kvl * nsplit * m->G * (c.head_dim + 2) * 4, "alloc attention partials") &&
               !alloc((void **)&m->freq_full, c.head_dim * 4, "alloc rope") && !alloc((void **)&m->freq_slide, c.head_dim * 4, "alloc rope") &&
               !alloc(&m->kc, kv_elems * esz, "alloc K cache") && !alloc(&m->vc, kv_elems * esz, "alloc V cache") &&
-              !alloc((void **)&m->state, 4 * sizeof(int), "alloc state") &&
+              !alloc((void **)&m->state, 8 * sizeof(int), "alloc state") &&
               !alloc((void **)&m->ctl, sizeof(DevCtl), "alloc control") &&
               !alloc((void **)&m->head_partial, 1024 * sizeof(unsigned long long), "alloc head partials") &&
               !alloc((void **)&m->head_counter, sizeof(unsigned int), "alloc head counter");
+    if (ok && t == 1) {
+        ok = !alloc((void **)&m->logits, (size_t)c.vocab * 4, "alloc logits");
+    } else if (ok) {
+        // one mailbox holds the exchange rows, the flags and this rank's logits shard
+        // (peers read the shard when a host forward asks for the whole vocabulary)
+        const size_t mb = tp_mailbox_bytes(t, c.hidden, &m->mail_flags_off, &m->mail_stride);
+        m->mail_logits_off = (mb + 255) / 256 * 256;
+        const size_t total = m->mail_logits_off + (size_t)m->vocab_l * 4;
+        ok = !alloc(&m->mailbox, total, "alloc tensor-parallel mailbox") &&
+             cudaMemset(m->mailbox, 0, total) == cudaSuccess && !alloc((void **)&m->pbuf, c.hidden * 4, "alloc partial") &&
+             !alloc((void **)&m->logits_full, (size_t)c.vocab * 4, "alloc gathered logits") &&
+             !alloc((void **)&m->tp_seq, sizeof(unsigned int), "alloc exchange counter") &&
+             cudaMemset(m->tp_seq, 0, sizeof(unsigned int)) == cudaSuccess;
+        if (ok) m->logits = (float *)((uint8_t *)m->mailbox + m->mail_logits_off);
+        else set_error("tensor-parallel allocation failed");
+    }
     if (ok && (cudaMallocHost((void **)&m->host_io, 4 * sizeof(int)) != cudaSuccess ||
                cudaMallocHost((void **)&m->host_ctl, sizeof(DevCtl)) != cudaSuccess))
         ok = !set_error("pinned staging allocation failed");
@@ -442,7 +530,7 @@ spk_model *spk_model_create(const spk_model_config *cfg, void *stream) {
         ok = cudaMemcpy(m->freq_full, ff.data(), c.head_dim * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
              cudaMemcpy(m->freq_slide, fs.data(), c.head_dim * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
              cudaMemset(m->kc, 0, kv_elems * esz) == cudaSuccess && cudaMemset(m->vc, 0, kv_elems * esz) == cudaSuccess &&
-             cudaMemset(m->state, 0, 4 * sizeof(int)) == cudaSuccess && cudaMemset(m->ctl, 0, sizeof(DevCtl)) == cudaSuccess &&
+             cudaMemset(m->state, 0, 8 * sizeof(int)) == cudaSuccess && cudaMemset(m->ctl, 0, sizeof(DevCtl)) == cudaSuccess &&
              cudaMemset(m->head_counter, 0, sizeof(unsigned int)) == cudaSuccess;
         if (!ok) set_error("model initialisation copies failed");
     }
@@ -457,8 +545,11 @@ void spk_model_destroy(spk_model *m) {
     if (!m) return;
     if (m->exec) cudaGraphExecDestroy(m->exec);
     if (m->graph) cudaGraphDestroy(m->graph);
-    void *ps[] = {m->h, m->qkv, m->gate, m->attn, m->act, m->logits, m->part, m->freq_full, m->freq_slide,
-                  m->kc, m->vc, m->state, m->ctl, m->head_partial, m->head_counter};
+    for (int r = 0; r < TP_MAX; r++)
+        if (m->peer_open[r]) cudaIpcCloseMemHandle(m->peer_open[r]);
+    void *ps[] = {m->h, m->qkv, m->gate, m->attn, m->act, m->tp_world > 1 ? nullptr : m->logits, m->part,
+                  m->freq_full, m->freq_slide, m->kc, m->vc, m->state, m->ctl, m->head_partial, m->head_counter,
+                  m->mailbox, m->pbuf, m->logits_full, m->tp_seq};
     for (void *p : ps)
         if (p) cudaFree(p);
     if (m->host_io) cudaFreeHost(m->host_io);
@@ -483,9 +574,9 @@ int spk_model_set_layer(spk_model *m, int layer, const spk_vq_matrix *qkv, const
     if (!m) return set_error("model is null");
     if (layer < 0 || layer >= m->cfg.layers) return set_error("layer %d is outside the %d layers", layer, m->cfg.layers);
     const spk_model_config &c = m->cfg;
-    if (check_mat(qkv, m->q_dim + 2 * m->kv_dim, c.hidden, "q_k_v_proj") || check_mat(attn_gate, c.heads, c.hidden, "g_proj") ||
-        check_mat(out, c.hidden, m->q_dim, "out_proj") || check_mat(gate, c.inter, c.hidden, "gate_proj") ||
-        check_mat(up, c.inter, c.hidden, "up_proj") || check_mat(down, c.hidden, c.inter, "down_proj"))
+    if (check_mat(qkv, m->q_dim + 2 * m->kv_dim, c.hidden, "q_k_v_proj") || check_mat(attn_gate, m->hl, c.hidden, "g_proj") ||
+        check_mat(out, c.hidden, m->q_dim, "out_proj") || check_mat(gate, m->inter_l, c.hidden, "gate_proj") ||
+        check_mat(up, m->inter_l, c.hidden, "up_proj") || check_mat(down, c.hidden, m->inter_l, "down_proj"))
         return -1;
     if (gate->nstages != up->nstages || gate->dim != up->dim || gate->nc != up->nc || gate->v3 != up->v3)
         return set_error("gate_proj and up_proj must share one encoding to run as a pair");
@@ -525,8 +616,17 @@ int spk_model_forward(spk_model *m, int token, int pos, float *logits_host, int 
     if (e != cudaSuccess) return cuda_fail("state upload", e);
     if (run_step(m)) return -1;
     e = cudaMemcpyAsync(m->host_io + 2, m->state + 2, sizeof(int), cudaMemcpyDeviceToHost, m->stream);
+    const float *full = m->logits;
+    if (e == cudaSuccess && logits_host && m->tp_world > 1) {
+        // every rank's shard is final once this rank's argmax exchange has completed,
+        // and no rank can overwrite it before this rank joins the next step
+        for (int r = 0; r < m->tp_world && e == cudaSuccess; r++)
+            e = cudaMemcpyAsync(m->logits_full + (size_t)r * m->vocab_l, m->peer_logits[r], (size_t)m->vocab_l * 4,
+                                cudaMemcpyDefault, m->stream);
+        full = m->logits_full;
+    }
     if (e == cudaSuccess && logits_host)
-        e = cudaMemcpyAsync(logits_host, m->logits, (size_t)m->cfg.vocab * 4, cudaMemcpyDeviceToHost, m->stream);
+        e = cudaMemcpyAsync(logits_host, full, (size_t)m->cfg.vocab * 4, cudaMemcpyDeviceToHost, m->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
     if (e != cudaSuccess) return cuda_fail("forward", e);
     if (check_device_error("forward")) return -1;
@@ -583,5 +683,74 @@ int spk_model_advance_len(spk_model *m, int n) {
     m->len += n;
     return 0;
 }
+
+/* The mailbox's IPC handle, for the other ranks' spk_model_tp_attach. */
+int spk_model_tp_handle(spk_model *m, void *handle_out, int n) {
+    if (!m || m->tp_world < 2 || !m->mailbox) return set_error("the model is not tensor-parallel");
+    if (!handle_out || n < (int)sizeof(cudaIpcMemHandle_t)) return set_error("the handle buffer needs %d bytes", (int)sizeof(cudaIpcMemHandle_t));
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, m->mailbox);
+    if (e != cudaSuccess) return cuda_fail("export the mailbox", e);
+    memcpy(handle_out, &h, sizeof h);
+    return 0;
+}
+
+static int tp_wire(spk_model *m, void *const *bases, int wait_ms) {
+    if (wait_ms <= 0) return set_error("the exchange wait limit must be positive");
+    TpView &v = m->tpv;
+    v = TpView{};
+    for (int r = 0; r < m->tp_world; r++) {
+        v.mail[r] = (float *)bases[r];
+        v.flags[r] = (unsigned int *)((uint8_t *)bases[r] + m->mail_flags_off);
+        m->peer_logits[r] = (const float *)((const uint8_t *)bases[r] + m->mail_logits_off);
+    }
+    v.rank = m->tp_rank;
+    v.world = m->tp_world;
+    v.stride = m->mail_stride;
+    v.seq = m->tp_seq;
+    v.wait_ns = (unsigned long long)wait_ms * 1000000ull;
+    v.err = device_error_ptr();
+    m->tp_ready = true;
+    return 0;
+}
+
+/* Every rank's mailbox handle in rank order (this rank's own entry is ignored). */
+int spk_model_tp_attach(spk_model *m, const void *handles, int n, int wait_ms) {
+    if (!m || m->tp_world < 2) return set_error("the model is not tensor-parallel");
+    if (m->exec || m->eager_steps || m->tp_ready) return set_error("attach before the first step, once");
+    const int hs = (int)sizeof(cudaIpcMemHandle_t);
+    if (!handles || n != hs * m->tp_world) return set_error("expected %d handles of %d bytes", m->tp_world, hs);
+    void *bases[TP_MAX] = {};
+    for (int r = 0; r < m->tp_world; r++) {
+        if (r == m->tp_rank) {
+            bases[r] = m->mailbox;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, (const uint8_t *)handles + (size_t)r * hs, hs);
+        cudaError_t e = cudaIpcOpenMemHandle(&bases[r], h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) return cuda_fail("open a peer mailbox", e);
+        m->peer_open[r] = bases[r];
+    }
+    return tp_wire(m, bases, wait_ms);
+}
+
+/* Mailboxes as pointers valid in this process, rank order; mailboxes[tp_rank] must be
+ * this model's own (pass NULL there to have it filled in). */
+int spk_model_tp_attach_ptrs(spk_model *m, void *const *mailboxes, int world, int wait_ms) {
+    if (!m || m->tp_world < 2) return set_error("the model is not tensor-parallel");
+    if (m->exec || m->eager_steps || m->tp_ready) return set_error("attach before the first step, once");
+    if (!mailboxes || world != m->tp_world) return set_error("expected %d mailboxes", m->tp_world);
+    void *bases[TP_MAX] = {};
+    for (int r = 0; r < world; r++) {
+        bases[r] = r == m->tp_rank ? m->mailbox : mailboxes[r];
+        if (!bases[r]) return set_error("mailbox %d is null", r);
+        if (r == m->tp_rank && mailboxes[r] && mailboxes[r] != m->mailbox) return set_error("mailbox %d is not this model's", r);
+    }
+    return tp_wire(m, bases, wait_ms);
+}
+
+/* This model's mailbox (for spk_model_tp_attach_ptrs in a single-process setup). */
+void *spk_model_tp_mailbox(spk_model *m) { return m ? m->mailbox : nullptr; }
 
 }  // extern "C"

@@ -1,0 +1,44 @@
+// tp.cuh — tensor-parallel exchanges of the decode step over peer memory.
+//
+// Every rank owns one device allocation (its "mailbox"), exported to the other
+// ranks with CUDA IPC (or passed as plain pointers by a single process that
+// drives several GPUs with peer access):
+//   float        mail[2][world][stride]   slot-major, one row per sender
+//   unsigned int flags[2][TP_MAX]         flags[slot][sender] = last sequence number
+// An exchange with sequence number s uses slot s & 1. Each rank stores its row
+// into every rank's mailbox (NVLink stores), releases its flag at system scope,
+// then waits, bounded in time, until every sender's flag has reached s, and
+// reduces the rows it received in rank order 0..world-1, so all ranks end with
+// bit-identical results. Two slots suffice: a rank can only start exchange s+2
+// after every rank has stored its row of s+1, which each does only after it has
+// finished reading s.
+#pragma once
+#include "common.cuh"
+
+namespace spk {
+
+constexpr int TP_MAX = 8;
+
+struct TpView {
+    float *mail[TP_MAX];            // every rank's mailbox, as mapped in this process
+    unsigned int *flags[TP_MAX];    // every rank's flag array
+    int rank, world;
+    int stride;                     // floats per mailbox row (>= the exchanged length, a multiple of 64)
+    unsigned int *seq;              // this rank's exchange counter (device, starts at 0)
+    unsigned long long wait_ns;     // give-up time of a wait
+    int *err;                       // device error word
+};
+
+// Bytes of one mailbox for `world` ranks and rows of up to n floats; *flags_off
+// receives the byte offset of the flag array inside it.
+size_t tp_mailbox_bytes(int world, int n, size_t *flags_off, int *stride);
+
+// h[i] += sum over ranks r (in rank order) of part_r[i], i < n (n a multiple of 4).
+int tp_sum(const TpView &v, const float *part, float *h, int n, cudaStream_t s);
+
+// Global greedy id over vocabulary shards: rank r holds rows [row0_r, row0_r + n_r)
+// with logits[] and its local first-max index *amax_local; *amax receives the
+// first index of the global maximum (NaN never wins, -0 equals +0).
+int tp_argmax(const TpView &v, const float *logits, const int *amax_local, int row0, int *amax, cudaStream_t s);
+
+}  // namespace spk

@@ -101,6 +101,12 @@ struct FastArgs {
     uint32_t main_slot, plane_slot, slot_bytes;
     int nbuf;                  // ring depth (2 or 3, whatever fits shared memory)
     int *err;
+    // Optional second matrix of the same encoding and input (NG 1): the last CTA
+    // computes all of it (xy = X RMSNorm?(x)) while the others share the main rows.
+    int has_x;
+    const uint8_t *xst[MAXQ];
+    Layout XL;
+    float *xy;
 };
 
 template <int F>
@@ -155,17 +161,16 @@ __device__ __forceinline__ float row_chunk(const uint8_t *row, const uint8_t *pl
 // [r0, r0+nr) of every stream (stream.cuh). The contract gives every stage
 // payload 8 zeroed slack bytes, so a copy may round up to at most 8 bytes past
 // the payload end.
-__device__ __forceinline__ void issue_tile(const FastArgs &a, int nq, int ext, uint8_t *slot, uint64_t *bar,
-                                           int r0, int nr) {
-    const Layout &L = a.L;
+__device__ __forceinline__ void issue_tile(const FastArgs &a, const uint8_t *const *stp, const Layout &L, int nq,
+                                           int ext, uint8_t *slot, uint64_t *bar, int r0, int nr) {
     const size_t payload = L.stream_off + (size_t)L.rows * (L.mrow + L.prow);
     BulkList bl;
     bl.n = 0;
     bl.tx = 0;
     for (int q = 0; q < nq; q++) {
-        const uintptr_t limit = (uintptr_t)(a.st[q] + payload + 8);
+        const uintptr_t limit = (uintptr_t)(stp[q] + payload + 8);
         for (int part = 0; part < 1 + ext; part++) {
-            const uint8_t *base = a.st[q] + L.stream_off +
+            const uint8_t *base = stp[q] + L.stream_off +
                                   (part ? (size_t)L.rows * L.mrow + (size_t)r0 * L.prow : (size_t)r0 * L.mrow);
             const size_t bytes = (size_t)nr * (part ? L.prow : L.mrow);
             uint8_t *d = slot + (part ? (nq * a.main_slot + q * a.plane_slot) : q * a.main_slot);
@@ -183,7 +188,10 @@ __global__ void __launch_bounds__(Warps<F>::W * 32, 1) vq_fast_kernel(const Fast
     // 16-byte chunks, so 8 lanes' float4 reads hit 8 distinct bank quads
     constexpr int XS = 4 * (F + 1 + (F & 1));
     extern __shared__ __align__(16) uint8_t smem[];
-    const Layout &L = a.L;
+    const bool xt = NG == 1 && a.has_x && blockIdx.x == gridDim.x - 1;   // this CTA runs the second matrix
+    const Layout &L = xt ? a.XL : a.L;
+    const uint8_t *const *stp = xt ? a.xst : a.st;
+    float *const yout = xt ? a.xy : a.y;
     const int nc = L.nc;
     const int ks_n = a.ks, tr = a.tr, NB = a.nbuf;
     uint2 *cb = reinterpret_cast<uint2 *>(smem);
@@ -199,8 +207,9 @@ __global__ void __launch_bounds__(Warps<F>::W * 32, 1) vq_fast_kernel(const Fast
     const int ks = warp % ks_n, g = (warp / ks_n) % NG, rw = warp / (ks_n * NG);
     const bool direct = (NG == 1) && (ks_n == 1);   // the row's warp finishes the row itself
 
-    const int G = gridDim.x;
-    const int rb = (int)(((long long)blockIdx.x * L.rows) / G), re = (int)(((long long)(blockIdx.x + 1) * L.rows) / G);
+    const int G = gridDim.x - (NG == 1 && a.has_x ? 1 : 0);
+    const int rb = xt ? 0 : (int)(((long long)blockIdx.x * L.rows) / G);
+    const int re = xt ? L.rows : (int)(((long long)(blockIdx.x + 1) * L.rows) / G);
     const int ntile = (re - rb + tr - 1) / tr;
 
     if (tid == 0) {
@@ -214,12 +223,12 @@ __global__ void __launch_bounds__(Warps<F>::W * 32, 1) vq_fast_kernel(const Fast
     if (tid == 0) {
         for (int t = 0; t < NB - 1 && t < ntile; t++) {
             const int r0 = rb + t * tr;
-            issue_tile(a, NQ, EXT, ring + (size_t)t * a.slot_bytes, &full[t], r0, min(tr, re - r0));
+            issue_tile(a, stp, L, NQ, EXT, ring + (size_t)t * a.slot_bytes, &full[t], r0, min(tr, re - r0));
         }
     }
     // Codebooks: NQ x nc code words of 8 bytes (the payload keeps them 8-byte aligned).
     for (int q = 0; q < NQ; q++) {
-        const uint2 *src = reinterpret_cast<const uint2 *>(a.st[q] + L.cb_off);
+        const uint2 *src = reinterpret_cast<const uint2 *>(stp[q] + L.cb_off);
         for (int v = tid; v < nc; v += FAST_THREADS) cb[q * nc + v] = __ldg(src + v);
     }
     // Activations: coalesced loads (with the optional RMSNorm folded in) into a
@@ -255,7 +264,7 @@ __global__ void __launch_bounds__(Warps<F>::W * 32, 1) vq_fast_kernel(const Fast
             const int tn = t + NB - 1, r0n = rb + tn * tr, sn = tn % NB;
             // the slot last held tile tn - NBUF: wait until every warp released it
             if (tn >= NB && !mbar_wait(&empty[sn], (uint32_t)(((tn / NB) - 1) & 1), a.err)) return;
-            issue_tile(a, NQ, EXT, ring + (size_t)sn * a.slot_bytes, &full[sn], r0n, min(tr, re - r0n));
+            issue_tile(a, stp, L, NQ, EXT, ring + (size_t)sn * a.slot_bytes, &full[sn], r0n, min(tr, re - r0n));
         }
         const int r0 = rb + t * tr, nr = min(tr, re - r0);
         const int r = r0 + rw;
@@ -263,8 +272,8 @@ __global__ void __launch_bounds__(Warps<F>::W * 32, 1) vq_fast_kernel(const Fast
         if (direct && lane == 0 && rw < nr) {   // issued before the gathers, consumed after
 #pragma unroll
             for (int s = 0; s < NSTG; s++)
-                gain[s] = h2f_bits(*reinterpret_cast<const uint16_t *>(a.st[s] + L.gain_off + 2 * (size_t)r));
-            if (a.accumulate) yold = a.y[r];
+                gain[s] = h2f_bits(*reinterpret_cast<const uint16_t *>(stp[s] + L.gain_off + 2 * (size_t)r));
+            if (a.accumulate) yold = yout[r];
         }
         if (!mbar_wait(&full[slot], (uint32_t)((t / NB) & 1), a.err)) return;
         float *pt = part + (size_t)(t & 1) * tr * NG * ks_n * NSTG;
@@ -274,11 +283,11 @@ __global__ void __launch_bounds__(Warps<F>::W * 32, 1) vq_fast_kernel(const Fast
 #pragma unroll
             for (int s = 0; s < NSTG; s++) {
                 const int q = g * NSTG + s;
-                const uintptr_t A = (uintptr_t)(a.st[q] + L.stream_off + (size_t)r0 * L.mrow);
+                const uintptr_t A = (uintptr_t)(stp[q] + L.stream_off + (size_t)r0 * L.mrow);
                 const uint8_t *row = sb + q * a.main_slot + (A & 15) + (size_t)rw * L.mrow;
                 const uint8_t *pl = nullptr;
                 if (EXT) {
-                    const uintptr_t P = (uintptr_t)(a.st[q] + L.stream_off + (size_t)L.rows * L.mrow +
+                    const uintptr_t P = (uintptr_t)(stp[q] + L.stream_off + (size_t)L.rows * L.mrow +
                                                     (size_t)r0 * L.prow);
                     pl = sb + NQ * a.main_slot + q * a.plane_slot + (P & 15) + (size_t)rw * L.prow;
                 }
@@ -295,7 +304,7 @@ __global__ void __launch_bounds__(Warps<F>::W * 32, 1) vq_fast_kernel(const Fast
                     float o = yold;
 #pragma unroll
                     for (int s = 0; s < NSTG; s++) o = __fadd_rn(o, __fmul_rn(acc[s], gain[s]));
-                    a.y[r] = o;
+                    yout[r] = o;
                 } else {
 #pragma unroll
                     for (int s = 0; s < NSTG; s++) pt[((rw * NG + g) * ks_n + ks) * NSTG + s] = acc[s];
@@ -309,21 +318,21 @@ __global__ void __launch_bounds__(Warps<F>::W * 32, 1) vq_fast_kernel(const Fast
             float outv[NG];
 #pragma unroll
             for (int gg = 0; gg < NG; gg++) {
-                float o = (NG == 1 && a.accumulate) ? a.y[rr] : 0.0f;
+                float o = (NG == 1 && a.accumulate) ? yout[rr] : 0.0f;
 #pragma unroll
                 for (int s = 0; s < NSTG; s++) {
                     float v = 0.f;
                     for (int k = 0; k < ks_n; k++) v += pt[((tid * NG + gg) * ks_n + k) * NSTG + s];
                     const uint16_t gh =
-                        *reinterpret_cast<const uint16_t *>(a.st[gg * NSTG + s] + L.gain_off + 2 * (size_t)rr);
+                        *reinterpret_cast<const uint16_t *>(stp[gg * NSTG + s] + L.gain_off + 2 * (size_t)rr);
                     o = __fadd_rn(o, __fmul_rn(v, h2f_bits(gh)));
                 }
                 outv[gg] = o;
             }
             if (NG == 1)
-                a.y[rr] = outv[0];
+                yout[rr] = outv[0];
             else
-                a.y[rr] = __fmul_rn(gelu_erf(outv[0]), outv[NG - 1]);
+                yout[rr] = __fmul_rn(gelu_erf(outv[0]), outv[NG - 1]);
         }
     }
 }
@@ -505,7 +514,8 @@ int launch_fast_t(const FastPlan &P, cudaStream_t s) {
         opted[dev & 63] = P.smem;
     }
     const int ntr = (P.args.L.rows + P.tr - 1) / P.tr;
-    const int grid = ntr < sm_count() ? ntr : sm_count();
+    const int cap = sm_count() - (P.args.has_x ? 1 : 0);
+    const int grid = (ntr < cap ? ntr : cap) + (P.args.has_x ? 1 : 0);
     k<<<grid, Warps<F>::W * 32, P.smem, s>>>(P.args);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? 0 : cuda_fail("vq fast kernel launch", e);
@@ -592,6 +602,43 @@ int vq_gemv_impl(const void *const *stages, int nstg, int ng, const Layout &L, c
     if (variant == 3) return set_error("the DQV3 block kernel does not take this geometry");
     return launch_generic(st, nstg, ng, L, x, norm_w, eps, y, accumulate, threads, s);
 }
+
+}  // namespace
+
+// y = W RMSNorm?(x) and xy = X RMSNorm?(x) for two matrices of one encoding and
+// input width (QKV and g_proj) in one launch, the last CTA taking all of X.
+// Returns 0 launched, 1 not taken (the fast kernel does not take the pair), -1 error.
+int spk::vq_gemv_with_extra(const void *const *stages, int nstg, const Layout &L, const void *const *xstages,
+                       const Layout &XL, const float *x, const float *norm_w, float eps, float *y, float *xy,
+                       int accumulate, cudaStream_t s) {
+    const uint8_t *st[MAXQ], *xst[MAXQ];
+    if (nstg < 1 || nstg > 2) return set_error("%d stages: the paired launch takes 1 or 2", nstg);
+    for (int q = 0; q < nstg; q++) {
+        if (!stages[q] || !xstages[q]) return set_error("stage %d payload pointer is null", q);
+        st[q] = (const uint8_t *)stages[q];
+        xst[q] = (const uint8_t *)xstages[q];
+    }
+    if (check_geometry(L.dim, L.nc, L.rows, L.cols, L.v3) || check_geometry(XL.dim, XL.nc, XL.rows, XL.cols, XL.v3))
+        return -1;
+    FastPlan P, PX;
+    const bool same = XL.dim == L.dim && XL.nc == L.nc && XL.cols == L.cols && XL.v3 == L.v3 && XL.rows <= 64;
+    if (same && fast_plan(st, nstg, 1, L, &P) && fast_plan(xst, nstg, 1, XL, &PX) && PX.F == P.F && PX.tr == P.tr) {
+        P.args.x = x;
+        P.args.norm_w = norm_w;
+        P.args.eps = eps;
+        P.args.y = y;
+        P.args.accumulate = accumulate;
+        P.args.err = device_error_ptr();
+        P.args.has_x = 1;
+        for (int q = 0; q < nstg; q++) P.args.xst[q] = xst[q];
+        P.args.XL = XL;
+        P.args.xy = xy;
+        return launch_fast(P, nstg, 1, s);
+    }
+    return 1;
+}
+
+namespace {
 
 int timed(int iters, double *ms, int (*fn)(void *), void *ctx) {
     cudaEvent_t a, b;

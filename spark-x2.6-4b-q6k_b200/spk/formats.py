@@ -351,3 +351,80 @@ def q6k_row_bytes(cols: int) -> int:
 
 def q80_row_bytes(cols: int) -> int:
     return cols // Q80_BLOCK_WEIGHTS * Q80_BLOCK_BYTES
+
+
+# ------------------------------------------------- tensor-parallel re-cuts ---
+# A DQV3 stream is row-local, so a shard of rows or of whole index columns is an
+# exact re-cut of the payload: the same codebook, the same indices, the same gains.
+# The decoded shard is bit-identical to the corresponding block of the decoded matrix.
+
+def _unpack_bits_rows(raw: np.ndarray, bits: int, n: int) -> np.ndarray:
+    """Inverse of _pack_bits_rows: ``raw`` [rows][row_bytes] -> uint32 [rows][n]."""
+    rows = raw.shape[0]
+    if bits == 12 and n % 2 == 0 and raw.shape[1] == n * 12 // 8:
+        t = raw.reshape(rows, n // 2, 3).astype(np.uint32)
+        w = t[..., 0] | (t[..., 1] << 8) | (t[..., 2] << 16)
+        out = np.empty((rows, n), np.uint32)
+        out[:, 0::2] = w & 0xFFF
+        out[:, 1::2] = w >> 12
+        return out
+    bitarr = np.unpackbits(raw, axis=1, bitorder="little")[:, :n * bits].reshape(rows, n, bits).astype(np.uint32)
+    return (bitarr << np.arange(bits, dtype=np.uint32)).sum(axis=2, dtype=np.uint32)
+
+
+def v3_unpack(stage: bytes):
+    """One DQV3 stage payload -> (geom, codebook f16 bits, gains f16 bits, indices [rows][nidx_row])."""
+    if stage[:4] != b"DQV3":
+        raise ValueError("not a DQV3 stage")
+    dim, nc, rows, cols, _flags, _pad = struct.unpack_from("<HHIIII", stage, 4)
+    g = StageGeom(dim, nc, rows, cols, True)
+    a = np.frombuffer(stage, np.uint8)
+    o = g.header_bytes
+    cb = a[o:o + nc * dim * 2].view("<u2").copy()
+    o += nc * dim * 2
+    gains = a[o:o + rows * 2].view("<u2").copy()
+    o += rows * 2
+    idx = _unpack_bits_rows(a[o:o + rows * g.mrow].reshape(rows, g.mrow), g.mb, g.nidx_row)
+    o += rows * g.mrow
+    if g.prow:
+        plane = _unpack_bits_rows(a[o:o + rows * g.prow].reshape(rows, g.prow), 1, g.nidx_row)
+        idx |= plane << 12
+    return g, cb, gains, idx
+
+
+def _stages(buf: bytes):
+    c = parse_container(buf)
+    if not c.v3:
+        raise ValueError("tensor-parallel re-cuts take DQV3 containers")
+    return c, [buf[c.stage_offset(s):c.stage_offset(s) + c.stage_bytes] for s in range(c.nstages)]
+
+
+def shard_rows(buf: bytes, rows) -> bytes:
+    """The RQVQ container of the listed rows (in order) of a DQV3 container."""
+    c, stages = _stages(buf)
+    rows = np.asarray(rows, np.int64)
+    out = []
+    for st in stages:
+        g, cb, gains, idx = v3_unpack(st)
+        out.append(v3_pack(cb, gains[rows], idx[rows], len(rows), c.cols, c.dim, c.nc))
+    return rqvq(out, c.dim, c.nc, len(rows), c.cols)
+
+
+def shard_cols(buf: bytes, c0: int, c1: int) -> bytes:
+    """The RQVQ container of input columns [c0, c1) of a DQV3 container (whole indices:
+    c0 and c1 multiples of dim). The per-row gains are kept, so the shards' partial
+    products sum to the full product."""
+    c, stages = _stages(buf)
+    if c0 % c.dim or c1 % c.dim or not 0 <= c0 < c1 <= c.cols:
+        raise ValueError(f"columns [{c0}, {c1}) do not cut whole {c.dim}-wide indices of {c.cols}")
+    out = []
+    for st in stages:
+        g, cb, gains, idx = v3_unpack(st)
+        out.append(v3_pack(cb, gains, idx[:, c0 // c.dim:c1 // c.dim], c.rows, c1 - c0, c.dim, c.nc))
+    return rqvq(out, c.dim, c.nc, c.rows, c1 - c0)
+
+
+def shard_q80_rows(buf: bytes, cols: int, r0: int, r1: int) -> bytes:
+    """Rows [r0, r1) of a row-major Q8_0 matrix (a contiguous byte range)."""
+    rb = q80_row_bytes(cols)
+    return buf[r0 * rb:r1 * rb]

@@ -99,12 +99,63 @@ def synth_weights(cfg: ModelConfig, seed: int = 0, nc: int = 4096, stages: int =
     return {"layers": layers, "embed": embed, "norm": norm}
 
 
+def tp_layout(cfg: ModelConfig, rank: int, world: int) -> dict:
+    """What rank `rank` of `world` holds (the sharding libspk's tensor-parallel step runs):
+    q heads [h0, h0+hl), KV heads [k0, k0+kl) (replicated when world > kv_heads),
+    intermediate rows [i0, i0+il), vocabulary rows [v0, v0+vl)."""
+    t = world
+    if cfg.heads % t or (cfg.kv_heads % t and t % cfg.kv_heads) or cfg.inter % t or cfg.vocab % t:
+        raise ValueError(f"{t}-way tensor parallelism does not divide this geometry")
+    hl = cfg.heads // t
+    kl = cfg.kv_heads // t if cfg.kv_heads >= t else 1
+    k0 = rank * kl if cfg.kv_heads >= t else rank * cfg.kv_heads // t
+    il, vl = cfg.inter // t, cfg.vocab // t
+    return {"h0": rank * hl, "hl": hl, "k0": k0, "kl": kl, "i0": rank * il, "il": il, "v0": rank * vl, "vl": vl}
+
+
+def tp_shard(cfg: ModelConfig, weights: dict, rank: int, world: int) -> dict:
+    """Rank `rank`'s shard of full weights (exact re-cuts of the DQV3 containers,
+    formats.shard_rows / shard_cols): q_k_v_proj rows of its q and KV heads, g_proj rows
+    of its heads, out_proj input columns of its heads, gate/up rows and down input
+    columns of its intermediate slice. The Q8_0 embedding (also the head) and the
+    norms stay whole; the head GEMV reads the rank's vocabulary rows of it."""
+    if world <= 1:
+        return weights
+    lay = tp_layout(cfg, rank, world)
+    hd, qd = cfg.head_dim, cfg.q_dim
+    q_rows = np.arange(lay["h0"] * hd, (lay["h0"] + lay["hl"]) * hd)
+    kv = np.arange(lay["k0"] * hd, (lay["k0"] + lay["kl"]) * hd)
+    qkv_rows = np.concatenate([q_rows, qd + kv, qd + cfg.kv_dim + kv])
+    i0, i1 = lay["i0"], lay["i0"] + lay["il"]
+    layers = []
+    for Lw in weights["layers"]:
+        layers.append({
+            "qkv": F.shard_rows(Lw["qkv"], qkv_rows),
+            "attn_gate": F.shard_rows(Lw["attn_gate"], np.arange(lay["h0"], lay["h0"] + lay["hl"])),
+            "out": F.shard_cols(Lw["out"], lay["h0"] * hd, (lay["h0"] + lay["hl"]) * hd),
+            "gate": F.shard_rows(Lw["gate"], np.arange(i0, i1)),
+            "up": F.shard_rows(Lw["up"], np.arange(i0, i1)),
+            "down": F.shard_cols(Lw["down"], i0, i1),
+            "in_norm": Lw["in_norm"], "post_norm": Lw["post_norm"]})
+    return {"layers": layers, "embed": weights["embed"], "norm": weights["norm"], "tp": (rank, world)}
+
+
+def exchange_handles(handle: bytes, group=None) -> list:
+    """Every rank's mailbox handle, in rank order, over torch.distributed (any backend)."""
+    import torch.distributed as dist
+
+    out = [None] * dist.get_world_size(group)
+    dist.all_gather_object(out, handle, group=group)
+    return out
+
+
 class _Cfg(C.Structure):
     _fields_ = [("hidden", C.c_int), ("layers", C.c_int), ("heads", C.c_int), ("kv_heads", C.c_int),
                 ("head_dim", C.c_int), ("inter", C.c_int), ("vocab", C.c_int), ("window", C.c_int),
                 ("eps", C.c_float), ("rope_theta_full", C.c_float), ("rope_partial_full", C.c_float),
                 ("rope_theta_slide", C.c_float), ("rope_partial_slide", C.c_float),
-                ("full", C.POINTER(C.c_int)), ("max_ctx", C.c_int), ("kv_f16", C.c_int)]
+                ("full", C.POINTER(C.c_int)), ("max_ctx", C.c_int), ("kv_f16", C.c_int),
+                ("tp_rank", C.c_int), ("tp_world", C.c_int)]
 
 
 class VqMatrix(C.Structure):
@@ -133,6 +184,8 @@ class DeviceModel:
 
     def __init__(self, cfg: ModelConfig, weights: dict, max_ctx: int, kv_f16: bool = False, device="cuda:0",
                  stream=None):
+        """``weights`` are full weights, or one rank's shard from ``tp_shard`` (then the model is
+        that tensor-parallel rank and needs ``tp_connect`` before its first step)."""
         import torch
 
         self.cfg = cfg
@@ -142,7 +195,8 @@ class DeviceModel:
         self._full = (C.c_int * cfg.layers)(*[int(f) for f in cfg.full])
         c = _Cfg(cfg.hidden, cfg.layers, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.inter, cfg.vocab, cfg.window,
                  cfg.eps, cfg.rope_theta_full, cfg.rope_partial_full, cfg.rope_theta_slide, cfg.rope_partial_slide,
-                 self._full, max_ctx, int(kv_f16))
+                 self._full, max_ctx, int(kv_f16), *weights.get("tp", (0, 1)))
+        self.tp = weights.get("tp", (0, 1))
         L = lib()
         L.spk_model_create.restype = C.c_void_p
         self.h = L.spk_model_create(C.byref(c), C.c_void_p(self.stream.cuda_stream))
@@ -172,6 +226,28 @@ class DeviceModel:
         check(L.spk_model_set_head(self.h, emb.data_ptr(), norm.data_ptr()), "head")
         self._logits = np.empty(cfg.vocab, np.float32)
         torch.cuda.synchronize(self.device)   # uploads ran on torch's stream; the model runs on its own
+
+    def tp_handle(self) -> bytes:
+        """This rank's mailbox as a cudaIpcMemHandle_t (64 bytes)."""
+        buf = C.create_string_buffer(64)
+        check(lib().spk_model_tp_handle(self.h, buf, 64), "tp_handle")
+        return buf.raw
+
+    def tp_attach(self, handles: list, wait_ms: int = 5000):
+        blob = b"".join(handles)
+        check(lib().spk_model_tp_attach(self.h, blob, len(blob), wait_ms), "tp_attach")
+
+    def tp_connect(self, group=None, wait_ms: int = 5000):
+        """Exchange mailbox handles with the other ranks (torch.distributed) and attach."""
+        self.tp_attach(exchange_handles(self.tp_handle(), group), wait_ms)
+
+    def tp_mailbox(self) -> int:
+        return lib().spk_model_tp_mailbox(self.h) or 0
+
+    def tp_attach_ptrs(self, mailboxes: list, wait_ms: int = 5000):
+        """Mailboxes as pointers valid in this process (None for this rank's own)."""
+        arr = (C.c_void_p * len(mailboxes))(*[m or None for m in mailboxes])
+        check(lib().spk_model_tp_attach_ptrs(self.h, arr, len(mailboxes), wait_ms), "tp_attach_ptrs")
 
     def forward(self, token: int, pos: int, want_logits: bool = True):
         """Model::forward: returns (next_id, logits or None) through host buffers."""
