@@ -44,7 +44,7 @@ struct AttnArgs {
     const float *qkv;          // [q_dim + 2 kv_dim] this token's projections (pre-rope)
     void *kc, *vc;             // this layer's caches: [kv_heads][slots][hd], f32 or f16
     int kv_f16;
-    int slots;                 // ctx (full layer) or window (sliding layer, a ring)
+    int slots;                 // cache positions (the capacity: every layer keeps its whole history)
     int full, window;
     const float *freq;         // [pdim/2] rope frequencies of this layer type (model.rs:416-429)
     int pdim;
@@ -102,7 +102,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_partial_kernel(const AttnArg
     rope_smem(kn, a.freq, a.pdim, pos);
     __syncthreads();
     // The split that owns `pos` writes the new row; nobody else reads that slot now.
-    const int wslot = a.full ? pos : pos % a.window;
+    const int wslot = pos % a.slots;
     if (c0 <= pos && pos < c1) {
         for (int i = threadIdx.x; i < HD; i += blockDim.x) {
             const size_t o = ((size_t)kvh * a.slots + wslot) * HD + i;
@@ -144,7 +144,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_partial_kernel(const AttnArg
                 vr[d] = vn[lane * DPL + d];
             }
         } else {
-            const int slot = a.full ? j : j % a.window;
+            const int slot = j % a.slots;
             const size_t base = ((size_t)kvh * a.slots + slot) * HD + lane * DPL;
 #pragma unroll
             for (int d = 0; d < DPL; d++) {
@@ -486,7 +486,11 @@ spk_model *spk_model_create(const spk_model_config *cfg, void *stream) {
     m->nsplit_slide = std::max(1, std::min(per_head, (std::min(c.window, c.max_ctx) + 15) / 16));
     size_t kv_elems = 0;
     for (int li = 0; li < c.layers; li++) {
-        const int slots = m->full[li] ? c.max_ctx : std::min(c.window, c.max_ctx);
+        // Sliding layers keep their whole history too (not a window-sized ring), as
+        // model.rs:398-412 does: Model::rollback to any earlier position stays exact,
+        // which a speculative verify that rejects rows relies on. 27 sliding layers
+        // at 131072 positions are 14.5 GB in f16: HBM affords it.
+        const int slots = c.max_ctx;
         m->kv_off.push_back(kv_elems);
         m->kv_slots.push_back(slots);
         kv_elems += (size_t)m->kvl * slots * c.head_dim;

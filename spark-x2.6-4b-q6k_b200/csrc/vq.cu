@@ -260,11 +260,13 @@ __global__ void __launch_bounds__(Warps<F>::W * 32, 1) vq_fast_kernel(const Fast
 
     for (int t = 0; t < ntile; t++) {
         const int slot = t % NB;
+        // A wait that runs out records the error and skips the work it guarded, but no
+        // thread leaves the loop: every warp still reaches its row's barrier below.
         if (tid == 0 && t + NB - 1 < ntile) {
             const int tn = t + NB - 1, r0n = rb + tn * tr, sn = tn % NB;
             // the slot last held tile tn - NBUF: wait until every warp released it
-            if (tn >= NB && !mbar_wait(&empty[sn], (uint32_t)(((tn / NB) - 1) & 1), a.err)) return;
-            issue_tile(a, stp, L, NQ, EXT, ring + (size_t)sn * a.slot_bytes, &full[sn], r0n, min(tr, re - r0n));
+            if (tn < NB || mbar_wait(&empty[sn], (uint32_t)(((tn / NB) - 1) & 1), a.err))
+                issue_tile(a, stp, L, NQ, EXT, ring + (size_t)sn * a.slot_bytes, &full[sn], r0n, min(tr, re - r0n));
         }
         const int r0 = rb + t * tr, nr = min(tr, re - r0);
         const int r = r0 + rw;
@@ -275,10 +277,12 @@ __global__ void __launch_bounds__(Warps<F>::W * 32, 1) vq_fast_kernel(const Fast
                 gain[s] = h2f_bits(*reinterpret_cast<const uint16_t *>(stp[s] + L.gain_off + 2 * (size_t)r));
             if (a.accumulate) yold = yout[r];
         }
-        if (!mbar_wait(&full[slot], (uint32_t)((t / NB) & 1), a.err)) return;
+        const bool have = mbar_wait(&full[slot], (uint32_t)((t / NB) & 1), a.err);
         float *pt = part + (size_t)(t & 1) * tr * NG * ks_n * NSTG;
         float acc[NSTG];
-        if (rw < nr) {
+#pragma unroll
+        for (int s = 0; s < NSTG; s++) acc[s] = 0.f;
+        if (rw < nr && have) {
             const uint8_t *sb = ring + (size_t)slot * a.slot_bytes;
 #pragma unroll
             for (int s = 0; s < NSTG; s++) {
@@ -312,9 +316,13 @@ __global__ void __launch_bounds__(Warps<F>::W * 32, 1) vq_fast_kernel(const Fast
             }
         }
         if (direct) continue;
-        __syncthreads();
-        if (tid < nr) {
-            const int rr = r0 + tid;
+        // The row's ks_n x NG warps meet on a named barrier (id 1 + rw; tr <= 8 here)
+        // and the first of them finishes the row; the other rows' warps run on.
+        // pt is double-buffered by tile parity, and a warp can only reach tile t+2
+        // after passing tile t+1's barrier, so the reader is done with tile t by then.
+        asm volatile("bar.sync %0, %1;" ::"r"(1 + rw), "r"(32 * ks_n * NG) : "memory");
+        if (ks == 0 && g == 0 && lane == 0 && rw < nr) {
+            const int rr = r0 + rw;
             float outv[NG];
 #pragma unroll
             for (int gg = 0; gg < NG; gg++) {
@@ -322,7 +330,7 @@ __global__ void __launch_bounds__(Warps<F>::W * 32, 1) vq_fast_kernel(const Fast
 #pragma unroll
                 for (int s = 0; s < NSTG; s++) {
                     float v = 0.f;
-                    for (int k = 0; k < ks_n; k++) v += pt[((tid * NG + gg) * ks_n + k) * NSTG + s];
+                    for (int k = 0; k < ks_n; k++) v += pt[((rw * NG + gg) * ks_n + k) * NSTG + s];
                     const uint16_t gh =
                         *reinterpret_cast<const uint16_t *>(stp[gg * NSTG + s] + L.gain_off + 2 * (size_t)rr);
                     o = __fadd_rn(o, __fmul_rn(v, h2f_bits(gh)));
