@@ -192,6 +192,14 @@ int spk_model_reset(spk_model *m);
 int spk_model_len(spk_model *m);
 int spk_model_advance_len(spk_model *m, int n);
 
+/* Per-launch device times of one decode step (no counterpart in the reference): runs
+ * one step from the device state, as spk_model_run does, from a second captured graph
+ * with a timing event after every launch; us[i] receives launch i's microseconds in
+ * enqueue order: embedding row; per layer QKV+g_proj, attention, combine, out_proj,
+ * [tp_sum], gate+up, down, [tp_sum]; head; [tp_argmax]; advance. Returns the launch
+ * count or -1. Needs one step run before; with tp_world > 1 every rank traces together. */
+int spk_model_trace(spk_model *m, float *us, int cap);
+
 /* Tensor-parallel wiring (no counterpart in the reference). Each rank's model owns a
  * mailbox in device memory; the residual reductions and the head's argmax store rows
  * into every rank's mailbox over NVLink and wait on release flags there, bounded by

@@ -305,6 +305,11 @@ struct spk_model {
     cudaStream_t stream = nullptr;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
+    // spk_model_trace: a second capture of the step with a timing event after every launch
+    std::vector<cudaEvent_t> tev;
+    int tracing = 0, nmark = 0;
+    cudaGraph_t tgraph = nullptr;
+    cudaGraphExec_t texec = nullptr;
     int eager_steps = 0;
     int len = 0;                  // positions cached (host view, for rollback checks)
 };
@@ -340,16 +345,24 @@ int attn_launch(const AttnArgs &a, cudaStream_t s) {
     return e == cudaSuccess ? 0 : cuda_fail("attention launch", e);
 }
 
+// Under spk_model_trace's capture: an event after the launch just enqueued.
+int mark(spk_model *m) {
+    if (!m->tracing) return 0;
+    if (m->nmark >= (int)m->tev.size()) return set_error("trace: more launches than events");
+    cudaError_t e = cudaEventRecordWithFlags(m->tev[m->nmark++], m->stream, cudaEventRecordExternal);
+    return e == cudaSuccess ? 0 : cuda_fail("trace event", e);
+}
+
 // Enqueue one decode step on m->stream: reads pos/token from m->state.
 int enqueue_step(spk_model *m) {
     const spk_model_config &c = m->cfg;
     cudaStream_t s = m->stream;
     int *pos = m->state, *token = m->state + 1, *amax = m->state + 2, *amax_l = m->state + 4;
     const bool tp = m->tp_world > 1;
-    if (spk_q80_row(m->embed, c.vocab, c.hidden, 0, token, m->h, s)) return -1;
+    if (mark(m) || spk_q80_row(m->embed, c.vocab, c.hidden, 0, token, m->h, s) || mark(m)) return -1;
     for (int li = 0; li < c.layers; li++) {
         const spk_model::Layer &L = m->layers[li];
-        if (qkv_gate(L, m->h, c.eps, m->qkv, m->gate, s)) return -1;
+        if (qkv_gate(L, m->h, c.eps, m->qkv, m->gate, s) || mark(m)) return -1;
         AttnArgs a;
         a.qkv = m->qkv;
         const size_t esz = c.kv_f16 ? 2 : 4;
@@ -367,30 +380,32 @@ int enqueue_step(spk_model *m) {
         a.pos = pos;
         a.nsplit = a.full ? m->nsplit_full : m->nsplit_slide;
         a.part = m->part;
-        if ((c.head_dim == 256 ? attn_launch<256>(a, s) : attn_launch<128>(a, s))) return -1;
+        if ((c.head_dim == 256 ? attn_launch<256>(a, s) : attn_launch<128>(a, s)) || mark(m)) return -1;
         attn_combine_kernel<<<m->hl, 128, 0, s>>>(m->part, a.nsplit, m->hl, m->kvl, c.head_dim, m->gate, m->attn);
+        if (mark(m)) return -1;
         if (tp) {
-            if (vq_call(L.m[2], 1, nullptr, m->attn, nullptr, 0.f, m->pbuf, 0, s)) return -1;
-            if (tp_sum(m->tpv, m->pbuf, m->h, c.hidden, s)) return -1;
-        } else if (vq_call(L.m[2], 1, nullptr, m->attn, nullptr, 0.f, m->h, 1, s)) {
+            if (vq_call(L.m[2], 1, nullptr, m->attn, nullptr, 0.f, m->pbuf, 0, s) || mark(m)) return -1;
+            if (tp_sum(m->tpv, m->pbuf, m->h, c.hidden, s) || mark(m)) return -1;
+        } else if (vq_call(L.m[2], 1, nullptr, m->attn, nullptr, 0.f, m->h, 1, s) || mark(m)) {
             return -1;
         }
-        if (vq_call(L.m[3], 2, &L.m[4], m->h, L.post_norm, c.eps, m->act, 0, s)) return -1;
+        if (vq_call(L.m[3], 2, &L.m[4], m->h, L.post_norm, c.eps, m->act, 0, s) || mark(m)) return -1;
         if (tp) {
-            if (vq_call(L.m[5], 1, nullptr, m->act, nullptr, 0.f, m->pbuf, 0, s)) return -1;
-            if (tp_sum(m->tpv, m->pbuf, m->h, c.hidden, s)) return -1;
-        } else if (vq_call(L.m[5], 1, nullptr, m->act, nullptr, 0.f, m->h, 1, s)) {
+            if (vq_call(L.m[5], 1, nullptr, m->act, nullptr, 0.f, m->pbuf, 0, s) || mark(m)) return -1;
+            if (tp_sum(m->tpv, m->pbuf, m->h, c.hidden, s) || mark(m)) return -1;
+        } else if (vq_call(L.m[5], 1, nullptr, m->act, nullptr, 0.f, m->h, 1, s) || mark(m)) {
             return -1;
         }
     }
     const uint8_t *head_rows = (const uint8_t *)m->embed + (size_t)m->row0 * (c.hidden / 32) * 34;
     if (q80_head_launch(head_rows, m->vocab_l, c.hidden, m->h, m->final_norm, c.eps, m->logits, tp ? amax_l : amax,
-                        m->head_partial, m->head_counter, s))
+                        m->head_partial, m->head_counter, s) || mark(m))
         return -1;
-    if (tp && tp_argmax(m->tpv, m->logits, amax_l, m->row0, amax, s)) return -1;
+    if (tp && (tp_argmax(m->tpv, m->logits, amax_l, m->row0, amax, s) || mark(m))) return -1;
     advance_kernel<<<1, 1, 0, s>>>(pos, token, amax, m->ctl, m->state + 3);
     cudaError_t e = cudaGetLastError();
-    return e == cudaSuccess ? 0 : cuda_fail("decode step launch", e);
+    if (e != cudaSuccess) return cuda_fail("decode step launch", e);
+    return mark(m);
 }
 
 bool ready(const spk_model *m) {
@@ -549,6 +564,9 @@ void spk_model_destroy(spk_model *m) {
     if (!m) return;
     if (m->exec) cudaGraphExecDestroy(m->exec);
     if (m->graph) cudaGraphDestroy(m->graph);
+    if (m->texec) cudaGraphExecDestroy(m->texec);
+    if (m->tgraph) cudaGraphDestroy(m->tgraph);
+    for (cudaEvent_t e : m->tev) cudaEventDestroy(e);
     for (int r = 0; r < TP_MAX; r++)
         if (m->peer_open[r]) cudaIpcCloseMemHandle(m->peer_open[r]);
     void *ps[] = {m->h, m->qkv, m->gate, m->attn, m->act, m->tp_world > 1 ? nullptr : m->logits, m->part,
@@ -686,6 +704,58 @@ int spk_model_advance_len(spk_model *m, int n) {
     if (!m || n < 0 || m->len + n > m->cfg.max_ctx) return set_error("bad length advance");
     m->len += n;
     return 0;
+}
+
+/* One decode step from the device state (as spk_model_run does) with the device time
+ * of every launch: us[i] = microseconds of launch i in enqueue order (embedding row;
+ * per layer QKV+g_proj, attention, combine, out_proj, [tp_sum], gate+up, down,
+ * [tp_sum]; head; [tp_argmax]; advance). Returns the number of launches, or -1.
+ * Needs one step run before (it reuses the kernels' one-time set-up); with
+ * tensor parallelism every rank traces the same step. */
+int spk_model_trace(spk_model *m, float *us, int cap) {
+    if (!m) return set_error("model is null");
+    if (!ready(m)) return set_error("model weights are not all set");
+    if (!m->eager_steps) return set_error("trace needs one step run first");
+    const int tp = m->tp_world > 1 ? 1 : 0;
+    const int n = 1 + 1 + m->cfg.layers * (6 + 2 * tp) + 1 + tp + 1;   // marks, the first one before any launch
+    if (!us || cap < n - 1) return set_error("trace needs room for %d launches", n - 1);
+    if (!m->texec) {
+        for (int i = 0; i < n; i++) {
+            cudaEvent_t e;
+            if (cudaEventCreate(&e) != cudaSuccess) return cuda_fail("trace events", cudaGetLastError());
+            m->tev.push_back(e);
+        }
+        cudaError_t e = cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal);
+        if (e != cudaSuccess) return cuda_fail("begin trace capture", e);
+        m->tracing = 1;
+        m->nmark = 0;
+        const int rc = enqueue_step(m);
+        m->tracing = 0;
+        cudaGraph_t g = nullptr;
+        e = cudaStreamEndCapture(m->stream, &g);
+        if (rc || e != cudaSuccess) {
+            if (g) cudaGraphDestroy(g);
+            return rc ? -1 : cuda_fail("end trace capture", e);
+        }
+        if (m->nmark != n) {
+            cudaGraphDestroy(g);
+            return set_error("trace: %d marks, expected %d", m->nmark, n);
+        }
+        m->tgraph = g;
+        e = cudaGraphInstantiate(&m->texec, g, 0);
+        if (e != cudaSuccess) return cuda_fail("instantiate trace graph", e);
+    }
+    cudaError_t e = cudaGraphLaunch(m->texec, m->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+    if (e != cudaSuccess) return cuda_fail("trace step", e);
+    if (check_device_error("trace step")) return -1;
+    for (int i = 0; i + 1 < n; i++) {
+        float ms = 0.f;
+        e = cudaEventElapsedTime(&ms, m->tev[i], m->tev[i + 1]);
+        if (e != cudaSuccess) return cuda_fail("trace elapsed", e);
+        us[i] = ms * 1000.f;
+    }
+    return n - 1;
 }
 
 /* The mailbox's IPC handle, for the other ranks' spk_model_tp_attach. */

@@ -249,6 +249,19 @@ class DeviceModel:
         arr = (C.c_void_p * len(mailboxes))(*[m or None for m in mailboxes])
         check(lib().spk_model_tp_attach_ptrs(self.h, arr, len(mailboxes), wait_ms), "tp_attach_ptrs")
 
+    def trace(self) -> list:
+        """One decode step (as run() does) with every launch's device time: [(name, us), ...]
+        in enqueue order (spk_model_trace). All tensor-parallel ranks trace together."""
+        tp = self.tp[1] > 1
+        layer = ["qkv_g", "attention", "combine", "out"] + (["tp_sum"] if tp else []) + ["gate_up", "down"] + \
+                (["tp_sum"] if tp else [])
+        names = ["embed"] + layer * self.cfg.layers + ["head"] + (["tp_argmax"] if tp else []) + ["advance"]
+        buf = (C.c_float * len(names))()
+        n = lib().spk_model_trace(self.h, buf, len(names))
+        if n != len(names):
+            raise SpkError(f"trace: {lib().spk_last_error().decode()}")
+        return list(zip(names, [float(v) for v in buf]))
+
     def forward(self, token: int, pos: int, want_logits: bool = True):
         """Model::forward: returns (next_id, logits or None) through host buffers."""
         nxt = C.c_int()

@@ -90,6 +90,30 @@ def test_device_loop_matches_host_steps(small, cuda):
     b.close()
 
 
+def test_trace_step_times_every_launch(small, cuda):
+    """spk_model_trace: one step with per-launch device times; it is an ordinary step
+    (the id it produces is the next id of the host loop)."""
+    import torch
+
+    cfg, W = small
+    a = DeviceModel(cfg, W, max_ctx=8)
+    want = []
+    tok = 11
+    for pos in range(3):
+        tok, _ = a.forward(tok, pos, want_logits=False)
+        want.append(tok)
+    a.rollback(2)
+    ids = torch.zeros(1, dtype=torch.int32, device=cuda)
+    a.begin(want[1], 2, ids, 1)
+    tr = a.trace()
+    a.stream.synchronize()
+    assert ids.item() == want[2]
+    names = [n for n, _ in tr]
+    assert len(tr) == 1 + 6 * cfg.layers + 2 and names[0] == "embed" and names[-2:] == ["head", "advance"]
+    assert all(us > 0 for _, us in tr)
+    a.close()
+
+
 def test_rollback_reproduces(small):
     cfg, W = small
     dev = DeviceModel(cfg, W, max_ctx=64)
