@@ -273,7 +273,9 @@ def run_ours(args) -> None:
     # one more step with per-launch device times (every rank together), summed by kernel
     trace = {}
     for name, us in m.trace():
-        trace[name] = trace.get(name, 0.0) + us
+        trace.setdefault(name, []).append(us)
+    trace = {k: {"sum_us": round(float(np.sum(v)), 1), "median_us": round(float(np.median(v)), 2), "n": len(v)}
+             for k, v in trace.items()}
     bytes_per_token = m.weight_bytes   # this rank's shard (+ its vocabulary rows of the head below)
     if world > 1:
         bytes_per_token -= len_embed(cfg) - len_embed(cfg) // world
@@ -294,7 +296,7 @@ def run_ours(args) -> None:
                        "parallelism": f"tp{world}" if world > 1 else "single", "l2": "weights 3.2 GB > L2, no flush",
                        "step_bytes_per_gpu": bytes_per_token + kv_bytes,
                        "step_hbm_gbs_per_gpu": (bytes_per_token + kv_bytes) * args.steps / dt / 1e9,
-                       "step_trace_us_rank0": {k: round(v, 1) for k, v in trace.items()}},
+                       "step_trace_rank0": trace},
             "roofline": {"bound": "hbm",
                          "kernel": f"vq_fast_kernel gate+up pair {rows_l}x2560 x2 stages (RMSNorm, GELU), rank 0",
                          "achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",

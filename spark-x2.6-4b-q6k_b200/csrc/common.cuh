@@ -88,6 +88,33 @@ int vq_gemv_with_extra(const void *const *stages, int nstg, const Layout &L, con
 int q80_head_launch(const void *w, int rows, int cols, const float *x, const float *norm_w, float eps, float *logits,
                     int *argmax_out, unsigned long long *partial, unsigned int *counter, cudaStream_t s);
 
+// ------------------------------------------- programmatic dependent launch ---
+// Every kernel of the decode path is launched with programmatic stream
+// serialization: it may become resident (on SMs its predecessor has left) before
+// the predecessor finishes, and do work that reads only immutable data (weights:
+// codebooks, index streams, scales) until pdl_wait(). pdl_wait() returns when the
+// preceding kernel has completed and its writes are visible; since every such
+// kernel calls it on every path before it finishes, all earlier kernels of the
+// stream have completed too. Without the launch attribute pdl_wait() returns at
+// once. pdl_trigger() lets the next kernel start launching.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k, args...);
+}
+
 // ------------------------------------------------------ device helpers ---
 #define SPK_WAIT_LIMIT (1u << 26)
 

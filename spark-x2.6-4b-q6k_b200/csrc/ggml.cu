@@ -162,6 +162,8 @@ __global__ void q80_head_kernel(const HeadArgs a) {
     __shared__ unsigned long long best_w[32];
     __shared__ bool last;
     const BlkArgs &b = a.b;
+    pdl_trigger();
+    pdl_wait();
     float inv = 1.0f;
     if (b.norm_w) inv = block_rms_inv(b.x, b.cols, b.eps, red);
     const int wib = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarp = blockDim.x >> 5;
@@ -227,6 +229,8 @@ __global__ void q80_dequant_kernel(const uint8_t *w, size_t nblk, float *out) {
 
 // One row of a Q8_0 matrix (the token embedding of the tied head).
 __global__ void q80_row_kernel(const uint8_t *w, int rows, int cols, const int *tok, int row, float *out, int *err) {
+    pdl_trigger();
+    pdl_wait();   // *tok and out belong to the preceding kernels
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= cols) return;
     int r = tok ? *tok : row;
@@ -366,6 +370,7 @@ __global__ void __launch_bounds__(GF_THREADS, 1) blk_fast_kernel(const GFArgs a)
     const int rb = (int)(((long long)blockIdx.x * a.rows) / G), re = (int)(((long long)(blockIdx.x + 1) * a.rows) / G);
     const int ntile = (re - rb + tr - 1) / tr;
 
+    pdl_trigger();
     if (tid == 0) {
         for (int b = 0; b < GF_NBUF; b++) mbar_init(&full[b], 1);
         fence_mbar_init();
@@ -376,6 +381,7 @@ __global__ void __launch_bounds__(GF_THREADS, 1) blk_fast_kernel(const GFArgs a)
             const int r0 = rb + t * tr;
             gf_issue(a, ring + (size_t)t * a.slot_bytes, &full[t], r0, min(tr, re - r0));
         }
+    pdl_wait();   // the weight tiles above are immutable; x, y and the scratch are not
     float inv = 1.0f;
     if (a.norm_w) inv = block_rms_inv(a.x, a.cols, a.eps, red);
     float xr[U][Fm::WPU];
@@ -398,7 +404,9 @@ __global__ void __launch_bounds__(GF_THREADS, 1) blk_fast_kernel(const GFArgs a)
             gf_issue(a, ring + (size_t)(tn % GF_NBUF) * a.slot_bytes, &full[tn % GF_NBUF], r0n, min(tr, re - r0n));
         }
         const int r0 = rb + t * tr, nr = min(tr, re - r0);
-        if (!mbar_wait(&full[slot], (uint32_t)((t / GF_NBUF) & 1), a.err)) return;
+        // a wait that runs out records the error and skips the tile; every thread
+        // still reaches the barrier below
+        const bool have = mbar_wait(&full[slot], (uint32_t)((t / GF_NBUF) & 1), a.err);
         float *pt = part + (size_t)(t & 1) * tr * ks_n;
         if (rw < nr) {
             const uintptr_t A = (uintptr_t)(a.w + (size_t)r0 * a.rb_bytes);
@@ -406,6 +414,7 @@ __global__ void __launch_bounds__(GF_THREADS, 1) blk_fast_kernel(const GFArgs a)
             float acc = 0.f;
 #pragma unroll
             for (int k = 0; k < U; k++) {
+                if (!have) break;
                 if constexpr (FMT == 0)
                     acc += q6k_unit_s(row, u0 + 32 * k, reinterpret_cast<const float(&)[16]>(xr[k]));
                 else
@@ -507,8 +516,7 @@ int gf_launch_t(const GFPlan &P, cudaStream_t s) {
     }
     const int ntr = (P.a.rows + P.a.tr - 1) / P.a.tr;
     const int grid = ntr < sm_count() ? ntr : sm_count();
-    k<<<grid, GF_THREADS, P.smem, s>>>(P.a);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(k, dim3(grid), dim3(GF_THREADS), P.smem, s, P.a);
     return e == cudaSuccess ? 0 : cuda_fail("ggml fast kernel launch", e);
 }
 
@@ -664,8 +672,7 @@ int q80_head_launch(const void *w, int rows, int cols, const float *x, const flo
     a.partial = partial;
     a.counter = counter;
     a.argmax_out = argmax_out;
-    q80_head_kernel<<<2 * sm_count() < 1024 ? 2 * sm_count() : 1024, 256, 0, s>>>(a);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(q80_head_kernel, dim3(2 * sm_count() < 1024 ? 2 * sm_count() : 1024), dim3(256), 0, s, a);
     return e == cudaSuccess ? 0 : cuda_fail("q8_0 head launch", e);
 }
 }  // namespace spk
@@ -694,9 +701,8 @@ int spk_q80_dequant(const void *w, size_t nblocks, float *out, void *stream) {
 int spk_q80_row(const void *w, int rows, int cols, int row, const int *token, float *out, void *stream) {
     if (check_blocks(w, rows, cols, 32)) return -1;
     if (!token && (row < 0 || row >= rows)) return set_error("row %d is outside %d", row, rows);
-    q80_row_kernel<<<(cols + 255) / 256, 256, 0, (cudaStream_t)stream>>>((const uint8_t *)w, rows, cols, token, row, out,
-                                                                       device_error_ptr());
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(q80_row_kernel, dim3((cols + 255) / 256), dim3(256), 0, (cudaStream_t)stream,
+                               (const uint8_t *)w, rows, cols, token, row, out, device_error_ptr());
     return e == cudaSuccess ? 0 : cuda_fail("q8_0 row launch", e);
 }
 

@@ -82,6 +82,8 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_partial_kernel(const AttnArg
     __shared__ float kn[HD], vn[HD];
     __shared__ float wm[ATT_WARPS][MAX_GROUP], wl[ATT_WARPS][MAX_GROUP];
     __shared__ float wo[ATT_WARPS][MAX_GROUP][HD];
+    pdl_trigger();
+    pdl_wait();
     const int kvh = blockIdx.x, split = blockIdx.y;
     const int G = a.heads / a.kv_heads;
     const int qd = a.heads * HD, kvd = a.kv_heads * HD;
@@ -215,6 +217,8 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const float *part, in
                                                            int hd, const float *gate, float *attn) {
     __shared__ float w[COMB_MAX_SPLIT];
     __shared__ float red[4];
+    pdl_trigger();
+    pdl_wait();
     const int h = blockIdx.x, G = heads / kv_heads, kvh = h / G, gi = h % G;
     const float *p0 = part + (size_t)kvh * nsplit * G * (hd + 2) + (size_t)gi * (hd + 2);
     const size_t stride = (size_t)G * (hd + 2);
@@ -253,6 +257,8 @@ struct DevCtl {
 };
 
 __global__ void advance_kernel(int *pos, int *token, const int *argmax, const DevCtl *ctl, int *step) {
+    pdl_trigger();
+    pdl_wait();
     const int s = *step;
     if (ctl->ids && s < ctl->cap) ctl->ids[s] = *argmax;
     *token = *argmax;
@@ -340,8 +346,7 @@ int qkv_gate(const spk_model::Layer &L, const float *h, float eps, float *qkv, f
 
 template <int HD>
 int attn_launch(const AttnArgs &a, cudaStream_t s) {
-    attn_partial_kernel<HD><<<dim3(a.kv_heads, a.nsplit), ATT_THREADS, 0, s>>>(a);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(attn_partial_kernel<HD>, dim3(a.kv_heads, a.nsplit), dim3(ATT_THREADS), 0, s, a);
     return e == cudaSuccess ? 0 : cuda_fail("attention launch", e);
 }
 
@@ -381,7 +386,9 @@ int enqueue_step(spk_model *m) {
         a.nsplit = a.full ? m->nsplit_full : m->nsplit_slide;
         a.part = m->part;
         if ((c.head_dim == 256 ? attn_launch<256>(a, s) : attn_launch<128>(a, s)) || mark(m)) return -1;
-        attn_combine_kernel<<<m->hl, 128, 0, s>>>(m->part, a.nsplit, m->hl, m->kvl, c.head_dim, m->gate, m->attn);
+        cudaError_t ce = launch_pdl(attn_combine_kernel, dim3(m->hl), dim3(128), 0, s, (const float *)m->part, a.nsplit,
+                                    m->hl, m->kvl, c.head_dim, (const float *)m->gate, m->attn);
+        if (ce != cudaSuccess) return cuda_fail("attention combine launch", ce);
         if (mark(m)) return -1;
         if (tp) {
             if (vq_call(L.m[2], 1, nullptr, m->attn, nullptr, 0.f, m->pbuf, 0, s) || mark(m)) return -1;
@@ -402,8 +409,8 @@ int enqueue_step(spk_model *m) {
                         m->head_partial, m->head_counter, s) || mark(m))
         return -1;
     if (tp && (tp_argmax(m->tpv, m->logits, amax_l, m->row0, amax, s) || mark(m))) return -1;
-    advance_kernel<<<1, 1, 0, s>>>(pos, token, amax, m->ctl, m->state + 3);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(advance_kernel, dim3(1), dim3(1), 0, s, pos, token, (const int *)amax,
+                               (const DevCtl *)m->ctl, m->state + 3);
     if (e != cudaSuccess) return cuda_fail("decode step launch", e);
     return mark(m);
 }

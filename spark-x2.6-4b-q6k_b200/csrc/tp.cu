@@ -67,6 +67,8 @@ __device__ bool wait_all(const TpView &v, int slot, unsigned int seq) {
 __global__ void __launch_bounds__(TP_THREADS) tp_sum_kernel(const TpView v, const float *__restrict__ part,
                                                             float *__restrict__ h, int n) {
     __shared__ unsigned int s_seq;
+    pdl_trigger();
+    pdl_wait();
     if (threadIdx.x == 0) s_seq = *v.seq + 1u;
     __syncthreads();
     const unsigned int seq = s_seq;
@@ -102,6 +104,8 @@ __device__ __forceinline__ unsigned long long argmax_key(float x, int idx) {
 __global__ void tp_argmax_kernel(const TpView v, const float *__restrict__ logits, const int *__restrict__ amax_local,
                                  int row0, int *__restrict__ amax) {
     __shared__ unsigned int s_seq;
+    pdl_trigger();
+    pdl_wait();
     if (threadIdx.x == 0) s_seq = *v.seq + 1u;
     __syncthreads();
     const unsigned int seq = s_seq;
@@ -139,14 +143,12 @@ size_t tp_mailbox_bytes(int world, int n, size_t *flags_off, int *stride) {
 
 int tp_sum(const TpView &v, const float *part, float *h, int n, cudaStream_t s) {
     if (n % 4 || n > v.stride) return set_error("tp_sum: %d floats do not fit the %d-float mailbox rows", n, v.stride);
-    tp_sum_kernel<<<1, TP_THREADS, 0, s>>>(v, part, h, n);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(tp_sum_kernel, dim3(1), dim3(TP_THREADS), 0, s, v, part, h, n);
     return e == cudaSuccess ? 0 : cuda_fail("tp_sum launch", e);
 }
 
 int tp_argmax(const TpView &v, const float *logits, const int *amax_local, int row0, int *amax, cudaStream_t s) {
-    tp_argmax_kernel<<<1, 32, 0, s>>>(v, logits, amax_local, row0, amax);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(tp_argmax_kernel, dim3(1), dim3(32), 0, s, v, logits, amax_local, row0, amax);
     return e == cudaSuccess ? 0 : cuda_fail("tp_argmax launch", e);
 }
 

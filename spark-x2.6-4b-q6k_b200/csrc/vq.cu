@@ -212,6 +212,7 @@ __global__ void __launch_bounds__(Warps<F>::W * 32, 1) vq_fast_kernel(const Fast
     const int re = xt ? L.rows : (int)(((long long)(blockIdx.x + 1) * L.rows) / G);
     const int ntile = (re - rb + tr - 1) / tr;
 
+    pdl_trigger();
     if (tid == 0) {
         for (int b = 0; b < NB; b++) {
             mbar_init(&full[b], 1);
@@ -231,6 +232,9 @@ __global__ void __launch_bounds__(Warps<F>::W * 32, 1) vq_fast_kernel(const Fast
         const uint2 *src = reinterpret_cast<const uint2 *>(stp[q] + L.cb_off);
         for (int v = tid; v < nc; v += FAST_THREADS) cb[q * nc + v] = __ldg(src + v);
     }
+    // Everything above read weights only; x (and y, when accumulating) come from
+    // the preceding kernels.
+    pdl_wait();
     // Activations: coalesced loads (with the optional RMSNorm folded in) into a
     // per-lane padded layout, then each lane takes its 4F values with 16-byte
     // shared loads that hit distinct banks.
@@ -361,6 +365,8 @@ struct GenArgs {
 __global__ void vq_generic_kernel(const GenArgs a) {
     __shared__ double red[32];
     const Layout &L = a.L;
+    pdl_trigger();
+    pdl_wait();
     float inv = 1.0f;
     if (a.norm_w) inv = block_rms_inv(a.x, L.cols, a.eps, red);
     const int warp = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
@@ -524,8 +530,7 @@ int launch_fast_t(const FastPlan &P, cudaStream_t s) {
     const int ntr = (P.args.L.rows + P.tr - 1) / P.tr;
     const int cap = sm_count() - (P.args.has_x ? 1 : 0);
     const int grid = (ntr < cap ? ntr : cap) + (P.args.has_x ? 1 : 0);
-    k<<<grid, Warps<F>::W * 32, P.smem, s>>>(P.args);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(k, dim3(grid), dim3(Warps<F>::W * 32), P.smem, s, P.args);
     return e == cudaSuccess ? 0 : cuda_fail("vq fast kernel launch", e);
 }
 
@@ -569,8 +574,7 @@ int launch_generic(const uint8_t *const *st, int nstg, int ng, const Layout &L, 
     a.y = y;
     a.accumulate = accumulate;
     const int blocks = (int)(((size_t)L.rows * 32 + threads - 1) / threads);
-    vq_generic_kernel<<<blocks, threads, 0, s>>>(a);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(vq_generic_kernel, dim3(blocks), dim3(threads), 0, s, a);
     return e == cudaSuccess ? 0 : cuda_fail("vq generic kernel launch", e);
 }
 
