@@ -303,7 +303,7 @@ def run_ours(args) -> None:
                          "frac": achieved / peak, "traffic": traffic, "alg_bytes_per_launch": alg_bytes,
                          "us_per_launch": t_kernel * 1e6},
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4},
-            "gpu_launches": args.steps * (3 + 6 * cfg.layers + (2 * cfg.layers + 1 if world > 1 else 0)),
+            "gpu_launches": args.steps * (3 + 5 * cfg.layers + (2 * cfg.layers + 1 if world > 1 else 0)),
             "clocks": clk.summary(),
         }
         if cb:

@@ -133,6 +133,16 @@ int spk_q80_dequant(const void *w, size_t nblocks, float *out, void *stream);
  * int *token when token != NULL (replaces the embedding row of vq-model-gpu.cu:783-788). */
 int spk_q80_row(const void *w, int rows, int cols, int row, const int *token, float *out, void *stream);
 
+/* --------------------------------------------------- verify batch (M <= 8) ---
+ * The speculative verify's GEMM: one pass over a VQ matrix for up to 8 tokens
+ * (replaces the tiled prefill GEMM the reference runs for a draft block,
+ * gemm_tiled_kernel decode-gpu.cu:359-501 via forward_batch vq-model-gpu.cu:858-943).
+ * x: ntok rows of cols floats, stride ldx; y: ntok rows of rows floats, stride ldy;
+ * norm_w (optional) applies RMSNorm to every x row first. */
+int spk_verify_gemm(const void *const *stages, int nstages, int dim, int nc, int rows, int cols, int v3, int ntok,
+                    const float *x, int ldx, const float *norm_w, float eps, float *y, int ldy, int accumulate,
+                    void *stream);
+
 /* --------------------------------------------------- decode step (model) ---
  * The model-level ABI the Rust host side (tools/vq-runtime/src/model.rs Model)
  * needs: forward(token, pos) -> logits / next id, rollback, reset. Weights are
@@ -178,6 +188,13 @@ int spk_model_set_head(spk_model *m, const void *embed_q80, const float *final_n
 /* Model::forward (model.rs:442-591) + Model::argmax (594-604) through HOST buffers:
  * logits_host (may be NULL) receives vocab f32, *next_host the greedy id. Synchronizes. */
 int spk_model_forward(spk_model *m, int token, int pos, float *logits_host, int *next_host);
+/* The speculative verify (vq-model-gpu.cu:947-969 verify_logits, tools/dspark/src/
+ * spec.rs:197-205): tokens[0..ntok) (ntok <= 8: the anchor and 7 proposals) at
+ * positions pos..pos+ntok-1 in one batched forward; next_host[t] = greedy id after
+ * tokens[t]; logits_host (may be NULL) receives [ntok][vocab]. Leaves len = pos + ntok:
+ * keep the accepted prefix with spk_model_rollback(m, pos + k + 1) as spec.rs:241 does.
+ * Synchronizes. */
+int spk_model_verify(spk_model *m, const int *tokens, int ntok, int pos, int *next_host, float *logits_host);
 /* Device-resident greedy loop: set the start (token, pos) and a device int buffer
  * for the generated ids; spk_model_run then replays the captured step `steps` times
  * with no host round trip (asynchronous on the model's stream). */
@@ -195,7 +212,7 @@ int spk_model_advance_len(spk_model *m, int n);
 /* Per-launch device times of one decode step (no counterpart in the reference): runs
  * one step from the device state, as spk_model_run does, from a second captured graph
  * with a timing event after every launch; us[i] receives launch i's microseconds in
- * enqueue order: embedding row; per layer QKV+g_proj, attention, combine, out_proj,
+ * enqueue order: embedding row; per layer QKV+g_proj, attention, out_proj,
  * [tp_sum], gate+up, down, [tp_sum]; head; [tp_argmax]; advance. Returns the launch
  * count or -1. Needs one step run before; with tp_world > 1 every rank traces together. */
 int spk_model_trace(spk_model *m, float *us, int cap);

@@ -1,0 +1,334 @@
+// attn.cu — GQA decode attention (model.rs:508-557) on B200.
+//
+// One CTA = one (token, KV head, sequence split). It ropes the token's q heads of
+// the KV head's group and its k (model.rs:431-439), and — for a single token —
+// the CTA whose split holds the token's own position writes the new K/V row. Its
+// 8 warps walk the split's positions 4 at a time (4 independent K/V row loads
+// per warp in flight: the loop is latency-bound, not compute-bound), form the
+// group's scores with butterfly sums and keep an online softmax per q head. The
+// warps merge in shared memory into the split's (o, m, l), and the last split of
+// each (token, KV head) to finish — an atomic ticket — merges all splits in a
+// fixed order and applies the per-head sigmoid gate (model.rs:538-550). The
+// ticket is reset by that CTA, so a captured graph replays without a memset.
+#include "attn.cuh"
+
+namespace spk {
+namespace {
+
+constexpr int ATT_THREADS = 256;
+constexpr int ATT_WARPS = ATT_THREADS / 32;
+constexpr int ATT_U = 4;   // positions per warp per iteration
+
+// NeoX rotate-half on the first pdim elements of x (shared memory), model.rs:431-439:
+//   x[i] = a cos - b sin ; x[i+half] = b cos + a sin, each product rounded.
+__device__ void rope_smem(float *x, const float *freq, int pdim, int pos) {
+    const int half = pdim / 2;
+    for (int i = threadIdx.x; i < half; i += blockDim.x) {
+        const float ang = __fmul_rn((float)pos, freq[i]);
+        const float c = cosf(ang), s = sinf(ang);
+        const float a = x[i], b = x[i + half];
+        x[i] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+        x[i + half] = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
+    }
+}
+
+template <int DPL, int F16>
+__device__ __forceinline__ void load_row(const void *base, size_t off, float (&r)[DPL]) {
+    if (F16) {
+        const __half *p = reinterpret_cast<const __half *>(base) + off;
+        if constexpr (DPL == 8) {
+            const uint4 w = *reinterpret_cast<const uint4 *>(p);
+            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&ws[i]));
+                r[2 * i] = f.x;
+                r[2 * i + 1] = f.y;
+            }
+        } else {
+            const uint2 w = *reinterpret_cast<const uint2 *>(p);
+            const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&w.x));
+            const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&w.y));
+            r[0] = f0.x;
+            r[1] = f0.y;
+            r[2] = f1.x;
+            r[3] = f1.y;
+        }
+    } else {
+        const float4 *p = reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(base) + off);
+#pragma unroll
+        for (int i = 0; i < DPL / 4; i++) {
+            const float4 f = p[i];
+            r[4 * i] = f.x;
+            r[4 * i + 1] = f.y;
+            r[4 * i + 2] = f.z;
+            r[4 * i + 3] = f.w;
+        }
+    }
+}
+
+template <int HD, int F16>
+__global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnArgs a) {
+    constexpr int DPL = HD / 32;   // dims per lane
+    constexpr int MG = ATT_MAX_GROUP;
+    __shared__ float qs[MG][HD];
+    __shared__ float kn[HD], vn[HD];
+    __shared__ float wm[ATT_WARPS][MG], wl[ATT_WARPS][MG];
+    __shared__ float wo[ATT_WARPS][MG][HD];
+    __shared__ float cw[MG][ATT_MAX_SPLIT];
+    __shared__ float cl[MG];
+    __shared__ int is_last;
+    pdl_trigger();
+    pdl_wait();
+    const int kvh = blockIdx.x, split = blockIdx.y, tok = blockIdx.z;
+    const int G = a.heads / a.kv_heads;
+    const int qd = a.heads * HD, kvd = a.kv_heads * HD;
+    const int pos = *a.pos + tok;
+    const int start = a.full ? 0 : max(0, pos + 1 - a.window);
+    const int n = pos + 1 - start;
+    const int csz = max((n + a.nsplit - 1) / a.nsplit, 16);
+    const int c0 = start + split * csz, c1 = min(pos + 1, c0 + csz);
+    const float *qrow = a.qkv + (size_t)tok * a.ldqkv;
+    const size_t pbase = ((size_t)tok * a.kv_heads + kvh) * a.nsplit;   // this (token, KV head)'s splits
+    constexpr int PR = HD + 4;   // a partial row: o[HD], m, l, 2 pad (16-byte rows)
+    const size_t pstride = (size_t)G * PR;
+    float *out = a.part + (pbase + split) * pstride;
+
+    for (int i = threadIdx.x; i < G * HD; i += blockDim.x) qs[i / HD][i % HD] = qrow[(size_t)(kvh * G + i / HD) * HD + i % HD];
+    for (int i = threadIdx.x; i < HD; i += blockDim.x) {
+        kn[i] = qrow[qd + (size_t)kvh * HD + i];
+        vn[i] = qrow[qd + kvd + (size_t)kvh * HD + i];
+    }
+    __syncthreads();
+    for (int h = 0; h < G; h++) rope_smem(qs[h], a.freq, a.pdim, pos);
+    rope_smem(kn, a.freq, a.pdim, pos);
+    __syncthreads();
+    // a single token's own K/V row: written by the split that owns `pos`; nobody reads that slot now
+    if (a.store && c0 <= pos && pos < c1) {
+        for (int i = threadIdx.x; i < HD; i += blockDim.x) {
+            const size_t o = ((size_t)kvh * a.slots + pos % a.slots) * HD + i;
+            if (F16) {
+                reinterpret_cast<__half *>(a.kc)[o] = __float2half_rn(kn[i]);
+                reinterpret_cast<__half *>(a.vc)[o] = __float2half_rn(vn[i]);
+            } else {
+                reinterpret_cast<float *>(a.kc)[o] = kn[i];
+                reinterpret_cast<float *>(a.vc)[o] = vn[i];
+            }
+        }
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (c0 < c1) {
+        float q[MG][DPL], o[MG][DPL], m[MG], l[MG];
+        const float scale = 1.0f / sqrtf((float)HD);
+#pragma unroll
+        for (int h = 0; h < MG; h++) {
+            m[h] = -INFINITY;
+            l[h] = 0.f;
+#pragma unroll
+            for (int d = 0; d < DPL; d++) {
+                q[h][d] = h < G ? qs[h][lane * DPL + d] : 0.f;
+                o[h][d] = 0.f;
+            }
+        }
+        for (int j0 = c0 + warp * ATT_U; j0 < c1; j0 += ATT_WARPS * ATT_U) {
+            float kr[ATT_U][DPL], vr[ATT_U][DPL];
+#pragma unroll
+            for (int u = 0; u < ATT_U; u++) {
+                const int j = j0 + u;
+                if (j >= c1) {
+#pragma unroll
+                    for (int d = 0; d < DPL; d++) kr[u][d] = vr[u][d] = 0.f;
+                } else if (j == pos) {   // this token's own row: f32, before any f16 rounding
+#pragma unroll
+                    for (int d = 0; d < DPL; d++) {
+                        kr[u][d] = kn[lane * DPL + d];
+                        vr[u][d] = vn[lane * DPL + d];
+                    }
+                } else {
+                    const size_t base = ((size_t)kvh * a.slots + j % a.slots) * HD + lane * DPL;
+                    load_row<DPL, F16>(a.kc, base, kr[u]);
+                    load_row<DPL, F16>(a.vc, base, vr[u]);
+                }
+            }
+            float s[ATT_U][MG];
+#pragma unroll
+            for (int u = 0; u < ATT_U; u++)
+#pragma unroll
+                for (int h = 0; h < MG; h++) {
+                    float t = 0.f;
+#pragma unroll
+                    for (int d = 0; d < DPL; d++) t = fmaf(q[h][d], kr[u][d], t);
+                    s[u][h] = t;
+                }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+                for (int u = 0; u < ATT_U; u++)
+#pragma unroll
+                    for (int h = 0; h < MG; h++) s[u][h] += __shfl_xor_sync(0xffffffffu, s[u][h], off);
+#pragma unroll
+            for (int h = 0; h < MG; h++) {
+                if (h >= G) break;
+                float mx = -INFINITY;
+#pragma unroll
+                for (int u = 0; u < ATT_U; u++)
+                    if (j0 + u < c1) mx = fmaxf(mx, s[u][h] * scale);
+                const float mn = fmaxf(m[h], mx);
+                const float corr = expf(m[h] - mn);
+                float p[ATT_U], ps = 0.f;
+#pragma unroll
+                for (int u = 0; u < ATT_U; u++) {
+                    p[u] = j0 + u < c1 ? expf(s[u][h] * scale - mn) : 0.f;
+                    ps += p[u];
+                }
+                l[h] = l[h] * corr + ps;
+#pragma unroll
+                for (int d = 0; d < DPL; d++) {
+                    float v = o[h][d] * corr;
+#pragma unroll
+                    for (int u = 0; u < ATT_U; u++) v = fmaf(p[u], vr[u][d], v);
+                    o[h][d] = v;
+                }
+                m[h] = mn;
+            }
+        }
+        // merge the warps into this split's (o, m, l)
+        if (lane == 0)
+            for (int h = 0; h < G; h++) {
+                wm[warp][h] = m[h];
+                wl[warp][h] = l[h];
+            }
+        for (int h = 0; h < G; h++)
+#pragma unroll
+            for (int d = 0; d < DPL; d++) wo[warp][h][lane * DPL + d] = o[h][d];
+        __syncthreads();
+        for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
+            const int h = i / HD, d = i % HD;
+            float M = -INFINITY;
+            for (int w = 0; w < ATT_WARPS; w++) M = fmaxf(M, wm[w][h]);
+            float L = 0.f, O = 0.f;
+            for (int w = 0; w < ATT_WARPS; w++) {
+                if (wm[w][h] == -INFINITY) continue;
+                const float e = expf(wm[w][h] - M);
+                L += wl[w][h] * e;
+                O += wo[w][h][d] * e;
+            }
+            out[h * PR + d] = O;
+            if (d == 0) {
+                out[h * PR + HD] = M;
+                out[h * PR + HD + 1] = L;
+            }
+        }
+    } else {   // an empty split: weight 0 in the merge
+        for (int i = threadIdx.x; i < G * PR; i += blockDim.x) out[i] = (i % PR) == HD ? -INFINITY : 0.f;
+    }
+    // the last split of this (token, KV head) to finish merges all of them
+    __threadfence();
+    __syncthreads();
+    unsigned int *ticket = a.count + (size_t)tok * a.kv_heads + kvh;
+    if (threadIdx.x == 0) is_last = atomicAdd(ticket, 1u) == (unsigned int)(a.nsplit - 1);
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    const float *p0 = a.part + pbase * pstride;
+    for (int i = threadIdx.x; i < G * a.nsplit; i += blockDim.x) {
+        const int h = i / a.nsplit, c = i - h * a.nsplit;
+        cw[h][c] = __ldcg(p0 + c * pstride + h * PR + HD);
+    }
+    __syncthreads();
+    if (warp < G) {   // warp h: the split weights e^{m_c - M} and the total L of head h
+        const int h = warp;
+        float M = -INFINITY;
+        for (int c = lane; c < a.nsplit; c += 32) M = fmaxf(M, cw[h][c]);
+        for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+        float L = 0.f;
+        for (int c = lane; c < a.nsplit; c += 32) {
+            const float mc = cw[h][c];
+            const float e = mc == -INFINITY ? 0.f : expf(mc - M);
+            L += __ldcg(p0 + c * pstride + h * PR + HD + 1) * e;
+            cw[h][c] = e;
+        }
+        L = warp_sum(L);
+        if (lane == 0) cl[h] = L;
+    }
+    __syncthreads();
+    // one thread per 4 output dims, 8 float4 loads in flight per thread
+    for (int i = threadIdx.x; i < G * (HD / 4); i += blockDim.x) {
+        const int h = i / (HD / 4), d4 = i - h * (HD / 4);
+        const float *ph = p0 + h * PR + 4 * d4;
+        float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+        for (int c = 0; c < a.nsplit; c++) {
+            const float4 v = __ldcg(reinterpret_cast<const float4 *>(ph + c * pstride));
+            const float w = cw[h][c];
+            O.x = fmaf(v.x, w, O.x);
+            O.y = fmaf(v.y, w, O.y);
+            O.z = fmaf(v.z, w, O.z);
+            O.w = fmaf(v.w, w, O.w);
+        }
+        const int qh = kvh * G + h;
+        const float gsig = 1.0f / (1.0f + expf(-a.gate[(size_t)tok * a.ldgate + qh]));
+        float *dst = a.out + (size_t)tok * a.ldout + (size_t)qh * HD + 4 * d4;
+        dst[0] = (O.x / cl[h]) * gsig;
+        dst[1] = (O.y / cl[h]) * gsig;
+        dst[2] = (O.z / cl[h]) * gsig;
+        dst[3] = (O.w / cl[h]) * gsig;
+    }
+    if (threadIdx.x == 0) *ticket = 0u;
+}
+
+// Rope K and store the K/V rows of ntok consecutive tokens: block t = token t.
+template <int F16>
+__global__ void attn_store_kernel(const AttnArgs a) {
+    extern __shared__ float ks[];   // [kv_heads * hd]
+    pdl_trigger();
+    pdl_wait();
+    const int tok = blockIdx.x, pos = *a.pos + tok;
+    const int qd = a.heads * a.hd, kvd = a.kv_heads * a.hd;
+    const float *row = a.qkv + (size_t)tok * a.ldqkv;
+    for (int i = threadIdx.x; i < kvd; i += blockDim.x) ks[i] = row[qd + i];
+    __syncthreads();
+    for (int h = 0; h < a.kv_heads; h++) rope_smem(ks + (size_t)h * a.hd, a.freq, a.pdim, pos);
+    __syncthreads();
+    for (int i = threadIdx.x; i < kvd; i += blockDim.x) {
+        const int h = i / a.hd, d = i - h * a.hd;
+        const size_t o = ((size_t)h * a.slots + pos % a.slots) * a.hd + d;
+        const float v = row[qd + kvd + i];
+        if (F16) {
+            reinterpret_cast<__half *>(a.kc)[o] = __float2half_rn(ks[i]);
+            reinterpret_cast<__half *>(a.vc)[o] = __float2half_rn(v);
+        } else {
+            reinterpret_cast<float *>(a.kc)[o] = ks[i];
+            reinterpret_cast<float *>(a.vc)[o] = v;
+        }
+    }
+}
+
+}  // namespace
+
+int attn_decode(const AttnArgs &a, cudaStream_t s) {
+    if (a.heads % a.kv_heads || a.heads / a.kv_heads > ATT_MAX_GROUP) return set_error("attention: GQA group above %d", ATT_MAX_GROUP);
+    if (a.nsplit < 1 || a.nsplit > ATT_MAX_SPLIT || a.ntok < 1 || a.ntok > ATT_MAX_TOK)
+        return set_error("attention: %d splits x %d tokens out of range", a.nsplit, a.ntok);
+    if (a.store && a.ntok != 1) return set_error("attention: in-kernel K/V store takes one token");
+    const dim3 grid(a.kv_heads, a.nsplit, a.ntok);
+    cudaError_t e;
+    if (a.hd == 256)
+        e = a.kv_f16 ? launch_pdl(attn_kernel<256, 1>, grid, dim3(ATT_THREADS), 0, s, a)
+                     : launch_pdl(attn_kernel<256, 0>, grid, dim3(ATT_THREADS), 0, s, a);
+    else if (a.hd == 128)
+        e = a.kv_f16 ? launch_pdl(attn_kernel<128, 1>, grid, dim3(ATT_THREADS), 0, s, a)
+                     : launch_pdl(attn_kernel<128, 0>, grid, dim3(ATT_THREADS), 0, s, a);
+    else
+        return set_error("attention: head_dim %d (128 or 256)", a.hd);
+    return e == cudaSuccess ? 0 : cuda_fail("attention launch", e);
+}
+
+int attn_store_batch(const AttnArgs &a, cudaStream_t s) {
+    const size_t sm = (size_t)a.kv_heads * a.hd * sizeof(float);
+    cudaError_t e = a.kv_f16 ? launch_pdl(attn_store_kernel<1>, dim3(a.ntok), dim3(256), sm, s, a)
+                             : launch_pdl(attn_store_kernel<0>, dim3(a.ntok), dim3(256), sm, s, a);
+    return e == cudaSuccess ? 0 : cuda_fail("attention K/V store launch", e);
+}
+
+}  // namespace spk

@@ -1,0 +1,41 @@
+// attn.cuh — GQA decode attention over the KV cache (model.rs:508-557), for one
+// token or a verify batch of up to 8 consecutive tokens.
+#pragma once
+#include "common.cuh"
+
+namespace spk {
+
+constexpr int ATT_MAX_GROUP = 4;     // q heads per KV head
+constexpr int ATT_MAX_SPLIT = 256;   // sequence splits per KV head
+constexpr int ATT_MAX_TOK = 8;
+
+struct AttnArgs {
+    const float *qkv;          // [ntok][ldqkv]: q (heads*hd) | k (kv_heads*hd) | v, pre-rope
+    int ldqkv;
+    void *kc, *vc;             // this layer's caches: [kv_heads][slots][hd], f32 or f16
+    int kv_f16;
+    int slots;                 // cache positions
+    int full, window;
+    const float *freq;         // [pdim/2] rope frequencies of this layer type (model.rs:416-429)
+    int pdim;
+    int heads, kv_heads, hd;   // this rank's heads
+    const int *pos;            // device position of token 0; token t sits at pos + t
+    int ntok;                  // grid.z
+    int store;                 // 1: the kernel writes each token's K/V row itself (ntok 1)
+    int nsplit;                // grid.y: sequence splits
+    float *part;               // [ntok][kv_heads][nsplit][group][hd + 4]: o, m, l (+2 pad) per split
+    unsigned int *count;       // [ntok][kv_heads], zero; the last split of each resets its own
+    const float *gate;         // [ntok][ldgate] g_proj output (pre-sigmoid)
+    int ldgate;
+    float *out;                // [ntok][ldout] sigmoid(g_h) * softmax(q_h K^T / sqrt(hd)) V
+    int ldout;
+    int *err;
+};
+
+// Split-K flash-decode with the merge in the last CTA of every (token, KV head).
+int attn_decode(const AttnArgs &a, cudaStream_t s);
+
+// Rope K and store K/V rows of a batch of ntok tokens (before attn_decode with store 0).
+int attn_store_batch(const AttnArgs &a, cudaStream_t s);
+
+}  // namespace spk

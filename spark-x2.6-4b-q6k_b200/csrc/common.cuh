@@ -74,10 +74,6 @@ inline bool v3_width_ok(int nc) {
 int sm_count();
 size_t smem_optin_max();
 
-// Tensor-core VQ GEMV (vq_mma.cu): 1 launched, 0 geometry not taken, -1 error.
-int vq_mma_gemv(const void *const *stages, int nstg, const Layout &L, const float *x, const float *norm_w, float eps,
-                float *y, int accumulate, int mode, const float *aux, cudaStream_t s);
-
 // QKV and g_proj in one launch (vq.cu): y = W RMSNorm?(x), xy = X RMSNorm?(x).
 // 0 launched, 1 geometry not taken, -1 error.
 int vq_gemv_with_extra(const void *const *stages, int nstg, const Layout &L, const void *const *xstages,

@@ -8,13 +8,12 @@
 //   logits = W_embed rmsnorm(h); next = argmax(logits)
 // The launches per layer (the reference issues ~218 launches and one host sync
 // per token, vq-model-gpu.cu:776-835):
-//   1. QKV GEMV with the RMSNorm prologue              (vq.cu, persistent TMA kernel)
-//   2. g_proj GEMV with the RMSNorm prologue
-//   3. attention partials: rope, KV store, split-K flash-decode over the cache
-//   4. attention combine: merge the splits, sigmoid gate
-//   5. out_proj GEMV accumulating into h
-//   6. gate+up GEMV pair with RMSNorm prologue and erf-GELU(gate)*up epilogue
-//   7. down GEMV accumulating into h
+//   1. QKV and g_proj GEMVs in one launch, RMSNorm prologue (vq.cu, persistent TMA kernel)
+//   2. attention: rope, KV store, split-K flash-decode over the cache, the splits
+//      merged and the sigmoid gate applied by the last CTA (attn.cu)
+//   3. out_proj GEMV accumulating into h
+//   4. gate+up GEMV pair with RMSNorm prologue and erf-GELU(gate)*up epilogue
+//   5. down GEMV accumulating into h
 // then the tied Q8_0 head with fused argmax (ggml.cu) and a one-thread advance
 // kernel (pos += 1, token = argmax). Token and position live in device memory,
 // so the whole step is captured once in a CUDA graph and replayed per token.
@@ -28,227 +27,15 @@
 
 #include <vector>
 
+#include "attn.cuh"
 #include "common.cuh"
 #include "spk.h"
 #include "tp.cuh"
+#include "vq_mma.cuh"
 
 using namespace spk;
 
 namespace {
-
-constexpr int ATT_THREADS = 256;
-constexpr int ATT_WARPS = ATT_THREADS / 32;
-constexpr int MAX_GROUP = 4;   // q heads per kv head handled by one CTA
-
-struct AttnArgs {
-    const float *qkv;          // [q_dim + 2 kv_dim] this token's projections (pre-rope)
-    void *kc, *vc;             // this layer's caches: [kv_heads][slots][hd], f32 or f16
-    int kv_f16;
-    int slots;                 // cache positions (the capacity: every layer keeps its whole history)
-    int full, window;
-    const float *freq;         // [pdim/2] rope frequencies of this layer type (model.rs:416-429)
-    int pdim;
-    int heads, kv_heads, hd;
-    const int *pos;            // device position of this token
-    int nsplit;                // grid.y: sequence splits
-    float *part;               // [kv_heads][nsplit][group][hd + 2]: o, m, l
-};
-
-__device__ __forceinline__ float kv_load(const void *base, int kv_f16, size_t idx) {
-    return kv_f16 ? __half2float(reinterpret_cast<const __half *>(base)[idx]) : reinterpret_cast<const float *>(base)[idx];
-}
-
-// NeoX rotate-half on the first pdim elements of x (shared memory), model.rs:431-439:
-//   x[i] = a cos - b sin ; x[i+half] = b cos + a sin, each product rounded.
-__device__ void rope_smem(float *x, const float *freq, int pdim, int pos) {
-    const int half = pdim / 2;
-    for (int i = threadIdx.x; i < half; i += blockDim.x) {
-        const float ang = __fmul_rn((float)pos, freq[i]);
-        const float c = cosf(ang), s = sinf(ang);
-        const float a = x[i], b = x[i + half];
-        x[i] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
-        x[i + half] = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
-    }
-}
-
-// One CTA = one kv head x one split of the visible positions, for all the q
-// heads of its GQA group (their K/V reads are shared). Per position a warp
-// reads one K row (lane d-slice), forms the group's scores with a butterfly
-// sum, and keeps an online softmax; warps are merged at the end.
-template <int HD>
-__global__ void __launch_bounds__(ATT_THREADS) attn_partial_kernel(const AttnArgs a) {
-    constexpr int DPL = HD / 32;   // dims per lane
-    __shared__ float qs[MAX_GROUP][HD];
-    __shared__ float kn[HD], vn[HD];
-    __shared__ float wm[ATT_WARPS][MAX_GROUP], wl[ATT_WARPS][MAX_GROUP];
-    __shared__ float wo[ATT_WARPS][MAX_GROUP][HD];
-    pdl_trigger();
-    pdl_wait();
-    const int kvh = blockIdx.x, split = blockIdx.y;
-    const int G = a.heads / a.kv_heads;
-    const int qd = a.heads * HD, kvd = a.kv_heads * HD;
-    const int pos = *a.pos;
-    const int start = a.full ? 0 : max(0, pos + 1 - a.window);
-    const int n = pos + 1 - start;
-    const int csz = max((n + a.nsplit - 1) / a.nsplit, 16);
-    const int c0 = start + split * csz, c1 = min(pos + 1, c0 + csz);
-    float *out = a.part + ((size_t)kvh * a.nsplit + split) * G * (HD + 2);
-
-    for (int i = threadIdx.x; i < G * HD; i += blockDim.x) qs[i / HD][i % HD] = a.qkv[(size_t)(kvh * G + i / HD) * HD + i % HD];
-    for (int i = threadIdx.x; i < HD; i += blockDim.x) {
-        kn[i] = a.qkv[qd + (size_t)kvh * HD + i];
-        vn[i] = a.qkv[qd + kvd + (size_t)kvh * HD + i];
-    }
-    __syncthreads();
-    for (int h = 0; h < G; h++) rope_smem(qs[h], a.freq, a.pdim, pos);
-    rope_smem(kn, a.freq, a.pdim, pos);
-    __syncthreads();
-    // The split that owns `pos` writes the new row; nobody else reads that slot now.
-    const int wslot = pos % a.slots;
-    if (c0 <= pos && pos < c1) {
-        for (int i = threadIdx.x; i < HD; i += blockDim.x) {
-            const size_t o = ((size_t)kvh * a.slots + wslot) * HD + i;
-            if (a.kv_f16) {
-                reinterpret_cast<__half *>(a.kc)[o] = __float2half_rn(kn[i]);
-                reinterpret_cast<__half *>(a.vc)[o] = __float2half_rn(vn[i]);
-            } else {
-                reinterpret_cast<float *>(a.kc)[o] = kn[i];
-                reinterpret_cast<float *>(a.vc)[o] = vn[i];
-            }
-        }
-    }
-    if (c0 >= c1) {   // an empty split: weight 0 in the merge (o zeroed so 0 * o stays 0)
-        for (int i = threadIdx.x; i < G * (HD + 2); i += blockDim.x) {
-            const int d = i % (HD + 2);
-            out[i] = d == HD ? -INFINITY : 0.f;
-        }
-        return;
-    }
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    float q[MAX_GROUP][DPL], o[MAX_GROUP][DPL], m[MAX_GROUP], l[MAX_GROUP];
-    const float scale = 1.0f / sqrtf((float)HD);
-#pragma unroll
-    for (int h = 0; h < MAX_GROUP; h++) {
-        m[h] = -INFINITY;
-        l[h] = 0.f;
-#pragma unroll
-        for (int d = 0; d < DPL; d++) {
-            q[h][d] = h < G ? qs[h][lane * DPL + d] : 0.f;
-            o[h][d] = 0.f;
-        }
-    }
-    for (int j = c0 + warp; j < c1; j += ATT_WARPS) {
-        float kr[DPL], vr[DPL];
-        if (j == pos) {
-#pragma unroll
-            for (int d = 0; d < DPL; d++) {
-                kr[d] = kn[lane * DPL + d];
-                vr[d] = vn[lane * DPL + d];
-            }
-        } else {
-            const int slot = j % a.slots;
-            const size_t base = ((size_t)kvh * a.slots + slot) * HD + lane * DPL;
-#pragma unroll
-            for (int d = 0; d < DPL; d++) {
-                kr[d] = kv_load(a.kc, a.kv_f16, base + d);
-                vr[d] = kv_load(a.vc, a.kv_f16, base + d);
-            }
-        }
-        float s[MAX_GROUP];
-#pragma unroll
-        for (int h = 0; h < MAX_GROUP; h++) {
-            float t = 0.f;
-#pragma unroll
-            for (int d = 0; d < DPL; d++) t = fmaf(q[h][d], kr[d], t);
-            s[h] = t;
-        }
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1)
-#pragma unroll
-            for (int h = 0; h < MAX_GROUP; h++) s[h] += __shfl_xor_sync(0xffffffffu, s[h], off);
-#pragma unroll
-        for (int h = 0; h < MAX_GROUP; h++) {
-            if (h >= G) break;
-            const float sc = s[h] * scale;
-            const float mn = fmaxf(m[h], sc);
-            const float corr = expf(m[h] - mn), p = expf(sc - mn);
-            l[h] = l[h] * corr + p;
-#pragma unroll
-            for (int d = 0; d < DPL; d++) o[h][d] = fmaf(p, vr[d], o[h][d] * corr);
-            m[h] = mn;
-        }
-    }
-    // merge the warps
-    if (lane == 0)
-        for (int h = 0; h < G; h++) {
-            wm[warp][h] = m[h];
-            wl[warp][h] = l[h];
-        }
-    for (int h = 0; h < G; h++)
-#pragma unroll
-        for (int d = 0; d < DPL; d++) wo[warp][h][lane * DPL + d] = o[h][d];
-    __syncthreads();
-    for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
-        const int h = i / HD, d = i % HD;
-        float M = -INFINITY;
-        for (int w = 0; w < ATT_WARPS; w++) M = fmaxf(M, wm[w][h]);
-        float L = 0.f, O = 0.f;
-        for (int w = 0; w < ATT_WARPS; w++) {
-            if (wm[w][h] == -INFINITY) continue;
-            const float e = expf(wm[w][h] - M);
-            L += wl[w][h] * e;
-            O += wo[w][h][d] * e;
-        }
-        out[h * (HD + 2) + d] = O;
-        if (d == 0) {
-            out[h * (HD + 2) + HD] = M;
-            out[h * (HD + 2) + HD + 1] = L;
-        }
-    }
-}
-
-// Merge the splits of every q head and apply the per-head sigmoid gate
-// (model.rs:538-550): attn[h][d] = (sum_c o_c e^{m_c-M}) / (sum_c l_c e^{m_c-M}) * sigmoid(g_h).
-// One CTA per q head: the split maxima and weights are formed once in shared
-// memory (one thread per split), then every thread sums its dims over the splits
-// with independent loads.
-constexpr int COMB_MAX_SPLIT = 256;
-__global__ void __launch_bounds__(128) attn_combine_kernel(const float *part, int nsplit, int heads, int kv_heads,
-                                                           int hd, const float *gate, float *attn) {
-    __shared__ float w[COMB_MAX_SPLIT];
-    __shared__ float red[4];
-    pdl_trigger();
-    pdl_wait();
-    const int h = blockIdx.x, G = heads / kv_heads, kvh = h / G, gi = h % G;
-    const float *p0 = part + (size_t)kvh * nsplit * G * (hd + 2) + (size_t)gi * (hd + 2);
-    const size_t stride = (size_t)G * (hd + 2);
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    float mc = -INFINITY;
-    for (int c = threadIdx.x; c < nsplit; c += blockDim.x) mc = fmaxf(mc, p0[c * stride + hd]);
-    for (int o = 16; o > 0; o >>= 1) mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, o));
-    if (lane == 0) red[warp] = mc;
-    __syncthreads();
-    const float M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-    __syncthreads();
-    float lsum = 0.f;
-    for (int c = threadIdx.x; c < nsplit; c += blockDim.x) {
-        const float m = p0[c * stride + hd];
-        const float e = m == -INFINITY ? 0.f : expf(m - M);
-        w[c] = e;
-        lsum += p0[c * stride + hd + 1] * e;
-    }
-    lsum = warp_sum(lsum);
-    if (lane == 0) red[warp] = lsum;
-    __syncthreads();
-    const float L = (red[0] + red[1]) + (red[2] + red[3]);
-    const float gsig = 1.0f / (1.0f + expf(-gate[h]));
-    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-        float O = 0.f;
-#pragma unroll 8
-        for (int c = 0; c < nsplit; c++) O += p0[c * stride + d] * w[c];
-        attn[(size_t)h * hd + d] = (O / L) * gsig;
-    }
-}
 
 // End of a step: record the generated id, feed it back as the next token, advance.
 struct DevCtl {
@@ -293,7 +80,12 @@ struct spk_model {
     int mail_stride = 0;
     void *peer_open[TP_MAX] = {};   // IPC mappings to close
     const float *peer_logits[TP_MAX] = {};
-    float *pbuf = nullptr, *logits_full = nullptr;
+    float *pbuf = nullptr, *logits_full = nullptr, *gbuf = nullptr;
+    int *vtok = nullptr;                 // verify batch tokens (device)
+    cudaGraphExec_t vexec[ATT_MAX_TOK + 1] = {};   // captured verify steps, by batch size
+    cudaGraph_t vgraph[ATT_MAX_TOK + 1] = {};
+    int veager[ATT_MAX_TOK + 1] = {};
+    unsigned int *att_count = nullptr;   // attention merge tickets [ATT_MAX_TOK][kv heads]
     unsigned int *tp_seq = nullptr;
     TpView tpv = {};
     bool tp_ready = false;
@@ -302,12 +94,12 @@ struct spk_model {
     void *kc = nullptr, *vc = nullptr;
     std::vector<size_t> kv_off;   // per layer element offset into kc / vc
     std::vector<int> kv_slots;
-    int *state = nullptr;         // device: pos, token, argmax, step, local argmax
+    int *state = nullptr;         // device: pos, token, argmax, step, local argmax; [8..16) verify ids, [16..24) local
     DevCtl *ctl = nullptr;        // device: id buffer of spk_model_run
     DevCtl *host_ctl = nullptr;   // pinned staging for it
     unsigned long long *head_partial = nullptr;
     unsigned int *head_counter = nullptr;
-    int *host_io = nullptr;       // pinned: pos, token, argmax
+    int *host_io = nullptr;       // pinned: pos, token, argmax; [8..16) verify tokens, [16..24) verify ids
     cudaStream_t stream = nullptr;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
@@ -344,10 +136,38 @@ int qkv_gate(const spk_model::Layer &L, const float *h, float eps, float *qkv, f
     return vq_call(G, 1, nullptr, h, L.in_norm, eps, gate, 0, s);
 }
 
-template <int HD>
-int attn_launch(const AttnArgs &a, cudaStream_t s) {
-    cudaError_t e = launch_pdl(attn_partial_kernel<HD>, dim3(a.kv_heads, a.nsplit), dim3(ATT_THREADS), 0, s, a);
-    return e == cudaSuccess ? 0 : cuda_fail("attention launch", e);
+
+// The attention arguments of layer li for a batch of ntok tokens starting at the
+// device position (buffers [ntok][...]: qkv, gate, attn).
+AttnArgs attn_args(spk_model *m, int li, int ntok) {
+    const spk_model_config &c = m->cfg;
+    AttnArgs a;
+    memset(&a, 0, sizeof a);
+    const size_t esz = c.kv_f16 ? 2 : 4;
+    a.qkv = m->qkv;
+    a.ldqkv = m->q_dim + 2 * m->kv_dim;
+    a.kc = (uint8_t *)m->kc + m->kv_off[li] * esz;
+    a.vc = (uint8_t *)m->vc + m->kv_off[li] * esz;
+    a.kv_f16 = c.kv_f16;
+    a.slots = m->kv_slots[li];
+    a.full = m->full[li];
+    a.window = c.window;
+    a.freq = a.full ? m->freq_full : m->freq_slide;
+    a.pdim = a.full ? m->pdim_full : m->pdim_slide;
+    a.heads = m->hl;
+    a.kv_heads = m->kvl;
+    a.hd = c.head_dim;
+    a.pos = m->state;
+    a.ntok = ntok;
+    a.nsplit = a.full ? m->nsplit_full : m->nsplit_slide;
+    a.part = m->part;
+    a.count = m->att_count;
+    a.gate = m->gate;
+    a.ldgate = m->hl;
+    a.out = m->attn;
+    a.ldout = m->q_dim;
+    a.err = device_error_ptr();
+    return a;
 }
 
 // Under spk_model_trace's capture: an event after the launch just enqueued.
@@ -368,28 +188,9 @@ int enqueue_step(spk_model *m) {
     for (int li = 0; li < c.layers; li++) {
         const spk_model::Layer &L = m->layers[li];
         if (qkv_gate(L, m->h, c.eps, m->qkv, m->gate, s) || mark(m)) return -1;
-        AttnArgs a;
-        a.qkv = m->qkv;
-        const size_t esz = c.kv_f16 ? 2 : 4;
-        a.kc = (uint8_t *)m->kc + m->kv_off[li] * esz;
-        a.vc = (uint8_t *)m->vc + m->kv_off[li] * esz;
-        a.kv_f16 = c.kv_f16;
-        a.slots = m->kv_slots[li];
-        a.full = m->full[li];
-        a.window = c.window;
-        a.freq = a.full ? m->freq_full : m->freq_slide;
-        a.pdim = a.full ? m->pdim_full : m->pdim_slide;
-        a.heads = m->hl;
-        a.kv_heads = m->kvl;
-        a.hd = c.head_dim;
-        a.pos = pos;
-        a.nsplit = a.full ? m->nsplit_full : m->nsplit_slide;
-        a.part = m->part;
-        if ((c.head_dim == 256 ? attn_launch<256>(a, s) : attn_launch<128>(a, s)) || mark(m)) return -1;
-        cudaError_t ce = launch_pdl(attn_combine_kernel, dim3(m->hl), dim3(128), 0, s, (const float *)m->part, a.nsplit,
-                                    m->hl, m->kvl, c.head_dim, (const float *)m->gate, m->attn);
-        if (ce != cudaSuccess) return cuda_fail("attention combine launch", ce);
-        if (mark(m)) return -1;
+        AttnArgs a = attn_args(m, li, 1);
+        a.store = 1;
+        if (attn_decode(a, s) || mark(m)) return -1;
         if (tp) {
             if (vq_call(L.m[2], 1, nullptr, m->attn, nullptr, 0.f, m->pbuf, 0, s) || mark(m)) return -1;
             if (tp_sum(m->tpv, m->pbuf, m->h, c.hidden, s) || mark(m)) return -1;
@@ -408,11 +209,75 @@ int enqueue_step(spk_model *m) {
     if (q80_head_launch(head_rows, m->vocab_l, c.hidden, m->h, m->final_norm, c.eps, m->logits, tp ? amax_l : amax,
                         m->head_partial, m->head_counter, s) || mark(m))
         return -1;
-    if (tp && (tp_argmax(m->tpv, m->logits, amax_l, m->row0, amax, s) || mark(m))) return -1;
+    if (tp && (tp_argmax(m->tpv, m->logits, m->vocab_l, amax_l, m->row0, amax, 1, s) || mark(m))) return -1;
     cudaError_t e = launch_pdl(advance_kernel, dim3(1), dim3(1), 0, s, pos, token, (const int *)amax,
                                (const DevCtl *)m->ctl, m->state + 3);
     if (e != cudaSuccess) return cuda_fail("decode step launch", e);
     return mark(m);
+}
+
+// ---------------------------------------------------------- verify batch ---
+// y[n] (=|+=) W RMSNorm?(x[n]) for a batch of ntok token rows.
+int vq_batch(const spk_vq_matrix &M, int ntok, const float *x, int ldx, const float *norm_w, float eps, float *y,
+             int ldy, int accumulate, cudaStream_t s) {
+    return spk_verify_gemm(M.stages, M.nstages, M.dim, M.nc, M.rows, M.cols, M.v3, ntok, x, ldx, norm_w, eps, y, ldy,
+                           accumulate, s);
+}
+
+// act[n] = gelu_erf(W_gate xn) * (W_up xn) for the batch: gate into g, then up with the
+// GELU epilogue on the tensor-core kernel; else the SIMT pair token by token.
+int ffn_batch(const spk_model::Layer &L, int ntok, const float *h, int ldh, float eps, float *g, float *act, int ld,
+              cudaStream_t s) {
+    const spk_vq_matrix &Gm = L.m[3], &U = L.m[4];
+    if (Gm.nstages <= 2 && Gm.nstages == U.nstages) {
+        const Layout LG = make_layout(Gm.dim, Gm.nc, Gm.rows, Gm.cols, Gm.v3);
+        const Layout LU = make_layout(U.dim, U.nc, U.rows, U.cols, U.v3);
+        int rc = vq_mma_batch(Gm.stages, Gm.nstages, LG, ntok, h, ldh, L.post_norm, eps, g, ld, 0, 0, nullptr, s);
+        if (rc < 0) return -1;
+        if (rc == 1) {
+            rc = vq_mma_batch(U.stages, U.nstages, LU, ntok, h, ldh, L.post_norm, eps, act, ld, 0, 1, g, s);
+            if (rc != 0) return rc < 0 ? -1 : 0;
+        }
+    }
+    for (int t = 0; t < ntok; t++)
+        if (vq_call(Gm, 2, &U, h + (size_t)t * ldh, L.post_norm, eps, act + (size_t)t * ld, 0, s)) return -1;
+    return 0;
+}
+
+// The verify forward of ntok tokens (device m->vtok) at positions state[0] + t:
+// per-row greedy ids into state[8 + t]. Same math as ntok decode steps: every
+// token's K/V row is stored before any token attends, and each token sees the
+// positions up to its own.
+int enqueue_verify(spk_model *m, int ntok) {
+    const spk_model_config &c = m->cfg;
+    cudaStream_t s = m->stream;
+    const bool tp = m->tp_world > 1;
+    int *vam = m->state + 8, *vam_l = m->state + 16;
+    const int H = c.hidden, ldqkv = m->q_dim + 2 * m->kv_dim;
+    for (int t = 0; t < ntok; t++)
+        if (spk_q80_row(m->embed, c.vocab, H, 0, m->vtok + t, m->h + (size_t)t * H, s)) return -1;
+    for (int li = 0; li < c.layers; li++) {
+        const spk_model::Layer &L = m->layers[li];
+        if (vq_batch(L.m[0], ntok, m->h, H, L.in_norm, c.eps, m->qkv, ldqkv, 0, s) ||
+            vq_batch(L.m[1], ntok, m->h, H, L.in_norm, c.eps, m->gate, m->hl, 0, s))
+            return -1;
+        AttnArgs a = attn_args(m, li, ntok);
+        a.store = 0;
+        if (attn_store_batch(a, s) || attn_decode(a, s)) return -1;
+        if (vq_batch(L.m[2], ntok, m->attn, m->q_dim, nullptr, 0.f, tp ? m->pbuf : m->h, H, tp ? 0 : 1, s)) return -1;
+        if (tp && tp_sum(m->tpv, m->pbuf, m->h, ntok * H, s)) return -1;
+        if (ffn_batch(L, ntok, m->h, H, c.eps, m->gbuf, m->act, m->inter_l, s)) return -1;
+        if (vq_batch(L.m[5], ntok, m->act, m->inter_l, nullptr, 0.f, tp ? m->pbuf : m->h, H, tp ? 0 : 1, s)) return -1;
+        if (tp && tp_sum(m->tpv, m->pbuf, m->h, ntok * H, s)) return -1;
+    }
+    const uint8_t *head_rows = (const uint8_t *)m->embed + (size_t)m->row0 * (H / 32) * 34;
+    for (int t = 0; t < ntok; t++)
+        if (q80_head_launch(head_rows, m->vocab_l, H, m->h + (size_t)t * H, m->final_norm, c.eps,
+                            m->logits + (size_t)t * m->vocab_l, (tp ? vam_l : vam) + t, m->head_partial,
+                            m->head_counter, s))
+            return -1;
+    if (tp && tp_argmax(m->tpv, m->logits, m->vocab_l, vam_l, m->row0, vam, ntok, s)) return -1;
+    return 0;
 }
 
 bool ready(const spk_model *m) {
@@ -450,6 +315,32 @@ int run_step(spk_model *m) {
     return e == cudaSuccess ? 0 : cuda_fail("step graph launch", e);
 }
 
+// One verify batch: eager the first time for a batch size, then from a graph captured
+// for that size.
+int run_verify(spk_model *m, int ntok) {
+    if (!m->veager[ntok]) {
+        m->veager[ntok] = 1;
+        return enqueue_verify(m, ntok);
+    }
+    if (!m->vexec[ntok]) {
+        cudaError_t e = cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal);
+        if (e != cudaSuccess) return cuda_fail("begin verify capture", e);
+        const int rc = enqueue_verify(m, ntok);
+        cudaGraph_t g = nullptr;
+        e = cudaStreamEndCapture(m->stream, &g);
+        if (rc) {
+            if (g) cudaGraphDestroy(g);
+            return -1;
+        }
+        if (e != cudaSuccess) return cuda_fail("end verify capture", e);
+        m->vgraph[ntok] = g;
+        e = cudaGraphInstantiate(&m->vexec[ntok], g, 0);
+        if (e != cudaSuccess) return cuda_fail("instantiate verify graph", e);
+    }
+    cudaError_t e = cudaGraphLaunch(m->vexec[ntok], m->stream);
+    return e == cudaSuccess ? 0 : cuda_fail("verify graph launch", e);
+}
+
 int alloc(void **p, size_t bytes, const char *what) {
     cudaError_t e = cudaMalloc(p, bytes ? bytes : 16);
     if (e != cudaSuccess) return cuda_fail(what, e);
@@ -469,7 +360,7 @@ spk_model *spk_model_create(const spk_model_config *cfg, void *stream) {
     }
     const spk_model_config &c = *cfg;
     if (c.hidden <= 0 || c.layers <= 0 || c.heads <= 0 || c.kv_heads <= 0 || c.heads % c.kv_heads ||
-        c.heads / c.kv_heads > MAX_GROUP || (c.head_dim != 128 && c.head_dim != 256) || c.inter <= 0 ||
+        c.heads / c.kv_heads > ATT_MAX_GROUP || (c.head_dim != 128 && c.head_dim != 256) || c.inter <= 0 ||
         c.vocab <= 0 || c.window <= 0 || c.max_ctx <= 0 || c.hidden % 32 || c.hidden > 65536) {
         set_error("unsupported model geometry (head_dim 128/256, GQA group <= 4, hidden a multiple of 32)");
         return nullptr;
@@ -503,9 +394,10 @@ spk_model *spk_model_create(const spk_model_config *cfg, void *stream) {
     };
     m->pdim_full = pdim(c.rope_partial_full);
     m->pdim_slide = pdim(c.rope_partial_slide);
-    const int per_head = std::min(COMB_MAX_SPLIT, sm_count() / m->kvl > 0 ? sm_count() / m->kvl : 1);
-    m->nsplit_full = std::max(1, std::min(per_head, (c.max_ctx + 15) / 16));
-    m->nsplit_slide = std::max(1, std::min(per_head, (std::min(c.window, c.max_ctx) + 15) / 16));
+    // about 128 positions per split, at most one CTA per SM per KV head
+    const int per_head = std::min(ATT_MAX_SPLIT, sm_count() / m->kvl > 0 ? sm_count() / m->kvl : 1);
+    m->nsplit_full = std::max(1, std::min(per_head, (c.max_ctx + 127) / 128));
+    m->nsplit_slide = std::max(1, std::min(per_head, (std::min(c.window, c.max_ctx) + 127) / 128));
     size_t kv_elems = 0;
     for (int li = 0; li < c.layers; li++) {
         // Sliding layers keep their whole history too (not a window-sized ring), as
@@ -519,33 +411,38 @@ spk_model *spk_model_create(const spk_model_config *cfg, void *stream) {
     }
     const size_t esz = c.kv_f16 ? 2 : 4;
     const int nsplit = std::max(m->nsplit_full, m->nsplit_slide);
-    bool ok = !alloc((void **)&m->h, c.hidden * 4, "alloc h") && !alloc((void **)&m->qkv, (m->q_dim + 2 * m->kv_dim) * 4, "alloc qkv") &&
-              !alloc((void **)&m->gate, m->hl * 4, "alloc gate") && !alloc((void **)&m->attn, m->q_dim * 4, "alloc attn") &&
-              !alloc((void **)&m->act, (size_t)m->inter_l * 4, "alloc act") &&
-              !alloc((void **)&m->part, (size_t)m->kvl * nsplit * m->G * (c.head_dim + 2) * 4, "alloc attention partials") &&
+    // activations hold up to ATT_MAX_TOK rows (a verify batch); the decode step uses row 0
+    const size_t R = ATT_MAX_TOK;
+    bool ok = !alloc((void **)&m->h, R * c.hidden * 4, "alloc h") &&
+              !alloc((void **)&m->qkv, R * (m->q_dim + 2 * m->kv_dim) * 4, "alloc qkv") &&
+              !alloc((void **)&m->gate, R * m->hl * 4, "alloc gate") && !alloc((void **)&m->attn, R * m->q_dim * 4, "alloc attn") &&
+              !alloc((void **)&m->act, R * m->inter_l * 4, "alloc act") && !alloc((void **)&m->gbuf, R * m->inter_l * 4, "alloc g") &&
+              !alloc((void **)&m->vtok, R * sizeof(int), "alloc verify tokens") &&
+              !alloc((void **)&m->part, (size_t)ATT_MAX_TOK * m->kvl * nsplit * m->G * (c.head_dim + 4) * 4, "alloc attention partials") &&
+              !alloc((void **)&m->att_count, (size_t)ATT_MAX_TOK * m->kvl * sizeof(unsigned int), "alloc attention tickets") &&
               !alloc((void **)&m->freq_full, c.head_dim * 4, "alloc rope") && !alloc((void **)&m->freq_slide, c.head_dim * 4, "alloc rope") &&
               !alloc(&m->kc, kv_elems * esz, "alloc K cache") && !alloc(&m->vc, kv_elems * esz, "alloc V cache") &&
-              !alloc((void **)&m->state, 8 * sizeof(int), "alloc state") &&
+              !alloc((void **)&m->state, 32 * sizeof(int), "alloc state") &&
               !alloc((void **)&m->ctl, sizeof(DevCtl), "alloc control") &&
               !alloc((void **)&m->head_partial, 1024 * sizeof(unsigned long long), "alloc head partials") &&
               !alloc((void **)&m->head_counter, sizeof(unsigned int), "alloc head counter");
     if (ok && t == 1) {
-        ok = !alloc((void **)&m->logits, (size_t)c.vocab * 4, "alloc logits");
+        ok = !alloc((void **)&m->logits, R * c.vocab * 4, "alloc logits");
     } else if (ok) {
         // one mailbox holds the exchange rows, the flags and this rank's logits shard
         // (peers read the shard when a host forward asks for the whole vocabulary)
-        const size_t mb = tp_mailbox_bytes(t, c.hidden, &m->mail_flags_off, &m->mail_stride);
+        const size_t mb = tp_mailbox_bytes(t, (int)R * c.hidden, &m->mail_flags_off, &m->mail_stride);
         m->mail_logits_off = (mb + 255) / 256 * 256;
-        const size_t total = m->mail_logits_off + (size_t)m->vocab_l * 4;
+        const size_t total = m->mail_logits_off + R * m->vocab_l * 4;
         ok = !alloc(&m->mailbox, total, "alloc tensor-parallel mailbox") &&
-             cudaMemset(m->mailbox, 0, total) == cudaSuccess && !alloc((void **)&m->pbuf, c.hidden * 4, "alloc partial") &&
-             !alloc((void **)&m->logits_full, (size_t)c.vocab * 4, "alloc gathered logits") &&
+             cudaMemset(m->mailbox, 0, total) == cudaSuccess && !alloc((void **)&m->pbuf, R * c.hidden * 4, "alloc partial") &&
+             !alloc((void **)&m->logits_full, R * c.vocab * 4, "alloc gathered logits") &&
              !alloc((void **)&m->tp_seq, sizeof(unsigned int), "alloc exchange counter") &&
              cudaMemset(m->tp_seq, 0, sizeof(unsigned int)) == cudaSuccess;
         if (ok) m->logits = (float *)((uint8_t *)m->mailbox + m->mail_logits_off);
         else set_error("tensor-parallel allocation failed");
     }
-    if (ok && (cudaMallocHost((void **)&m->host_io, 4 * sizeof(int)) != cudaSuccess ||
+    if (ok && (cudaMallocHost((void **)&m->host_io, 32 * sizeof(int)) != cudaSuccess ||
                cudaMallocHost((void **)&m->host_ctl, sizeof(DevCtl)) != cudaSuccess))
         ok = !set_error("pinned staging allocation failed");
     if (ok) {
@@ -556,8 +453,9 @@ spk_model *spk_model_create(const spk_model_config *cfg, void *stream) {
         ok = cudaMemcpy(m->freq_full, ff.data(), c.head_dim * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
              cudaMemcpy(m->freq_slide, fs.data(), c.head_dim * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
              cudaMemset(m->kc, 0, kv_elems * esz) == cudaSuccess && cudaMemset(m->vc, 0, kv_elems * esz) == cudaSuccess &&
-             cudaMemset(m->state, 0, 8 * sizeof(int)) == cudaSuccess && cudaMemset(m->ctl, 0, sizeof(DevCtl)) == cudaSuccess &&
-             cudaMemset(m->head_counter, 0, sizeof(unsigned int)) == cudaSuccess;
+             cudaMemset(m->state, 0, 32 * sizeof(int)) == cudaSuccess && cudaMemset(m->ctl, 0, sizeof(DevCtl)) == cudaSuccess &&
+             cudaMemset(m->head_counter, 0, sizeof(unsigned int)) == cudaSuccess &&
+             cudaMemset(m->att_count, 0, (size_t)ATT_MAX_TOK * m->kvl * sizeof(unsigned int)) == cudaSuccess;
         if (!ok) set_error("model initialisation copies failed");
     }
     if (!ok) {
@@ -574,11 +472,15 @@ void spk_model_destroy(spk_model *m) {
     if (m->texec) cudaGraphExecDestroy(m->texec);
     if (m->tgraph) cudaGraphDestroy(m->tgraph);
     for (cudaEvent_t e : m->tev) cudaEventDestroy(e);
+    for (int k = 0; k <= ATT_MAX_TOK; k++) {
+        if (m->vexec[k]) cudaGraphExecDestroy(m->vexec[k]);
+        if (m->vgraph[k]) cudaGraphDestroy(m->vgraph[k]);
+    }
     for (int r = 0; r < TP_MAX; r++)
         if (m->peer_open[r]) cudaIpcCloseMemHandle(m->peer_open[r]);
     void *ps[] = {m->h, m->qkv, m->gate, m->attn, m->act, m->tp_world > 1 ? nullptr : m->logits, m->part,
                   m->freq_full, m->freq_slide, m->kc, m->vc, m->state, m->ctl, m->head_partial, m->head_counter,
-                  m->mailbox, m->pbuf, m->logits_full, m->tp_seq};
+                  m->mailbox, m->pbuf, m->logits_full, m->tp_seq, m->att_count, m->gbuf, m->vtok};
     for (void *p : ps)
         if (p) cudaFree(p);
     if (m->host_io) cudaFreeHost(m->host_io);
@@ -664,6 +566,46 @@ int spk_model_forward(spk_model *m, int token, int pos, float *logits_host, int 
     return 0;
 }
 
+/* The speculative verify (vq-model-gpu.cu:947-969 verify_logits, spec.rs:197-205):
+ * tokens[0..ntok) at positions pos..pos+ntok-1 in one batched forward; next_host[t]
+ * receives the greedy id after tokens[t] (Model::argmax of that row), logits_host
+ * (optional) the [ntok][vocab] logits. Afterwards len = pos + ntok; the caller keeps
+ * the accepted prefix with spk_model_rollback, as spec.rs:241 does. Synchronizes. */
+int spk_model_verify(spk_model *m, const int *tokens, int ntok, int pos, int *next_host, float *logits_host) {
+    if (!m) return set_error("model is null");
+    if (!ready(m)) return set_error("model weights are not all set");
+    if (!tokens || ntok < 1 || ntok > ATT_MAX_TOK) return set_error("verify takes 1..%d tokens, not %d", ATT_MAX_TOK, ntok);
+    for (int t = 0; t < ntok; t++)
+        if (tokens[t] < 0 || tokens[t] >= m->cfg.vocab) return set_error("token %d is outside the vocabulary", tokens[t]);
+    if (pos < 0 || pos + ntok > m->cfg.max_ctx) return set_error("positions %d..%d exceed the %d-token cache", pos, pos + ntok - 1, m->cfg.max_ctx);
+    if (pos > m->len) return set_error("position %d skips cached positions (%d cached)", pos, m->len);
+    m->host_io[0] = pos;
+    for (int t = 0; t < ntok; t++) m->host_io[8 + t] = tokens[t];
+    cudaError_t e = cudaMemcpyAsync(m->state, m->host_io, sizeof(int), cudaMemcpyHostToDevice, m->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(m->vtok, m->host_io + 8, ntok * sizeof(int), cudaMemcpyHostToDevice, m->stream);
+    if (e != cudaSuccess) return cuda_fail("verify upload", e);
+    if (run_verify(m, ntok)) return -1;
+    e = cudaMemcpyAsync(m->host_io + 16, m->state + 8, ntok * sizeof(int), cudaMemcpyDeviceToHost, m->stream);
+    const float *full = m->logits;
+    if (e == cudaSuccess && logits_host && m->tp_world > 1) {
+        for (int t = 0; t < ntok && e == cudaSuccess; t++)
+            for (int r = 0; r < m->tp_world && e == cudaSuccess; r++)
+                e = cudaMemcpyAsync(m->logits_full + (size_t)t * m->cfg.vocab + (size_t)r * m->vocab_l,
+                                    m->peer_logits[r] + (size_t)t * m->vocab_l, (size_t)m->vocab_l * 4,
+                                    cudaMemcpyDefault, m->stream);
+        full = m->logits_full;
+    }
+    if (e == cudaSuccess && logits_host)
+        e = cudaMemcpyAsync(logits_host, full, (size_t)ntok * m->cfg.vocab * 4, cudaMemcpyDeviceToHost, m->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+    if (e != cudaSuccess) return cuda_fail("verify", e);
+    if (check_device_error("verify")) return -1;
+    if (next_host)
+        for (int t = 0; t < ntok; t++) next_host[t] = m->host_io[16 + t];
+    m->len = pos + ntok;
+    return 0;
+}
+
 /* Device-resident greedy decoding: set (pos, token) and the device id buffer
  * that spk_model_run fills, one id per step. */
 int spk_model_begin(spk_model *m, int token, int pos, int *ids_dev, int ids_cap) {
@@ -715,7 +657,7 @@ int spk_model_advance_len(spk_model *m, int n) {
 
 /* One decode step from the device state (as spk_model_run does) with the device time
  * of every launch: us[i] = microseconds of launch i in enqueue order (embedding row;
- * per layer QKV+g_proj, attention, combine, out_proj, [tp_sum], gate+up, down,
+ * per layer QKV+g_proj, attention, out_proj, [tp_sum], gate+up, down,
  * [tp_sum]; head; [tp_argmax]; advance). Returns the number of launches, or -1.
  * Needs one step run before (it reuses the kernels' one-time set-up); with
  * tensor parallelism every rank traces the same step. */
@@ -724,7 +666,7 @@ int spk_model_trace(spk_model *m, float *us, int cap) {
     if (!ready(m)) return set_error("model weights are not all set");
     if (!m->eager_steps) return set_error("trace needs one step run first");
     const int tp = m->tp_world > 1 ? 1 : 0;
-    const int n = 1 + 1 + m->cfg.layers * (6 + 2 * tp) + 1 + tp + 1;   // marks, the first one before any launch
+    const int n = 1 + 1 + m->cfg.layers * (5 + 2 * tp) + 1 + tp + 1;   // marks, the first one before any launch
     if (!us || cap < n - 1) return set_error("trace needs room for %d launches", n - 1);
     if (!m->texec) {
         for (int i = 0; i < n; i++) {

@@ -101,8 +101,8 @@ __device__ __forceinline__ unsigned long long argmax_key(float x, int idx) {
     return ((unsigned long long)k << 32) | (unsigned long long)(0xFFFFFFFFu - (unsigned int)idx);
 }
 
-__global__ void tp_argmax_kernel(const TpView v, const float *__restrict__ logits, const int *__restrict__ amax_local,
-                                 int row0, int *__restrict__ amax) {
+__global__ void tp_argmax_kernel(const TpView v, const float *__restrict__ logits, int ldl,
+                                 const int *__restrict__ amax_local, int row0, int *__restrict__ amax, int ntok) {
     __shared__ unsigned int s_seq;
     pdl_trigger();
     pdl_wait();
@@ -111,23 +111,26 @@ __global__ void tp_argmax_kernel(const TpView v, const float *__restrict__ logit
     const unsigned int seq = s_seq;
     const int slot = (int)(seq & 1u);
     const size_t row = ((size_t)slot * v.world + v.rank) * v.stride;
-    if (threadIdx.x == 0) {
-        const int li = *amax_local;
-        const unsigned long long key = argmax_key(logits[li], row0 + li);
-        for (int q = 0; q < v.world; q++) *reinterpret_cast<unsigned long long *>(v.mail[q] + row) = key;
+    const int t = threadIdx.x;   // token row t of the batch
+    if (t < ntok) {
+        const int li = amax_local[t];
+        const unsigned long long key = argmax_key(logits[(size_t)t * ldl + li], row0 + li);
+        for (int q = 0; q < v.world; q++) reinterpret_cast<unsigned long long *>(v.mail[q] + row)[t] = key;
     }
     publish(v, slot, seq);
     wait_all(v, slot, seq);
-    if (threadIdx.x == 0) {
+    if (t < ntok) {
         const float *mine = v.mail[v.rank] + (size_t)slot * v.world * v.stride;
         unsigned long long best = 0ull;
         for (int r = 0; r < v.world; r++) {
-            const unsigned long long k = __ldcg(reinterpret_cast<const unsigned long long *>(mine + (size_t)r * v.stride));
+            const unsigned long long k =
+                __ldcg(reinterpret_cast<const unsigned long long *>(mine + (size_t)r * v.stride) + t);
             best = k > best ? k : best;
         }
-        *amax = (int)(0xFFFFFFFFu - (unsigned int)(best & 0xFFFFFFFFull));
-        *v.seq = seq;
+        amax[t] = (int)(0xFFFFFFFFu - (unsigned int)(best & 0xFFFFFFFFull));
     }
+    __syncthreads();
+    if (t == 0) *v.seq = seq;
 }
 
 }  // namespace
@@ -147,8 +150,10 @@ int tp_sum(const TpView &v, const float *part, float *h, int n, cudaStream_t s) 
     return e == cudaSuccess ? 0 : cuda_fail("tp_sum launch", e);
 }
 
-int tp_argmax(const TpView &v, const float *logits, const int *amax_local, int row0, int *amax, cudaStream_t s) {
-    cudaError_t e = launch_pdl(tp_argmax_kernel, dim3(1), dim3(32), 0, s, v, logits, amax_local, row0, amax);
+int tp_argmax(const TpView &v, const float *logits, int ldl, const int *amax_local, int row0, int *amax, int ntok,
+              cudaStream_t s) {
+    if (ntok < 1 || ntok > 32 || 2 * ntok > v.stride) return set_error("tp_argmax: %d rows", ntok);
+    cudaError_t e = launch_pdl(tp_argmax_kernel, dim3(1), dim3(32), 0, s, v, logits, ldl, amax_local, row0, amax, ntok);
     return e == cudaSuccess ? 0 : cuda_fail("tp_argmax launch", e);
 }
 

@@ -36,9 +36,11 @@ size_t tp_mailbox_bytes(int world, int n, size_t *flags_off, int *stride);
 // h[i] += sum over ranks r (in rank order) of part_r[i], i < n (n a multiple of 4).
 int tp_sum(const TpView &v, const float *part, float *h, int n, cudaStream_t s);
 
-// Global greedy id over vocabulary shards: rank r holds rows [row0_r, row0_r + n_r)
-// with logits[] and its local first-max index *amax_local; *amax receives the
-// first index of the global maximum (NaN never wins, -0 equals +0).
-int tp_argmax(const TpView &v, const float *logits, const int *amax_local, int row0, int *amax, cudaStream_t s);
+// Global greedy ids over vocabulary shards, for ntok token rows: rank r holds
+// vocabulary rows [row0_r, row0_r + n_r), token t's logits at logits[t*ldl ..] and
+// its local first-max index amax_local[t]; amax[t] receives the first index of the
+// global maximum (NaN never wins, -0 equals +0).
+int tp_argmax(const TpView &v, const float *logits, int ldl, const int *amax_local, int row0, int *amax, int ntok,
+              cudaStream_t s);
 
 }  // namespace spk

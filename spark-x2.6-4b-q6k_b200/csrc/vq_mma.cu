@@ -1,12 +1,13 @@
-// vq_mma.cu — the tensor-core VQ decode-GEMV (see vq_mma.cuh for the fragment map).
+// vq_mma.cu — the batched (M <= 8) VQ decode-GEMM of the speculative verify
+// (see vq_mma.cuh for the fragment map).
 //
-// Persistent CTA per SM, 32 warps, over a contiguous row range. Row tiles of
-// TRR (16 or 8) rows of every stage's index stream arrive by TMA bulk copy into
-// a ring of shared-memory slots (mbarrier full/empty pairs). Every warp owns a
-// fixed K range of 4S groups of each row (so its B fragments — x as f16 hi/lo —
-// are computed once and stay in registers) and, per tile, runs S mma steps per
-// stage over the tile's 16 rows. Warp partials are summed in a fixed order, so
-// results are deterministic.
+// Persistent CTA per SM, 32 warps, over a contiguous row range. Tiles of 16 rows
+// of every stage's index stream arrive by TMA bulk copy into a ring of shared-
+// memory slots (mbarrier full/empty pairs); the stages' codebooks sit in shared
+// memory. A row's K range is cut into `passes` passes of 32 warps x 4 threads x
+// S groups; per pass every thread builds its B fragments (its token column of X,
+// RMSNorm folded in, split hi/lo) from L2-resident X, then runs S MMA steps per
+// stage. Warp partials are summed in a fixed order, so results are deterministic.
 #include "common.cuh"
 #include "spk.h"
 #include "stream.cuh"
@@ -18,6 +19,8 @@ namespace {
 
 constexpr int MW = 32;           // warps per CTA
 constexpr int MTHREADS = MW * 32;
+constexpr int MAXT = 8;          // tokens per batch (the 8 columns of B)
+constexpr int TRR = 16;          // rows per tile (the 16 rows of A)
 
 struct MmaArgs {
     const uint8_t *st[2];
@@ -25,26 +28,14 @@ struct MmaArgs {
     const float *x, *norm_w, *aux;
     float eps;
     float *y;
+    int ldx, ldy, ntok;
     int accumulate, mode;   // mode 0: y = (acc ? y : 0) + W x;  mode 1: y = gelu_erf(aux) * (W x)
-    int trr, nbuf;
+    int nbuf, passes;
     uint32_t main_slot, plane_slot, slot_bytes;
     int *err;
 };
 
 __device__ __forceinline__ float h2f_u16(uint16_t h) { return __half2float(__ushort_as_half(h)); }
-
-__device__ float rms_inv_block(const float *x, int n, float eps, double *red) {
-    double s = 0.0;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) s += (double)x[i] * (double)x[i];
-    s = warp_sum_d(s);
-    const int w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
-    if ((threadIdx.x & 31) == 0) red[w] = s;
-    __syncthreads();
-    double t = 0.0;
-    for (int k = 0; k < nw; k++) t += red[k];
-    __syncthreads();
-    return (float)(1.0 / sqrt(t / (double)n + (double)eps));
-}
 
 __device__ __forceinline__ void mma_issue(const MmaArgs &a, int nq, uint8_t *slot, uint64_t *bar, int r0, int nr) {
     const Layout &L = a.L;
@@ -65,23 +56,60 @@ __device__ __forceinline__ void mma_issue(const MmaArgs &a, int nq, uint8_t *slo
     bulk_issue(bl, bar);
 }
 
-template <int NSTG, int S, int EXT>
+// This thread's B fragments for one pass: column n = g of B is token n (TWO) or,
+// packed, token g (hi) for g < 4 and token g - 4 (lo) for g >= 4.
+template <int S, int TWO>
+__device__ __forceinline__ void load_b(const MmaArgs &a, const float *inv, int g, int cg0, uint32_t (&b0)[S],
+                                       uint32_t (&b1)[S], uint32_t (&l0)[S], uint32_t (&l1)[S]) {
+    const int tok = TWO ? g : (g & 3);
+    const bool lo_col = !TWO && g >= 4;
+    const bool live = tok < a.ntok;
+#pragma unroll
+    for (int s = 0; s < S; s++) {
+        b0[s] = b1[s] = l0[s] = l1[s] = 0u;
+        if (!live) continue;
+        const int c = cg0 + s;
+        float4 v = *reinterpret_cast<const float4 *>(a.x + (size_t)tok * a.ldx + 4 * c);
+        if (a.norm_w) {
+            const float4 w = *reinterpret_cast<const float4 *>(a.norm_w + 4 * c);
+            const float iv = inv[tok];
+            v.x = __fmul_rn(__fmul_rn(v.x, iv), w.x);
+            v.y = __fmul_rn(__fmul_rn(v.y, iv), w.y);
+            v.z = __fmul_rn(__fmul_rn(v.z, iv), w.z);
+            v.w = __fmul_rn(__fmul_rn(v.w, iv), w.w);
+        }
+        uint2 hi, lo;
+        split_f16x4(v, hi, lo);
+        if (TWO) {
+            b0[s] = hi.x;
+            b1[s] = hi.y;
+            l0[s] = lo.x;
+            l1[s] = lo.y;
+        } else {
+            b0[s] = lo_col ? lo.x : hi.x;
+            b1[s] = lo_col ? lo.y : hi.y;
+        }
+    }
+}
+
+template <int NSTG, int S, int EXT, int TWO>
 __global__ void __launch_bounds__(MTHREADS, 1) vq_mma_kernel(const MmaArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
     const Layout &L = a.L;
-    const int nc = L.nc, TRR = a.trr, NB = a.nbuf;
+    const int nc = L.nc, NB = a.nbuf;
     uint8_t *cbb = smem;
     uint8_t *ring = smem + (((size_t)NSTG * nc * 8 + 15) & ~(size_t)15);
     uint64_t *full = reinterpret_cast<uint64_t *>(ring + (size_t)NB * a.slot_bytes);
     uint64_t *empty = full + NB;
-    float *part = reinterpret_cast<float *>(empty + NB);   // [2][NSTG][MW][16]
-    double *red = reinterpret_cast<double *>(part + 2 * NSTG * MW * 16);
+    float *part = reinterpret_cast<float *>(empty + NB);   // [NSTG][MW][16][8]
+    float *inv = part + NSTG * MW * 16 * 8;                // [MAXT]
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
     const int G = gridDim.x;
     const int rb = (int)(((long long)blockIdx.x * L.rows) / G), re = (int)(((long long)(blockIdx.x + 1) * L.rows) / G);
     const int ntile = (re - rb + TRR - 1) / TRR;
 
+    pdl_trigger();
     if (tid == 0) {
         for (int b = 0; b < NB; b++) {
             mbar_init(&full[b], 1);
@@ -100,113 +128,117 @@ __global__ void __launch_bounds__(MTHREADS, 1) vq_mma_kernel(const MmaArgs a) {
         uint2 *dst = reinterpret_cast<uint2 *>(cbb + (size_t)q * nc * 8);
         for (int v = tid; v < nc; v += MTHREADS) dst[v] = __ldg(src + v);
     }
-    float inv = 1.0f;
-    if (a.norm_w) inv = rms_inv_block(a.x, L.cols, a.eps, red);
-    // B fragments: this warp's K range is groups [warp*4S, (warp+1)*4S); thread t
-    // walks [warp*4S + t*S, +S). Column g=0 holds x_hi, g=1 x_lo, others zero.
-    const int c0 = warp * 4 * S + t * S;
-    uint32_t bx[S], by[S];
-#pragma unroll
-    for (int s = 0; s < S; s++) {
-        bx[s] = 0u;
-        by[s] = 0u;
-        if (g < 2) {
-            const int c = c0 + s;
-            float4 v = *reinterpret_cast<const float4 *>(a.x + 4 * c);
-            if (a.norm_w) {
-                const float4 w = *reinterpret_cast<const float4 *>(a.norm_w + 4 * c);
-                v.x = __fmul_rn(__fmul_rn(v.x, inv), w.x);
-                v.y = __fmul_rn(__fmul_rn(v.y, inv), w.y);
-                v.z = __fmul_rn(__fmul_rn(v.z, inv), w.z);
-                v.w = __fmul_rn(__fmul_rn(v.w, inv), w.w);
-            }
-            uint2 hi, lo;
-            split_f16x4(v, hi, lo);
-            bx[s] = g == 0 ? hi.x : lo.x;
-            by[s] = g == 0 ? hi.y : lo.y;
+    pdl_wait();   // weights above; X, Y and AUX come from the preceding kernels
+    // per-token RMSNorm scale (f64 sum of squares, model.rs:236-245): warp n does token n
+    if (warp < MAXT) {
+        float iv = 1.0f;
+        if (a.norm_w && warp < a.ntok) {
+            const float *xr = a.x + (size_t)warp * a.ldx;
+            double sq = 0.0;
+            for (int i = lane; i < L.cols; i += 32) sq += (double)xr[i] * (double)xr[i];
+            sq = warp_sum_d(sq);
+            iv = (float)(1.0 / sqrt(sq / (double)L.cols + (double)a.eps));
         }
+        if (lane == 0) inv[warp] = iv;
     }
     __syncthreads();
-    const uint32_t bit0 = 12u * (uint32_t)c0, pbit0 = (uint32_t)c0;
+
+    const int per_pass = MW * 4 * S;   // groups per pass
+    uint32_t b0[S], b1[S], l0[S], l1[S];
+    if (a.passes == 1) load_b<S, TWO>(a, inv, g, warp * 4 * S + t * S, b0, b1, l0, l1);
 
     for (int k = 0; k < ntile; k++) {
         const int slot = k % NB;
+        // A wait that runs out records the error and skips the work it guarded; no
+        // thread leaves the loop, so the CTA barriers below are always complete.
         if (tid == 0 && k + NB - 1 < ntile) {
             const int kn = k + NB - 1, r0n = rb + kn * TRR, sn = kn % NB;
-            if (kn >= NB && !mbar_wait(&empty[sn], (uint32_t)(((kn / NB) - 1) & 1), a.err)) return;
-            mma_issue(a, NSTG, ring + (size_t)sn * a.slot_bytes, &full[sn], r0n, min(TRR, re - r0n));
+            if (kn < NB || mbar_wait(&empty[sn], (uint32_t)(((kn / NB) - 1) & 1), a.err))
+                mma_issue(a, NSTG, ring + (size_t)sn * a.slot_bytes, &full[sn], r0n, min(TRR, re - r0n));
         }
         const int r0 = rb + k * TRR, nr = min(TRR, re - r0);
-        if (!mbar_wait(&full[slot], (uint32_t)((k / NB) & 1), a.err)) return;
+        const bool have = mbar_wait(&full[slot], (uint32_t)((k / NB) & 1), a.err);
         const uint8_t *sb = ring + (size_t)slot * a.slot_bytes;
-        const bool v0 = g < nr, v1 = g + 8 < nr;
+        const bool v0 = have && g < nr, v1 = have && g + 8 < nr;
         float d[NSTG][4];
 #pragma unroll
-        for (int q = 0; q < NSTG; q++) {
-            d[q][0] = d[q][1] = d[q][2] = d[q][3] = 0.f;
-            const uintptr_t A = (uintptr_t)(a.st[q] + L.stream_off + (size_t)r0 * L.mrow);
-            const uint8_t *rowA = sb + q * a.main_slot + (A & 15) + (size_t)g * L.mrow;
-            const uint8_t *rowB = rowA + (size_t)8 * L.mrow;
-            Run<S> ra, rbn;
-            ra.load(rowA, bit0, v0);
-            rbn.load(rowB, bit0, v1);
-            uint32_t pa = 0, pb = 0;
-            if (EXT) {
-                const uintptr_t P = (uintptr_t)(a.st[q] + L.stream_off + (size_t)L.rows * L.mrow + (size_t)r0 * L.prow);
-                const uint8_t *plA = sb + NSTG * a.main_slot + q * a.plane_slot + (P & 15) + (size_t)g * L.prow;
-                const uint32_t *ppA = reinterpret_cast<const uint32_t *>(plA) + (pbit0 >> 5);
-                const uint32_t *ppB = reinterpret_cast<const uint32_t *>(plA + (size_t)8 * L.prow) + (pbit0 >> 5);
-                if (v0) pa = __funnelshift_r(ppA[0], ppA[1], pbit0 & 31u);
-                if (v1) pb = __funnelshift_r(ppB[0], ppB[1], pbit0 & 31u);
-            }
-            const uint8_t *cq = cbb + (size_t)q * nc * 8;
+        for (int q = 0; q < NSTG; q++) d[q][0] = d[q][1] = d[q][2] = d[q][3] = 0.f;
+        for (int p = 0; p < a.passes; p++) {
+            const int cg0 = p * per_pass + warp * 4 * S + t * S;   // this thread's first group
+            if (a.passes > 1) load_b<S, TWO>(a, inv, g, cg0, b0, b1, l0, l1);
+            const uint32_t bit0 = 12u * (uint32_t)cg0, pbit0 = (uint32_t)cg0;
 #pragma unroll
-            for (int s = 0; s < S; s++) {
-                uint32_t oa = ra.off(s), ob = rbn.off(s);
+            for (int q = 0; q < NSTG; q++) {
+                const uintptr_t A = (uintptr_t)(a.st[q] + L.stream_off + (size_t)r0 * L.mrow);
+                const uint8_t *rowA = sb + q * a.main_slot + (A & 15) + (size_t)g * L.mrow;
+                const uint8_t *rowB = rowA + (size_t)8 * L.mrow;
+                Run<S> ra, rbn;
+                ra.load(rowA, bit0, v0);
+                rbn.load(rowB, bit0, v1);
+                uint32_t pa = 0, pb = 0;
                 if (EXT) {
-                    oa |= ((pa >> s) & 1u) << 15;
-                    ob |= ((pb >> s) & 1u) << 15;
+                    const uintptr_t P =
+                        (uintptr_t)(a.st[q] + L.stream_off + (size_t)L.rows * L.mrow + (size_t)r0 * L.prow);
+                    const uint8_t *plA = sb + NSTG * a.main_slot + q * a.plane_slot + (P & 15) + (size_t)g * L.prow;
+                    const uint32_t *ppA = reinterpret_cast<const uint32_t *>(plA) + (pbit0 >> 5);
+                    const uint32_t *ppB = reinterpret_cast<const uint32_t *>(plA + (size_t)8 * L.prow) + (pbit0 >> 5);
+                    if (v0) pa = __funnelshift_r(ppA[0], ppA[1], pbit0 & 31u);
+                    if (v1) pb = __funnelshift_r(ppB[0], ppB[1], pbit0 & 31u);
                 }
-                uint2 ca = make_uint2(0u, 0u), cbw = make_uint2(0u, 0u);
-                if (v0) ca = *reinterpret_cast<const uint2 *>(cq + oa);
-                if (v1) cbw = *reinterpret_cast<const uint2 *>(cq + ob);
-                mma_16816(d[q], ca.x, cbw.x, ca.y, cbw.y, bx[s], by[s]);
+                const uint8_t *cq = cbb + (size_t)q * nc * 8;
+#pragma unroll
+                for (int s = 0; s < S; s++) {
+                    uint32_t oa = ra.off(s), ob = rbn.off(s);
+                    if (EXT) {
+                        oa |= ((pa >> s) & 1u) << 15;
+                        ob |= ((pb >> s) & 1u) << 15;
+                    }
+                    uint2 ca = make_uint2(0u, 0u), cbw = make_uint2(0u, 0u);
+                    if (v0) ca = *reinterpret_cast<const uint2 *>(cq + oa);
+                    if (v1) cbw = *reinterpret_cast<const uint2 *>(cq + ob);
+                    mma_16816(d[q], ca.x, cbw.x, ca.y, cbw.y, b0[s], b1[s]);
+                    if (TWO) mma_16816(d[q], ca.x, cbw.x, ca.y, cbw.y, l0[s], l1[s]);
+                }
             }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
-        float *pt = part + (size_t)(k & 1) * NSTG * MW * 16;
-        if (t == 0) {
 #pragma unroll
-            for (int q = 0; q < NSTG; q++) {
-                pt[(q * MW + warp) * 16 + g] = d[q][0] + d[q][1];
-                pt[(q * MW + warp) * 16 + g + 8] = d[q][2] + d[q][3];
-            }
+        for (int q = 0; q < NSTG; q++) {
+            float *pw = part + ((size_t)q * MW + warp) * 16 * 8;
+            pw[g * 8 + 2 * t] = d[q][0];
+            pw[g * 8 + 2 * t + 1] = d[q][1];
+            pw[(g + 8) * 8 + 2 * t] = d[q][2];
+            pw[(g + 8) * 8 + 2 * t + 1] = d[q][3];
         }
         __syncthreads();
-        if (tid < nr) {
-            const int r = r0 + tid;
-            float o = (a.mode == 0 && a.accumulate) ? a.y[r] : 0.0f;
+        for (int idx = tid; idx < nr * a.ntok; idx += MTHREADS) {
+            const int rl = idx / a.ntok, n = idx - rl * a.ntok, r = r0 + rl;
+            float o = (a.mode == 0 && a.accumulate) ? a.y[(size_t)n * a.ldy + r] : 0.0f;
 #pragma unroll
             for (int q = 0; q < NSTG; q++) {
                 float v = 0.f;
-                for (int w = 0; w < MW; w++) v += pt[(q * MW + w) * 16 + tid];
+                for (int w = 0; w < MW; w++) {
+                    const float *pw = part + ((size_t)q * MW + w) * 16 * 8 + rl * 8;
+                    v += TWO ? pw[n] : (pw[n] + pw[n + 4]);
+                }
                 const float gq = h2f_u16(*reinterpret_cast<const uint16_t *>(a.st[q] + L.gain_off + 2 * (size_t)r));
                 o = __fadd_rn(o, __fmul_rn(v, gq));
             }
             if (a.mode == 1) {
-                const float gv = a.aux[r];
+                const float gv = a.aux[(size_t)n * a.ldy + r];
                 const double e = erf((double)gv * 0.70710678118654752440);
                 o = __fmul_rn(__fmul_rn(__fmul_rn(0.5f, gv), __fadd_rn(1.0f, (float)e)), o);
             }
-            a.y[r] = o;
+            a.y[(size_t)n * a.ldy + r] = o;
         }
+        __syncthreads();   // the partials are reused by the next tile
     }
 }
 
-template <int NSTG, int S, int EXT>
+template <int NSTG, int S, int EXT, int TWO>
 int mma_launch_t(const MmaArgs &A, size_t smem, cudaStream_t s) {
-    auto k = vq_mma_kernel<NSTG, S, EXT>;
+    auto k = vq_mma_kernel<NSTG, S, EXT, TWO>;
     static size_t opted[64];
     int dev = 0;
     cudaGetDevice(&dev);
@@ -215,16 +247,20 @@ int mma_launch_t(const MmaArgs &A, size_t smem, cudaStream_t s) {
         if (e != cudaSuccess) return cuda_fail("vq mma kernel shared-memory opt-in", e);
         opted[dev & 63] = smem;
     }
-    const int ntr = (A.L.rows + A.trr - 1) / A.trr;
+    const int ntr = (A.L.rows + TRR - 1) / TRR;
     const int grid = ntr < sm_count() ? ntr : sm_count();
-    k<<<grid, MTHREADS, smem, s>>>(A);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(k, dim3(grid), dim3(MTHREADS), smem, s, A);
     return e == cudaSuccess ? 0 : cuda_fail("vq mma kernel launch", e);
+}
+
+template <int NSTG, int S, int EXT>
+int mma_launch_w(const MmaArgs &A, size_t smem, cudaStream_t s) {
+    return A.ntok > 4 ? mma_launch_t<NSTG, S, EXT, 1>(A, smem, s) : mma_launch_t<NSTG, S, EXT, 0>(A, smem, s);
 }
 
 template <int NSTG, int S>
 int mma_launch_e(const MmaArgs &A, size_t smem, cudaStream_t s) {
-    return A.L.prow ? mma_launch_t<NSTG, S, 1>(A, smem, s) : mma_launch_t<NSTG, S, 0>(A, smem, s);
+    return A.L.prow ? mma_launch_w<NSTG, S, 1>(A, smem, s) : mma_launch_w<NSTG, S, 0>(A, smem, s);
 }
 
 template <int NSTG>
@@ -241,50 +277,89 @@ int mma_launch_s(int S, const MmaArgs &A, size_t smem, cudaStream_t s) {
 
 }  // namespace
 
-// The tensor-core path for a single matrix of 1-2 stages (dim 4, 12/13-bit DQV3,
-// whole 128-index lane runs): 1 = launched, 0 = geometry not taken (the caller
-// uses another kernel), -1 = error. mode 1 computes gelu_erf(aux) * (W x).
-int vq_mma_gemv(const void *const *stages, int nstg, const Layout &L, const float *x, const float *norm_w, float eps,
-                float *y, int accumulate, int mode, const float *aux, cudaStream_t s) {
+int vq_mma_batch(const void *const *stages, int nstg, const Layout &L, int ntok, const float *x, int ldx,
+                 const float *norm_w, float eps, float *y, int ldy, int accumulate, int mode, const float *aux,
+                 cudaStream_t s) {
+    if (ntok < 1 || ntok > MAXT) return 0;
     if (L.dim != 4 || !L.v3 || L.nbit < 12 || nstg < 1 || nstg > 2) return 0;
     if (L.nidx_row % (4 * MW) || L.mrow % 4 || L.stream_off % 4 || (L.prow && L.prow % 4)) return 0;
-    const int S = (int)(L.nidx_row / (4 * MW));
-    // S 10 and 20 would hold 20-40 B-fragment registers per lane and spill at 64 registers
-    if (!(S == 1 || S == 2 || S == 4 || S == 5 || S == 8)) return 0;
+    // S groups per thread per pass: the largest of 8, 5, 4, 2, 1 that divides the row
+    const int per = (int)(L.nidx_row / (4 * MW));
+    int S = 0;
+    for (int c : {8, 5, 4, 2, 1})
+        if (per % c == 0) {
+            S = c;
+            break;
+        }
     for (int q = 0; q < nstg; q++)
         if (((uintptr_t)stages[q] & 7) != 0) return 0;
-    if (((uintptr_t)x & 15) || (norm_w && ((uintptr_t)norm_w & 15))) return 0;
+    if (((uintptr_t)x & 15) || (ldx & 3) || (norm_w && ((uintptr_t)norm_w & 15))) return 0;
     const size_t cb = (((size_t)nstg * L.nc * 8 + 15) & ~(size_t)15);
-    const size_t fixed = cb + (size_t)2 * nstg * MW * 16 * 4 + 32 * 8;
-    for (int trr = 16; trr >= 8; trr /= 2) {
-        const uint32_t main_slot = (uint32_t)(((size_t)trr * L.mrow + 32 + 15) & ~(size_t)15);
-        const uint32_t plane_slot = L.prow ? (uint32_t)(((size_t)trr * L.prow + 32 + 15) & ~(size_t)15) : 0u;
-        const uint32_t slot = nstg * (main_slot + plane_slot);
-        for (int nb = 4; nb >= 2; nb--) {
-            const size_t smem = fixed + (size_t)nb * slot + 2 * (size_t)nb * 8;
-            if (smem > smem_optin_max()) continue;
-            MmaArgs A;
-            memset(&A, 0, sizeof A);
-            for (int q = 0; q < nstg; q++) A.st[q] = (const uint8_t *)stages[q];
-            A.L = L;
-            A.x = x;
-            A.norm_w = norm_w;
-            A.aux = aux;
-            A.eps = eps;
-            A.y = y;
-            A.accumulate = accumulate;
-            A.mode = mode;
-            A.trr = trr;
-            A.nbuf = nb;
-            A.main_slot = main_slot;
-            A.plane_slot = plane_slot;
-            A.slot_bytes = slot;
-            A.err = device_error_ptr();
-            const int rc = nstg == 1 ? mma_launch_s<1>(S, A, smem, s) : mma_launch_s<2>(S, A, smem, s);
-            return rc ? -1 : 1;
-        }
+    const size_t fixed = cb + (size_t)nstg * MW * 16 * 8 * 4 + MAXT * 4;
+    const uint32_t main_slot = (uint32_t)(((size_t)TRR * L.mrow + 32 + 15) & ~(size_t)15);
+    const uint32_t plane_slot = L.prow ? (uint32_t)(((size_t)TRR * L.prow + 32 + 15) & ~(size_t)15) : 0u;
+    const uint32_t slot = nstg * (main_slot + plane_slot);
+    for (int nb = 3; nb >= 2; nb--) {
+        const size_t smem = ((fixed + 15) & ~(size_t)15) + (size_t)nb * slot + 2 * (size_t)nb * 8;
+        if (smem > smem_optin_max()) continue;
+        MmaArgs A;
+        memset(&A, 0, sizeof A);
+        for (int q = 0; q < nstg; q++) A.st[q] = (const uint8_t *)stages[q];
+        A.L = L;
+        A.x = x;
+        A.norm_w = norm_w;
+        A.aux = aux;
+        A.eps = eps;
+        A.y = y;
+        A.ldx = ldx;
+        A.ldy = ldy;
+        A.ntok = ntok;
+        A.accumulate = accumulate;
+        A.mode = mode;
+        A.nbuf = nb;
+        A.passes = per / S;
+        A.main_slot = main_slot;
+        A.plane_slot = plane_slot;
+        A.slot_bytes = slot;
+        A.err = device_error_ptr();
+        const int rc = nstg == 1 ? mma_launch_s<1>(S, A, smem, s) : mma_launch_s<2>(S, A, smem, s);
+        return rc ? -1 : 1;
     }
     return 0;
 }
 
 }  // namespace spk
+
+using namespace spk;
+
+extern "C" {
+
+/* The verify-batch GEMM (replaces the reference's tiled prefill GEMM for a draft
+ * block, gemm_tiled_kernel decode-gpu.cu:359-501, at M = 1 + 7): for every token n
+ * of ntok <= 8, y[n*ldy + r] = (accumulate ? y : 0) + (W RMSNorm?(x[n*ldx ..]))[r]
+ * with W the sum of the stages. Geometries the tensor-core kernel does not take
+ * run token by token on the GEMV path. */
+int spk_verify_gemm(const void *const *stages, int nstages, int dim, int nc, int rows, int cols, int v3, int ntok,
+                    const float *x, int ldx, const float *norm_w, float eps, float *y, int ldy, int accumulate,
+                    void *stream) {
+    if (!stages || nstages < 1 || nstages > 4) return set_error("verify gemm needs 1..4 stages");
+    if (ntok < 1 || ntok > 8) return set_error("verify gemm takes 1..8 tokens, not %d", ntok);
+    if (!x || !y || ldx < cols || ldy < rows) return set_error("verify gemm: bad activation buffers");
+    if (v3 && !v3_width_ok(nc)) return set_error("DQV3 carries 13 index bits, nc %d is too wide", nc);
+    if (rows <= 0 || cols <= 0 || dim <= 0 || cols % dim) return set_error("verify gemm: bad geometry");
+    for (int q = 0; q < nstages; q++)
+        if (!stages[q]) return set_error("stage %d payload pointer is null", q);
+    const Layout L = make_layout(dim, nc, rows, cols, v3);
+    cudaStream_t s = (cudaStream_t)stream;
+    if (nstages <= 2) {
+        const int rc = vq_mma_batch(stages, nstages, L, ntok, x, ldx, norm_w, eps, y, ldy, accumulate, 0, nullptr, s);
+        if (rc != 0) return rc < 0 ? -1 : 0;
+    }
+    for (int n = 0; n < ntok; n++)
+        if (spk_vq_gemv(stages, nstages, 1, dim, nc, rows, cols, v3, x + (size_t)n * ldx, norm_w, eps,
+                        y + (size_t)n * ldy, accumulate, stream))
+            return -1;
+    return 0;
+}
+
+}  // extern "C"

@@ -1,24 +1,24 @@
-// vq_mma.cuh — VQ decode-GEMV with the tensor cores as the dot-product engine.
+// vq_mma.cuh — VQ decode-GEMM for a small token batch (the speculative verify,
+// M = 1 + 7 tokens) with the tensor cores as the contraction engine.
 //
-// y[r] = sum_s gain_s[r] * sum_i cb_s[idx_s(r,i)] . x[4i..4i+3]   (dim 4, 12-bit DQV3)
+// Y[n][r] = sum_s gain_s[r] * sum_i cb_s[idx_s(r,i)] . X[n][4i..4i+3]   (dim 4, 12/13-bit DQV3)
 //
-// Why tensor cores at batch 1: the cost of this GEMV on B200 is the random
-// 8-byte codebook gather from shared memory and the f16->f32 conversions and
-// FMAs around it. A warp-level mma.sync m16n8k16 (f16 x f16 -> f32) takes the
-// gathered code words as its A fragment straight from registers: no
-// conversion, no FMA, ~4 instructions per looked-up code word instead of ~11,
-// and no activations held in registers across the main loop.
+// The weights' cost is the random 8-byte code-word gather from shared memory;
+// with M tokens every gathered code word feeds M dot products, which SIMT lanes
+// cannot hold activations for (4F values x M tokens per lane), so the gathered
+// words go straight from registers into mma.sync m16n8k16 (f16 x f16 -> f32) as
+// the A fragment, and the tokens are the 8 columns of B.
 //
 // Fragment mapping (PTX ISA, mma.m16n8k16 .row.col f16): thread (g = lane/4,
 // t = lane%4) holds A rows g and g+8 at k-slots {2t, 2t+1, 2t+8, 2t+9}. K is
 // permuted so that those four k-slots are the four dims of ONE code word, of
 // group c_t: A regs {0, 2} = code word of row g (halves .x, .y), regs {1, 3} =
-// code word of row g+8. B (16x8) column n of thread (g, t) holds the same four
-// k-slots of group c_t: column 0 = x rounded to f16 (hi), column 1 = the f16
-// rounding of the remainder x - hi (lo), columns 2..7 zero. Products of f16
-// values are exact in f32, so D[.,0] + D[.,1] = sum cw . (hi + lo) carries x to
-// ~22 bits. Thread t walks a contiguous run of S groups, so its 12-bit fields
-// sit at compile-time bit offsets after one funnel-shift alignment.
+// code word of row g+8. B column n of thread (g, t) holds the same four k-slots
+// of group c_t for column n = g. X is carried to ~22 bits as an f16 pair
+// hi = rn(x), lo = rn(x - hi); products of f16 values are exact in f32:
+//   M <= 4: one MMA, columns 0..3 = tokens' hi, 4..7 = tokens' lo (Y = D[n] + D[n+4]);
+//   M 5..8: two MMAs into one accumulator, B_hi then B_lo (Y = D[n]).
+// D (16x8 f32) of thread (g, t) is rows g, g+8 x columns 2t, 2t+1.
 #pragma once
 #include "common.cuh"
 
@@ -33,7 +33,7 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// x as an exact-ish f16 pair: hi = rn(x), lo = rn(x - hi).
+// x as an f16 pair: hi = rn(x), lo = rn(x - hi).
 __device__ __forceinline__ void split_f16x4(float4 v, uint2 &hi, uint2 &lo) {
     const __half h0 = __float2half_rn(v.x), h1 = __float2half_rn(v.y), h2 = __float2half_rn(v.z),
                  h3 = __float2half_rn(v.w);
@@ -60,7 +60,6 @@ struct Run {
         for (int j = 0; j < NW; j++) w[j] = valid ? wp[j] : 0u;
 #pragma unroll
         for (int j = 0; j < NU; j++) u[j] = __funnelshift_r(w[j], j + 1 < NW ? w[j + 1] : 0u, sh);
-        (void)valid;
     }
     // byte offset (index * 8) of field s
     __device__ __forceinline__ uint32_t off(int s) const {
@@ -73,5 +72,13 @@ struct Run {
         return (v & 0xFFFu) << 3;
     }
 };
+
+// The batched GEMM (vq_mma.cu): 1 launched, 0 geometry not taken, -1 error.
+//   mode 0: Y[n][r] = (accumulate ? Y[n][r] : 0) + (W RMSNorm?(X[n]))[r]
+//   mode 1: Y[n][r] = gelu_erf(AUX[n][r]) * (W RMSNorm?(X[n]))[r]
+// X rows have stride ldx floats, Y / AUX rows stride ldy.
+int vq_mma_batch(const void *const *stages, int nstg, const Layout &L, int ntok, const float *x, int ldx,
+                 const float *norm_w, float eps, float *y, int ldy, int accumulate, int mode, const float *aux,
+                 cudaStream_t s);
 
 }  // namespace spk

@@ -61,6 +61,7 @@ _PROTOS = {
     "spk_q6k_dequant": ([_vp, C.c_size_t, _vp, _vp], _i),
     "spk_q80_dequant": ([_vp, C.c_size_t, _vp, _vp], _i),
     "spk_q80_row": ([_vp, _i, _i, _i, _vp, _vp, _vp], _i),
+    "spk_verify_gemm": ([_vp, _i, _i, _i, _i, _i, _i, _i, _vp, _i, _vp, _f, _vp, _i, _i, _vp], _i),
     "spk_model_create": ([_vp, _vp], _vp),
     "spk_model_destroy": ([_vp], None),
     "spk_model_set_layer": ([_vp, _i] + [_vp] * 8, _i),
@@ -73,6 +74,7 @@ _PROTOS = {
     "spk_model_reset": ([_vp], _i),
     "spk_model_len": ([_vp], _i),
     "spk_model_advance_len": ([_vp, _i], _i),
+    "spk_model_verify": ([_vp, _vp, _i, _i, _vp, _vp], _i),
     "spk_model_trace": ([_vp, _vp, _i], _i),
     "spk_model_tp_handle": ([_vp, _vp, _i], _i),
     "spk_model_tp_attach": ([_vp, _vp, _i, _i], _i),

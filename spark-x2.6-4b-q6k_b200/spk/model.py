@@ -249,11 +249,33 @@ class DeviceModel:
         arr = (C.c_void_p * len(mailboxes))(*[m or None for m in mailboxes])
         check(lib().spk_model_tp_attach_ptrs(self.h, arr, len(mailboxes), wait_ms), "tp_attach_ptrs")
 
+    def verify(self, tokens, pos: int, want_logits: bool = False):
+        """Speculative verify (spec.rs:197-205): tokens (anchor + proposals, <= 8) at positions
+        pos.. in one batched forward. Returns (greedy ids after each token, logits [n][vocab]
+        or None); afterwards len = pos + len(tokens)."""
+        n = len(tokens)
+        tk = (C.c_int * n)(*[int(t) for t in tokens])
+        nxt = (C.c_int * n)()
+        lg = np.empty((n, self.cfg.vocab), np.float32) if want_logits else None
+        check(lib().spk_model_verify(self.h, tk, n, pos, nxt, lg.ctypes.data_as(C.c_void_p) if lg is not None else None),
+              f"verify({n} tokens at {pos})")
+        return list(nxt), lg
+
+    def spec_round(self, anchor: int, proposals, pos0: int):
+        """One verify round of spec.rs:177-245: returns (accepted proposals k, the target's
+        token after them, the ids) and leaves the cache at pos0 + k + 1 positions."""
+        tgt, _ = self.verify([anchor] + list(proposals), pos0)
+        k = 0
+        while k < len(proposals) and tgt[k] == proposals[k]:
+            k += 1
+        self.rollback(pos0 + k + 1)
+        return k, tgt[k], tgt
+
     def trace(self) -> list:
         """One decode step (as run() does) with every launch's device time: [(name, us), ...]
         in enqueue order (spk_model_trace). All tensor-parallel ranks trace together."""
         tp = self.tp[1] > 1
-        layer = ["qkv_g", "attention", "combine", "out"] + (["tp_sum"] if tp else []) + ["gate_up", "down"] + \
+        layer = ["qkv_g", "attention", "out"] + (["tp_sum"] if tp else []) + ["gate_up", "down"] + \
                 (["tp_sum"] if tp else [])
         names = ["embed"] + layer * self.cfg.layers + ["head"] + (["tp_argmax"] if tp else []) + ["advance"]
         buf = (C.c_float * len(names))()

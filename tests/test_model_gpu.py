@@ -109,7 +109,7 @@ def test_trace_step_times_every_launch(small, cuda):
     a.stream.synchronize()
     assert ids.item() == want[2]
     names = [n for n, _ in tr]
-    assert len(tr) == 1 + 6 * cfg.layers + 2 and names[0] == "embed" and names[-2:] == ["head", "advance"]
+    assert len(tr) == 1 + 5 * cfg.layers + 2 and names[0] == "embed" and names[-2:] == ["head", "advance"]
     assert all(us > 0 for _, us in tr)
     a.close()
 

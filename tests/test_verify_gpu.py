@@ -1,0 +1,135 @@
+"""The speculative verify on the GPU: the M <= 8 batched VQ GEMM against the oracle,
+and the verify forward against M sequential decode steps (spec.rs:197-249)."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import oracle
+from spk import formats as F
+from spk.model import DeviceModel, small_config, synth_weights
+
+pytestmark = pytest.mark.gpu
+GEMM_TOL = 1e-5     # f16 hi/lo activations carry ~22 bits; north-star tolerance is 1e-3
+LOGIT_TOL = 1e-4
+EPS_MARGIN = 1e-3
+
+
+def rel(a, b):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def rms(x, w, eps=1e-6):
+    x = x.astype(np.float64)
+    return (x / np.sqrt(np.mean(x * x) + eps) * w).astype(np.float32)
+
+
+# rows, cols, nc, stages: tensor-core geometries (one pass, K passes, 13-bit plane) and fallbacks
+GEMMS = [(1002, 2560, 4096, 2), (300, 4096, 4096, 2), (256, 10240, 4096, 2), (96, 1024, 8192, 2),
+         (16, 2560, 4096, 1), (200, 1000, 4096, 2), (64, 512, 4096, 3)]
+
+
+@pytest.mark.parametrize("geom", GEMMS)
+@pytest.mark.parametrize("ntok", [1, 3, 4, 5, 8])
+def test_verify_gemm_matches_oracle(cuda, geom, ntok):
+    import torch
+
+    import spk
+
+    rows, cols, nc, stages = geom
+    buf = F.random_rvq(rows, cols, 4, nc, stages, seed=rows + ntok)
+    c = F.parse_container(buf)
+    W = oracle.decode(buf).reshape(rows, cols)
+    rng = np.random.default_rng(ntok)
+    X = rng.normal(0, 1, (ntok, cols)).astype(np.float32)
+    nw = (1 + 0.1 * rng.normal(0, 1, cols)).astype(np.float32)
+    keep = [spk.dev_bytes(buf[c.stage_offset(s):c.stage_offset(s) + c.stage_bytes], cuda) for s in range(stages)]
+    st = (C.c_void_p * stages)(*[t.data_ptr() for t in keep])
+    x = torch.from_numpy(X).to(cuda)
+    w = torch.from_numpy(nw).to(cuda)
+    L = spk.lib()
+    for norm in (False, True):
+        Y0 = rng.normal(0, 1, (ntok, rows)).astype(np.float32)
+        y = torch.from_numpy(Y0).to(cuda)
+        torch.cuda.synchronize()
+        spk.check(L.spk_verify_gemm(st, stages, 4, nc, rows, cols, 1, ntok, x.data_ptr(), cols,
+                                    w.data_ptr() if norm else None, 1e-6, y.data_ptr(), rows, 1, None))
+        torch.cuda.synchronize()
+        got = y.cpu().numpy()
+        for n in range(ntok):
+            xin = rms(X[n], nw) if norm else X[n]
+            want = Y0[n] + W.astype(np.float64) @ xin.astype(np.float64)
+            assert rel(got[n], want) < GEMM_TOL, (geom, ntok, norm, n, rel(got[n], want))
+
+
+def test_verify_gemm_rejects_bad_arguments(cuda):
+    import spk
+
+    L = spk.lib()
+    st = (C.c_void_p * 2)(None, None)
+    assert L.spk_verify_gemm(st, 2, 4, 4096, 64, 512, 1, 9, None, 512, None, 0.0, None, 64, 0, None) == -1
+    assert b"tokens" in L.spk_last_error()
+    assert L.spk_verify_gemm(st, 2, 4, 4096, 64, 512, 1, 2, None, 512, None, 0.0, None, 64, 0, None) == -1
+
+
+@pytest.fixture(scope="module")
+def small(cuda):
+    cfg = small_config()
+    return cfg, synth_weights(cfg, seed=3, exact_q80=True)
+
+
+def test_verify_matches_sequential_steps(small):
+    """Verify of 1+7 tokens == 8 decode steps: logits per row, greedy ids, and the cache it
+    leaves (a rollback to the accepted prefix, then decode continues as sequentially)."""
+    cfg, W = small
+    prompt = [5, 17, 301, 42, 4000, 7]
+    seq = DeviceModel(cfg, W, max_ctx=64)
+    ids, logits, tok = [], [], prompt[0]
+    for pos in range(len(prompt) + 10):
+        nxt, lg = seq.forward(tok, pos)
+        ids.append(nxt)
+        logits.append(lg)
+        tok = prompt[pos + 1] if pos + 1 < len(prompt) else nxt
+    seq.close()
+    p0 = len(prompt) - 1
+    block = [prompt[-1]] + ids[p0:p0 + 7]   # anchor + 7 proposals: the target's own continuation
+    dev = DeviceModel(cfg, W, max_ctx=64)
+    for pos in range(p0):
+        dev.forward(prompt[pos], pos, want_logits=False)
+    for rnd in range(2):   # eager, then from the captured verify graph
+        tgt, lg = dev.verify(block, p0, want_logits=True)
+        for t in range(8):
+            assert rel(lg[t], logits[p0 + t]) < LOGIT_TOL, (rnd, t)
+            if tgt[t] != ids[p0 + t]:
+                s = np.sort(logits[p0 + t])[-2:]
+                assert s[1] - s[0] < EPS_MARGIN
+        assert dev.len == p0 + 8
+        dev.rollback(p0)
+    # a wrong proposal at index 3: k = 3 accepted, the target's token after them, cache at p0 + 4
+    bad = list(block[1:])
+    bad[3] = (bad[3] + 1) % cfg.vocab
+    k, nxt, tgt = dev.spec_round(block[0], bad, p0)
+    assert k == 3 and nxt == tgt[3] and dev.len == p0 + 4
+    # decoding resumes from the accepted prefix exactly as the sequential run
+    for pos in range(p0 + 4, p0 + 8):
+        feed = nxt if pos == p0 + 4 else nid
+        nid, lg = dev.forward(feed, pos)
+        assert rel(lg, logits[pos]) < LOGIT_TOL, pos
+    dev.close()
+
+
+def test_verify_rejects_bad_inputs(small):
+    import spk
+
+    cfg, W = small
+    dev = DeviceModel(cfg, W, max_ctx=16)
+    with pytest.raises(spk.SpkError):
+        dev.verify([1] * 9, 0)
+    with pytest.raises(spk.SpkError):
+        dev.verify([cfg.vocab], 0)
+    with pytest.raises(spk.SpkError):
+        dev.verify([1, 2], 3)   # skips cached positions
+    with pytest.raises(spk.SpkError):
+        dev.verify([1] * 8, 12)  # past the cache
+    dev.close()
