@@ -143,6 +143,36 @@ int spk_verify_gemm(const void *const *stages, int nstages, int dim, int nc, int
                     const float *x, int ldx, const float *norm_w, float eps, float *y, int ldy, int accumulate,
                     void *stream);
 
+/* ------------------------------------------------------- GQA attention ---
+ * Decode attention over a KV cache (model.rs:508-557; the reference's attn_kernel,
+ * vq-model-gpu.cu:408-461), for one token or a batch of up to 8 consecutive tokens.
+ * Per token t (position *pos_dev + t): rope q and k (NeoX on the first pdim dims,
+ * freq[pdim/2] = 1/theta^(2i/pdim)), and — when store is 1 (ntok 1) — write k, v into
+ * the cache at slot pos % slots; with store 0 the rows must already be there (see
+ * spk_attn_store). Then out[t][h] = sigmoid(gate[t][h]) * softmax(q_h K^T / sqrt(hd)) V
+ * over positions [0, pos] (full) or [pos+1-window, pos] (sliding), GQA group
+ * heads/kv_heads <= 4. The workspace (spk_attn_workspace_bytes, zeroed once before
+ * first use) holds the split partials and merge tickets; it is left zeroed after each
+ * call. */
+typedef struct {
+    const float *qkv;           /* [ntok][ldqkv]: q (heads*hd) | k (kv_heads*hd) | v */
+    int ldqkv;
+    void *k_cache, *v_cache;    /* [kv_heads][slots][hd], f32 or f16 */
+    int kv_f16, slots, full, window;
+    const float *freq;          /* device [pdim/2] */
+    int pdim, heads, kv_heads, head_dim;
+    const int *pos_dev;         /* device int: position of token 0 */
+    int ntok, store, nsplit;    /* nsplit 1..256 sequence splits per KV head */
+    const float *gate;          /* [ntok][ldgate] pre-sigmoid */
+    int ldgate;
+    float *out;                 /* [ntok][ldout] */
+    int ldout;
+    void *workspace;
+} spk_attn_args;
+size_t spk_attn_workspace_bytes(int ntok, int heads, int kv_heads, int head_dim, int nsplit);
+int spk_attn_decode(const spk_attn_args *a, void *stream);
+int spk_attn_store(const spk_attn_args *a, void *stream);
+
 /* --------------------------------------------------- decode step (model) ---
  * The model-level ABI the Rust host side (tools/vq-runtime/src/model.rs Model)
  * needs: forward(token, pos) -> logits / next id, rollback, reset. Weights are

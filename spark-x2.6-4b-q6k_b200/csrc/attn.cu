@@ -11,13 +11,13 @@
 // fixed order and applies the per-head sigmoid gate (model.rs:538-550). The
 // ticket is reset by that CTA, so a captured graph replays without a memset.
 #include "attn.cuh"
+#include "spk.h"
 
 namespace spk {
 namespace {
 
 constexpr int ATT_THREADS = 256;
 constexpr int ATT_WARPS = ATT_THREADS / 32;
-constexpr int ATT_U = 4;   // positions per warp per iteration
 
 // NeoX rotate-half on the first pdim elements of x (shared memory), model.rs:431-439:
 //   x[i] = a cos - b sin ; x[i+half] = b cos + a sin, each product rounded.
@@ -67,7 +67,9 @@ __device__ __forceinline__ void load_row(const void *base, size_t off, float (&r
     }
 }
 
-template <int HD, int F16>
+// ATT_U: positions per warp per iteration (4 for long splits, 2 for short ones so
+// that all 8 warps have a position).
+template <int HD, int F16, int ATT_U>
 __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnArgs a) {
     constexpr int DPL = HD / 32;   // dims per lane
     constexpr int MG = ATT_MAX_GROUP;
@@ -312,15 +314,26 @@ int attn_decode(const AttnArgs &a, cudaStream_t s) {
         return set_error("attention: %d splits x %d tokens out of range", a.nsplit, a.ntok);
     if (a.store && a.ntok != 1) return set_error("attention: in-kernel K/V store takes one token");
     const dim3 grid(a.kv_heads, a.nsplit, a.ntok);
+    // the longest split this layer can see: the cache span over the splits
+    const int span = a.full ? a.slots : (a.window < a.slots ? a.window : a.slots);
+    const bool longs = (span + a.nsplit - 1) / a.nsplit >= 64;
     cudaError_t e;
-    if (a.hd == 256)
-        e = a.kv_f16 ? launch_pdl(attn_kernel<256, 1>, grid, dim3(ATT_THREADS), 0, s, a)
-                     : launch_pdl(attn_kernel<256, 0>, grid, dim3(ATT_THREADS), 0, s, a);
-    else if (a.hd == 128)
-        e = a.kv_f16 ? launch_pdl(attn_kernel<128, 1>, grid, dim3(ATT_THREADS), 0, s, a)
-                     : launch_pdl(attn_kernel<128, 0>, grid, dim3(ATT_THREADS), 0, s, a);
-    else
-        return set_error("attention: head_dim %d (128 or 256)", a.hd);
+    if (a.hd != 256 && a.hd != 128) return set_error("attention: head_dim %d (128 or 256)", a.hd);
+    if (a.hd == 256) {
+        if (a.kv_f16)
+            e = longs ? launch_pdl(attn_kernel<256, 1, 4>, grid, dim3(ATT_THREADS), 0, s, a)
+                      : launch_pdl(attn_kernel<256, 1, 2>, grid, dim3(ATT_THREADS), 0, s, a);
+        else
+            e = longs ? launch_pdl(attn_kernel<256, 0, 4>, grid, dim3(ATT_THREADS), 0, s, a)
+                      : launch_pdl(attn_kernel<256, 0, 2>, grid, dim3(ATT_THREADS), 0, s, a);
+    } else {
+        if (a.kv_f16)
+            e = longs ? launch_pdl(attn_kernel<128, 1, 4>, grid, dim3(ATT_THREADS), 0, s, a)
+                      : launch_pdl(attn_kernel<128, 1, 2>, grid, dim3(ATT_THREADS), 0, s, a);
+        else
+            e = longs ? launch_pdl(attn_kernel<128, 0, 4>, grid, dim3(ATT_THREADS), 0, s, a)
+                      : launch_pdl(attn_kernel<128, 0, 2>, grid, dim3(ATT_THREADS), 0, s, a);
+    }
     return e == cudaSuccess ? 0 : cuda_fail("attention launch", e);
 }
 
@@ -332,3 +345,68 @@ int attn_store_batch(const AttnArgs &a, cudaStream_t s) {
 }
 
 }  // namespace spk
+
+using namespace spk;
+
+namespace {
+bool to_args(const spk_attn_args *u, AttnArgs *a) {
+    if (!u || !u->qkv || !u->k_cache || !u->v_cache || !u->freq || !u->pos_dev || !u->gate || !u->out || !u->workspace) {
+        set_error("attention: a buffer is missing");
+        return false;
+    }
+    if (u->kv_heads <= 0 || u->heads <= 0 || u->slots <= 0 || u->window <= 0 || u->pdim < 2 || u->pdim > u->head_dim) {
+        set_error("attention: bad geometry");
+        return false;
+    }
+    memset(a, 0, sizeof *a);
+    a->qkv = u->qkv;
+    a->ldqkv = u->ldqkv;
+    a->kc = u->k_cache;
+    a->vc = u->v_cache;
+    a->kv_f16 = u->kv_f16;
+    a->slots = u->slots;
+    a->full = u->full;
+    a->window = u->window;
+    a->freq = u->freq;
+    a->pdim = u->pdim;
+    a->heads = u->heads;
+    a->kv_heads = u->kv_heads;
+    a->hd = u->head_dim;
+    a->pos = u->pos_dev;
+    a->ntok = u->ntok;
+    a->store = u->store;
+    a->nsplit = u->nsplit;
+    a->gate = u->gate;
+    a->ldgate = u->ldgate;
+    a->out = u->out;
+    a->ldout = u->ldout;
+    a->count = reinterpret_cast<unsigned int *>(u->workspace);
+    a->part = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(u->workspace) + 256 * sizeof(unsigned int));
+    a->err = device_error_ptr();
+    return true;
+}
+}  // namespace
+
+extern "C" {
+
+size_t spk_attn_workspace_bytes(int ntok, int heads, int kv_heads, int head_dim, int nsplit) {
+    if (ntok < 1 || kv_heads < 1 || heads < kv_heads || nsplit < 1) return 0;
+    return 256 * sizeof(unsigned int) +
+           (size_t)ntok * kv_heads * nsplit * (heads / kv_heads) * (head_dim + 4) * sizeof(float);
+}
+
+int spk_attn_decode(const spk_attn_args *u, void *stream) {
+    AttnArgs a;
+    if (!to_args(u, &a)) return -1;
+    if ((size_t)a.ntok * a.kv_heads > 256) return set_error("attention: %d token x KV-head tickets exceed 256", a.ntok * a.kv_heads);
+    return attn_decode(a, (cudaStream_t)stream);
+}
+
+int spk_attn_store(const spk_attn_args *u, void *stream) {
+    AttnArgs a;
+    if (!to_args(u, &a)) return -1;
+    if (a.ntok < 1 || a.ntok > ATT_MAX_TOK) return set_error("attention store: %d tokens", a.ntok);
+    return attn_store_batch(a, (cudaStream_t)stream);
+}
+
+}  // extern "C"

@@ -394,10 +394,11 @@ spk_model *spk_model_create(const spk_model_config *cfg, void *stream) {
     };
     m->pdim_full = pdim(c.rope_partial_full);
     m->pdim_slide = pdim(c.rope_partial_slide);
-    // about 128 positions per split, at most one CTA per SM per KV head
+    // as many splits as SMs per KV head (the attention is latency-bound: every CTA's
+    // row loads in flight at once), with at least 16 positions per split
     const int per_head = std::min(ATT_MAX_SPLIT, sm_count() / m->kvl > 0 ? sm_count() / m->kvl : 1);
-    m->nsplit_full = std::max(1, std::min(per_head, (c.max_ctx + 127) / 128));
-    m->nsplit_slide = std::max(1, std::min(per_head, (std::min(c.window, c.max_ctx) + 127) / 128));
+    m->nsplit_full = std::max(1, std::min(per_head, (c.max_ctx + 15) / 16));
+    m->nsplit_slide = std::max(1, std::min(per_head, (std::min(c.window, c.max_ctx) + 15) / 16));
     size_t kv_elems = 0;
     for (int li = 0; li < c.layers; li++) {
         // Sliding layers keep their whole history too (not a window-sized ring), as

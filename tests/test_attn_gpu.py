@@ -1,0 +1,111 @@
+"""spk_attn_decode / spk_attn_store (GQA decode attention, model.rs:508-557) against a
+float64 numpy restatement: one token with the in-kernel K/V store, and verify batches."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-5
+
+
+class AttnArgs(C.Structure):
+    _fields_ = [("qkv", C.c_void_p), ("ldqkv", C.c_int), ("k_cache", C.c_void_p), ("v_cache", C.c_void_p),
+                ("kv_f16", C.c_int), ("slots", C.c_int), ("full", C.c_int), ("window", C.c_int),
+                ("freq", C.c_void_p), ("pdim", C.c_int), ("heads", C.c_int), ("kv_heads", C.c_int),
+                ("head_dim", C.c_int), ("pos_dev", C.c_void_p), ("ntok", C.c_int), ("store", C.c_int),
+                ("nsplit", C.c_int), ("gate", C.c_void_p), ("ldgate", C.c_int), ("out", C.c_void_p),
+                ("ldout", C.c_int), ("workspace", C.c_void_p)]
+
+
+def rope(x, pos, freq, pdim):
+    half = pdim // 2
+    ang = np.float32(pos) * freq[:half].astype(np.float32)
+    c, s = np.cos(ang.astype(np.float64)), np.sin(ang.astype(np.float64))
+    a, b = x[..., :half].copy(), x[..., half:pdim].copy()
+    x[..., :half], x[..., half:pdim] = a * c - b * s, b * c + a * s
+    return x
+
+
+def reference(qkv, K, V, own, pos0, ntok, heads, kvh, hd, full, window, freq, pdim, gate):
+    """K/V [kvh][slots][hd] holding the batch rows as the cache stores them (roped K);
+    own[t] = token t's unrounded (k, v), which the kernel uses for its own position."""
+    G = heads // kvh
+    out = np.zeros((ntok, heads * hd))
+    for t in range(ntok):
+        pos = pos0 + t
+        start = 0 if full else max(0, pos + 1 - window)
+        q = rope(qkv[t, :heads * hd].reshape(heads, hd).astype(np.float64), pos, freq, pdim)
+        Kt, Vt = K.copy(), V.copy()
+        Kt[:, pos], Vt[:, pos] = own[t]
+        for h in range(heads):
+            k = Kt[h // G, start:pos + 1]
+            v = Vt[h // G, start:pos + 1]
+            sc = k @ q[h] / np.sqrt(hd)
+            p = np.exp(sc - sc.max())
+            out[t, h * hd:(h + 1) * hd] = (p / p.sum()) @ v / (1 + np.exp(-gate[t, h]))
+    return out
+
+
+@pytest.mark.parametrize("hd,heads,kvh", [(256, 16, 4), (128, 4, 1)])
+@pytest.mark.parametrize("full", [1, 0])
+@pytest.mark.parametrize("ntok,f16", [(1, 0), (1, 1), (8, 0), (5, 1)])
+def test_attention_matches_reference(cuda, hd, heads, kvh, full, ntok, f16):
+    import torch
+
+    import spk
+
+    L = spk.lib()
+    rng = np.random.default_rng(hd + 7 * ntok + full)
+    slots, window, pos0, nsplit = 640, 64, 300, 37
+    pdim = hd // 4 if full else hd
+    freq = np.zeros(hd, np.float32)
+    theta = 5e6 if full else 1e4
+    freq[:pdim // 2] = (1.0 / np.power(np.float32(theta), np.arange(pdim // 2, dtype=np.float32) * 2 / pdim)).astype(np.float32)
+    ld = (heads + 2 * kvh) * hd
+    qkv = rng.normal(0, 1, (ntok, ld)).astype(np.float32)
+    gate = rng.normal(0, 1, (ntok, heads)).astype(np.float32)
+    dt = np.float16 if f16 else np.float32
+    K = rng.normal(0, 1, (kvh, slots, hd)).astype(dt)
+    V = rng.normal(0, 1, (kvh, slots, hd)).astype(dt)
+    Kref, Vref = K.astype(np.float64), V.astype(np.float64)
+    own = []
+    for t in range(ntok):   # the rows the kernel writes: roped k, v (rounded to the cache type)
+        k = rope(qkv[t, heads * hd:(heads + kvh) * hd].reshape(kvh, hd).astype(np.float64), pos0 + t, freq, pdim)
+        v = qkv[t, (heads + kvh) * hd:].reshape(kvh, hd).astype(np.float64)
+        own.append((k, v))
+        Kref[:, pos0 + t] = k.astype(np.float32).astype(dt)
+        Vref[:, pos0 + t] = v.astype(np.float32).astype(dt)
+    want = reference(qkv, Kref, Vref, own, pos0, ntok, heads, kvh, hd, full, window, freq, pdim, gate)
+
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+    t_qkv, t_gate, t_freq = dev(qkv), dev(gate), dev(freq)
+    t_k, t_v = dev(K), dev(V)
+    t_pos = torch.tensor([pos0], dtype=torch.int32, device=cuda)
+    t_out = torch.zeros(ntok, heads * hd, device=cuda)
+    ws = torch.zeros(L.spk_attn_workspace_bytes(ntok, heads, kvh, hd, nsplit), dtype=torch.uint8, device=cuda)
+    a = AttnArgs(t_qkv.data_ptr(), ld, t_k.data_ptr(), t_v.data_ptr(), f16, slots, full, window, t_freq.data_ptr(),
+                 pdim, heads, kvh, hd, t_pos.data_ptr(), ntok, 1 if ntok == 1 else 0, nsplit, t_gate.data_ptr(),
+                 heads, t_out.data_ptr(), heads * hd, ws.data_ptr())
+    torch.cuda.synchronize()
+    if ntok > 1:
+        spk.check(L.spk_attn_store(C.byref(a), None))
+    for _ in range(2):   # the workspace is left ready for the next call
+        spk.check(L.spk_attn_decode(C.byref(a), None))
+        torch.cuda.synchronize()
+        got = t_out.cpu().numpy()
+        err = np.linalg.norm(got - want) / np.linalg.norm(want)
+        assert err < TOL, err
+    if ntok == 1:   # the in-kernel store wrote the roped row
+        kc = t_k.cpu().numpy().astype(np.float64)
+        assert np.allclose(kc[:, pos0], Kref[:, pos0], rtol=1e-3 if f16 else 1e-5, atol=1e-3 if f16 else 1e-5)
+    assert ws.cpu().numpy()[:1024].max() == 0   # tickets reset
+
+
+def test_attention_rejects_bad_args(cuda):
+    import spk
+
+    L = spk.lib()
+    a = AttnArgs()
+    assert L.spk_attn_decode(C.byref(a), None) == -1
+    assert L.spk_attn_workspace_bytes(0, 16, 4, 256, 37) == 0
