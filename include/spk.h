@@ -100,9 +100,6 @@ int spk_vq_gemv(const void *const *stages, int nstages, int ngroups, int dim, in
                 const float *x, const float *norm_w, float eps, float *y, int accumulate, void *stream);
 /* 1 if spk_vq_gemv runs the persistent TMA kernel for this geometry, 0 if the generic one. */
 int spk_vq_gemv_fast_ok(int nstages, int ngroups, int dim, int nc, int rows, int cols, int v3);
-/* Measurement hook (no counterpart in the reference; like vqg_gemv_t's `threads`): rows
- * per warp of the fast VQ kernel, 0 = the planner's choice, 1 or 2. */
-int spk_vq_tune(int rows_per_warp);
 /* Bit-exact stage decode on a stream: out += decoded stage (vqg_dequant without timing). */
 int spk_vq_dequant(const void *payload, int dim, int nc, int rows, int cols, int v3, float *out, void *stream);
 

@@ -118,63 +118,50 @@ struct Chunk {
     static constexpr int NWU = (12 * F + 31) / 32;           // words used after the shift
 };
 
-// One lane's partial dots over its F indices of R rows (row k at row + k*rstride)
-// of one stage. The R rows' gathers are independent and interleaved: the lane's
-// activations serve every row, so R rows give R times the gathers in flight.
-template <int F, int EXT, int R>
-__device__ __forceinline__ void row_chunk(const uint8_t *row, size_t rstride, const uint8_t *plane, size_t pstride,
-                                          const uint2 *cb, const float (&xr)[4 * F], uint32_t bit0, uint32_t pbit0,
-                                          float (&out)[R]) {
+// One lane's partial dot over its F indices of one row of one stage.
+template <int F, int EXT>
+__device__ __forceinline__ float row_chunk(const uint8_t *row, const uint8_t *plane, const uint2 *cb,
+                                           const float (&xr)[4 * F], uint32_t bit0, uint32_t pbit0) {
     using C = Chunk<F>;
-    uint32_t u[R][C::NWU];
-    uint32_t pb[R];
+    const uint32_t *wp = reinterpret_cast<const uint32_t *>(row) + (bit0 >> 5);
+    const uint32_t sh = bit0 & 31u;
+    uint32_t w[C::NWR];
 #pragma unroll
-    for (int k = 0; k < R; k++) {
-        const uint32_t *wp = reinterpret_cast<const uint32_t *>(row + k * rstride) + (bit0 >> 5);
-        const uint32_t sh = bit0 & 31u;
-        uint32_t w[C::NWR];
+    for (int j = 0; j < C::NWR; j++) w[j] = wp[j];
+    uint32_t u[C::NWU];
 #pragma unroll
-        for (int j = 0; j < C::NWR; j++) w[j] = wp[j];
-#pragma unroll
-        for (int j = 0; j < C::NWU; j++) u[k][j] = __funnelshift_r(w[j], (j + 1 < C::NWR) ? w[j + 1] : 0u, sh);
-        pb[k] = 0;
-        if (EXT) {
-            const uint32_t *pp = reinterpret_cast<const uint32_t *>(plane + k * pstride) + (pbit0 >> 5);
-            pb[k] = __funnelshift_r(pp[0], pp[1], pbit0 & 31u);
-        }
+    for (int j = 0; j < C::NWU; j++) u[j] = __funnelshift_r(w[j], (j + 1 < C::NWR) ? w[j + 1] : 0u, sh);
+    uint32_t pb = 0;
+    if (EXT) {
+        const uint32_t *pp = reinterpret_cast<const uint32_t *>(plane) + (pbit0 >> 5);
+        pb = __funnelshift_r(pp[0], pp[1], pbit0 & 31u);
     }
-    float a0[R], a1[R];
-#pragma unroll
-    for (int k = 0; k < R; k++) a0[k] = a1[k] = 0.f;
+    float a0 = 0.f, a1 = 0.f;
 #pragma unroll
     for (int j = 0; j < F; j++) {
         const int b = 12 * j, wi = b >> 5, s = b & 31;
-#pragma unroll
-        for (int k = 0; k < R; k++) {
-            uint32_t v;
-            if (s + 12 <= 32)
-                v = (u[k][wi] >> s) & 0xFFFu;
-            else
-                v = __funnelshift_r(u[k][wi], u[k][wi + 1], s) & 0xFFFu;
-            if (EXT) v |= ((pb[k] >> j) & 1u) << 12;
-            const uint2 c = cb[v];
-            const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&c.x));
-            const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&c.y));
-            a0[k] = fmaf(lo.x, xr[4 * j + 0], a0[k]);
-            a1[k] = fmaf(lo.y, xr[4 * j + 1], a1[k]);
-            a0[k] = fmaf(hi.x, xr[4 * j + 2], a0[k]);
-            a1[k] = fmaf(hi.y, xr[4 * j + 3], a1[k]);
-        }
+        uint32_t v;
+        if (s + 12 <= 32)
+            v = (u[wi] >> s) & 0xFFFu;
+        else
+            v = __funnelshift_r(u[wi], u[wi + 1], s) & 0xFFFu;
+        if (EXT) v |= ((pb >> j) & 1u) << 12;
+        const uint2 c = cb[v];
+        const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&c.x));
+        const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&c.y));
+        a0 = fmaf(lo.x, xr[4 * j + 0], a0);
+        a1 = fmaf(lo.y, xr[4 * j + 1], a1);
+        a0 = fmaf(hi.x, xr[4 * j + 2], a0);
+        a1 = fmaf(hi.y, xr[4 * j + 3], a1);
     }
-#pragma unroll
-    for (int k = 0; k < R; k++) out[k] = a0[k] + a1[k];
+    return a0 + a1;
 }
 
 // Producer: thread 0 fills one ring slot with the index streams of rows
 // [r0, r0+nr) of every stream (stream.cuh). The contract gives every stage
 // payload 8 zeroed slack bytes, so a copy may round up to at most 8 bytes past
 // the payload end.
-__device__ __forceinline__ void issue_tile(const FastArgs &a, const uint8_t *const (&stp)[MAXQ], const Layout &L, int nq,
+__device__ __forceinline__ void issue_tile(const FastArgs &a, const uint8_t *const *stp, const Layout &L, int nq,
                                            int ext, uint8_t *slot, uint64_t *bar, int r0, int nr) {
     const size_t payload = L.stream_off + (size_t)L.rows * (L.mrow + L.prow);
     BulkList bl;
@@ -193,35 +180,30 @@ __device__ __forceinline__ void issue_tile(const FastArgs &a, const uint8_t *con
     bulk_issue(bl, bar);
 }
 
-// R: rows per warp per tile (the tile has R * warps / (ks * NG) rows).
-// The body takes the CTA's matrix (layout, stage pointers, output) by reference to
-// the kernel parameters themselves, so both uses — the main matrix and the second
-// one of a paired launch — read them from parameter space.
-template <int NSTG, int NG, int F, int EXT, int R>
-__device__ __forceinline__ void fast_body(const FastArgs &a, const Layout &L, const uint8_t *const (&stp)[MAXQ],
-                                          float *const yout, const bool xt) {
+template <int NSTG, int NG, int F, int EXT>
+__global__ void __launch_bounds__(Warps<F>::W * 32, 1) vq_fast_kernel(const FastArgs a) {
     constexpr int FAST_WARPS = Warps<F>::W, FAST_THREADS = FAST_WARPS * 32;
     constexpr int NQ = NSTG * NG;
     // padded per-lane stride of the staged activations (floats): an odd number of
     // 16-byte chunks, so 8 lanes' float4 reads hit 8 distinct bank quads
     constexpr int XS = 4 * (F + 1 + (F & 1));
     extern __shared__ __align__(16) uint8_t smem[];
+    const bool xt = NG == 1 && a.has_x && blockIdx.x == gridDim.x - 1;   // this CTA runs the second matrix
+    const Layout &L = xt ? a.XL : a.L;
+    const uint8_t *const *stp = xt ? a.xst : a.st;
+    float *const yout = xt ? a.xy : a.y;
     const int nc = L.nc;
     const int ks_n = a.ks, tr = a.tr, NB = a.nbuf;
-    // codebook q occupies [q*CBS, (q+1)*CBS): bulk-copied from its 16-byte-aligned floor,
-    // so code word v sits at q*CBS + (address & 15) + 8v
-    const size_t CBS = (size_t)nc * 8 + 16;
-    uint8_t *cbr = smem;
-    float *xs = reinterpret_cast<float *>(smem + NQ * CBS);
+    uint2 *cb = reinterpret_cast<uint2 *>(smem);
+    float *xs = reinterpret_cast<float *>(smem + (((size_t)NQ * nc * 8 + 15) & ~(size_t)15));
     uint8_t *ring = reinterpret_cast<uint8_t *>(xs + (size_t)ks_n * 32 * XS);
     uint64_t *full = reinterpret_cast<uint64_t *>(ring + (size_t)NB * a.slot_bytes);
     uint64_t *empty = full + NB;
-    uint64_t *cbar = empty + NB;                          // the codebook copies
-    float *part = reinterpret_cast<float *>(cbar + 1);    // [2][tr][NG][ks][NSTG]
+    float *part = reinterpret_cast<float *>(empty + NB);   // [2][tr][NG][ks][NSTG]
     double *red = reinterpret_cast<double *>(part + 2 * tr * NG * ks_n * NSTG);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    // warp -> (row slot in tile, group, k chunk); slot rw holds tile rows rw*R .. rw*R+R-1
+    // warp -> (row in tile, group, k chunk)
     const int ks = warp % ks_n, g = (warp / ks_n) % NG, rw = warp / (ks_n * NG);
     const bool direct = (NG == 1) && (ks_n == 1);   // the row's warp finishes the row itself
 
@@ -236,7 +218,6 @@ __device__ __forceinline__ void fast_body(const FastArgs &a, const Layout &L, co
             mbar_init(&full[b], 1);
             mbar_init(&empty[b], FAST_WARPS);
         }
-        mbar_init(cbar, 1);
         fence_mbar_init();
     }
     __syncthreads();
@@ -246,18 +227,10 @@ __device__ __forceinline__ void fast_body(const FastArgs &a, const Layout &L, co
             issue_tile(a, stp, L, NQ, EXT, ring + (size_t)t * a.slot_bytes, &full[t], r0, min(tr, re - r0));
         }
     }
-    // Codebooks: NQ x nc code words of 8 bytes, one bulk copy each, in flight while
-    // the activations are staged (they lie inside the payload, so rounding the copy
-    // to 16-byte bounds stays inside it).
-    if (tid == 0) {
-        BulkList bl;
-        bl.n = 0;
-        bl.tx = 0;
-        for (int q = 0; q < NQ; q++) {
-            const uintptr_t A = (uintptr_t)(stp[q] + L.cb_off);
-            bulk_plan(bl, cbr + q * CBS, A, A + (size_t)nc * 8, (uintptr_t)(stp[q] + L.stream_off));
-        }
-        bulk_issue(bl, cbar);
+    // Codebooks: NQ x nc code words of 8 bytes (the payload keeps them 8-byte aligned).
+    for (int q = 0; q < NQ; q++) {
+        const uint2 *src = reinterpret_cast<const uint2 *>(stp[q] + L.cb_off);
+        for (int v = tid; v < nc; v += FAST_THREADS) cb[q * nc + v] = __ldg(src + v);
     }
     // Everything above read weights only; x (and y, when accumulating) come from
     // the preceding kernels.
@@ -288,7 +261,6 @@ __device__ __forceinline__ void fast_body(const FastArgs &a, const Layout &L, co
     }
     const int i0 = ks * 32 * F + lane * F;
     const uint32_t bit0 = 12u * (uint32_t)i0, pbit0 = (uint32_t)i0;
-    mbar_wait(cbar, 0u, a.err);   // a copy that never lands leaves stale code words and the error set
 
     for (int t = 0; t < ntile; t++) {
         const int slot = t % NB;
@@ -301,61 +273,49 @@ __device__ __forceinline__ void fast_body(const FastArgs &a, const Layout &L, co
                 issue_tile(a, stp, L, NQ, EXT, ring + (size_t)sn * a.slot_bytes, &full[sn], r0n, min(tr, re - r0n));
         }
         const int r0 = rb + t * tr, nr = min(tr, re - r0);
-        const int rl0 = rw * R;   // this warp's first row in the tile
-        float gain[NSTG][R], yold[R];
+        const int r = r0 + rw;
+        float gain[NSTG], yold = 0.f;
+        if (direct && lane == 0 && rw < nr) {   // issued before the gathers, consumed after
 #pragma unroll
-        for (int k = 0; k < R; k++) {
-            yold[k] = 0.f;
-            if (direct && lane == 0 && rl0 + k < nr) {   // issued before the gathers, consumed after
-#pragma unroll
-                for (int s = 0; s < NSTG; s++)
-                    gain[s][k] = h2f_bits(
-                        *reinterpret_cast<const uint16_t *>(stp[s] + L.gain_off + 2 * (size_t)(r0 + rl0 + k)));
-                if (a.accumulate) yold[k] = yout[r0 + rl0 + k];
-            }
+            for (int s = 0; s < NSTG; s++)
+                gain[s] = h2f_bits(*reinterpret_cast<const uint16_t *>(stp[s] + L.gain_off + 2 * (size_t)r));
+            if (a.accumulate) yold = yout[r];
         }
         const bool have = mbar_wait(&full[slot], (uint32_t)((t / NB) & 1), a.err);
         float *pt = part + (size_t)(t & 1) * tr * NG * ks_n * NSTG;
-        float acc[NSTG][R];
+        float acc[NSTG];
 #pragma unroll
-        for (int s = 0; s < NSTG; s++)
-#pragma unroll
-            for (int k = 0; k < R; k++) acc[s][k] = 0.f;
-        // rows past the tile end read in-slot bytes (a whole slot is always there) and are dropped
-        if (rl0 < nr && have) {
+        for (int s = 0; s < NSTG; s++) acc[s] = 0.f;
+        if (rw < nr && have) {
             const uint8_t *sb = ring + (size_t)slot * a.slot_bytes;
 #pragma unroll
             for (int s = 0; s < NSTG; s++) {
                 const int q = g * NSTG + s;
                 const uintptr_t A = (uintptr_t)(stp[q] + L.stream_off + (size_t)r0 * L.mrow);
-                const uint8_t *row = sb + q * a.main_slot + (A & 15) + (size_t)rl0 * L.mrow;
+                const uint8_t *row = sb + q * a.main_slot + (A & 15) + (size_t)rw * L.mrow;
                 const uint8_t *pl = nullptr;
                 if (EXT) {
                     const uintptr_t P = (uintptr_t)(stp[q] + L.stream_off + (size_t)L.rows * L.mrow +
                                                     (size_t)r0 * L.prow);
-                    pl = sb + NQ * a.main_slot + q * a.plane_slot + (P & 15) + (size_t)rl0 * L.prow;
+                    pl = sb + NQ * a.main_slot + q * a.plane_slot + (P & 15) + (size_t)rw * L.prow;
                 }
-                const uint2 *cbq =
-                    reinterpret_cast<const uint2 *>(cbr + q * CBS + ((uintptr_t)(stp[q] + L.cb_off) & 15));
-                row_chunk<F, EXT, R>(row, L.mrow, pl, L.prow, cbq, xr, bit0, pbit0, acc[s]);
+                acc[s] = row_chunk<F, EXT>(row, pl, cb + (size_t)q * nc, xr, bit0, pbit0);
             }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);   // this warp is done reading the slot
+        if (rw < nr) {
 #pragma unroll
-        for (int k = 0; k < R; k++) {
-            if (rl0 + k >= nr) break;
-#pragma unroll
-            for (int s = 0; s < NSTG; s++) acc[s][k] = warp_sum(acc[s][k]);
+            for (int s = 0; s < NSTG; s++) acc[s] = warp_sum(acc[s]);
             if (lane == 0) {
                 if (direct) {
-                    float o = yold[k];
+                    float o = yold;
 #pragma unroll
-                    for (int s = 0; s < NSTG; s++) o = __fadd_rn(o, __fmul_rn(acc[s][k], gain[s][k]));
-                    yout[r0 + rl0 + k] = o;
+                    for (int s = 0; s < NSTG; s++) o = __fadd_rn(o, __fmul_rn(acc[s], gain[s]));
+                    yout[r] = o;
                 } else {
 #pragma unroll
-                    for (int s = 0; s < NSTG; s++) pt[(((rl0 + k) * NG + g) * ks_n + ks) * NSTG + s] = acc[s][k];
+                    for (int s = 0; s < NSTG; s++) pt[((rw * NG + g) * ks_n + ks) * NSTG + s] = acc[s];
                 }
             }
         }
@@ -365,11 +325,8 @@ __device__ __forceinline__ void fast_body(const FastArgs &a, const Layout &L, co
         // pt is double-buffered by tile parity, and a warp can only reach tile t+2
         // after passing tile t+1's barrier, so the reader is done with tile t by then.
         asm volatile("bar.sync %0, %1;" ::"r"(1 + rw), "r"(32 * ks_n * NG) : "memory");
-#pragma unroll
-        for (int k = 0; k < R; k++) {
-            const int rt = rl0 + k;   // row in tile
-            if (!(ks == 0 && g == 0 && lane == 0 && rt < nr)) continue;
-            const int rr = r0 + rt;
+        if (ks == 0 && g == 0 && lane == 0 && rw < nr) {
+            const int rr = r0 + rw;
             float outv[NG];
 #pragma unroll
             for (int gg = 0; gg < NG; gg++) {
@@ -377,7 +334,7 @@ __device__ __forceinline__ void fast_body(const FastArgs &a, const Layout &L, co
 #pragma unroll
                 for (int s = 0; s < NSTG; s++) {
                     float v = 0.f;
-                    for (int kk = 0; kk < ks_n; kk++) v += pt[((rt * NG + gg) * ks_n + kk) * NSTG + s];
+                    for (int k = 0; k < ks_n; k++) v += pt[((rw * NG + gg) * ks_n + k) * NSTG + s];
                     const uint16_t gh =
                         *reinterpret_cast<const uint16_t *>(stp[gg * NSTG + s] + L.gain_off + 2 * (size_t)rr);
                     o = __fadd_rn(o, __fmul_rn(v, h2f_bits(gh)));
@@ -390,14 +347,6 @@ __device__ __forceinline__ void fast_body(const FastArgs &a, const Layout &L, co
                 yout[rr] = __fmul_rn(gelu_erf(outv[0]), outv[NG - 1]);
         }
     }
-}
-
-template <int NSTG, int NG, int F, int EXT, int R>
-__global__ void __launch_bounds__(Warps<F>::W * 32, 1) vq_fast_kernel(const FastArgs a) {
-    if (NG == 1 && a.has_x && blockIdx.x == gridDim.x - 1)   // this CTA runs the second matrix
-        fast_body<NSTG, NG, F, EXT, R>(a, a.XL, a.xst, a.xy, true);
-    else
-        fast_body<NSTG, NG, F, EXT, R>(a, a.L, a.st, a.y, false);
 }
 
 // ========================================================= generic path ===
@@ -524,14 +473,10 @@ int pick_split(const Layout &L, int *F) {
 }
 
 struct FastPlan {
-    int ks, F, tr, R;
+    int ks, F, tr;
     size_t smem;
     FastArgs args;
 };
-
-// Rows per warp of the fast kernel: 0 = the planner's choice (2 where the ring
-// still fits, else 1); spk_vq_tune sets 1 or 2 for measurements.
-int g_rows_per_warp = 0;
 
 bool fast_plan(const uint8_t *const *st, int nstg, int ng, const Layout &L, FastPlan *P) {
     if (L.dim != 4 || !blk_ok(L) || nstg < 1 || nstg > 2 || ng < 1 || ng > 2) return false;
@@ -541,24 +486,19 @@ bool fast_plan(const uint8_t *const *st, int nstg, int ng, const Layout &L, Fast
     const int ks = pick_split(L, &F);
     const int W = Warps<20>::W;
     if (!ks || ks * ng > W || W % (ks * ng)) return false;
+    const int tr = W / (ks * ng);
     const int nq = nstg * ng, ext = L.prow ? 1 : 0;
-    int R = 0, tr = 0, nbuf = 0;
-    uint32_t main_slot = 0, plane_slot = 0, slot = 0;
+    const uint32_t main_slot = (uint32_t)(((size_t)tr * L.mrow + 32 + 15) & ~(size_t)15);
+    const uint32_t plane_slot = ext ? (uint32_t)(((size_t)tr * L.prow + 32 + 15) & ~(size_t)15) : 0u;
+    const uint32_t slot = nq * (main_slot + plane_slot);
+    int nbuf = FAST_NBUF;
     size_t smem = 0;
-    for (int r = 2; r >= 1 && !R; r--) {
-        if (g_rows_per_warp && r != g_rows_per_warp) continue;
-        tr = r * W / (ks * ng);
-        main_slot = (uint32_t)(((size_t)tr * L.mrow + 32 + 15) & ~(size_t)15);
-        plane_slot = ext ? (uint32_t)(((size_t)tr * L.prow + 32 + 15) & ~(size_t)15) : 0u;
-        slot = nq * (main_slot + plane_slot);
-        for (nbuf = FAST_NBUF; nbuf >= 2; nbuf--) {
-            smem = (size_t)nq * ((size_t)L.nc * 8 + 16) + (size_t)ks * 32 * (4 * (F + 1 + (F & 1))) * 4 +
-                   (size_t)nbuf * slot + (2 * (size_t)nbuf + 1) * 8 + (size_t)2 * tr * ng * ks * nstg * 4 + 32 * 8;
-            if (smem <= smem_optin_max()) break;
-        }
-        if (nbuf >= 2) R = r;
+    for (; nbuf >= 2; nbuf--) {
+        smem = (((size_t)nq * L.nc * 8 + 15) & ~(size_t)15) + (size_t)ks * 32 * (4 * (F + 1 + (F & 1))) * 4 + (size_t)nbuf * slot +
+               2 * (size_t)nbuf * 8 + (size_t)2 * tr * ng * ks * nstg * 4 + 32 * 8;
+        if (smem <= smem_optin_max()) break;
     }
-    if (!R) return false;
+    if (nbuf < 2) return false;
     FastArgs &a = P->args;
     memset(&a, 0, sizeof a);
     for (int q = 0; q < nq; q++) a.st[q] = st[q];
@@ -572,14 +512,13 @@ bool fast_plan(const uint8_t *const *st, int nstg, int ng, const Layout &L, Fast
     P->ks = ks;
     P->F = F;
     P->tr = tr;
-    P->R = R;
     P->smem = smem;
     return true;
 }
 
-template <int NSTG, int NG, int F, int EXT, int R>
+template <int NSTG, int NG, int F, int EXT>
 int launch_fast_t(const FastPlan &P, cudaStream_t s) {
-    auto k = vq_fast_kernel<NSTG, NG, F, EXT, R>;
+    auto k = vq_fast_kernel<NSTG, NG, F, EXT>;
     static size_t opted[64];
     int dev = 0;
     cudaGetDevice(&dev);
@@ -595,14 +534,9 @@ int launch_fast_t(const FastPlan &P, cudaStream_t s) {
     return e == cudaSuccess ? 0 : cuda_fail("vq fast kernel launch", e);
 }
 
-template <int NSTG, int NG, int F, int R>
-int launch_fast_r(const FastPlan &P, cudaStream_t s) {
-    return P.args.L.prow ? launch_fast_t<NSTG, NG, F, 1, R>(P, s) : launch_fast_t<NSTG, NG, F, 0, R>(P, s);
-}
-
 template <int NSTG, int NG, int F>
 int launch_fast_e(const FastPlan &P, cudaStream_t s) {
-    return P.R == 2 ? launch_fast_r<NSTG, NG, F, 2>(P, s) : launch_fast_r<NSTG, NG, F, 1>(P, s);
+    return P.args.L.prow ? launch_fast_t<NSTG, NG, F, 1>(P, s) : launch_fast_t<NSTG, NG, F, 0>(P, s);
 }
 
 template <int NSTG, int NG>
@@ -880,14 +814,6 @@ int spk_vq_gemv(const void *const *stages, int nstages, int ngroups, int dim, in
 }
 
 /* Which kernel spk_vq_gemv would run: 1 = the persistent TMA kernel, 0 = generic. */
-/* Measurement hook: rows per warp of the fast kernel (0 = the planner's choice, 1, 2).
- * Takes effect for launches planned afterwards; graphs already captured keep theirs. */
-int spk_vq_tune(int rows_per_warp) {
-    if (rows_per_warp < 0 || rows_per_warp > 2) return set_error("rows per warp %d (0, 1 or 2)", rows_per_warp);
-    g_rows_per_warp = rows_per_warp;
-    return 0;
-}
-
 int spk_vq_gemv_fast_ok(int nstages, int ngroups, int dim, int nc, int rows, int cols, int v3) {
     if (dim <= 0 || nc <= 0 || rows <= 0 || cols <= 0) return 0;
     const Layout L = make_layout(dim, nc, rows, cols, v3);

@@ -61,7 +61,6 @@ _PROTOS = {
     "spk_q6k_dequant": ([_vp, C.c_size_t, _vp, _vp], _i),
     "spk_q80_dequant": ([_vp, C.c_size_t, _vp, _vp], _i),
     "spk_q80_row": ([_vp, _i, _i, _i, _vp, _vp, _vp], _i),
-    "spk_vq_tune": ([_i], _i),
     "spk_verify_gemm": ([_vp, _i, _i, _i, _i, _i, _i, _i, _vp, _i, _vp, _f, _vp, _i, _i, _vp], _i),
     "spk_attn_workspace_bytes": ([_i, _i, _i, _i, _i], C.c_size_t),
     "spk_attn_decode": ([_vp, _vp], _i),

@@ -82,39 +82,6 @@ def test_spk_vq_gemv_all_stages_vs_oracle(cuda, geom):
         assert rel(got, ref) < GEMV_TOL, (accumulate, rel(got, ref))
 
 
-@pytest.mark.parametrize("rpw", [1, 2])
-@pytest.mark.parametrize("geom", GEOMS[:6] + GEOMS[7:9], ids=[f"{g[0]}x{g[1]}" for g in GEOMS[:6] + GEOMS[7:9]])
-def test_fast_kernel_rows_per_warp(cuda, geom, rpw):
-    """The fast kernel with 1 and 2 rows per warp (spk_vq_tune), single matrices and the
-    gate/up pair, against the oracle."""
-    import torch
-
-    rows, cols, dim, nc, st, v3 = geom
-    L = spk.lib()
-    bufs = [F.random_rvq(rows, cols, dim, nc, st, seed=rows + g, unit_gains=False, v3=v3) for g in range(2)]
-    c = F.parse_container(bufs[0])
-    x = np.random.default_rng(5).normal(0, 1, cols).astype(np.float32)
-    keep = [stage_bufs(b, c, cuda) for b in bufs]
-    xd = torch.from_numpy(x).to(cuda)
-    spk.check(L.spk_vq_tune(rpw))
-    try:
-        ptrs = (C.c_void_p * st)(*[b.data_ptr() for b in keep[0]])
-        yd = torch.zeros(rows, device=cuda)
-        spk.check(L.spk_vq_gemv(ptrs, st, 1, dim, nc, rows, cols, int(v3), spk.ptr(xd), None, 0.0, spk.ptr(yd), 0, None))
-        torch.cuda.synchronize()
-        assert rel(yd.cpu().numpy(), oracle.gemv_fused(bufs[0], x)) < GEMV_TOL
-        pair = (C.c_void_p * (2 * st))(*[b.data_ptr() for k in keep for b in k])
-        spk.check(L.spk_vq_gemv(pair, st, 2, dim, nc, rows, cols, int(v3), spk.ptr(xd), None, 0.0, spk.ptr(yd), 0, None))
-        torch.cuda.synchronize()
-        g, u = oracle.gemv_fused(bufs[0], x).astype(np.float64), oracle.gemv_fused(bufs[1], x).astype(np.float64)
-        import math
-        want = np.array([0.5 * a * (1 + math.erf(a / math.sqrt(2))) for a in g]) * u
-        assert rel(yd.cpu().numpy(), want) < GEMV_TOL
-        spk.check(L.spk_check_device_error())
-    finally:
-        L.spk_vq_tune(0)
-
-
 @pytest.mark.parametrize("geom", GEOMS[:6] + GEOMS[7:9], ids=[f"{g[0]}x{g[1]}" for g in GEOMS[:6] + GEOMS[7:9]])
 def test_fast_path_is_taken(cuda, geom):
     rows, cols, dim, nc, st, v3 = geom
