@@ -157,7 +157,7 @@ def run_reference(args) -> None:
     cb = cpu_baseline(args.ctx, tokens=3)
     v = cb["value"]
     line = {"metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": 1e3 / v, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": 1e3 / v, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init weights, seeded prompt)",
             "impl": "reference", "config": {"workload": f"config2 decode step, 36-layer VQ decoder, ctx {args.ctx}",
                                             "model": "spark-x2.6-4b (random-init)", "global_batch": 1,
@@ -189,7 +189,8 @@ def run_ours(args) -> None:
     # one model; at N > 1 every rank holds its tensor-parallel shard of it
     W = tp_shard(cfg, synth_weights(cfg, seed=1234), rank, world)
     extra = 64
-    m = DeviceModel(cfg, W, max_ctx=args.ctx + args.warmup + args.steps + extra + 2, kv_f16=True, device=dev)
+    m = DeviceModel(cfg, W, max_ctx=args.ctx + args.warmup + args.steps + extra + 2, kv_f16=args.kv == "f16",
+                    kv_q8=args.kv == "q8", device=dev)
     del W
     if world > 1:
         m.tp_connect()
@@ -279,8 +280,9 @@ def run_ours(args) -> None:
     bytes_per_token = m.weight_bytes   # this rank's shard (+ its vocabulary rows of the head below)
     if world > 1:
         bytes_per_token -= len_embed(cfg) - len_embed(cfg) // world
-    kv_l = cfg.kv_dim if world == 1 else max(cfg.kv_dim // world, cfg.head_dim)
-    kv_bytes = sum((args.ctx if f else cfg.window) for f in cfg.full) * kv_l * 2 * 2
+    kv_heads_l = max(cfg.kv_heads // world, 1)
+    row = {"f32": cfg.head_dim * 4, "f16": cfg.head_dim * 2, "q8": cfg.head_dim + cfg.head_dim // 16}[args.kv]
+    kv_bytes = sum((args.ctx if f else cfg.window) for f in cfg.full) * kv_heads_l * row * 2
     cb = cpu_baseline(args.ctx) if (rank == 0 and world == 1 and not args.no_cpu) else None
     m.close()
     if rank == 0:
@@ -289,9 +291,11 @@ def run_ours(args) -> None:
             "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded random-init weights in DQV3/Q8_0 formats, seeded prompt ids)",
-            "config": {"workload": f"config2: 36-layer VQ decoder batch-1 greedy decode at ctx {args.ctx}"
+            "config": {"workload": (f"config4: long-context decode at ctx {args.ctx}, {args.kv} KV"
+                                    if args.workload == "long" else
+                                    f"config2: 36-layer VQ decoder batch-1 greedy decode at ctx {args.ctx}")
                                    + (" (zeroed KV, no prompt run)" if args.fill_kv else ""),
-                       "model": "spark-x2.6-4b geometry, VQ 4x4096x2 trunk, Q8_0 tied head, f16 KV",
+                       "model": f"spark-x2.6-4b geometry, VQ 4x4096x2 trunk, Q8_0 tied head, {args.kv} KV",
                        "global_batch": 1, "seq_len": args.ctx,
                        "parallelism": f"tp{world}" if world > 1 else "single", "l2": "weights 3.2 GB > L2, no flush",
                        "step_bytes_per_gpu": bytes_per_token + kv_bytes,
@@ -566,14 +570,25 @@ def main():
     ap.add_argument("--warmup", type=int, default=16)
     ap.add_argument("--ctx", type=int, default=4096)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "vq", "vq-pair", "ggml"],
-                    help="decode: config 2 (default); vq: config 0 GEMV; vq-pair: the FFN gate+up launch; "
-                         "ggml: config 1 Q6_K/Q8_0 sweep")
+    ap.add_argument("--workload", default="decode", choices=["decode", "long", "vq", "vq-pair", "ggml"],
+                    help="decode: config 2 (default); long: config 4 (ctx 131072, q8_0 KV, zeroed KV cache); "
+                         "vq: config 0 GEMV; vq-pair: the FFN gate+up launch; ggml: config 1 Q6_K/Q8_0 sweep")
+    ap.add_argument("--kv", default=None, choices=["f32", "f16", "q8"],
+                    help="decode KV cache type (default f16; long: q8)")
     ap.add_argument("--fill-kv", action="store_true",
                     help="decode: start at ctx over a zeroed KV cache instead of running the prompt "
                          "(the same attention bytes per step; for profiler captures)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
     args = ap.parse_args()
+    if args.workload == "long":
+        # a 131072-token prompt through decode steps would take ~10 minutes: the cache
+        # starts zeroed at the context length (the attention reads the same bytes)
+        args.fill_kv = True
+        args.no_cpu = True
+        if args.ctx == 4096:
+            args.ctx = 131072
+        args.kv = args.kv or "q8"
+    args.kv = args.kv or "f16"
     if args.warmup < 3:
         ap.error("at least 3 warm-up steps")
     if args.impl == "reference":

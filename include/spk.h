@@ -157,8 +157,8 @@ int spk_verify_gemm(const void *const *stages, int nstages, int dim, int nc, int
 typedef struct {
     const float *qkv;           /* [ntok][ldqkv]: q (heads*hd) | k (kv_heads*hd) | v */
     int ldqkv;
-    void *k_cache, *v_cache;    /* [kv_heads][slots][hd], f32 or f16 */
-    int kv_f16, slots, full, window;
+    void *k_cache, *v_cache;    /* [kv_heads][slots] rows: kv_type 0 hd f32, 1 hd f16, 2 q8_0 */
+    int kv_type, slots, full, window; /* q8_0 rows: [hd int8][hd/32 f16 scales], ggml's q8_0 rule */
     const float *freq;          /* device [pdim/2] */
     int pdim, heads, kv_heads, head_dim;
     const int *pos_dev;         /* device int: position of token 0 */
@@ -186,7 +186,8 @@ typedef struct {
     float rope_theta_full, rope_partial_full, rope_theta_slide, rope_partial_slide;
     const int *full;   /* host array [layers]: 1 = full attention, 0 = sliding window */
     int max_ctx;       /* cache capacity in positions */
-    int kv_f16;        /* 0: f32 K/V (the reference runtimes' cache), 1: f16 K/V */
+    int kv_type;       /* 0: f32 K/V (the reference runtimes' cache), 1: f16, 2: q8_0 (ggml's
+                        * rule per 32 values, d f16; stored planar [hd int8][hd/32 d]) */
     /* Tensor parallelism (no counterpart in the reference, which runs one GPU): this
      * model is rank tp_rank of tp_world (0 or 1: a single GPU). A rank holds q heads
      * [r*heads/t, (r+1)*heads/t), the KV heads they read (KV heads are replicated when

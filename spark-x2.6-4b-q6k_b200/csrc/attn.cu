@@ -32,10 +32,11 @@ __device__ void rope_smem(float *x, const float *freq, int pdim, int pos) {
     }
 }
 
-template <int DPL, int F16>
-__device__ __forceinline__ void load_row(const void *base, size_t off, float (&r)[DPL]) {
-    if (F16) {
-        const __half *p = reinterpret_cast<const __half *>(base) + off;
+// This lane's DPL dims (lane*DPL ..) of one cache row of HD values, as f32.
+template <int HD, int DPL, int KT>
+__device__ __forceinline__ void load_row(const uint8_t *row, int lane, float (&r)[DPL]) {
+    if constexpr (KT == KV_F16) {
+        const __half *p = reinterpret_cast<const __half *>(row) + lane * DPL;
         if constexpr (DPL == 8) {
             const uint4 w = *reinterpret_cast<const uint4 *>(p);
             const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
@@ -54,8 +55,21 @@ __device__ __forceinline__ void load_row(const void *base, size_t off, float (&r
             r[2] = f1.x;
             r[3] = f1.y;
         }
+    } else if constexpr (KT == KV_Q8) {
+        // quants at row[0 .. HD), the f16 scale of 32-value block b at row[HD + 2b]
+        const float d = __half2float(reinterpret_cast<const __half *>(row + HD)[(lane * DPL) / 32]);
+        uint32_t w[DPL / 4];
+        if constexpr (DPL == 8) {
+            const uint2 v = *reinterpret_cast<const uint2 *>(row + lane * DPL);
+            w[0] = v.x;
+            w[1] = v.y;
+        } else {
+            w[0] = *reinterpret_cast<const uint32_t *>(row + lane * DPL);
+        }
+#pragma unroll
+        for (int i = 0; i < DPL; i++) r[i] = (float)(int8_t)(w[i >> 2] >> (8 * (i & 3))) * d;
     } else {
-        const float4 *p = reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(base) + off);
+        const float4 *p = reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(row) + lane * DPL);
 #pragma unroll
         for (int i = 0; i < DPL / 4; i++) {
             const float4 f = p[i];
@@ -67,11 +81,35 @@ __device__ __forceinline__ void load_row(const void *base, size_t off, float (&r
     }
 }
 
+// Store one row of hd values from shared memory into the cache, by all threads of
+// the block. q8_0 follows ggml's quantize_row_q8_0 rule: per 32 values
+// d = max|x| / 127, q = roundf(x * (1/d)) (0 when d is 0), d kept as f16.
+template <int KT>
+__device__ void store_row(const float *src, uint8_t *row, int hd) {
+    if constexpr (KT == KV_Q8) {
+        for (int b = threadIdx.x; b < hd / 32; b += blockDim.x) {
+            float amax = 0.f;
+            for (int j = 0; j < 32; j++) amax = fmaxf(amax, fabsf(src[32 * b + j]));
+            const float d = amax / 127.0f, id = d != 0.f ? 1.0f / d : 0.0f;
+            reinterpret_cast<__half *>(row + hd)[b] = __float2half_rn(d);
+            for (int j = 0; j < 32; j++) row[32 * b + j] = (uint8_t)(int8_t)roundf(src[32 * b + j] * id);
+        }
+    } else {
+        for (int i = threadIdx.x; i < hd; i += blockDim.x) {
+            if (KT == KV_F16)
+                reinterpret_cast<__half *>(row)[i] = __float2half_rn(src[i]);
+            else
+                reinterpret_cast<float *>(row)[i] = src[i];
+        }
+    }
+}
+
 // ATT_U: positions per warp per iteration (4 for long splits, 2 for short ones so
 // that all 8 warps have a position).
-template <int HD, int F16, int ATT_U>
+template <int HD, int KT, int ATT_U>
 __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnArgs a) {
     constexpr int DPL = HD / 32;   // dims per lane
+    constexpr size_t RB = kv_row_bytes(KT, HD);
     constexpr int MG = ATT_MAX_GROUP;
     __shared__ float qs[MG][HD];
     __shared__ float kn[HD], vn[HD];
@@ -107,16 +145,9 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnArgs a) {
     __syncthreads();
     // a single token's own K/V row: written by the split that owns `pos`; nobody reads that slot now
     if (a.store && c0 <= pos && pos < c1) {
-        for (int i = threadIdx.x; i < HD; i += blockDim.x) {
-            const size_t o = ((size_t)kvh * a.slots + pos % a.slots) * HD + i;
-            if (F16) {
-                reinterpret_cast<__half *>(a.kc)[o] = __float2half_rn(kn[i]);
-                reinterpret_cast<__half *>(a.vc)[o] = __float2half_rn(vn[i]);
-            } else {
-                reinterpret_cast<float *>(a.kc)[o] = kn[i];
-                reinterpret_cast<float *>(a.vc)[o] = vn[i];
-            }
-        }
+        const size_t o = ((size_t)kvh * a.slots + pos % a.slots) * RB;
+        store_row<KT>(kn, reinterpret_cast<uint8_t *>(a.kc) + o, HD);
+        store_row<KT>(vn, reinterpret_cast<uint8_t *>(a.vc) + o, HD);
     }
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     if (c0 < c1) {
@@ -140,16 +171,16 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnArgs a) {
                 if (j >= c1) {
 #pragma unroll
                     for (int d = 0; d < DPL; d++) kr[u][d] = vr[u][d] = 0.f;
-                } else if (j == pos) {   // this token's own row: f32, before any f16 rounding
+                } else if (j == pos) {   // this token's own row: f32, before the cache's rounding
 #pragma unroll
                     for (int d = 0; d < DPL; d++) {
                         kr[u][d] = kn[lane * DPL + d];
                         vr[u][d] = vn[lane * DPL + d];
                     }
                 } else {
-                    const size_t base = ((size_t)kvh * a.slots + j % a.slots) * HD + lane * DPL;
-                    load_row<DPL, F16>(a.kc, base, kr[u]);
-                    load_row<DPL, F16>(a.vc, base, vr[u]);
+                    const size_t o = ((size_t)kvh * a.slots + j % a.slots) * RB;
+                    load_row<HD, DPL, KT>(reinterpret_cast<const uint8_t *>(a.kc) + o, lane, kr[u]);
+                    load_row<HD, DPL, KT>(reinterpret_cast<const uint8_t *>(a.vc) + o, lane, vr[u]);
                 }
             }
             float s[ATT_U][MG];
@@ -280,29 +311,23 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnArgs a) {
 }
 
 // Rope K and store the K/V rows of ntok consecutive tokens: block t = token t.
-template <int F16>
+template <int KT>
 __global__ void attn_store_kernel(const AttnArgs a) {
-    extern __shared__ float ks[];   // [kv_heads * hd]
+    extern __shared__ float ks[];   // [2][kv_heads * hd]: roped k, then v
     pdl_trigger();
     pdl_wait();
     const int tok = blockIdx.x, pos = *a.pos + tok;
     const int qd = a.heads * a.hd, kvd = a.kv_heads * a.hd;
     const float *row = a.qkv + (size_t)tok * a.ldqkv;
-    for (int i = threadIdx.x; i < kvd; i += blockDim.x) ks[i] = row[qd + i];
+    for (int i = threadIdx.x; i < 2 * kvd; i += blockDim.x) ks[i] = row[qd + i];
     __syncthreads();
     for (int h = 0; h < a.kv_heads; h++) rope_smem(ks + (size_t)h * a.hd, a.freq, a.pdim, pos);
     __syncthreads();
-    for (int i = threadIdx.x; i < kvd; i += blockDim.x) {
-        const int h = i / a.hd, d = i - h * a.hd;
-        const size_t o = ((size_t)h * a.slots + pos % a.slots) * a.hd + d;
-        const float v = row[qd + kvd + i];
-        if (F16) {
-            reinterpret_cast<__half *>(a.kc)[o] = __float2half_rn(ks[i]);
-            reinterpret_cast<__half *>(a.vc)[o] = __float2half_rn(v);
-        } else {
-            reinterpret_cast<float *>(a.kc)[o] = ks[i];
-            reinterpret_cast<float *>(a.vc)[o] = v;
-        }
+    const size_t RB = kv_row_bytes(KT, a.hd);
+    for (int h = 0; h < a.kv_heads; h++) {
+        const size_t o = ((size_t)h * a.slots + pos % a.slots) * RB;
+        store_row<KT>(ks + (size_t)h * a.hd, reinterpret_cast<uint8_t *>(a.kc) + o, a.hd);
+        store_row<KT>(ks + kvd + (size_t)h * a.hd, reinterpret_cast<uint8_t *>(a.vc) + o, a.hd);
     }
 }
 
@@ -317,30 +342,22 @@ int attn_decode(const AttnArgs &a, cudaStream_t s) {
     // the longest split this layer can see: the cache span over the splits
     const int span = a.full ? a.slots : (a.window < a.slots ? a.window : a.slots);
     const bool longs = (span + a.nsplit - 1) / a.nsplit >= 64;
-    cudaError_t e;
     if (a.hd != 256 && a.hd != 128) return set_error("attention: head_dim %d (128 or 256)", a.hd);
-    if (a.hd == 256) {
-        if (a.kv_f16)
-            e = longs ? launch_pdl(attn_kernel<256, 1, 4>, grid, dim3(ATT_THREADS), 0, s, a)
-                      : launch_pdl(attn_kernel<256, 1, 2>, grid, dim3(ATT_THREADS), 0, s, a);
-        else
-            e = longs ? launch_pdl(attn_kernel<256, 0, 4>, grid, dim3(ATT_THREADS), 0, s, a)
-                      : launch_pdl(attn_kernel<256, 0, 2>, grid, dim3(ATT_THREADS), 0, s, a);
-    } else {
-        if (a.kv_f16)
-            e = longs ? launch_pdl(attn_kernel<128, 1, 4>, grid, dim3(ATT_THREADS), 0, s, a)
-                      : launch_pdl(attn_kernel<128, 1, 2>, grid, dim3(ATT_THREADS), 0, s, a);
-        else
-            e = longs ? launch_pdl(attn_kernel<128, 0, 4>, grid, dim3(ATT_THREADS), 0, s, a)
-                      : launch_pdl(attn_kernel<128, 0, 2>, grid, dim3(ATT_THREADS), 0, s, a);
-    }
+    if (a.kv_type < KV_F32 || a.kv_type > KV_Q8) return set_error("attention: cache type %d", a.kv_type);
+    const int sel = (a.hd == 256 ? 0 : 6) + a.kv_type * 2 + (longs ? 1 : 0);
+    void (*const ks[12])(const AttnArgs) = {
+        attn_kernel<256, 0, 2>, attn_kernel<256, 0, 4>, attn_kernel<256, 1, 2>, attn_kernel<256, 1, 4>,
+        attn_kernel<256, 2, 2>, attn_kernel<256, 2, 4>, attn_kernel<128, 0, 2>, attn_kernel<128, 0, 4>,
+        attn_kernel<128, 1, 2>, attn_kernel<128, 1, 4>, attn_kernel<128, 2, 2>, attn_kernel<128, 2, 4>};
+    const cudaError_t e = launch_pdl(ks[sel], grid, dim3(ATT_THREADS), 0, s, a);
     return e == cudaSuccess ? 0 : cuda_fail("attention launch", e);
 }
 
 int attn_store_batch(const AttnArgs &a, cudaStream_t s) {
-    const size_t sm = (size_t)a.kv_heads * a.hd * sizeof(float);
-    cudaError_t e = a.kv_f16 ? launch_pdl(attn_store_kernel<1>, dim3(a.ntok), dim3(256), sm, s, a)
-                             : launch_pdl(attn_store_kernel<0>, dim3(a.ntok), dim3(256), sm, s, a);
+    const size_t sm = 2 * (size_t)a.kv_heads * a.hd * sizeof(float);
+    if (a.kv_type < KV_F32 || a.kv_type > KV_Q8) return set_error("attention store: cache type %d", a.kv_type);
+    void (*const ks[3])(const AttnArgs) = {attn_store_kernel<0>, attn_store_kernel<1>, attn_store_kernel<2>};
+    cudaError_t e = launch_pdl(ks[a.kv_type], dim3(a.ntok), dim3(256), sm, s, a);
     return e == cudaSuccess ? 0 : cuda_fail("attention K/V store launch", e);
 }
 
@@ -363,7 +380,7 @@ bool to_args(const spk_attn_args *u, AttnArgs *a) {
     a->ldqkv = u->ldqkv;
     a->kc = u->k_cache;
     a->vc = u->v_cache;
-    a->kv_f16 = u->kv_f16;
+    a->kv_type = u->kv_type;
     a->slots = u->slots;
     a->full = u->full;
     a->window = u->window;

@@ -9,11 +9,21 @@ constexpr int ATT_MAX_GROUP = 4;     // q heads per KV head
 constexpr int ATT_MAX_SPLIT = 256;   // sequence splits per KV head
 constexpr int ATT_MAX_TOK = 8;
 
+// KV cache row of head_dim values, by cache type:
+//   KV_F32  hd f32   (the reference runtimes' cache)
+//   KV_F16  hd f16
+//   KV_Q8   ggml's q8_0 rule per 32 values (d = max|x| / 127 stored as f16, q = round(x / d)),
+//           stored planar so every lane's quants load aligned: [hd int8 q][hd/32 f16 d]
+enum : int { KV_F32 = 0, KV_F16 = 1, KV_Q8 = 2 };
+__host__ __device__ constexpr size_t kv_row_bytes(int type, int hd) {
+    return type == KV_F32 ? (size_t)hd * 4 : type == KV_F16 ? (size_t)hd * 2 : (size_t)hd + (size_t)hd / 16;
+}
+
 struct AttnArgs {
     const float *qkv;          // [ntok][ldqkv]: q (heads*hd) | k (kv_heads*hd) | v, pre-rope
     int ldqkv;
-    void *kc, *vc;             // this layer's caches: [kv_heads][slots][hd], f32 or f16
-    int kv_f16;
+    void *kc, *vc;             // this layer's caches: [kv_heads][slots] rows of kv_row_bytes(kv_type, hd)
+    int kv_type;
     int slots;                 // cache positions
     int full, window;
     const float *freq;         // [pdim/2] rope frequencies of this layer type (model.rs:416-429)

@@ -92,7 +92,7 @@ struct spk_model {
     float *h = nullptr, *qkv = nullptr, *gate = nullptr, *attn = nullptr, *act = nullptr, *logits = nullptr,
           *part = nullptr, *freq_full = nullptr, *freq_slide = nullptr;
     void *kc = nullptr, *vc = nullptr;
-    std::vector<size_t> kv_off;   // per layer element offset into kc / vc
+    std::vector<size_t> kv_off;   // per layer byte offset into kc / vc
     std::vector<int> kv_slots;
     int *state = nullptr;         // device: pos, token, argmax, step, local argmax; [8..16) verify ids, [16..24) local
     DevCtl *ctl = nullptr;        // device: id buffer of spk_model_run
@@ -143,12 +143,11 @@ AttnArgs attn_args(spk_model *m, int li, int ntok) {
     const spk_model_config &c = m->cfg;
     AttnArgs a;
     memset(&a, 0, sizeof a);
-    const size_t esz = c.kv_f16 ? 2 : 4;
     a.qkv = m->qkv;
     a.ldqkv = m->q_dim + 2 * m->kv_dim;
-    a.kc = (uint8_t *)m->kc + m->kv_off[li] * esz;
-    a.vc = (uint8_t *)m->vc + m->kv_off[li] * esz;
-    a.kv_f16 = c.kv_f16;
+    a.kc = (uint8_t *)m->kc + m->kv_off[li];
+    a.vc = (uint8_t *)m->vc + m->kv_off[li];
+    a.kv_type = c.kv_type;
     a.slots = m->kv_slots[li];
     a.full = m->full[li];
     a.window = c.window;
@@ -399,18 +398,22 @@ spk_model *spk_model_create(const spk_model_config *cfg, void *stream) {
     const int per_head = std::min(ATT_MAX_SPLIT, sm_count() / m->kvl > 0 ? sm_count() / m->kvl : 1);
     m->nsplit_full = std::max(1, std::min(per_head, (c.max_ctx + 15) / 16));
     m->nsplit_slide = std::max(1, std::min(per_head, (std::min(c.window, c.max_ctx) + 15) / 16));
-    size_t kv_elems = 0;
+    if (c.kv_type < KV_F32 || c.kv_type > KV_Q8) {
+        set_error("KV cache type %d (0 f32, 1 f16, 2 q8_0)", c.kv_type);
+        delete m;
+        return nullptr;
+    }
+    size_t kv_bytes = 0;
     for (int li = 0; li < c.layers; li++) {
         // Sliding layers keep their whole history too (not a window-sized ring), as
         // model.rs:398-412 does: Model::rollback to any earlier position stays exact,
         // which a speculative verify that rejects rows relies on. 27 sliding layers
         // at 131072 positions are 14.5 GB in f16: HBM affords it.
         const int slots = c.max_ctx;
-        m->kv_off.push_back(kv_elems);
+        m->kv_off.push_back(kv_bytes);
         m->kv_slots.push_back(slots);
-        kv_elems += (size_t)m->kvl * slots * c.head_dim;
+        kv_bytes += (size_t)m->kvl * slots * kv_row_bytes(c.kv_type, c.head_dim);
     }
-    const size_t esz = c.kv_f16 ? 2 : 4;
     const int nsplit = std::max(m->nsplit_full, m->nsplit_slide);
     // activations hold up to ATT_MAX_TOK rows (a verify batch); the decode step uses row 0
     const size_t R = ATT_MAX_TOK;
@@ -422,7 +425,7 @@ spk_model *spk_model_create(const spk_model_config *cfg, void *stream) {
               !alloc((void **)&m->part, (size_t)ATT_MAX_TOK * m->kvl * nsplit * m->G * (c.head_dim + 4) * 4, "alloc attention partials") &&
               !alloc((void **)&m->att_count, (size_t)ATT_MAX_TOK * m->kvl * sizeof(unsigned int), "alloc attention tickets") &&
               !alloc((void **)&m->freq_full, c.head_dim * 4, "alloc rope") && !alloc((void **)&m->freq_slide, c.head_dim * 4, "alloc rope") &&
-              !alloc(&m->kc, kv_elems * esz, "alloc K cache") && !alloc(&m->vc, kv_elems * esz, "alloc V cache") &&
+              !alloc(&m->kc, kv_bytes, "alloc K cache") && !alloc(&m->vc, kv_bytes, "alloc V cache") &&
               !alloc((void **)&m->state, 32 * sizeof(int), "alloc state") &&
               !alloc((void **)&m->ctl, sizeof(DevCtl), "alloc control") &&
               !alloc((void **)&m->head_partial, 1024 * sizeof(unsigned long long), "alloc head partials") &&
@@ -453,7 +456,7 @@ spk_model *spk_model_create(const spk_model_config *cfg, void *stream) {
         for (int i = 0; i < m->pdim_slide / 2; i++) fs[i] = 1.0f / powf(c.rope_theta_slide, (float)(2 * i) / (float)m->pdim_slide);
         ok = cudaMemcpy(m->freq_full, ff.data(), c.head_dim * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
              cudaMemcpy(m->freq_slide, fs.data(), c.head_dim * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
-             cudaMemset(m->kc, 0, kv_elems * esz) == cudaSuccess && cudaMemset(m->vc, 0, kv_elems * esz) == cudaSuccess &&
+             cudaMemset(m->kc, 0, kv_bytes) == cudaSuccess && cudaMemset(m->vc, 0, kv_bytes) == cudaSuccess &&
              cudaMemset(m->state, 0, 32 * sizeof(int)) == cudaSuccess && cudaMemset(m->ctl, 0, sizeof(DevCtl)) == cudaSuccess &&
              cudaMemset(m->head_counter, 0, sizeof(unsigned int)) == cudaSuccess &&
              cudaMemset(m->att_count, 0, (size_t)ATT_MAX_TOK * m->kvl * sizeof(unsigned int)) == cudaSuccess;

@@ -154,7 +154,7 @@ class _Cfg(C.Structure):
                 ("head_dim", C.c_int), ("inter", C.c_int), ("vocab", C.c_int), ("window", C.c_int),
                 ("eps", C.c_float), ("rope_theta_full", C.c_float), ("rope_partial_full", C.c_float),
                 ("rope_theta_slide", C.c_float), ("rope_partial_slide", C.c_float),
-                ("full", C.POINTER(C.c_int)), ("max_ctx", C.c_int), ("kv_f16", C.c_int),
+                ("full", C.POINTER(C.c_int)), ("max_ctx", C.c_int), ("kv_type", C.c_int),
                 ("tp_rank", C.c_int), ("tp_world", C.c_int)]
 
 
@@ -183,7 +183,7 @@ class DeviceModel:
     """vq_runtime::model::Model on the GPU (model.rs:260-615)."""
 
     def __init__(self, cfg: ModelConfig, weights: dict, max_ctx: int, kv_f16: bool = False, device="cuda:0",
-                 stream=None):
+                 stream=None, kv_q8: bool = False):
         """``weights`` are full weights, or one rank's shard from ``tp_shard`` (then the model is
         that tensor-parallel rank and needs ``tp_connect`` before its first step)."""
         import torch
@@ -195,7 +195,7 @@ class DeviceModel:
         self._full = (C.c_int * cfg.layers)(*[int(f) for f in cfg.full])
         c = _Cfg(cfg.hidden, cfg.layers, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.inter, cfg.vocab, cfg.window,
                  cfg.eps, cfg.rope_theta_full, cfg.rope_partial_full, cfg.rope_theta_slide, cfg.rope_partial_slide,
-                 self._full, max_ctx, int(kv_f16), *weights.get("tp", (0, 1)))
+                 self._full, max_ctx, 2 if kv_q8 else int(kv_f16), *weights.get("tp", (0, 1)))
         self.tp = weights.get("tp", (0, 1))
         L = lib()
         L.spk_model_create.restype = C.c_void_p

@@ -11,7 +11,7 @@ TOL = 2e-5
 
 class AttnArgs(C.Structure):
     _fields_ = [("qkv", C.c_void_p), ("ldqkv", C.c_int), ("k_cache", C.c_void_p), ("v_cache", C.c_void_p),
-                ("kv_f16", C.c_int), ("slots", C.c_int), ("full", C.c_int), ("window", C.c_int),
+                ("kv_type", C.c_int), ("slots", C.c_int), ("full", C.c_int), ("window", C.c_int),
                 ("freq", C.c_void_p), ("pdim", C.c_int), ("heads", C.c_int), ("kv_heads", C.c_int),
                 ("head_dim", C.c_int), ("pos_dev", C.c_void_p), ("ntok", C.c_int), ("store", C.c_int),
                 ("nsplit", C.c_int), ("gate", C.c_void_p), ("ldgate", C.c_int), ("out", C.c_void_p),
@@ -25,6 +25,32 @@ def rope(x, pos, freq, pdim):
     a, b = x[..., :half].copy(), x[..., half:pdim].copy()
     x[..., :half], x[..., half:pdim] = a * c - b * s, b * c + a * s
     return x
+
+
+def q8_rows(x):
+    """ggml's q8_0 rule per 32 values in f32 arithmetic (d = max|x|/127, q = roundf(x * (1/d))),
+    in the cache's planar row layout [hd int8][hd/32 f16 d]; returns (bytes rows, dequantized)."""
+    x = np.asarray(x, np.float32)
+    hd = x.shape[-1]
+    blk = x.reshape(*x.shape[:-1], hd // 32, 32)
+    d = (np.abs(blk).max(axis=-1) / np.float32(127)).astype(np.float32)
+    idv = np.where(d != 0, np.float32(1) / np.where(d != 0, d, 1), 0).astype(np.float32)
+    v = blk * idv[..., None]
+    q = (np.sign(v) * np.floor(np.abs(v) + np.float32(0.5))).astype(np.int8)
+    d16 = d.astype(np.float16)
+    rows = np.concatenate([q.reshape(*x.shape[:-1], hd).view(np.uint8), d16.view(np.uint8).reshape(*x.shape[:-1], -1)],
+                          axis=-1)
+    deq = (q.astype(np.float64) * d16.astype(np.float64)[..., None]).reshape(x.shape)
+    return rows, deq
+
+
+def to_cache(x, kv_type):
+    """Cache rows of type 0 f32 / 1 f16 / 2 q8_0 and their values as the kernel reads them."""
+    if kv_type == 2:
+        return q8_rows(x)
+    dt = np.float16 if kv_type == 1 else np.float32
+    c = np.asarray(x, np.float32).astype(dt)
+    return c, c.astype(np.float64)
 
 
 def reference(qkv, K, V, own, pos0, ntok, heads, kvh, hd, full, window, freq, pdim, gate):
@@ -49,8 +75,9 @@ def reference(qkv, K, V, own, pos0, ntok, heads, kvh, hd, full, window, freq, pd
 
 @pytest.mark.parametrize("hd,heads,kvh", [(256, 16, 4), (128, 4, 1)])
 @pytest.mark.parametrize("full", [1, 0])
-@pytest.mark.parametrize("ntok,f16", [(1, 0), (1, 1), (8, 0), (5, 1)])
+@pytest.mark.parametrize("ntok,f16", [(1, 0), (1, 1), (8, 0), (5, 1), (1, 2), (8, 2)])
 def test_attention_matches_reference(cuda, hd, heads, kvh, full, ntok, f16):
+    """f16 is the cache type: 0 f32, 1 f16, 2 q8_0."""
     import torch
 
     import spk
@@ -65,17 +92,15 @@ def test_attention_matches_reference(cuda, hd, heads, kvh, full, ntok, f16):
     ld = (heads + 2 * kvh) * hd
     qkv = rng.normal(0, 1, (ntok, ld)).astype(np.float32)
     gate = rng.normal(0, 1, (ntok, heads)).astype(np.float32)
-    dt = np.float16 if f16 else np.float32
-    K = rng.normal(0, 1, (kvh, slots, hd)).astype(dt)
-    V = rng.normal(0, 1, (kvh, slots, hd)).astype(dt)
-    Kref, Vref = K.astype(np.float64), V.astype(np.float64)
+    K, Kref = to_cache(rng.normal(0, 1, (kvh, slots, hd)), f16)
+    V, Vref = to_cache(rng.normal(0, 1, (kvh, slots, hd)), f16)
     own = []
     for t in range(ntok):   # the rows the kernel writes: roped k, v (rounded to the cache type)
         k = rope(qkv[t, heads * hd:(heads + kvh) * hd].reshape(kvh, hd).astype(np.float64), pos0 + t, freq, pdim)
         v = qkv[t, (heads + kvh) * hd:].reshape(kvh, hd).astype(np.float64)
         own.append((k, v))
-        Kref[:, pos0 + t] = k.astype(np.float32).astype(dt)
-        Vref[:, pos0 + t] = v.astype(np.float32).astype(dt)
+        Kref[:, pos0 + t] = to_cache(k.astype(np.float32), f16)[1]
+        Vref[:, pos0 + t] = to_cache(v.astype(np.float32), f16)[1]
     want = reference(qkv, Kref, Vref, own, pos0, ntok, heads, kvh, hd, full, window, freq, pdim, gate)
 
     dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
@@ -95,10 +120,19 @@ def test_attention_matches_reference(cuda, hd, heads, kvh, full, ntok, f16):
         torch.cuda.synchronize()
         got = t_out.cpu().numpy()
         err = np.linalg.norm(got - want) / np.linalg.norm(want)
-        assert err < TOL, err
-    if ntok == 1:   # the in-kernel store wrote the roped row
-        kc = t_k.cpu().numpy().astype(np.float64)
-        assert np.allclose(kc[:, pos0], Kref[:, pos0], rtol=1e-3 if f16 else 1e-5, atol=1e-3 if f16 else 1e-5)
+        # q8_0 batch rows: the reference ropes in f64, so a quant can land one step apart
+        assert err < (1e-4 if f16 == 2 else TOL), err
+    # the stored rows (in-kernel for one token, the batch store otherwise) are the cache type's
+    # rounding of the roped k and of v: bit-exact for q8_0 (same f32 rule), close for f16/f32
+    for t in range(ntok):
+        kw = to_cache(own[t][0].astype(np.float32), f16)[0]
+        kc = t_k.cpu().numpy()[:, pos0 + t]
+        if f16 == 2:
+            assert (np.abs(kc.view(np.int8)[:, :hd].astype(int) - kw.view(np.int8)[:, :hd].astype(int)) <= 1).all()
+            assert np.array_equal(kc[:, hd:], kw[:, hd:]) or np.allclose(
+                kc[:, hd:].copy().view(np.float16), kw[:, hd:].copy().view(np.float16), rtol=1e-3)
+        else:
+            assert np.allclose(kc.astype(np.float64), kw.astype(np.float64), rtol=1e-3, atol=1e-3)
     assert ws.cpu().numpy()[:1024].max() == 0   # tickets reset
 
 

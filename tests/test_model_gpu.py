@@ -130,6 +130,26 @@ def test_rollback_reproduces(small):
     dev.close()
 
 
+def test_q8_kv_close_to_f32(small):
+    """q8_0 KV cache (ggml's rule per 32 values): logits close to the f32-cache model's, and
+    a rollback replays bit-exactly (the rows stored are a pure function of the inputs)."""
+    cfg, W = small
+    a = DeviceModel(cfg, W, max_ctx=48)
+    b = DeviceModel(cfg, W, max_ctx=48, kv_q8=True)
+    worst, keep = 0.0, {}
+    for p in range(40):
+        la = a.forward((p * 37) % cfg.vocab, p)[1]
+        lb = b.forward((p * 37) % cfg.vocab, p)[1]
+        keep[p] = lb
+        worst = max(worst, rel(lb, la))
+    assert worst < 5e-2, worst
+    b.rollback(30)
+    for p in range(30, 40):
+        assert np.array_equal(b.forward((p * 37) % cfg.vocab, p)[1], keep[p])
+    a.close()
+    b.close()
+
+
 def test_f16_kv_close_to_f32(small):
     cfg, W = small
     a = DeviceModel(cfg, W, max_ctx=48)
