@@ -441,8 +441,8 @@ spk_model *spk_model_create(const spk_model_config *cfg, void *stream) {
         ok = !alloc(&m->mailbox, total, "alloc tensor-parallel mailbox") &&
              cudaMemset(m->mailbox, 0, total) == cudaSuccess && !alloc((void **)&m->pbuf, R * c.hidden * 4, "alloc partial") &&
              !alloc((void **)&m->logits_full, R * c.vocab * 4, "alloc gathered logits") &&
-             !alloc((void **)&m->tp_seq, sizeof(unsigned int), "alloc exchange counter") &&
-             cudaMemset(m->tp_seq, 0, sizeof(unsigned int)) == cudaSuccess;
+             !alloc((void **)&m->tp_seq, 2 * sizeof(unsigned int), "alloc exchange counter") &&
+             cudaMemset(m->tp_seq, 0, 2 * sizeof(unsigned int)) == cudaSuccess;
         if (ok) m->logits = (float *)((uint8_t *)m->mailbox + m->mail_logits_off);
         else set_error("tensor-parallel allocation failed");
     }

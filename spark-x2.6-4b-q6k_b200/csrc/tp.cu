@@ -3,16 +3,16 @@
 // Megatron-style sharding (attention by head, FFN by intermediate column) leaves
 // two reductions of the 2560-wide residual per layer (after out_proj and after
 // down_proj) and one argmax over the vocabulary shards of the head. Each is one
-// single-CTA launch here: the rank's row goes to every peer's mailbox with
-// NVLink stores, a release flag follows, and the reduction runs on the rows
-// received. There is no library collective on this path.
+// launch here: every CTA sends its chunk of the rank's row to every peer's mailbox
+// with NVLink stores, a release flag follows, and the CTA reduces the chunk once
+// every rank's has arrived. There is no library collective on this path.
 #include "spk.h"
 #include "tp.cuh"
 
 namespace spk {
 namespace {
 
-constexpr int TP_THREADS = 512;
+constexpr int TP_THREADS = 128;
 
 __device__ __forceinline__ unsigned long long globaltimer_ns() {
     unsigned long long t;
@@ -30,13 +30,17 @@ __device__ __forceinline__ void st_release_sys(unsigned int *p, unsigned int v) 
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Threads 0..world-1 publish this rank's flag for `seq` to every rank (after the
-// CTA's mailbox stores, which the barrier orders before the release).
-__device__ __forceinline__ void publish(const TpView &v, int slot, unsigned int seq) {
+__device__ __forceinline__ unsigned int *flag_at(const TpView &v, int owner, int slot, int chunk, int sender) {
+    return v.flags[owner] + ((size_t)slot * TP_CHUNKS + chunk) * TP_MAX + sender;
+}
+
+// Threads 0..world-1 publish this rank's flag of `chunk` for `seq` to every rank
+// (after the CTA's mailbox stores, which the barrier orders before the release).
+__device__ __forceinline__ void publish(const TpView &v, int slot, int chunk, unsigned int seq) {
     __syncthreads();
     if ((int)threadIdx.x < v.world) {
         __threadfence_system();
-        st_release_sys(v.flags[threadIdx.x] + slot * TP_MAX + v.rank, seq);
+        st_release_sys(flag_at(v, threadIdx.x, slot, chunk, v.rank), seq);
     }
 }
 
@@ -45,12 +49,12 @@ __device__ __forceinline__ void publish(const TpView &v, int slot, unsigned int 
 // returns false; the kernel then finishes on whatever rows are present, and once
 // the error is recorded later exchanges do not wait at all (the step's results
 // are already invalid and the host reports the error).
-__device__ bool wait_all(const TpView &v, int slot, unsigned int seq) {
+__device__ bool wait_all(const TpView &v, int slot, int chunk, unsigned int seq) {
     __shared__ int ok;
     if (threadIdx.x == 0) ok = 1;
     __syncthreads();
     if ((int)threadIdx.x < v.world) {
-        const unsigned int *f = v.flags[v.rank] + slot * TP_MAX + threadIdx.x;
+        const unsigned int *f = flag_at(v, v.rank, slot, chunk, threadIdx.x);
         const unsigned long long t0 = globaltimer_ns();
         bool give_up = *reinterpret_cast<volatile int *>(v.err) == DEV_PEER_TIMEOUT;
         for (unsigned int it = 0; !give_up; it++) {
@@ -64,31 +68,50 @@ __device__ bool wait_all(const TpView &v, int slot, unsigned int seq) {
     return ok != 0;
 }
 
+// CTA c owns floats [c*chunk, min(n, (c+1)*chunk)), chunk a multiple of 4.
 __global__ void __launch_bounds__(TP_THREADS) tp_sum_kernel(const TpView v, const float *__restrict__ part,
-                                                            float *__restrict__ h, int n) {
+                                                            float *__restrict__ h, int n, int chunk) {
     __shared__ unsigned int s_seq;
+    __shared__ int s_last;
     pdl_trigger();
     pdl_wait();
-    if (threadIdx.x == 0) s_seq = *v.seq + 1u;
+    if (threadIdx.x == 0) s_seq = v.seq[0] + 1u;
     __syncthreads();
     const unsigned int seq = s_seq;
-    const int slot = (int)(seq & 1u);
+    const int slot = (int)(seq & 1u), c = blockIdx.x;
+    const int i0 = c * chunk / 4, i1 = min((c + 1) * chunk, n) / 4;   // this CTA's float4 range
     const size_t row = ((size_t)slot * v.world + v.rank) * v.stride;
-    const float4 *p4 = reinterpret_cast<const float4 *>(part);
-    for (int i = threadIdx.x; i < n / 4; i += blockDim.x) {
-        const float4 x = p4[i];
+    for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+        const float4 x = reinterpret_cast<const float4 *>(part)[i];
         for (int q = 0; q < v.world; q++) reinterpret_cast<float4 *>(v.mail[q] + row)[i] = x;
     }
-    publish(v, slot, seq);
-    wait_all(v, slot, seq);
-    const float *mine = v.mail[v.rank] + (size_t)slot * v.world * v.stride;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        float s = __ldcg(mine + i);
-        for (int r = 1; r < v.world; r++) s += __ldcg(mine + (size_t)r * v.stride + i);
-        h[i] = h[i] + s;
+    publish(v, slot, c, seq);
+    wait_all(v, slot, c, seq);
+    for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+        const float4 *mail = reinterpret_cast<const float4 *>(v.mail[v.rank] + (size_t)slot * v.world * v.stride);
+        float4 acc = __ldcg(mail + i);
+        for (int r = 1; r < v.world; r++) {
+            const float4 t = __ldcg(mail + (size_t)r * (v.stride / 4) + i);
+            acc.x += t.x;
+            acc.y += t.y;
+            acc.z += t.z;
+            acc.w += t.w;
+        }
+        float4 hv = reinterpret_cast<float4 *>(h)[i];
+        hv.x = hv.x + acc.x;
+        hv.y = hv.y + acc.y;
+        hv.z = hv.z + acc.z;
+        hv.w = hv.w + acc.w;
+        reinterpret_cast<float4 *>(h)[i] = hv;
     }
+    // the last CTA to finish advances the counter (every CTA has read it by then)
     __syncthreads();
-    if (threadIdx.x == 0) *v.seq = seq;
+    if (threadIdx.x == 0) s_last = atomicAdd(&v.seq[1], 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (s_last && threadIdx.x == 0) {
+        v.seq[1] = 0u;
+        v.seq[0] = seq;
+    }
 }
 
 // Order-preserving key of (value, index): larger value wins, then the smaller
@@ -106,7 +129,7 @@ __global__ void tp_argmax_kernel(const TpView v, const float *__restrict__ logit
     __shared__ unsigned int s_seq;
     pdl_trigger();
     pdl_wait();
-    if (threadIdx.x == 0) s_seq = *v.seq + 1u;
+    if (threadIdx.x == 0) s_seq = v.seq[0] + 1u;
     __syncthreads();
     const unsigned int seq = s_seq;
     const int slot = (int)(seq & 1u);
@@ -117,8 +140,8 @@ __global__ void tp_argmax_kernel(const TpView v, const float *__restrict__ logit
         const unsigned long long key = argmax_key(logits[(size_t)t * ldl + li], row0 + li);
         for (int q = 0; q < v.world; q++) reinterpret_cast<unsigned long long *>(v.mail[q] + row)[t] = key;
     }
-    publish(v, slot, seq);
-    wait_all(v, slot, seq);
+    publish(v, slot, 0, seq);
+    wait_all(v, slot, 0, seq);
     if (t < ntok) {
         const float *mine = v.mail[v.rank] + (size_t)slot * v.world * v.stride;
         unsigned long long best = 0ull;
@@ -130,7 +153,7 @@ __global__ void tp_argmax_kernel(const TpView v, const float *__restrict__ logit
         amax[t] = (int)(0xFFFFFFFFu - (unsigned int)(best & 0xFFFFFFFFull));
     }
     __syncthreads();
-    if (t == 0) *v.seq = seq;
+    if (t == 0) v.seq[0] = seq;
 }
 
 }  // namespace
@@ -141,12 +164,19 @@ size_t tp_mailbox_bytes(int world, int n, size_t *flags_off, int *stride) {
     const size_t off = (mail + 255) / 256 * 256;
     if (flags_off) *flags_off = off;
     if (stride) *stride = st;
-    return off + (size_t)2 * TP_MAX * sizeof(unsigned int);
+    return off + (size_t)2 * TP_CHUNKS * TP_MAX * sizeof(unsigned int);
 }
 
 int tp_sum(const TpView &v, const float *part, float *h, int n, cudaStream_t s) {
     if (n % 4 || n > v.stride) return set_error("tp_sum: %d floats do not fit the %d-float mailbox rows", n, v.stride);
-    cudaError_t e = launch_pdl(tp_sum_kernel, dim3(1), dim3(TP_THREADS), 0, s, v, part, h, n);
+    // chunks of 256 floats (10 CTAs for the 2560-wide residual), at most TP_CHUNKS
+    int chunk = 256, nb = (n + chunk - 1) / chunk;
+    if (nb > TP_CHUNKS) {
+        nb = TP_CHUNKS;
+        chunk = ((n + nb - 1) / nb + 3) / 4 * 4;
+        nb = (n + chunk - 1) / chunk;
+    }
+    cudaError_t e = launch_pdl(tp_sum_kernel, dim3(nb), dim3(TP_THREADS), 0, s, v, part, h, n, chunk);
     return e == cudaSuccess ? 0 : cuda_fail("tp_sum launch", e);
 }
 

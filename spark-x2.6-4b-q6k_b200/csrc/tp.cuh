@@ -3,28 +3,29 @@
 // Every rank owns one device allocation (its "mailbox"), exported to the other
 // ranks with CUDA IPC (or passed as plain pointers by a single process that
 // drives several GPUs with peer access):
-//   float        mail[2][world][stride]   slot-major, one row per sender
-//   unsigned int flags[2][TP_MAX]         flags[slot][sender] = last sequence number
-// An exchange with sequence number s uses slot s & 1. Each rank stores its row
-// into every rank's mailbox (NVLink stores), releases its flag at system scope,
-// then waits, bounded in time, until every sender's flag has reached s, and
-// reduces the rows it received in rank order 0..world-1, so all ranks end with
-// bit-identical results. Two slots suffice: a rank can only start exchange s+2
-// after every rank has stored its row of s+1, which each does only after it has
-// finished reading s.
+//   float        mail[2][world][stride]            slot-major, one row per sender
+//   unsigned int flags[2][TP_CHUNKS][TP_MAX]      flags[slot][chunk][sender] = last sequence number
+// An exchange with sequence number s uses slot s & 1. The row is cut into chunks,
+// one CTA each: a CTA stores its chunk into every rank's mailbox (NVLink stores),
+// releases its chunk's flag at system scope, then waits, bounded in time, until
+// every sender's flag for that chunk has reached s, and reduces the chunk in rank
+// order 0..world-1, so all ranks end with bit-identical results. Two slots
+// suffice: a rank can only start exchange s+2 after every rank has stored its row
+// of s+1, which each does only after it has finished reading s.
 #pragma once
 #include "common.cuh"
 
 namespace spk {
 
 constexpr int TP_MAX = 8;
+constexpr int TP_CHUNKS = 32;   // CTAs (row chunks) per exchange, at most
 
 struct TpView {
     float *mail[TP_MAX];            // every rank's mailbox, as mapped in this process
     unsigned int *flags[TP_MAX];    // every rank's flag array
     int rank, world;
     int stride;                     // floats per mailbox row (>= the exchanged length, a multiple of 64)
-    unsigned int *seq;              // this rank's exchange counter (device, starts at 0)
+    unsigned int *seq;              // this rank's [exchange counter, finished-CTA ticket] (device, zero)
     unsigned long long wait_ns;     // give-up time of a wait
     int *err;                       // device error word
 };

@@ -58,8 +58,12 @@ def _rank_main(rank, world, port, q):
         m.run(STEPS)
         m.stream.synchronize()
         dev_ids = ids.cpu().numpy().tolist()
+        # a verify batch (anchor + 7 proposals = the host loop's own ids): 8-row exchanges
+        p0 = len(PROMPT) - 1
+        m.rollback(p0)
+        tgt, _ = m.verify([PROMPT[-1]] + toks[p0:p0 + 7], p0)
         m.close()
-        q.put((rank, toks, np.stack(logits) if rank == 0 else None, dev_ids, None))
+        q.put((rank, toks, np.stack(logits) if rank == 0 else None, (dev_ids, tgt), None))
     except Exception as e:   # report, do not hang the parent
         q.put((rank, None, None, None, repr(e)))
     finally:
@@ -88,9 +92,11 @@ def test_tp2_matches_oracle(cuda):
         p.join(timeout=120)
     for r in (0, 1):
         assert res[r][4] is None, res[r][4]
-    toks0, logits, dev0 = res[0][1], res[0][2], res[0][3]
+    toks0, logits, (dev0, tgt0) = res[0][1], res[0][2], res[0][3]
     assert toks0 == res[1][1], "ranks disagree on the greedy ids"
-    assert dev0 == res[1][3]
+    assert (dev0, tgt0) == res[1][3]
+    p0 = len(PROMPT) - 1
+    assert tgt0 == toks0[p0:p0 + 8], "the verify batch disagrees with the sequential steps"
 
     cfg = _cfg()
     W = synth_weights(cfg, seed=3, exact_q80=True)
