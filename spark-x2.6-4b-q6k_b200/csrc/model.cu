@@ -435,7 +435,8 @@ spk_model *spk_model_create(const spk_model_config *cfg, void *stream) {
     } else if (ok) {
         // one mailbox holds the exchange rows, the flags and this rank's logits shard
         // (peers read the shard when a host forward asks for the whole vocabulary)
-        const size_t mb = tp_mailbox_bytes(t, (int)R * c.hidden, &m->mail_flags_off, &m->mail_stride);
+        // rows of (value, sequence) pairs: two floats' room per exchanged value
+        const size_t mb = tp_mailbox_bytes(t, 2 * (int)R * c.hidden, &m->mail_flags_off, &m->mail_stride);
         m->mail_logits_off = (mb + 255) / 256 * 256;
         const size_t total = m->mail_logits_off + R * m->vocab_l * 4;
         ok = !alloc(&m->mailbox, total, "alloc tensor-parallel mailbox") &&

@@ -4,8 +4,9 @@
 // two reductions of the 2560-wide residual per layer (after out_proj and after
 // down_proj) and one argmax over the vocabulary shards of the head. Each is one
 // launch here: every CTA sends its chunk of the rank's row to every peer's mailbox
-// with NVLink stores, a release flag follows, and the CTA reduces the chunk once
-// every rank's has arrived. There is no library collective on this path.
+// with NVLink stores and reduces the chunk once every rank's has arrived: every
+// value travels as a (value, sequence number) pair in one 8-byte store.
+// There is no library collective on this path.
 #include "spk.h"
 #include "tp.cuh"
 
@@ -20,55 +21,23 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
     return t;
 }
 
-__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int *p) {
-    unsigned int v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ void st_pair(uint2 *p, uint32_t value, uint32_t seq) {
+    asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(value), "r"(seq) : "memory");
+}
+
+__device__ __forceinline__ uint2 ld_pair(const uint2 *p) {
+    uint2 v;
+    asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
     return v;
 }
 
-__device__ __forceinline__ void st_release_sys(unsigned int *p, unsigned int v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ unsigned int *flag_at(const TpView &v, int owner, int slot, int chunk, int sender) {
-    return v.flags[owner] + ((size_t)slot * TP_CHUNKS + chunk) * TP_MAX + sender;
-}
-
-// Threads 0..world-1 publish this rank's flag of `chunk` for `seq` to every rank
-// (after the CTA's mailbox stores, which the barrier orders before the release).
-__device__ __forceinline__ void publish(const TpView &v, int slot, int chunk, unsigned int seq) {
-    __syncthreads();
-    if ((int)threadIdx.x < v.world) {
-        __threadfence_system();
-        st_release_sys(flag_at(v, threadIdx.x, slot, chunk, v.rank), seq);
-    }
-}
-
-// Wait until every sender's flag in this rank's mailbox has reached `seq`. The
-// wait gives up after v.wait_ns (or 2^30 polls), records DEV_PEER_TIMEOUT and
-// returns false; the kernel then finishes on whatever rows are present, and once
-// the error is recorded later exchanges do not wait at all (the step's results
-// are already invalid and the host reports the error).
-__device__ bool wait_all(const TpView &v, int slot, int chunk, unsigned int seq) {
-    __shared__ int ok;
-    if (threadIdx.x == 0) ok = 1;
-    __syncthreads();
-    if ((int)threadIdx.x < v.world) {
-        const unsigned int *f = flag_at(v, v.rank, slot, chunk, threadIdx.x);
-        const unsigned long long t0 = globaltimer_ns();
-        bool give_up = *reinterpret_cast<volatile int *>(v.err) == DEV_PEER_TIMEOUT;
-        for (unsigned int it = 0; !give_up; it++) {
-            if ((int)(ld_acquire_sys(f) - seq) >= 0) break;
-            give_up = it > (1u << 30) || globaltimer_ns() - t0 > v.wait_ns;
-            if (give_up) atomicExch(v.err, DEV_PEER_TIMEOUT);
-        }
-        if (give_up) ok = 0;
-    }
-    __syncthreads();
-    return ok != 0;
-}
-
-// CTA c owns floats [c*chunk, min(n, (c+1)*chunk)), chunk a multiple of 4.
+// The residual reduction, low-latency form: every value travels as an 8-byte
+// (value, sequence number) pair — one single-copy-atomic store — so a receiver
+// knows a value has arrived when its pair carries this exchange's number, and no
+// fence or separate flag is needed. The pair rows live in the mailbox's float area
+// (stride floats per sender row = stride/2 pairs). CTA c owns values
+// [c*chunk, min(n, (c+1)*chunk)). Each thread polls the pairs it reduces, bounded
+// in time; a wait that runs out records DEV_PEER_TIMEOUT and later waits skip.
 __global__ void __launch_bounds__(TP_THREADS) tp_sum_kernel(const TpView v, const float *__restrict__ part,
                                                             float *__restrict__ h, int n, int chunk) {
     __shared__ unsigned int s_seq;
@@ -79,30 +48,32 @@ __global__ void __launch_bounds__(TP_THREADS) tp_sum_kernel(const TpView v, cons
     __syncthreads();
     const unsigned int seq = s_seq;
     const int slot = (int)(seq & 1u), c = blockIdx.x;
-    const int i0 = c * chunk / 4, i1 = min((c + 1) * chunk, n) / 4;   // this CTA's float4 range
-    const size_t row = ((size_t)slot * v.world + v.rank) * v.stride;
+    const int i0 = c * chunk, i1 = min((c + 1) * chunk, n);
+    const size_t prow = (size_t)v.stride / 2;   // pairs per sender row
+    const size_t mine_row = ((size_t)slot * v.world + v.rank) * prow;
     for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
-        const float4 x = reinterpret_cast<const float4 *>(part)[i];
-        for (int q = 0; q < v.world; q++) reinterpret_cast<float4 *>(v.mail[q] + row)[i] = x;
+        const uint32_t x = __float_as_uint(part[i]);
+        for (int q = 0; q < v.world; q++) st_pair(reinterpret_cast<uint2 *>(v.mail[q]) + mine_row + i, x, seq);
     }
-    publish(v, slot, c, seq);
-    wait_all(v, slot, c, seq);
+    const uint2 *mail = reinterpret_cast<const uint2 *>(v.mail[v.rank]) + (size_t)slot * v.world * prow;
+    bool give_up = *reinterpret_cast<volatile int *>(v.err) == DEV_PEER_TIMEOUT;
+    const unsigned long long t0 = globaltimer_ns();
     for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
-        const float4 *mail = reinterpret_cast<const float4 *>(v.mail[v.rank] + (size_t)slot * v.world * v.stride);
-        float4 acc = __ldcg(mail + i);
-        for (int r = 1; r < v.world; r++) {
-            const float4 t = __ldcg(mail + (size_t)r * (v.stride / 4) + i);
-            acc.x += t.x;
-            acc.y += t.y;
-            acc.z += t.z;
-            acc.w += t.w;
+        float acc = 0.f;
+        for (int r = 0; r < v.world; r++) {
+            uint2 pr = ld_pair(mail + (size_t)r * prow + i);
+            for (unsigned int it = 0; pr.y != seq && !give_up; it++) {
+                if (it > (1u << 30) || globaltimer_ns() - t0 > v.wait_ns) {
+                    give_up = true;
+                    atomicExch(v.err, DEV_PEER_TIMEOUT);
+                    break;
+                }
+                pr = ld_pair(mail + (size_t)r * prow + i);
+            }
+            const float x = __uint_as_float(pr.x);
+            acc = r == 0 ? x : acc + x;
         }
-        float4 hv = reinterpret_cast<float4 *>(h)[i];
-        hv.x = hv.x + acc.x;
-        hv.y = hv.y + acc.y;
-        hv.z = hv.z + acc.z;
-        hv.w = hv.w + acc.w;
-        reinterpret_cast<float4 *>(h)[i] = hv;
+        h[i] = h[i] + acc;
     }
     // the last CTA to finish advances the counter (every CTA has read it by then)
     __syncthreads();
@@ -124,6 +95,8 @@ __device__ __forceinline__ unsigned long long argmax_key(float x, int idx) {
     return ((unsigned long long)k << 32) | (unsigned long long)(0xFFFFFFFFu - (unsigned int)idx);
 }
 
+// The vocabulary-shard argmax: token t's 64-bit key travels as two (half, sequence)
+// pairs at pair positions 2t, 2t+1 of the sender's row, like the residual's values.
 __global__ void tp_argmax_kernel(const TpView v, const float *__restrict__ logits, int ldl,
                                  const int *__restrict__ amax_local, int row0, int *__restrict__ amax, int ntok) {
     __shared__ unsigned int s_seq;
@@ -133,22 +106,38 @@ __global__ void tp_argmax_kernel(const TpView v, const float *__restrict__ logit
     __syncthreads();
     const unsigned int seq = s_seq;
     const int slot = (int)(seq & 1u);
-    const size_t row = ((size_t)slot * v.world + v.rank) * v.stride;
+    const size_t prow = (size_t)v.stride / 2;
     const int t = threadIdx.x;   // token row t of the batch
     if (t < ntok) {
         const int li = amax_local[t];
         const unsigned long long key = argmax_key(logits[(size_t)t * ldl + li], row0 + li);
-        for (int q = 0; q < v.world; q++) reinterpret_cast<unsigned long long *>(v.mail[q] + row)[t] = key;
+        for (int q = 0; q < v.world; q++) {
+            uint2 *dst = reinterpret_cast<uint2 *>(v.mail[q]) + ((size_t)slot * v.world + v.rank) * prow + 2 * t;
+            st_pair(dst, (uint32_t)key, seq);
+            st_pair(dst + 1, (uint32_t)(key >> 32), seq);
+        }
     }
-    publish(v, slot, 0, seq);
-    wait_all(v, slot, 0, seq);
     if (t < ntok) {
-        const float *mine = v.mail[v.rank] + (size_t)slot * v.world * v.stride;
+        const uint2 *mail = reinterpret_cast<const uint2 *>(v.mail[v.rank]) + (size_t)slot * v.world * prow;
+        bool give_up = *reinterpret_cast<volatile int *>(v.err) == DEV_PEER_TIMEOUT;
+        const unsigned long long t0 = globaltimer_ns();
         unsigned long long best = 0ull;
         for (int r = 0; r < v.world; r++) {
-            const unsigned long long k =
-                __ldcg(reinterpret_cast<const unsigned long long *>(mine + (size_t)r * v.stride) + t);
-            best = k > best ? k : best;
+            uint32_t half[2];
+            for (int k = 0; k < 2; k++) {
+                uint2 pr = ld_pair(mail + (size_t)r * prow + 2 * t + k);
+                for (unsigned int it = 0; pr.y != seq && !give_up; it++) {
+                    if (it > (1u << 30) || globaltimer_ns() - t0 > v.wait_ns) {
+                        give_up = true;
+                        atomicExch(v.err, DEV_PEER_TIMEOUT);
+                        break;
+                    }
+                    pr = ld_pair(mail + (size_t)r * prow + 2 * t + k);
+                }
+                half[k] = pr.x;
+            }
+            const unsigned long long kr = ((unsigned long long)half[1] << 32) | half[0];
+            best = kr > best ? kr : best;
         }
         amax[t] = (int)(0xFFFFFFFFu - (unsigned int)(best & 0xFFFFFFFFull));
     }
@@ -168,8 +157,8 @@ size_t tp_mailbox_bytes(int world, int n, size_t *flags_off, int *stride) {
 }
 
 int tp_sum(const TpView &v, const float *part, float *h, int n, cudaStream_t s) {
-    if (n % 4 || n > v.stride) return set_error("tp_sum: %d floats do not fit the %d-float mailbox rows", n, v.stride);
-    // chunks of 256 floats (10 CTAs for the 2560-wide residual), at most TP_CHUNKS
+    if (n % 4 || 2 * n > v.stride) return set_error("tp_sum: %d values do not fit the %d-float mailbox rows as pairs", n, v.stride);
+    // chunks of 256 values (10 CTAs for the 2560-wide residual), at most TP_CHUNKS
     int chunk = 256, nb = (n + chunk - 1) / chunk;
     if (nb > TP_CHUNKS) {
         nb = TP_CHUNKS;

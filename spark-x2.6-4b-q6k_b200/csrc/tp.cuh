@@ -3,13 +3,13 @@
 // Every rank owns one device allocation (its "mailbox"), exported to the other
 // ranks with CUDA IPC (or passed as plain pointers by a single process that
 // drives several GPUs with peer access):
-//   float        mail[2][world][stride]            slot-major, one row per sender
-//   unsigned int flags[2][TP_CHUNKS][TP_MAX]      flags[slot][chunk][sender] = last sequence number
+//   mail[2][world][stride / 2] 8-byte (value, sequence) pairs, slot-major, one row per sender
 // An exchange with sequence number s uses slot s & 1. The row is cut into chunks,
-// one CTA each: a CTA stores its chunk into every rank's mailbox (NVLink stores),
-// releases its chunk's flag at system scope, then waits, bounded in time, until
-// every sender's flag for that chunk has reached s, and reduces the chunk in rank
-// order 0..world-1, so all ranks end with bit-identical results. Two slots
+// one CTA each: a CTA stores its chunk into every rank's mailbox (NVLink stores,
+// each value paired with s in one single-copy-atomic 8-byte store), waits, bounded
+// in time, until every sender's pairs for its chunk carry s, and reduces the chunk
+// in rank order 0..world-1, so all ranks end with bit-identical results. Sequence
+// numbers are unique, so a stale pair never passes for a new one. Two slots
 // suffice: a rank can only start exchange s+2 after every rank has stored its row
 // of s+1, which each does only after it has finished reading s.
 #pragma once
@@ -22,7 +22,7 @@ constexpr int TP_CHUNKS = 32;   // CTAs (row chunks) per exchange, at most
 
 struct TpView {
     float *mail[TP_MAX];            // every rank's mailbox, as mapped in this process
-    unsigned int *flags[TP_MAX];    // every rank's flag array
+    unsigned int *flags[TP_MAX];    // every rank's area past the pair rows (unused by the exchanges)
     int rank, world;
     int stride;                     // floats per mailbox row (>= the exchanged length, a multiple of 64)
     unsigned int *seq;              // this rank's [exchange counter, finished-CTA ticket] (device, zero)
@@ -30,11 +30,12 @@ struct TpView {
     int *err;                       // device error word
 };
 
-// Bytes of one mailbox for `world` ranks and rows of up to n floats; *flags_off
-// receives the byte offset of the flag array inside it.
+// Bytes of one mailbox for `world` ranks and rows of up to n floats (n/2 pairs);
+// *flags_off receives the byte offset just past the rows.
 size_t tp_mailbox_bytes(int world, int n, size_t *flags_off, int *stride);
 
-// h[i] += sum over ranks r (in rank order) of part_r[i], i < n (n a multiple of 4).
+// h[i] += sum over ranks r (in rank order) of part_r[i], i < n (n a multiple of 4, the
+// mailbox rows at least 2n floats: the values travel as (value, sequence) pairs).
 int tp_sum(const TpView &v, const float *part, float *h, int n, cudaStream_t s);
 
 // Global greedy ids over vocabulary shards, for ntok token rows: rank r holds
