@@ -336,6 +336,84 @@ def hot_replay(g, stream, seconds: float = 0.4) -> None:
             g.replay()
 
 
+def run_spec(args) -> None:
+    """Config 3: speculative decode of the config-2 target at an 8192-token context. A round
+    is one verify batch (spk_model_verify: anchor + 7 proposals, M = 8, in one batched
+    forward), then the cache rolls back to the accepted prefix (spec.rs:197-245). Proposals
+    are synthetic: a seeded Bernoulli(p) acceptor decides per proposal whether it equals the
+    target's id (a random-init draft accepts ~0, which measures nothing); the round's output
+    is the accepted prefix plus the target's token, as spec.rs emits it. The draft model's own
+    time is not included (the DSpark draft is not built): value = accepted tokens per second
+    of verify time."""
+    import ctypes as C
+
+    import torch
+
+    import spk
+    from spk.model import DeviceModel, ModelConfig, synth_weights
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = ModelConfig()
+    W = synth_weights(cfg, seed=1234)
+    ctx, nd, p_acc = args.ctx, 7, args.accept
+    m = DeviceModel(cfg, W, max_ctx=ctx + (args.warmup + args.steps) * (nd + 1) + 16, kv_f16=True, device=dev)
+    del W
+    m.advance_len(ctx)   # a zeroed KV cache at the context length (the attention reads the same bytes)
+    rng = np.random.default_rng(11)
+    pos, anchor, emitted = ctx, 5, 0
+    tgt = [0] * (nd + 1)
+
+    def round_(count):
+        nonlocal pos, anchor, emitted, tgt
+        # proposals: the target's ids of the previous round shifted in where the acceptor says
+        # "agree", else a different token; the verify decides k exactly as spec.rs does
+        acc = rng.random(nd) < p_acc
+        props = [(int(tgt[i]) if acc[i] else (int(tgt[i]) + 1) % cfg.vocab) for i in range(nd)]
+        ids, _ = m.verify([anchor] + props, pos)
+        k = int(np.argmin(acc)) if not acc.all() else nd   # the acceptor's prefix length
+        m.rollback(pos + k + 1)
+        pos, anchor, tgt = pos + k + 1, ids[k], ids
+        if count:
+            emitted += k + 1
+
+    for _ in range(args.warmup):
+        round_(False)
+    torch.cuda.synchronize(dev)
+    rounds = args.steps
+    with Clocks(0) as clk:
+        t0 = time.perf_counter()
+        for _ in range(rounds):
+            round_(True)
+        t = time.perf_counter() - t0
+    # the verify forward alone, device-timed (one batch of 8 at the current position)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(m.stream)
+    spk.check(spk.lib().spk_model_verify(m.h, (C.c_int * 8)(*([anchor] * 8)), 8, pos, None, None))
+    e1.record(m.stream)
+    e1.synchronize()
+    m.rollback(pos)
+    t_verify = e0.elapsed_time(e1) / 1e3
+    peak, peak_kind = hbm_peak()
+    step_bytes = m.weight_bytes
+    m.close()
+    value = emitted / t
+    line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": 1, "steps": rounds, "warmup": args.warmup,
+            "ms_per_step": t / rounds * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic (seeded random-init target, seeded Bernoulli acceptor)",
+            "config": {"workload": f"config3: speculative verify rounds (M=1+7) of the config-2 target at ctx {ctx}, "
+                                   f"acceptance {p_acc}, draft time not included",
+                       "model": "spark-x2.6-4b geometry, VQ 4x4096x2 trunk, Q8_0 tied head, f16 KV",
+                       "accepted_per_round": emitted / rounds, "verify_ms_device": t_verify * 1e3,
+                       "verify_weight_gbs": step_bytes / t_verify / 1e9},
+            "roofline": {"bound": "hbm", "kernel": "verify forward (VQ mma.sync GEMMs, M=8)",
+                         "achieved": step_bytes / t_verify / 1e9, "peak": peak, "peak_kind": peak_kind,
+                         "unit": "GB/s", "frac": step_bytes / t_verify / 1e9 / peak, "traffic": None},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 32, "d2h_bytes_per_step": 32},
+            "gpu_launches": rounds * (16 + 8 * cfg.layers), "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+
+
 def _gemv_line(args, workload: str, value: float, alg: int, t_launch: float, kernel: str, traffic, extra: dict,
                e2e: float, h2d: int, d2h: int, cb, clk, launches: int) -> dict:
     peak, peak_kind = hbm_peak()
@@ -570,14 +648,16 @@ def main():
     ap.add_argument("--warmup", type=int, default=16)
     ap.add_argument("--ctx", type=int, default=4096)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "long", "vq", "vq-pair", "ggml"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "long", "spec", "vq", "vq-pair", "ggml"],
                     help="decode: config 2 (default); long: config 4 (ctx 131072, q8_0 KV, zeroed KV cache); "
+                         "spec: config 3 verify rounds (ctx 8192, synthetic acceptance); "
                          "vq: config 0 GEMV; vq-pair: the FFN gate+up launch; ggml: config 1 Q6_K/Q8_0 sweep")
     ap.add_argument("--kv", default=None, choices=["f32", "f16", "q8"],
                     help="decode KV cache type (default f16; long: q8)")
     ap.add_argument("--fill-kv", action="store_true",
                     help="decode: start at ctx over a zeroed KV cache instead of running the prompt "
                          "(the same attention bytes per step; for profiler captures)")
+    ap.add_argument("--accept", type=float, default=0.25, help="spec: acceptance probability per proposal")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
     args = ap.parse_args()
     if args.workload == "long":
@@ -589,6 +669,8 @@ def main():
             args.ctx = 131072
         args.kv = args.kv or "q8"
     args.kv = args.kv or "f16"
+    if args.workload == "spec" and args.ctx == 4096:
+        args.ctx = 8192
     if args.warmup < 3:
         ap.error("at least 3 warm-up steps")
     if args.impl == "reference":
@@ -597,6 +679,8 @@ def main():
         run_vq_gemv(args)
     elif args.workload == "ggml":
         run_ggml(args)
+    elif args.workload == "spec":
+        run_spec(args)
     else:
         run_ours(args)
 
