@@ -117,6 +117,12 @@ int spk_q80_gemv(const void *w, int rows, int cols, const float *x, const float 
  * argmax rule model.rs:594-604). Allocates a small per-device workspace on first use. */
 int spk_q80_head(const void *w, int rows, int cols, const float *x, const float *norm_w, float eps, float *logits,
                  int *argmax_out, void *stream);
+/* The head for a verify batch: ntok <= 8 rows of x (stride ldx) in one pass over W;
+ * logits [ntok][ldl], amax[ntok] the first-max index per row (model.rs:594-604; the
+ * reference runs its head GEMV once per row, vq-model-gpu.cu:957-966). Allocates a small
+ * per-device workspace on first use. */
+int spk_q80_head_batch(const void *w, int rows, int cols, int ntok, const float *x, int ldx, const float *norm_w,
+                       float eps, float *logits, int ldl, int *amax, void *stream);
 /* The same head without any allocation. No counterpart in the reference. For callers
  * that cannot call cudaMalloc: code inside a CUDA-graph capture, real-time loops that
  * must not stall on an allocation, and host frameworks that own all device memory.

@@ -80,6 +80,13 @@ int vq_gemv_with_extra(const void *const *stages, int nstg, const Layout &L, con
                        const Layout &XL, const float *x, const float *norm_w, float eps, float *y, float *xy,
                        int accumulate, cudaStream_t s);
 
+// The Q8_0 head for up to 8 token rows in one pass (head_batch.cu), caller scratch:
+// partial >= q80_head_batch_scratch() bytes, counter zeroed once. 1 launched, 0 not taken, -1 error.
+size_t q80_head_batch_scratch();
+int q80_head_batch_launch(const void *w, int rows, int cols, int ntok, const float *x, int ldx, const float *norm_w,
+                          float eps, float *logits, int ldl, int *amax, unsigned long long *partial,
+                          unsigned int *counter, cudaStream_t s);
+
 // Q8_0 head (logits + argmax) with caller-owned scratch (ggml.cu).
 int q80_head_launch(const void *w, int rows, int cols, const float *x, const float *norm_w, float eps, float *logits,
                     int *argmax_out, unsigned long long *partial, unsigned int *counter, cudaStream_t s);

@@ -99,6 +99,8 @@ struct spk_model {
     DevCtl *host_ctl = nullptr;   // pinned staging for it
     unsigned long long *head_partial = nullptr;
     unsigned int *head_counter = nullptr;
+    unsigned long long *vhead_partial = nullptr;   // the verify batch's head
+    unsigned int *vhead_counter = nullptr;
     int *host_io = nullptr;       // pinned: pos, token, argmax; [8..16) verify tokens, [16..24) verify ids
     cudaStream_t stream = nullptr;
     cudaGraph_t graph = nullptr;
@@ -270,7 +272,11 @@ int enqueue_verify(spk_model *m, int ntok) {
         if (tp && tp_sum(m->tpv, m->pbuf, m->h, ntok * H, s)) return -1;
     }
     const uint8_t *head_rows = (const uint8_t *)m->embed + (size_t)m->row0 * (H / 32) * 34;
-    for (int t = 0; t < ntok; t++)
+    // all rows in one pass over the table (head_batch.cu), else row by row
+    const int hb = q80_head_batch_launch(head_rows, m->vocab_l, H, ntok, m->h, H, m->final_norm, c.eps, m->logits,
+                                         m->vocab_l, tp ? vam_l : vam, m->vhead_partial, m->vhead_counter, s);
+    if (hb < 0) return -1;
+    for (int t = 0; hb == 0 && t < ntok; t++)
         if (q80_head_launch(head_rows, m->vocab_l, H, m->h + (size_t)t * H, m->final_norm, c.eps,
                             m->logits + (size_t)t * m->vocab_l, (tp ? vam_l : vam) + t, m->head_partial,
                             m->head_counter, s))
@@ -429,7 +435,9 @@ spk_model *spk_model_create(const spk_model_config *cfg, void *stream) {
               !alloc((void **)&m->state, 32 * sizeof(int), "alloc state") &&
               !alloc((void **)&m->ctl, sizeof(DevCtl), "alloc control") &&
               !alloc((void **)&m->head_partial, 1024 * sizeof(unsigned long long), "alloc head partials") &&
-              !alloc((void **)&m->head_counter, sizeof(unsigned int), "alloc head counter");
+              !alloc((void **)&m->head_counter, sizeof(unsigned int), "alloc head counter") &&
+              !alloc((void **)&m->vhead_partial, q80_head_batch_scratch(), "alloc batched head partials") &&
+              !alloc((void **)&m->vhead_counter, sizeof(unsigned int), "alloc batched head counter");
     if (ok && t == 1) {
         ok = !alloc((void **)&m->logits, R * c.vocab * 4, "alloc logits");
     } else if (ok) {
@@ -460,6 +468,7 @@ spk_model *spk_model_create(const spk_model_config *cfg, void *stream) {
              cudaMemset(m->kc, 0, kv_bytes) == cudaSuccess && cudaMemset(m->vc, 0, kv_bytes) == cudaSuccess &&
              cudaMemset(m->state, 0, 32 * sizeof(int)) == cudaSuccess && cudaMemset(m->ctl, 0, sizeof(DevCtl)) == cudaSuccess &&
              cudaMemset(m->head_counter, 0, sizeof(unsigned int)) == cudaSuccess &&
+             cudaMemset(m->vhead_counter, 0, sizeof(unsigned int)) == cudaSuccess &&
              cudaMemset(m->att_count, 0, (size_t)ATT_MAX_TOK * m->kvl * sizeof(unsigned int)) == cudaSuccess;
         if (!ok) set_error("model initialisation copies failed");
     }
@@ -485,7 +494,7 @@ void spk_model_destroy(spk_model *m) {
         if (m->peer_open[r]) cudaIpcCloseMemHandle(m->peer_open[r]);
     void *ps[] = {m->h, m->qkv, m->gate, m->attn, m->act, m->tp_world > 1 ? nullptr : m->logits, m->part,
                   m->freq_full, m->freq_slide, m->kc, m->vc, m->state, m->ctl, m->head_partial, m->head_counter,
-                  m->mailbox, m->pbuf, m->logits_full, m->tp_seq, m->att_count, m->gbuf, m->vtok};
+                  m->mailbox, m->pbuf, m->logits_full, m->tp_seq, m->att_count, m->gbuf, m->vtok, m->vhead_partial, m->vhead_counter};
     for (void *p : ps)
         if (p) cudaFree(p);
     if (m->host_io) cudaFreeHost(m->host_io);

@@ -20,7 +20,7 @@ namespace {
 constexpr int MW = 32;           // warps per CTA
 constexpr int MTHREADS = MW * 32;
 constexpr int MAXT = 8;          // tokens per batch (the 8 columns of B)
-constexpr int TRR = 16;          // rows per tile (the 16 rows of A)
+constexpr int TRR_MAX = 16;      // rows per tile: the 16 rows of A, or 8 (rows g+8 empty) for long rows
 
 struct MmaArgs {
     const uint8_t *st[2];
@@ -30,7 +30,7 @@ struct MmaArgs {
     float *y;
     int ldx, ldy, ntok;
     int accumulate, mode;   // mode 0: y = (acc ? y : 0) + W x;  mode 1: y = gelu_erf(aux) * (W x)
-    int nbuf, passes;
+    int nbuf, passes, trr;
     uint32_t main_slot, plane_slot, slot_bytes;
     int *err;
 };
@@ -107,6 +107,7 @@ __global__ void __launch_bounds__(MTHREADS, 1) vq_mma_kernel(const MmaArgs a) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
     const int G = gridDim.x;
     const int rb = (int)(((long long)blockIdx.x * L.rows) / G), re = (int)(((long long)(blockIdx.x + 1) * L.rows) / G);
+    const int TRR = a.trr;
     const int ntile = (re - rb + TRR - 1) / TRR;
 
     pdl_trigger();
@@ -159,7 +160,7 @@ __global__ void __launch_bounds__(MTHREADS, 1) vq_mma_kernel(const MmaArgs a) {
         const int r0 = rb + k * TRR, nr = min(TRR, re - r0);
         const bool have = mbar_wait(&full[slot], (uint32_t)((k / NB) & 1), a.err);
         const uint8_t *sb = ring + (size_t)slot * a.slot_bytes;
-        const bool v0 = have && g < nr, v1 = have && g + 8 < nr;
+        const bool v0 = have && g < nr, v1 = have && g + 8 < nr;   // nr <= TRR: rows g+8 exist only at 16
         float d[NSTG][4];
 #pragma unroll
         for (int q = 0; q < NSTG; q++) d[q][0] = d[q][1] = d[q][2] = d[q][3] = 0.f;
@@ -247,7 +248,7 @@ int mma_launch_t(const MmaArgs &A, size_t smem, cudaStream_t s) {
         if (e != cudaSuccess) return cuda_fail("vq mma kernel shared-memory opt-in", e);
         opted[dev & 63] = smem;
     }
-    const int ntr = (A.L.rows + TRR - 1) / TRR;
+    const int ntr = (A.L.rows + A.trr - 1) / A.trr;
     const int grid = ntr < sm_count() ? ntr : sm_count();
     cudaError_t e = launch_pdl(k, dim3(grid), dim3(MTHREADS), smem, s, A);
     return e == cudaSuccess ? 0 : cuda_fail("vq mma kernel launch", e);
@@ -296,10 +297,14 @@ int vq_mma_batch(const void *const *stages, int nstg, const Layout &L, int ntok,
     if (((uintptr_t)x & 15) || (ldx & 3) || (norm_w && ((uintptr_t)norm_w & 15))) return 0;
     const size_t cb = (((size_t)nstg * L.nc * 8 + 15) & ~(size_t)15);
     const size_t fixed = cb + (size_t)nstg * MW * 16 * 8 * 4 + MAXT * 4;
-    const uint32_t main_slot = (uint32_t)(((size_t)TRR * L.mrow + 32 + 15) & ~(size_t)15);
-    const uint32_t plane_slot = L.prow ? (uint32_t)(((size_t)TRR * L.prow + 32 + 15) & ~(size_t)15) : 0u;
+    // 16-row tiles, else 8-row tiles (half the A rows empty: the gathers, not the MMAs, bound
+    // the kernel) where a 16-row ring does not fit shared memory (long rows: down_proj)
+    for (int c = 0; c < 4; c++) {
+    const int trr = c < 2 ? TRR_MAX : TRR_MAX / 2, nb = 3 - (c & 1);
+    const uint32_t main_slot = (uint32_t)(((size_t)trr * L.mrow + 32 + 15) & ~(size_t)15);
+    const uint32_t plane_slot = L.prow ? (uint32_t)(((size_t)trr * L.prow + 32 + 15) & ~(size_t)15) : 0u;
     const uint32_t slot = nstg * (main_slot + plane_slot);
-    for (int nb = 3; nb >= 2; nb--) {
+    {
         const size_t smem = ((fixed + 15) & ~(size_t)15) + (size_t)nb * slot + 2 * (size_t)nb * 8;
         if (smem > smem_optin_max()) continue;
         MmaArgs A;
@@ -317,6 +322,7 @@ int vq_mma_batch(const void *const *stages, int nstg, const Layout &L, int ntok,
         A.accumulate = accumulate;
         A.mode = mode;
         A.nbuf = nb;
+        A.trr = trr;
         A.passes = per / S;
         A.main_slot = main_slot;
         A.plane_slot = plane_slot;
@@ -324,6 +330,7 @@ int vq_mma_batch(const void *const *stages, int nstg, const Layout &L, int ntok,
         A.err = device_error_ptr();
         const int rc = nstg == 1 ? mma_launch_s<1>(S, A, smem, s) : mma_launch_s<2>(S, A, smem, s);
         return rc ? -1 : 1;
+    }
     }
     return 0;
 }

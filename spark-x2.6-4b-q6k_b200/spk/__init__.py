@@ -65,6 +65,7 @@ _PROTOS = {
     "spk_attn_workspace_bytes": ([_i, _i, _i, _i, _i], C.c_size_t),
     "spk_attn_decode": ([_vp, _vp], _i),
     "spk_attn_store": ([_vp, _vp], _i),
+    "spk_q80_head_batch": ([_vp, _i, _i, _i, _vp, _i, _vp, _f, _vp, _i, _vp, _vp], _i),
     "spk_model_create": ([_vp, _vp], _vp),
     "spk_model_destroy": ([_vp], None),
     "spk_model_set_layer": ([_vp, _i] + [_vp] * 8, _i),

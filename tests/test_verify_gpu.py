@@ -133,3 +133,38 @@ def test_verify_rejects_bad_inputs(small):
     with pytest.raises(spk.SpkError):
         dev.verify([1] * 8, 12)  # past the cache
     dev.close()
+
+
+@pytest.mark.parametrize("ntok", [1, 3, 8])
+@pytest.mark.parametrize("rows,cols", [(131072, 2560), (1000, 512), (300, 1000)])
+def test_q80_head_batch_matches_per_row_head(cuda, ntok, rows, cols):
+    """spk_q80_head_batch (one pass, tensor cores) against spk_q80_head run row by row:
+    logits within GEMM_TOL and the same greedy ids (cols 1000 takes the per-row path)."""
+    import torch
+
+    import spk
+
+    L = spk.lib()
+    w = spk.dev_bytes(F.synth_q8_0(rows, cols, seed=ntok), cuda)
+    rng = np.random.default_rng(rows + ntok)
+    x = torch.from_numpy(rng.normal(0, 1, (ntok, cols)).astype(np.float32)).to(cuda)
+    nw = torch.from_numpy((1 + 0.1 * rng.normal(0, 1, cols)).astype(np.float32)).to(cuda)
+    lg = torch.zeros(ntok, rows, device=cuda)
+    am = torch.zeros(ntok, dtype=torch.int32, device=cuda)
+    ref = torch.zeros(ntok, rows, device=cuda)
+    ram = torch.zeros(ntok, dtype=torch.int32, device=cuda)
+    torch.cuda.synchronize()
+    for n in range(ntok):
+        spk.check(L.spk_q80_head(w.data_ptr(), rows, cols, x[n].data_ptr(), nw.data_ptr(), 1e-6, ref[n].data_ptr(),
+                                 ram[n:].data_ptr(), None))
+    for _ in range(2):   # the ticket is left reset for the next call
+        spk.check(L.spk_q80_head_batch(w.data_ptr(), rows, cols, ntok, x.data_ptr(), cols, nw.data_ptr(), 1e-6,
+                                       lg.data_ptr(), rows, am.data_ptr(), None))
+        torch.cuda.synchronize()
+        for n in range(ntok):
+            assert rel(lg[n].cpu().numpy(), ref[n].cpu().numpy()) < GEMM_TOL
+        a, b = am.cpu().numpy(), ram.cpu().numpy()
+        for n in range(ntok):
+            if a[n] != b[n]:   # only a near-tie may differ
+                r = ref[n].cpu().numpy()
+                assert abs(r[a[n]] - r[b[n]]) < 1e-5 * abs(r[b[n]]) + 1e-6
