@@ -136,10 +136,10 @@ def test_verify_rejects_bad_inputs(small):
 
 
 @pytest.mark.parametrize("ntok", [1, 3, 8])
-@pytest.mark.parametrize("rows,cols", [(131072, 2560), (1000, 512), (300, 1000)])
+@pytest.mark.parametrize("rows,cols", [(131072, 2560), (1000, 512), (300, 992)])
 def test_q80_head_batch_matches_per_row_head(cuda, ntok, rows, cols):
     """spk_q80_head_batch (one pass, tensor cores) against spk_q80_head run row by row:
-    logits within GEMM_TOL and the same greedy ids (cols 1000 takes the per-row path)."""
+    logits within GEMM_TOL and the same greedy ids (cols 992 takes the per-row path)."""
     import torch
 
     import spk
