@@ -101,8 +101,9 @@ __global__ void __launch_bounds__(MTHREADS, 1) vq_mma_kernel(const MmaArgs a) {
     uint8_t *ring = smem + (((size_t)NSTG * nc * 8 + 15) & ~(size_t)15);
     uint64_t *full = reinterpret_cast<uint64_t *>(ring + (size_t)NB * a.slot_bytes);
     uint64_t *empty = full + NB;
-    float *part = reinterpret_cast<float *>(empty + NB);   // [NSTG][MW][16][8]
-    float *inv = part + NSTG * MW * 16 * 8;                // [MAXT]
+    float *part = reinterpret_cast<float *>(empty + NB);   // [NSTG][MW][16 rows x 8 columns]
+    float *red = part + NSTG * MW * 16 * 8;                // [NSTG][8 warp groups][16 x 8]
+    float *inv = red + NSTG * 8 * 16 * 8;                  // [MAXT]
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
     const int G = gridDim.x;
@@ -158,6 +159,17 @@ __global__ void __launch_bounds__(MTHREADS, 1) vq_mma_kernel(const MmaArgs a) {
                 mma_issue(a, NSTG, ring + (size_t)sn * a.slot_bytes, &full[sn], r0n, min(TRR, re - r0n));
         }
         const int r0 = rb + k * TRR, nr = min(TRR, re - r0);
+        // the epilogue's per-row operands, fetched now so their latency hides under the tile
+        const int orl = tid >> 3, on_ = tid & 7;   // output (row orl, column on_) for tid < 128
+        const bool oown = tid < 128 && orl < nr && (TWO ? on_ : (on_ & 3)) < a.ntok && (TWO || on_ < 4);
+        float og[NSTG], oy = 0.f;
+        if (oown) {
+#pragma unroll
+            for (int q = 0; q < NSTG; q++)
+                og[q] = h2f_u16(*reinterpret_cast<const uint16_t *>(a.st[q] + L.gain_off + 2 * (size_t)(r0 + orl)));
+            if (a.mode == 1) oy = a.aux[(size_t)on_ * a.ldy + r0 + orl];
+            else if (a.accumulate) oy = a.y[(size_t)on_ * a.ldy + r0 + orl];
+        }
         const bool have = mbar_wait(&full[slot], (uint32_t)((k / NB) & 1), a.err);
         const uint8_t *sb = ring + (size_t)slot * a.slot_bytes;
         const bool v0 = have && g < nr, v1 = have && g + 8 < nr;   // nr <= TRR: rows g+8 exist only at 16
@@ -213,27 +225,42 @@ __global__ void __launch_bounds__(MTHREADS, 1) vq_mma_kernel(const MmaArgs a) {
             pw[(g + 8) * 8 + 2 * t + 1] = d[q][3];
         }
         __syncthreads();
-        for (int idx = tid; idx < nr * a.ntok; idx += MTHREADS) {
-            const int rl = idx / a.ntok, n = idx - rl * a.ntok, r = r0 + rl;
-            float o = (a.mode == 0 && a.accumulate) ? a.y[(size_t)n * a.ldy + r] : 0.0f;
+        // Phase 1, every thread: element e = tid & 127 of the 16 x 8 tile, summed over the
+        // 4 warps of group tid >> 7 per stage (a warp reads 32 consecutive floats: no bank
+        // conflict). Phase 2, thread e < 128: the 8 groups in order, gains, epilogue.
+        {
+            const int e = tid & 127, wg = tid >> 7;
+#pragma unroll
+            for (int q = 0; q < NSTG; q++) {
+                const float *pq = part + ((size_t)q * MW + wg * (MW / 8)) * 16 * 8 + e;
+                float v = 0.f;
+#pragma unroll
+                for (int w = 0; w < MW / 8; w++) v += pq[(size_t)w * 16 * 8];
+                red[((size_t)q * 8 + wg) * 16 * 8 + e] = v;
+            }
+        }
+        __syncthreads();
+        if (oown) {
+            float o = (a.mode == 0 && a.accumulate) ? oy : 0.0f;
 #pragma unroll
             for (int q = 0; q < NSTG; q++) {
                 float v = 0.f;
-                for (int w = 0; w < MW; w++) {
-                    const float *pw = part + ((size_t)q * MW + w) * 16 * 8 + rl * 8;
-                    v += TWO ? pw[n] : (pw[n] + pw[n + 4]);
+#pragma unroll
+                for (int w = 0; w < 8; w++) {
+                    const float *rw = red + ((size_t)q * 8 + w) * 16 * 8 + orl * 8;
+                    v += TWO ? rw[on_] : (rw[on_] + rw[on_ + 4]);
                 }
-                const float gq = h2f_u16(*reinterpret_cast<const uint16_t *>(a.st[q] + L.gain_off + 2 * (size_t)r));
-                o = __fadd_rn(o, __fmul_rn(v, gq));
+                o = __fadd_rn(o, __fmul_rn(v, og[q]));
             }
             if (a.mode == 1) {
-                const float gv = a.aux[(size_t)n * a.ldy + r];
-                const double e = erf((double)gv * 0.70710678118654752440);
-                o = __fmul_rn(__fmul_rn(__fmul_rn(0.5f, gv), __fadd_rn(1.0f, (float)e)), o);
+                const double e = erf((double)oy * 0.70710678118654752440);
+                o = __fmul_rn(__fmul_rn(__fmul_rn(0.5f, oy), __fadd_rn(1.0f, (float)e)), o);
             }
-            a.y[(size_t)n * a.ldy + r] = o;
+            a.y[(size_t)on_ * a.ldy + r0 + orl] = o;
         }
-        __syncthreads();   // the partials are reused by the next tile
+        // no third barrier: the next tile writes the partials only after every warp has
+        // passed the barrier above (phase 1 done), and phase 2 reads only `red`, which the
+        // next tile rewrites after its own first barrier
     }
 }
 
@@ -296,7 +323,7 @@ int vq_mma_batch(const void *const *stages, int nstg, const Layout &L, int ntok,
         if (((uintptr_t)stages[q] & 7) != 0) return 0;
     if (((uintptr_t)x & 15) || (ldx & 3) || (norm_w && ((uintptr_t)norm_w & 15))) return 0;
     const size_t cb = (((size_t)nstg * L.nc * 8 + 15) & ~(size_t)15);
-    const size_t fixed = cb + (size_t)nstg * MW * 16 * 8 * 4 + MAXT * 4;
+    const size_t fixed = cb + (size_t)nstg * MW * 16 * 8 * 4 + (size_t)nstg * 8 * 16 * 8 * 4 + MAXT * 4;
     // 16-row tiles, else 8-row tiles (half the A rows empty: the gathers, not the MMAs, bound
     // the kernel) where a 16-row ring does not fit shared memory (long rows: down_proj)
     for (int c = 0; c < 4; c++) {
