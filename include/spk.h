@@ -256,8 +256,9 @@ int spk_model_trace(spk_model *m, float *us, int cap);
 
 /* Tensor-parallel wiring (no counterpart in the reference). Each rank's model owns a
  * mailbox in device memory; the residual reductions and the head's argmax store rows
- * into every rank's mailbox over NVLink and wait on release flags there, bounded by
- * wait_ms (a wait that runs out sets a device error that spk_model_forward reports).
+ * into every rank's mailbox over NVLink as (value, sequence) pairs and wait until every
+ * rank's pairs carry the exchange's sequence, bounded by wait_ms (a wait that runs out
+ * sets a device error that spk_model_forward reports).
  * spk_model_tp_handle writes the mailbox's cudaIpcMemHandle_t (n >= 64 bytes);
  * spk_model_tp_attach takes every rank's handle in rank order (n = 64 * tp_world);
  * spk_model_tp_attach_ptrs takes the mailboxes as pointers valid in this process (one
@@ -269,6 +270,81 @@ int spk_model_tp_attach(spk_model *m, const void *handles, int n, int wait_ms);
 int spk_model_tp_attach_ptrs(spk_model *m, void *const *mailboxes, int world, int wait_ms);
 /* This rank's mailbox pointer (for spk_model_tp_attach_ptrs). */
 void *spk_model_tp_mailbox(spk_model *m);
+
+/* Model::enable_capture / captured (model.rs:322-348): from the next step on, the residual
+ * entering each listed layer is written at every position the decode step and the verify
+ * batch visit, into device memory [n][max_ctx][hidden] (slot k of position p at
+ * spk_model_captures(m, &stride)[k * stride + p * hidden]). At most 8 layers; n = 0 turns
+ * capture off. Rollback needs no action: later positions are rewritten when revisited. */
+int spk_model_enable_capture(spk_model *m, const int *layers, int n);
+const float *spk_model_captures(spk_model *m, size_t *slot_stride);
+
+/* ------------------------------------------------ DSpark draft (row D) ---
+ * The draft executor of tools/dspark/src/draft.rs (encode_features 567-628,
+ * decode_block 641-901), replacing the reference's GPU executor (dspark-gpu.h:914-1152:
+ * cuBLAS SGEMM on f32-expanded weights, a host sync per Markov row). BF16 weights are
+ * borrowed device pointers, row-major out x in (the manifest's GGUF shapes read as
+ * [ne1][ne0]); f32 vectors; NULL marks an absent optional tensor. */
+#define SPK_DRAFT_MAX_LAYERS 32
+
+/* The manifest header (tools/dspark/src/manifest.rs:84-110) plus the cache capacity. */
+typedef struct {
+    int hidden, layers, heads, kv_heads, head_dim, ffn, vocab, mask_token;
+    int rope_full_dims, rope_swa_dims;
+    float rope_full_theta, rope_swa_theta, eps;
+    int act;          /* 0: gelu (ggml's tanh form), 1: silu */
+    int swa_window, causal, block_size, sample_from_anchor;
+    int n_target;     /* target capture layers the encoder concatenates (fc: [hidden][n_target*hidden]) */
+    int rank;         /* Markov rank (markov_w1/w2 [vocab][rank]); 0 = no Markov head */
+    int max_ctx;      /* draft cache positions */
+    int swa_pattern[SPK_DRAFT_MAX_LAYERS];   /* per layer: 1 = sliding-window rope */
+} spk_draft_config;
+
+/* draft.rs:243-259 DraftLayer. Optional: gate, q_norm/k_norm (used together, as the
+ * reference does), attn_post, ffn_post; out_scale 0 = none. */
+typedef struct {
+    const void *q, *k, *v, *gate, *out, *ffn_gate, *ffn_up, *ffn_down;   /* bf16 */
+    const float *norm, *q_norm, *k_norm, *ffn_norm, *attn_post, *ffn_post;
+    float out_scale;
+} spk_draft_layer;
+
+/* draft.rs:261-272 globals. conf_proj is f32 [hidden + rank], or NULL. */
+typedef struct {
+    const void *fc;                      /* bf16 [hidden][n_target * hidden] */
+    const float *fc_norm;                /* [n_target][hidden] */
+    const float *enc_norm, *out_norm;
+    const void *markov_w1, *markov_w2;   /* bf16 [vocab][rank] */
+    const float *conf_proj;
+    float conf_bias;
+} spk_draft_globals;
+
+typedef struct spk_draft spk_draft;
+
+/* Draft::open's device state: the injected K/V cache and scratch, on the current device. */
+spk_draft *spk_draft_create(const spk_draft_config *cfg, void *stream);
+void spk_draft_destroy(spk_draft *d);
+int spk_draft_set_layer(spk_draft *d, int layer, const spk_draft_layer *w);
+int spk_draft_set_globals(spk_draft *d, const spk_draft_globals *g);
+/* encode_features for the committed positions [p0, p1) from the target's layer-input
+ * captures (device; slot k of position p at caps[k * slot_stride + p * hidden]). */
+int spk_draft_encode(spk_draft *d, const float *caps, size_t slot_stride, int p0, int p1);
+/* decode_block over the target's Q8_0 embedding [vocab][hidden] (device): ids (host,
+ * n_block) get the greedy argmax of every block row after the Markov bias, conf (host,
+ * optional) the confidence head (NaN where the reference leaves it). Returns n_block
+ * (n_draft with sample_from_anchor and a Markov head, else n_draft + 1) or -1.
+ * The injected window before pos0 must be encoded. Synchronizes the draft's stream. */
+int spk_draft_block(spk_draft *d, const void *embed, int vocab, int anchor, int pos0, int n_draft, int *ids,
+                    float *conf);
+/* The last block's biased logits, [n_block][vocab] f32 on device. */
+const float *spk_draft_logits(const spk_draft *d);
+
+/* The draft's skinny BF16 GEMM (dspark-gpu.h:897-907 draft_gemm): y[n*ldy + r] (=, or +=)
+ * (W x[n*ldx ..])[r] for n < ntok <= 8; W bf16 [rows][cols], 16-byte aligned, cols % 32 == 0. */
+int spk_bf16_gemm(const void *w, int rows, int cols, int ntok, const float *x, int ldx, float *y, int ldy,
+                  int accumulate, void *stream);
+/* The FFN pair y = act(G x) * (U x), act 0 = gelu (tanh form), 1 = silu (draft.rs:838-855). */
+int spk_bf16_gemm_pair(const void *gate, const void *up, int rows, int cols, int ntok, const float *x, int ldx,
+                       float *y, int ldy, int act, void *stream);
 
 #ifdef __cplusplus
 }

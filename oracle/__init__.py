@@ -57,6 +57,18 @@ def lib():
         L.orc_model_forward.argtypes = [C.c_void_p, C.c_uint32, C.c_int, _f32p]
         L.orc_model_forward.restype = C.c_int
         L.orc_model_fill_kv.argtypes = [C.c_void_p, C.c_int, C.c_uint64]
+        L.orc_model_capture.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]
+        L.orc_model_capture.restype = C.c_int
+        L.orc_draft_new.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int]
+        L.orc_draft_new.restype = C.c_void_p
+        L.orc_draft_free.argtypes = [C.c_void_p]
+        L.orc_draft_encode.argtypes = [C.c_void_p, _f32p, C.c_size_t, C.c_int, C.c_int]
+        L.orc_draft_encode.restype = C.c_int
+        L.orc_draft_decode_block.argtypes = [C.c_void_p, _f32p, C.c_int, C.c_uint32, C.c_int, C.c_int, _f32p, _f32p,
+                                             np.ctypeslib.ndpointer(np.uint32, flags="C_CONTIGUOUS")]
+        L.orc_draft_decode_block.restype = C.c_int
+        L.orc_draft_block_rows.argtypes = [C.c_void_p, C.c_int, C.c_int]
+        L.orc_draft_block_rows.restype = C.c_int
         _lib = L
     return _lib
 
@@ -200,6 +212,7 @@ class Model:
         self.embed = np.ascontiguousarray(embed, np.float32)
         self.norm = np.ascontiguousarray(norm, np.float32)
         self.vocab = cfg["vocab"]
+        self.hidden, self.max_ctx = cfg["hidden"], max_ctx
         self._keep += [c, arr]
         self.h = lib().orc_model_new(C.byref(c), arr, self.embed, self.norm, max_ctx, threads or threads_default())
         if not self.h:
@@ -211,6 +224,15 @@ class Model:
             raise ValueError(f"forward({token}, {pos}) rejected")
         return out
 
+    def enable_capture(self, layers: list[int]) -> np.ndarray:
+        """model.rs::enable_capture: the residual entering each listed layer is written, at
+        every forward position, to the returned [len(layers)][max_ctx][hidden] array."""
+        self.cap_layers = (C.c_int * len(layers))(*layers)
+        self.cap = np.zeros((len(layers), self.max_ctx, self.hidden), np.float32)
+        if lib().orc_model_capture(self.h, self.cap_layers, len(layers), self.cap.ctypes.data):
+            raise ValueError(f"capture layers {layers} rejected")
+        return self.cap
+
     def fill_kv(self, n: int, seed: int = 0):
         """Seeded K/V for the first n positions (CPU-baseline samples at long context)."""
         lib().orc_model_fill_kv(self.h, n, seed)
@@ -218,6 +240,97 @@ class Model:
     def close(self):
         if self.h:
             lib().orc_model_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+
+# ------------------------------------------------------------------ DSpark draft ---
+class _DraftCfg(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("hidden", "layers", "heads", "kv_heads", "head_dim", "ffn", "vocab",
+                                        "mask_token", "rope_full_dims", "rope_swa_dims")] + \
+               [(n, C.c_float) for n in ("rope_full_theta", "rope_swa_theta", "eps")] + \
+               [(n, C.c_int) for n in ("act", "swa_window", "causal", "block_size", "sample_from_anchor",
+                                        "n_target")] + [("swa_pattern", C.c_void_p)]
+
+
+_DRAFT_LAYER_F = ("norm", "q", "k", "v", "gate", "out", "q_norm", "k_norm", "ffn_norm", "ffn_gate", "ffn_up",
+                  "ffn_down", "attn_post", "ffn_post")
+
+
+class _DraftLayer(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in _DRAFT_LAYER_F] + [("out_scale", C.c_float)]
+
+
+class _DraftGlobals(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in ("fc", "fc_norm", "enc_norm", "out_norm", "markov_w1", "markov_w2",
+                                          "conf_proj")] + [("conf_bias", C.c_float), ("rank", C.c_int)]
+
+
+class Draft:
+    """draft.rs Draft over f32 weights (BF16 tensors expanded exactly). ``cfg`` holds the
+    manifest header fields (oracle_draft.h); ``layers`` is a list of dicts keyed like
+    DraftLayer (optional tensors absent or None); ``glob`` holds fc, fc_norm [n_target][hidden],
+    enc_norm, out_norm and optionally markov_w1/markov_w2 [vocab][rank], conf_proj, conf_bias."""
+
+    def __init__(self, cfg: dict, layers: list[dict], glob: dict, max_ctx: int, threads: int | None = None):
+        self._keep = []
+        self.cfg = dict(cfg)
+        swa = (C.c_int * cfg["layers"])(*[int(v) for v in cfg["swa_pattern"]])
+        c = _DraftCfg(*[int(cfg[n]) for n in ("hidden", "layers", "heads", "kv_heads", "head_dim", "ffn", "vocab",
+                                              "mask_token", "rope_full_dims", "rope_swa_dims")],
+                      *[float(cfg[n]) for n in ("rope_full_theta", "rope_swa_theta", "eps")],
+                      *[int(cfg[n]) for n in ("act", "swa_window", "causal", "block_size", "sample_from_anchor",
+                                              "n_target")], C.cast(swa, C.c_void_p))
+        arr = (_DraftLayer * cfg["layers"])()
+        for i, L in enumerate(layers):
+            for n in _DRAFT_LAYER_F:
+                setattr(arr[i], n, self._ptr(L.get(n)))
+            arr[i].out_scale = float(L.get("out_scale", 0.0))
+        g = _DraftGlobals(*[self._ptr(glob.get(n)) for n in ("fc", "fc_norm", "enc_norm", "out_norm", "markov_w1",
+                                                              "markov_w2", "conf_proj")],
+                          float(glob.get("conf_bias", 0.0)),
+                          int(glob["markov_w1"].shape[1]) if glob.get("markov_w1") is not None else 0)
+        self.has_markov = glob.get("markov_w1") is not None and glob.get("markov_w2") is not None
+        self._keep += [swa, c, arr, g]
+        self._c = c
+        self.h = lib().orc_draft_new(C.byref(c), arr, C.byref(g), max_ctx, threads or threads_default())
+        if not self.h:
+            raise MemoryError("oracle draft allocation failed")
+
+    def _ptr(self, a):
+        if a is None:
+            return None
+        a = np.ascontiguousarray(a, np.float32)
+        self._keep.append(a)
+        return a.ctypes.data
+
+    def block_rows(self, n_draft: int) -> int:
+        return lib().orc_draft_block_rows(C.byref(self._c), int(self.has_markov), n_draft)
+
+    def encode(self, caps: np.ndarray, p0: int, p1: int):
+        """encode_features for positions [p0, p1) of caps [n_target][ctx][hidden]."""
+        caps = np.ascontiguousarray(caps, np.float32)
+        if lib().orc_draft_encode(self.h, caps.reshape(-1), caps.shape[1] * caps.shape[2], p0, p1):
+            raise ValueError(f"encode [{p0}, {p1}) rejected")
+
+    def decode_block(self, embed: np.ndarray, anchor: int, pos0: int, n_draft: int):
+        """(logits [n_block][vocab], conf [n_block], argmax [n_block]) of decode_block."""
+        vocab = embed.shape[0]
+        nb = self.block_rows(n_draft)
+        lg = np.zeros((max(nb, 1), vocab), np.float32)
+        cf = np.zeros(max(nb, 1), np.float32)
+        am = np.zeros(max(nb, 1), np.uint32)
+        e = np.ascontiguousarray(embed, np.float32)
+        rc = lib().orc_draft_decode_block(self.h, e.reshape(-1), vocab, anchor, pos0, n_draft, lg.reshape(-1), cf, am)
+        if rc < 0:
+            raise ValueError(f"decode_block(anchor {anchor}, pos0 {pos0}, n_draft {n_draft}) rejected")
+        return lg[:rc], cf[:rc], am[:rc]
+
+    def close(self):
+        if self.h:
+            lib().orc_draft_free(self.h)
             self.h = None
 
     def __del__(self):

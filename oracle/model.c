@@ -22,6 +22,8 @@ struct orc_model {
     float *kv_k, *kv_v;   /* [layers][max_ctx][kv_dim] */
     float *h, *xn, *qkv, *gate, *attn, *o, *g, *u, *act, *cos, *sin;
     int *full;
+    int *cap_slot;   /* per layer: capture slot or -1 (model.rs:322-343) */
+    float *cap;      /* [slots][max_ctx][hidden] */
 };
 
 static void *xcalloc(size_t n, size_t s) { return calloc(n ? n : 1, s); }
@@ -36,6 +38,8 @@ orc_model *orc_model_new(const orc_cfg *c, const orc_layer *layers, const float 
     memcpy(m->L, layers, (size_t)c->layers * sizeof(orc_layer));
     memcpy(m->full, c->full, (size_t)c->layers * sizeof(int));
     m->c.full = m->full;
+    m->cap_slot = (int *)xcalloc((size_t)c->layers, sizeof(int));
+    for (int l = 0; l < c->layers; l++) m->cap_slot[l] = -1;
     m->embed = embed;
     m->norm = norm;
     m->max_ctx = max_ctx;
@@ -65,6 +69,7 @@ void orc_model_free(orc_model *m) {
     if (!m) return;
     free(m->L);
     free(m->full);
+    free(m->cap_slot);
     free(m->kv_k);
     free(m->kv_v);
     free(m->h);
@@ -125,6 +130,10 @@ int orc_model_forward(orc_model *m, uint32_t token, int pos, float *logits) {
     memcpy(m->h, m->embed + (size_t)token * hidden, (size_t)hidden * sizeof(float));
     for (int li = 0; li < c->layers; li++) {
         const orc_layer *L = &m->L[li];
+        /* the residual entering the layer (model.rs:466-472) */
+        if (m->cap && m->cap_slot[li] >= 0)
+            memcpy(m->cap + ((size_t)m->cap_slot[li] * m->max_ctx + (size_t)pos) * hidden, m->h,
+                   (size_t)hidden * sizeof(float));
         rope_table(m, pos, li);
         orc_rms_norm(m->h, L->in_norm, c->eps, (size_t)hidden, m->xn);
         orc_matvec(L->qkv, qd + 2 * kvd, (size_t)hidden, m->xn, m->qkv, threads);
@@ -187,6 +196,22 @@ int orc_model_forward(orc_model *m, uint32_t token, int pos, float *logits) {
 }
 
 /* model.rs:361-382 — positions >= pos are simply overwritten later. */
+/* model.rs:322-343: layer-input capture for the listed layers into dst [n][max_ctx][hidden]
+ * (caller-owned); -1 on a layer outside the model or listed twice. */
+int orc_model_capture(orc_model *m, const int *layers, int n, float *dst) {
+    for (int l = 0; l < m->c.layers; l++) m->cap_slot[l] = -1;
+    m->cap = NULL;
+    for (int k = 0; k < n; k++) {
+        if (layers[k] < 0 || layers[k] >= m->c.layers || m->cap_slot[layers[k]] >= 0) {
+            for (int l = 0; l < m->c.layers; l++) m->cap_slot[l] = -1;
+            return -1;
+        }
+        m->cap_slot[layers[k]] = k;
+    }
+    m->cap = n > 0 ? dst : NULL;
+    return 0;
+}
+
 int orc_model_rollback(orc_model *m, int pos) { return (pos < 0 || pos > m->max_ctx) ? -1 : 0; }
 
 /* The hidden state entering the final norm, for debugging parity. */

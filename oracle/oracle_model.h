@@ -30,6 +30,7 @@ void orc_model_free(orc_model *m);
 /* model.rs:442-591: logits (vocab f32) of the token at pos. */
 int orc_model_forward(orc_model *m, uint32_t token, int pos, float *logits);
 int orc_model_rollback(orc_model *m, int pos);
+int orc_model_capture(orc_model *m, const int *layers, int n, float *dst);
 int orc_rope_dim(const orc_cfg *c, int layer);
 const float *orc_model_hidden(const orc_model *m);
 void orc_model_fill_kv(orc_model *m, int n, uint64_t seed);

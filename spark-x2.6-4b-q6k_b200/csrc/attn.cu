@@ -124,10 +124,13 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnArgs a) {
     const int G = a.heads / a.kv_heads;
     const int qd = a.heads * HD, kvd = a.kv_heads * HD;
     const int pos = *a.pos + tok;
-    const int start = a.full ? 0 : max(0, pos + 1 - a.window);
-    const int n = pos + 1 - start;
+    // causal: token t reads [start, pos]; a block (span > 0) reads the anchor row's keys,
+    // the window before pos0 and the block's span rows, whatever its own row
+    const int last = a.span > 0 ? *a.pos + a.span - 1 : pos;
+    const int start = a.full ? 0 : max(0, (a.span > 0 ? *a.pos : pos) + 1 - a.window);
+    const int n = last + 1 - start;
     const int csz = max((n + a.nsplit - 1) / a.nsplit, 16);
-    const int c0 = start + split * csz, c1 = min(pos + 1, c0 + csz);
+    const int c0 = start + split * csz, c1 = min(last + 1, c0 + csz);
     const float *qrow = a.qkv + (size_t)tok * a.ldqkv;
     const size_t pbase = ((size_t)tok * a.kv_heads + kvh) * a.nsplit;   // this (token, KV head)'s splits
     constexpr int PR = HD + 4;   // a partial row: o[HD], m, l, 2 pad (16-byte rows)
@@ -171,7 +174,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnArgs a) {
                 if (j >= c1) {
 #pragma unroll
                     for (int d = 0; d < DPL; d++) kr[u][d] = vr[u][d] = 0.f;
-                } else if (j == pos) {   // this token's own row: f32, before the cache's rounding
+                } else if (j == pos && a.span == 0) {   // this token's own row: f32, before the cache's rounding
 #pragma unroll
                     for (int d = 0; d < DPL; d++) {
                         kr[u][d] = kn[lane * DPL + d];

@@ -32,6 +32,8 @@ struct AttnArgs {
     const int *pos;            // device position of token 0; token t sits at pos + t
     int ntok;                  // grid.z
     int store;                 // 1: the kernel writes each token's K/V row itself (ntok 1)
+    int span;                  // 0: causal rows; > 0: every row reads [pos0 + 1 - window, pos0 + span - 1]
+                               // (a non-causal draft block whose rows sit at pos0 .. pos0 + span - 1)
     int nsplit;                // grid.y: sequence splits
     float *part;               // [ntok][kv_heads][nsplit][group][hd + 4]: o, m, l (+2 pad) per split
     unsigned int *count;       // [ntok][kv_heads], zero; the last split of each resets its own

@@ -43,6 +43,18 @@ struct DevCtl {
     int cap;
 };
 
+// The residual rows entering a layer (ntok rows of h) into its capture slot at positions
+// *pos + t (model.rs:466-472, the layer-input rows the draft encoder reads).
+__global__ void capture_kernel(const float *h, int H, int ntok, const int *pos, float *dst) {
+    pdl_trigger();
+    pdl_wait();
+    const size_t p = (size_t)*pos;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < ntok * H; i += gridDim.x * blockDim.x) {
+        const int t = i / H;
+        dst[(p + t) * H + (i - t * H)] = h[i];
+    }
+}
+
 __global__ void advance_kernel(int *pos, int *token, const int *argmax, const DevCtl *ctl, int *step) {
     pdl_trigger();
     pdl_wait();
@@ -112,6 +124,9 @@ struct spk_model {
     cudaGraphExec_t texec = nullptr;
     int eager_steps = 0;
     int len = 0;                  // positions cached (host view, for rollback checks)
+    std::vector<int> cap_slot;    // per layer: capture slot or -1
+    float *cap = nullptr;         // [ncap][max_ctx][hidden]
+    int ncap = 0;
 };
 
 namespace {
@@ -171,6 +186,17 @@ AttnArgs attn_args(spk_model *m, int li, int ntok) {
     return a;
 }
 
+// Layer li's input rows into its capture slot, when capture is on (no trace mark: the
+// copy is counted with the launch after it).
+int capture_rows(spk_model *m, int li, int ntok, cudaStream_t s) {
+    if (!m->ncap || m->cap_slot[li] < 0) return 0;
+    const int H = m->cfg.hidden;
+    float *dst = m->cap + (size_t)m->cap_slot[li] * m->cfg.max_ctx * H;
+    cudaError_t e = launch_pdl(capture_kernel, dim3((ntok * H + 255) / 256), dim3(256), 0, s, (const float *)m->h, H,
+                               ntok, (const int *)m->state, dst);
+    return e == cudaSuccess ? 0 : cuda_fail("layer capture launch", e);
+}
+
 // Under spk_model_trace's capture: an event after the launch just enqueued.
 int mark(spk_model *m) {
     if (!m->tracing) return 0;
@@ -188,6 +214,7 @@ int enqueue_step(spk_model *m) {
     if (mark(m) || spk_q80_row(m->embed, c.vocab, c.hidden, 0, token, m->h, s) || mark(m)) return -1;
     for (int li = 0; li < c.layers; li++) {
         const spk_model::Layer &L = m->layers[li];
+        if (capture_rows(m, li, 1, s)) return -1;
         if (qkv_gate(L, m->h, c.eps, m->qkv, m->gate, s) || mark(m)) return -1;
         AttnArgs a = attn_args(m, li, 1);
         a.store = 1;
@@ -259,6 +286,7 @@ int enqueue_verify(spk_model *m, int ntok) {
         if (spk_q80_row(m->embed, c.vocab, H, 0, m->vtok + t, m->h + (size_t)t * H, s)) return -1;
     for (int li = 0; li < c.layers; li++) {
         const spk_model::Layer &L = m->layers[li];
+        if (capture_rows(m, li, ntok, s)) return -1;
         if (vq_batch(L.m[0], ntok, m->h, H, L.in_norm, c.eps, m->qkv, ldqkv, 0, s) ||
             vq_batch(L.m[1], ntok, m->h, H, L.in_norm, c.eps, m->gate, m->hl, 0, s))
             return -1;
@@ -389,6 +417,7 @@ spk_model *spk_model_create(const spk_model_config *cfg, void *stream) {
     m->full.assign(c.full, c.full + c.layers);
     m->cfg.full = m->full.data();
     m->layers.resize(c.layers);
+    m->cap_slot.assign(c.layers, -1);
     m->stream = (cudaStream_t)stream;
     m->q_dim = m->hl * c.head_dim;
     m->kv_dim = m->kvl * c.head_dim;
@@ -481,6 +510,7 @@ spk_model *spk_model_create(const spk_model_config *cfg, void *stream) {
 
 void spk_model_destroy(spk_model *m) {
     if (!m) return;
+    if (m->cap) cudaFree(m->cap);
     if (m->exec) cudaGraphExecDestroy(m->exec);
     if (m->graph) cudaGraphDestroy(m->graph);
     if (m->texec) cudaGraphExecDestroy(m->texec);
@@ -646,6 +676,54 @@ int spk_model_run(spk_model *m, int steps) {
 
 /* Device pointer of the last step's logits [vocab]. */
 const float *spk_model_logits(spk_model *m) { return m ? m->logits : nullptr; }
+
+/* Model::enable_capture (model.rs:322-343). The captured graphs are dropped so the next
+ * step and verify batch are captured again with the copies in them. */
+int spk_model_enable_capture(spk_model *m, const int *layers, int n) {
+    if (!m) return set_error("model is null");
+    if (n < 0 || n > 8 || (n && !layers)) return set_error("capture takes 0..8 layers, not %d", n);
+    std::vector<int> slot(m->cfg.layers, -1);
+    for (int k = 0; k < n; k++) {
+        if (layers[k] < 0 || layers[k] >= m->cfg.layers) return set_error("capture layer %d is outside the %d layers", layers[k], m->cfg.layers);
+        if (slot[layers[k]] >= 0) return set_error("capture layer %d is listed twice", layers[k]);
+        slot[layers[k]] = k;
+    }
+    cudaError_t e = cudaStreamSynchronize(m->stream);
+    if (e != cudaSuccess) return cuda_fail("capture set-up", e);
+    if (m->cap) cudaFree(m->cap);
+    m->cap = nullptr;
+    m->ncap = 0;
+    if (n) {
+        const size_t bytes = (size_t)n * m->cfg.max_ctx * m->cfg.hidden * sizeof(float);
+        if (alloc((void **)&m->cap, bytes, "alloc layer captures")) return -1;
+        if (cudaMemset(m->cap, 0, bytes) != cudaSuccess) return cuda_fail("clear layer captures", cudaGetLastError());
+    }
+    m->cap_slot = slot;
+    m->ncap = n;
+    if (m->exec) cudaGraphExecDestroy(m->exec);
+    if (m->graph) cudaGraphDestroy(m->graph);
+    m->exec = nullptr;
+    m->graph = nullptr;
+    if (m->texec) cudaGraphExecDestroy(m->texec);
+    if (m->tgraph) cudaGraphDestroy(m->tgraph);
+    m->texec = nullptr;
+    m->tgraph = nullptr;
+    for (int k = 0; k <= ATT_MAX_TOK; k++) {
+        if (m->vexec[k]) cudaGraphExecDestroy(m->vexec[k]);
+        if (m->vgraph[k]) cudaGraphDestroy(m->vgraph[k]);
+        m->vexec[k] = nullptr;
+        m->vgraph[k] = nullptr;
+    }
+    return 0;
+}
+
+/* Model::captured (model.rs:345-348): the capture rows on device, slot k of position p at
+ * [k * *slot_stride + p * hidden]. NULL while capture is off. */
+const float *spk_model_captures(spk_model *m, size_t *slot_stride) {
+    if (!m || !m->ncap) return nullptr;
+    if (slot_stride) *slot_stride = (size_t)m->cfg.max_ctx * m->cfg.hidden;
+    return m->cap;
+}
 
 /* Model::rollback (model.rs:361-382): keep the first `pos` cached positions. */
 int spk_model_rollback(spk_model *m, int pos) {

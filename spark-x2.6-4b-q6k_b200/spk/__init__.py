@@ -84,6 +84,17 @@ _PROTOS = {
     "spk_model_tp_attach": ([_vp, _vp, _i, _i], _i),
     "spk_model_tp_attach_ptrs": ([_vp, _vp, _i, _i], _i),
     "spk_model_tp_mailbox": ([_vp], _vp),
+    "spk_model_enable_capture": ([_vp, _vp, _i], _i),
+    "spk_model_captures": ([_vp, C.POINTER(C.c_size_t)], _vp),
+    "spk_draft_create": ([_vp, _vp], _vp),
+    "spk_draft_destroy": ([_vp], None),
+    "spk_draft_set_layer": ([_vp, _i, _vp], _i),
+    "spk_draft_set_globals": ([_vp, _vp], _i),
+    "spk_draft_encode": ([_vp, _vp, C.c_size_t, _i, _i], _i),
+    "spk_draft_block": ([_vp, _vp, _i, _i, _i, _i, _vp, _vp], _i),
+    "spk_draft_logits": ([_vp], _vp),
+    "spk_bf16_gemm": ([_vp, _i, _i, _i, _vp, _i, _vp, _i, _i, _vp], _i),
+    "spk_bf16_gemm_pair": ([_vp, _vp, _i, _i, _i, _vp, _i, _vp, _i, _i, _vp], _i),
 }
 
 

@@ -222,6 +222,7 @@ class DeviceModel:
         emb = dev_bytes(weights["embed"], self.device)
         norm = torch.from_numpy(np.ascontiguousarray(weights["norm"])).to(self.device)
         self._keep += [emb, norm]
+        self.embed_dev = emb   # the tied Q8_0 embedding/head (the draft's TargetEmbed)
         self.weight_bytes += len(weights["embed"])
         check(L.spk_model_set_head(self.h, emb.data_ptr(), norm.data_ptr()), "head")
         self._logits = np.empty(cfg.vocab, np.float32)
@@ -270,6 +271,20 @@ class DeviceModel:
             k += 1
         self.rollback(pos0 + k + 1)
         return k, tgt[k], tgt
+
+    def enable_capture(self, layers) -> None:
+        """Model::enable_capture (model.rs:322-343): the residual entering each listed layer is
+        kept on device at every position the step and the verify batch visit."""
+        arr = (C.c_int * len(layers))(*[int(v) for v in layers])
+        check(lib().spk_model_enable_capture(self.h, arr, len(layers)), "enable_capture")
+
+    def captures(self) -> tuple[int, int]:
+        """(device pointer, slot stride in floats) of the layer-input captures (Model::captured)."""
+        st = C.c_size_t()
+        p = lib().spk_model_captures(self.h, C.byref(st))
+        if not p:
+            raise SpkError("capture is not enabled")
+        return p, st.value
 
     def trace(self) -> list:
         """One decode step (as run() does) with every launch's device time: [(name, us), ...]
