@@ -337,45 +337,63 @@ def hot_replay(g, stream, seconds: float = 0.4) -> None:
 
 
 def run_spec(args) -> None:
-    """Config 3: speculative decode of the config-2 target at an 8192-token context. A round
-    is one verify batch (spk_model_verify: anchor + 7 proposals, M = 8, in one batched
-    forward), then the cache rolls back to the accepted prefix (spec.rs:197-245). Proposals
-    are synthetic: a seeded Bernoulli(p) acceptor decides per proposal whether it equals the
-    target's id (a random-init draft accepts ~0, which measures nothing); the round's output
-    is the accepted prefix plus the target's token, as spec.rs emits it. The draft model's own
-    time is not included (the DSpark draft is not built): value = accepted tokens per second
-    of verify time."""
+    """Config 3: speculative decode of the config-2 target at an 8192-token context with the
+    5-layer BF16 DSpark draft (624 M parameters, random-init). A round is spec.rs:177-245's:
+    the draft proposes a block of 7 at pos0 (spk_draft_block: anchor + 6 mask rows through
+    the draft, the target's tied head, the Markov chain on device), the target verifies
+    [anchor, 7 proposals] in one M = 8 batch (spk_model_verify), the cache rolls back to the
+    accepted prefix, and the draft encodes the committed rows' layer-input captures
+    (spk_draft_encode). Acceptance is synthetic: a random-init draft and target agree ~never,
+    so a seeded Bernoulli(p) acceptor sets the accepted prefix length k; every kernel runs on
+    the real proposals. value = committed tokens (k + 1 per round) per second of wall time
+    for whole rounds (draft + verify + encode, host round trips included)."""
     import ctypes as C
 
     import torch
 
     import spk
+    from spk.draft import DeviceDraft, DraftConfig, synth_draft
     from spk.model import DeviceModel, ModelConfig, synth_weights
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    cfg = ModelConfig()
+    cfg, dcfg = ModelConfig(), DraftConfig()
     W = synth_weights(cfg, seed=1234)
-    ctx, nd, p_acc = args.ctx, 7, args.accept
-    m = DeviceModel(cfg, W, max_ctx=ctx + (args.warmup + args.steps) * (nd + 1) + 16, kv_f16=True, device=dev)
+    ctx, nd, p_acc = args.ctx, dcfg.draft_max(), args.accept
+    max_ctx = ctx + (args.warmup + args.steps) * (nd + 1) + 16
+    m = DeviceModel(cfg, W, max_ctx=max_ctx, kv_f16=True, device=dev)
     del W
+    DW = synth_draft(dcfg, seed=4321)
+    d = DeviceDraft(dcfg, DW, max_ctx=max_ctx, device=dev, stream=m.stream)
+    del DW
+    m.enable_capture(dcfg.target_layers)
+    caps, stride = m.captures()
     m.advance_len(ctx)   # a zeroed KV cache at the context length (the attention reads the same bytes)
+    d.encode_features(caps, stride, ctx - dcfg.swa_window - 1, ctx)   # the draft's window before pos0
+    embed = m.embed_dev.data_ptr()
     rng = np.random.default_rng(11)
     pos, anchor, emitted = ctx, 5, 0
-    tgt = [0] * (nd + 1)
+    t_draft = t_verify = t_enc = 0.0
 
     def round_(count):
-        nonlocal pos, anchor, emitted, tgt
-        # proposals: the target's ids of the previous round shifted in where the acceptor says
-        # "agree", else a different token; the verify decides k exactly as spec.rs does
+        nonlocal pos, anchor, emitted, t_draft, t_verify, t_enc
+        t0 = time.perf_counter()
+        props, _, _ = d.decode_block(embed, cfg.vocab, anchor, pos, nd)
+        t1 = time.perf_counter()
+        ids, _ = m.verify([anchor] + props[dcfg.i_beg():], pos)
+        t2 = time.perf_counter()
         acc = rng.random(nd) < p_acc
-        props = [(int(tgt[i]) if acc[i] else (int(tgt[i]) + 1) % cfg.vocab) for i in range(nd)]
-        ids, _ = m.verify([anchor] + props, pos)
         k = int(np.argmin(acc)) if not acc.all() else nd   # the acceptor's prefix length
         m.rollback(pos + k + 1)
-        pos, anchor, tgt = pos + k + 1, ids[k], ids
+        d.encode_features(caps, stride, pos, pos + k + 1)
+        m.stream.synchronize()
+        t3 = time.perf_counter()
+        pos, anchor = pos + k + 1, ids[k]
         if count:
             emitted += k + 1
+            t_draft += t1 - t0
+            t_verify += t2 - t1
+            t_enc += t3 - t2
 
     for _ in range(args.warmup):
         round_(False)
@@ -393,24 +411,30 @@ def run_spec(args) -> None:
     e1.record(m.stream)
     e1.synchronize()
     m.rollback(pos)
-    t_verify = e0.elapsed_time(e1) / 1e3
+    t_vdev = e0.elapsed_time(e1) / 1e3
     peak, peak_kind = hbm_peak()
     step_bytes = m.weight_bytes
+    draft_bytes = d.weight_bytes
+    d.close()
     m.close()
     value = emitted / t
+    per = lambda x: x / rounds * 1e3
     line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": 1, "steps": rounds, "warmup": args.warmup,
             "ms_per_step": t / rounds * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "f32", "data": "synthetic (seeded random-init target, seeded Bernoulli acceptor)",
-            "config": {"workload": f"config3: speculative verify rounds (M=1+7) of the config-2 target at ctx {ctx}, "
-                                   f"acceptance {p_acc}, draft time not included",
-                       "model": "spark-x2.6-4b geometry, VQ 4x4096x2 trunk, Q8_0 tied head, f16 KV",
-                       "accepted_per_round": emitted / rounds, "verify_ms_device": t_verify * 1e3,
-                       "verify_weight_gbs": step_bytes / t_verify / 1e9},
+            "dtype": "f32", "data": "synthetic (seeded random-init target and draft, seeded Bernoulli acceptor)",
+            "config": {"workload": f"config3: speculative rounds (DSpark 5-layer BF16 draft, block 7; M=1+7 verify) "
+                                   f"of the config-2 target at ctx {ctx}, acceptance {p_acc}",
+                       "model": "spark-x2.6-4b geometry, VQ 4x4096x2 trunk, Q8_0 tied head, f16 KV; draft 624M bf16",
+                       "accepted_per_round": emitted / rounds, "draft_ms": per(t_draft), "verify_ms": per(t_verify),
+                       "encode_ms": per(t_enc), "verify_ms_device": t_vdev * 1e3,
+                       "verify_weight_gbs": step_bytes / t_vdev / 1e9, "draft_weight_bytes": draft_bytes},
             "roofline": {"bound": "hbm", "kernel": "verify forward (VQ mma.sync GEMMs, M=8)",
-                         "achieved": step_bytes / t_verify / 1e9, "peak": peak, "peak_kind": peak_kind,
-                         "unit": "GB/s", "frac": step_bytes / t_verify / 1e9 / peak, "traffic": None},
-            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 32, "d2h_bytes_per_step": 32},
-            "gpu_launches": rounds * (16 + 8 * cfg.layers), "clocks": clk.summary()}
+                         "achieved": step_bytes / t_vdev / 1e9, "peak": peak, "peak_kind": peak_kind,
+                         "unit": "GB/s", "frac": step_bytes / t_vdev / 1e9 / peak, "traffic": None},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 4 * (2 + nd + 1),
+                    "d2h_bytes_per_step": 4 * (2 * nd + 1 + nd + 1)},
+            "gpu_launches": rounds * ((16 + 8 * cfg.layers) + (2 + 8 * dcfg.layers + 1 + nd) + (3 + 2 * dcfg.layers)),
+            "clocks": clk.summary()}
     print(json.dumps(line), flush=True)
 
 
@@ -650,7 +674,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="decode", choices=["decode", "long", "spec", "vq", "vq-pair", "ggml"],
                     help="decode: config 2 (default); long: config 4 (ctx 131072, q8_0 KV, zeroed KV cache); "
-                         "spec: config 3 verify rounds (ctx 8192, synthetic acceptance); "
+                         "spec: config 3 speculative rounds, draft + verify (ctx 8192, synthetic acceptance); "
                          "vq: config 0 GEMV; vq-pair: the FFN gate+up launch; ggml: config 1 Q6_K/Q8_0 sweep")
     ap.add_argument("--kv", default=None, choices=["f32", "f16", "q8"],
                     help="decode KV cache type (default f16; long: q8)")

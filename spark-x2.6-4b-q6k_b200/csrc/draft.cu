@@ -765,7 +765,7 @@ int spk_draft_block(spk_draft *d, const void *embed, int vocab, int anchor, int 
             m.rank = c.rank;
             m.vocab_m = c.vocab;
             m.vocab = vocab;
-            m.prev = i == 0 ? nullptr : d->amax + i - 1;
+            m.prev = i == i_beg ? nullptr : d->amax + i - 1;   // the chain starts at the anchor (draft.rs:862)
             m.prev_host = anchor;
             m.logits = d->logits + (size_t)i * vocab;
             m.amax = d->amax + i;

@@ -1,10 +1,10 @@
 // vq_mma.cu — the batched (M <= 8) VQ decode-GEMM of the speculative verify
 // (see vq_mma.cuh for the fragment map).
 //
-// Persistent CTA per SM, 32 warps, over a contiguous row range. Tiles of 16 rows
+// Persistent CTA per SM, 16 or 32 warps, over a contiguous row range. Tiles of 16 rows
 // of every stage's index stream arrive by TMA bulk copy into a ring of shared-
 // memory slots (mbarrier full/empty pairs); the stages' codebooks sit in shared
-// memory. A row's K range is cut into `passes` passes of 32 warps x 4 threads x
+// memory. A row's K range is cut into `passes` passes of MW warps x 4 threads x
 // S groups; per pass every thread builds its B fragments (its token column of X,
 // RMSNorm folded in, split hi/lo) from L2-resident X, then runs S MMA steps per
 // stage. Warp partials are summed in a fixed order, so results are deterministic.
@@ -17,8 +17,11 @@ namespace spk {
 
 namespace {
 
-constexpr int MW = 32;           // warps per CTA
-constexpr int MTHREADS = MW * 32;
+// Warps per CTA, by S: 16 (512 threads, 128 registers a thread) for S = 10, the single
+// pass over a 2560-wide row; 32 otherwise, where more warps split a long row into fewer
+// passes (a pass rebuilds the B fragments) at 64 registers a thread.
+__host__ __device__ constexpr int warps_for(int S) { return S == 10 ? 16 : 32; }
+constexpr int MW_MAX = 32;
 constexpr int MAXT = 8;          // tokens per batch (the 8 columns of B)
 constexpr int TRR_MAX = 16;      // rows per tile: the 16 rows of A, or 8 (rows g+8 empty) for long rows
 
@@ -93,7 +96,10 @@ __device__ __forceinline__ void load_b(const MmaArgs &a, const float *inv, int g
 }
 
 template <int NSTG, int S, int EXT, int TWO>
-__global__ void __launch_bounds__(MTHREADS, 1) vq_mma_kernel(const MmaArgs a) {
+__global__ void __launch_bounds__(warps_for(S) * 32, 1) vq_mma_kernel(const MmaArgs a) {
+    constexpr int MW = warps_for(S), MTHREADS = MW * 32;
+    constexpr int NG = MTHREADS / 128;   // epilogue warp groups: thread e of group k sums WPG warps' element e
+    constexpr int WPG = MW / NG;
     extern __shared__ __align__(16) uint8_t smem[];
     const Layout &L = a.L;
     const int nc = L.nc, NB = a.nbuf;
@@ -102,8 +108,8 @@ __global__ void __launch_bounds__(MTHREADS, 1) vq_mma_kernel(const MmaArgs a) {
     uint64_t *full = reinterpret_cast<uint64_t *>(ring + (size_t)NB * a.slot_bytes);
     uint64_t *empty = full + NB;
     float *part = reinterpret_cast<float *>(empty + NB);   // [NSTG][MW][16 rows x 8 columns]
-    float *red = part + NSTG * MW * 16 * 8;                // [NSTG][8 warp groups][16 x 8]
-    float *inv = red + NSTG * 8 * 16 * 8;                  // [MAXT]
+    float *red = part + NSTG * MW * 16 * 8;                // [NSTG][NG warp groups][16 x 8]
+    float *inv = red + NSTG * NG * 16 * 8;                 // [MAXT]
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
     const int G = gridDim.x;
@@ -159,17 +165,6 @@ __global__ void __launch_bounds__(MTHREADS, 1) vq_mma_kernel(const MmaArgs a) {
                 mma_issue(a, NSTG, ring + (size_t)sn * a.slot_bytes, &full[sn], r0n, min(TRR, re - r0n));
         }
         const int r0 = rb + k * TRR, nr = min(TRR, re - r0);
-        // the epilogue's per-row operands, fetched now so their latency hides under the tile
-        const int orl = tid >> 3, on_ = tid & 7;   // output (row orl, column on_) for tid < 128
-        const bool oown = tid < 128 && orl < nr && (TWO ? on_ : (on_ & 3)) < a.ntok && (TWO || on_ < 4);
-        float og[NSTG], oy = 0.f;
-        if (oown) {
-#pragma unroll
-            for (int q = 0; q < NSTG; q++)
-                og[q] = h2f_u16(*reinterpret_cast<const uint16_t *>(a.st[q] + L.gain_off + 2 * (size_t)(r0 + orl)));
-            if (a.mode == 1) oy = a.aux[(size_t)on_ * a.ldy + r0 + orl];
-            else if (a.accumulate) oy = a.y[(size_t)on_ * a.ldy + r0 + orl];
-        }
         const bool have = mbar_wait(&full[slot], (uint32_t)((k / NB) & 1), a.err);
         const uint8_t *sb = ring + (size_t)slot * a.slot_bytes;
         const bool v0 = have && g < nr, v1 = have && g + 8 < nr;   // nr <= TRR: rows g+8 exist only at 16
@@ -216,6 +211,18 @@ __global__ void __launch_bounds__(MTHREADS, 1) vq_mma_kernel(const MmaArgs a) {
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
+        // the epilogue's per-row operands, fetched after the main loop (not live across it)
+        // and before the partials' barrier, which hides their latency
+        const int orl = tid >> 3, on_ = tid & 7;   // output (row orl, column on_) for tid < 128
+        const bool oown = tid < 128 && orl < nr && (TWO ? on_ : (on_ & 3)) < a.ntok && (TWO || on_ < 4);
+        float og[NSTG], oy = 0.f;
+        if (oown) {
+#pragma unroll
+            for (int q = 0; q < NSTG; q++)
+                og[q] = h2f_u16(*reinterpret_cast<const uint16_t *>(a.st[q] + L.gain_off + 2 * (size_t)(r0 + orl)));
+            if (a.mode == 1) oy = a.aux[(size_t)on_ * a.ldy + r0 + orl];
+            else if (a.accumulate) oy = a.y[(size_t)on_ * a.ldy + r0 + orl];
+        }
 #pragma unroll
         for (int q = 0; q < NSTG; q++) {
             float *pw = part + ((size_t)q * MW + warp) * 16 * 8;
@@ -226,17 +233,17 @@ __global__ void __launch_bounds__(MTHREADS, 1) vq_mma_kernel(const MmaArgs a) {
         }
         __syncthreads();
         // Phase 1, every thread: element e = tid & 127 of the 16 x 8 tile, summed over the
-        // 4 warps of group tid >> 7 per stage (a warp reads 32 consecutive floats: no bank
+        // WPG warps of group tid >> 7 per stage (a warp reads 32 consecutive floats: no bank
         // conflict). Phase 2, thread e < 128: the 8 groups in order, gains, epilogue.
         {
             const int e = tid & 127, wg = tid >> 7;
 #pragma unroll
             for (int q = 0; q < NSTG; q++) {
-                const float *pq = part + ((size_t)q * MW + wg * (MW / 8)) * 16 * 8 + e;
+                const float *pq = part + ((size_t)q * MW + wg * WPG) * 16 * 8 + e;
                 float v = 0.f;
 #pragma unroll
-                for (int w = 0; w < MW / 8; w++) v += pq[(size_t)w * 16 * 8];
-                red[((size_t)q * 8 + wg) * 16 * 8 + e] = v;
+                for (int w = 0; w < WPG; w++) v += pq[(size_t)w * 16 * 8];
+                red[((size_t)q * NG + wg) * 16 * 8 + e] = v;
             }
         }
         __syncthreads();
@@ -246,8 +253,8 @@ __global__ void __launch_bounds__(MTHREADS, 1) vq_mma_kernel(const MmaArgs a) {
             for (int q = 0; q < NSTG; q++) {
                 float v = 0.f;
 #pragma unroll
-                for (int w = 0; w < 8; w++) {
-                    const float *rw = red + ((size_t)q * 8 + w) * 16 * 8 + orl * 8;
+                for (int w = 0; w < NG; w++) {
+                    const float *rw = red + ((size_t)q * NG + w) * 16 * 8 + orl * 8;
                     v += TWO ? rw[on_] : (rw[on_] + rw[on_ + 4]);
                 }
                 o = __fadd_rn(o, __fmul_rn(v, og[q]));
@@ -277,7 +284,7 @@ int mma_launch_t(const MmaArgs &A, size_t smem, cudaStream_t s) {
     }
     const int ntr = (A.L.rows + A.trr - 1) / A.trr;
     const int grid = ntr < sm_count() ? ntr : sm_count();
-    cudaError_t e = launch_pdl(k, dim3(grid), dim3(MTHREADS), smem, s, A);
+    cudaError_t e = launch_pdl(k, dim3(grid), dim3(warps_for(S) * 32), smem, s, A);
     return e == cudaSuccess ? 0 : cuda_fail("vq mma kernel launch", e);
 }
 
@@ -299,6 +306,7 @@ int mma_launch_s(int S, const MmaArgs &A, size_t smem, cudaStream_t s) {
         case 4: return mma_launch_e<NSTG, 4>(A, smem, s);
         case 5: return mma_launch_e<NSTG, 5>(A, smem, s);
         case 8: return mma_launch_e<NSTG, 8>(A, smem, s);
+        case 10: return mma_launch_e<NSTG, 10>(A, smem, s);
     }
     return set_error("vq mma kernel: no instantiation for S=%d", S);
 }
@@ -310,20 +318,27 @@ int vq_mma_batch(const void *const *stages, int nstg, const Layout &L, int ntok,
                  cudaStream_t s) {
     if (ntok < 1 || ntok > MAXT) return 0;
     if (L.dim != 4 || !L.v3 || L.nbit < 12 || nstg < 1 || nstg > 2) return 0;
-    if (L.nidx_row % (4 * MW) || L.mrow % 4 || L.stream_off % 4 || (L.prow && L.prow % 4)) return 0;
-    // S groups per thread per pass: the largest of 8, 5, 4, 2, 1 that divides the row
-    const int per = (int)(L.nidx_row / (4 * MW));
+    if (L.nidx_row % (4 * MW_MAX) || L.mrow % 4 || L.stream_off % 4 || (L.prow && L.prow % 4)) return 0;
+    // S groups per thread per pass: 10 with 16 warps when that is the whole row in one pass,
+    // else the largest of 8, 5, 4, 2, 1 that divides the row's share of 32 warps
     int S = 0;
-    for (int c : {8, 5, 4, 2, 1})
-        if (per % c == 0) {
-            S = c;
-            break;
-        }
+    if (L.nidx_row == 4 * warps_for(10) * 10) {
+        S = 10;
+    } else {
+        const int per32 = (int)(L.nidx_row / (4 * MW_MAX));
+        for (int c : {8, 5, 4, 2, 1})
+            if (per32 % c == 0) {
+                S = c;
+                break;
+            }
+    }
+    const int MW = warps_for(S), NG = MW * 32 / 128;
+    const int per = (int)(L.nidx_row / (4 * MW));
     for (int q = 0; q < nstg; q++)
         if (((uintptr_t)stages[q] & 7) != 0) return 0;
     if (((uintptr_t)x & 15) || (ldx & 3) || (norm_w && ((uintptr_t)norm_w & 15))) return 0;
     const size_t cb = (((size_t)nstg * L.nc * 8 + 15) & ~(size_t)15);
-    const size_t fixed = cb + (size_t)nstg * MW * 16 * 8 * 4 + (size_t)nstg * 8 * 16 * 8 * 4 + MAXT * 4;
+    const size_t fixed = cb + (size_t)nstg * MW * 16 * 8 * 4 + (size_t)nstg * NG * 16 * 8 * 4 + MAXT * 4;
     // 16-row tiles, else 8-row tiles (half the A rows empty: the gathers, not the MMAs, bound
     // the kernel) where a 16-row ring does not fit shared memory (long rows: down_proj)
     for (int c = 0; c < 4; c++) {

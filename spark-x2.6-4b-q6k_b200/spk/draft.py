@@ -274,10 +274,10 @@ class DeviceDraft:
 
 
 class _DeviceView:
-    """A read-only f32 view of a library-owned device buffer (__cuda_array_interface__)."""
+    """An f32 view of a library-owned device buffer (__cuda_array_interface__); copy it out."""
 
     def __init__(self, ptr: int, shape: tuple):
         if not ptr:
             raise SpkError("no device buffer")
-        self.__cuda_array_interface__ = {"shape": shape, "typestr": "<f4", "data": (int(ptr), True), "version": 3,
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": "<f4", "data": (int(ptr), False), "version": 3,
                                          "strides": None}
