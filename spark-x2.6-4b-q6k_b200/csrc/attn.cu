@@ -104,6 +104,69 @@ __device__ void store_row(const float *src, uint8_t *row, int hd) {
     }
 }
 
+// The split's partial is written; the last split of this (token, KV head) to finish
+// (an atomic ticket, reset by it) merges all splits in a fixed order and applies the
+// per-head sigmoid gate (model.rs:538-550).
+template <int HD>
+__device__ void finish_splits(const AttnArgs &a, int kvh, int tok, int G, size_t pbase, size_t pstride,
+                              float (*cw)[ATT_MAX_SPLIT], float *cl, int *is_last_p) {
+    constexpr int PR = HD + 4;
+    int &is_last = *is_last_p;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    __threadfence();
+    __syncthreads();
+    unsigned int *ticket = a.count + (size_t)tok * a.kv_heads + kvh;
+    if (threadIdx.x == 0) is_last = atomicAdd(ticket, 1u) == (unsigned int)(a.nsplit - 1);
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    const float *p0 = a.part + pbase * pstride;
+    for (int i = threadIdx.x; i < G * a.nsplit; i += blockDim.x) {
+        const int h = i / a.nsplit, c = i - h * a.nsplit;
+        cw[h][c] = __ldcg(p0 + c * pstride + h * PR + HD);
+    }
+    __syncthreads();
+    if (warp < G) {   // warp h: the split weights e^{m_c - M} and the total L of head h
+        const int h = warp;
+        float M = -INFINITY;
+        for (int c = lane; c < a.nsplit; c += 32) M = fmaxf(M, cw[h][c]);
+        for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+        float L = 0.f;
+        for (int c = lane; c < a.nsplit; c += 32) {
+            const float mc = cw[h][c];
+            const float e = mc == -INFINITY ? 0.f : expf(mc - M);
+            L += __ldcg(p0 + c * pstride + h * PR + HD + 1) * e;
+            cw[h][c] = e;
+        }
+        L = warp_sum(L);
+        if (lane == 0) cl[h] = L;
+    }
+    __syncthreads();
+    // one thread per 4 output dims, 8 float4 loads in flight per thread
+    for (int i = threadIdx.x; i < G * (HD / 4); i += blockDim.x) {
+        const int h = i / (HD / 4), d4 = i - h * (HD / 4);
+        const float *ph = p0 + h * PR + 4 * d4;
+        float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+        for (int c = 0; c < a.nsplit; c++) {
+            const float4 v = __ldcg(reinterpret_cast<const float4 *>(ph + c * pstride));
+            const float w = cw[h][c];
+            O.x = fmaf(v.x, w, O.x);
+            O.y = fmaf(v.y, w, O.y);
+            O.z = fmaf(v.z, w, O.z);
+            O.w = fmaf(v.w, w, O.w);
+        }
+        const int qh = kvh * G + h;
+        const float gsig = 1.0f / (1.0f + expf(-a.gate[(size_t)tok * a.ldgate + qh]));
+        float *dst = a.out + (size_t)tok * a.ldout + (size_t)qh * HD + 4 * d4;
+        dst[0] = (O.x / cl[h]) * gsig;
+        dst[1] = (O.y / cl[h]) * gsig;
+        dst[2] = (O.z / cl[h]) * gsig;
+        dst[3] = (O.w / cl[h]) * gsig;
+    }
+    if (threadIdx.x == 0) *ticket = 0u;
+}
+
 // ATT_U: positions per warp per iteration (4 for long splits, 2 for short ones so
 // that all 8 warps have a position).
 template <int HD, int KT, int ATT_U>
@@ -258,59 +321,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnArgs a) {
     } else {   // an empty split: weight 0 in the merge
         for (int i = threadIdx.x; i < G * PR; i += blockDim.x) out[i] = (i % PR) == HD ? -INFINITY : 0.f;
     }
-    // the last split of this (token, KV head) to finish merges all of them
-    __threadfence();
-    __syncthreads();
-    unsigned int *ticket = a.count + (size_t)tok * a.kv_heads + kvh;
-    if (threadIdx.x == 0) is_last = atomicAdd(ticket, 1u) == (unsigned int)(a.nsplit - 1);
-    __syncthreads();
-    if (!is_last) return;
-    __threadfence();
-    const float *p0 = a.part + pbase * pstride;
-    for (int i = threadIdx.x; i < G * a.nsplit; i += blockDim.x) {
-        const int h = i / a.nsplit, c = i - h * a.nsplit;
-        cw[h][c] = __ldcg(p0 + c * pstride + h * PR + HD);
-    }
-    __syncthreads();
-    if (warp < G) {   // warp h: the split weights e^{m_c - M} and the total L of head h
-        const int h = warp;
-        float M = -INFINITY;
-        for (int c = lane; c < a.nsplit; c += 32) M = fmaxf(M, cw[h][c]);
-        for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-        float L = 0.f;
-        for (int c = lane; c < a.nsplit; c += 32) {
-            const float mc = cw[h][c];
-            const float e = mc == -INFINITY ? 0.f : expf(mc - M);
-            L += __ldcg(p0 + c * pstride + h * PR + HD + 1) * e;
-            cw[h][c] = e;
-        }
-        L = warp_sum(L);
-        if (lane == 0) cl[h] = L;
-    }
-    __syncthreads();
-    // one thread per 4 output dims, 8 float4 loads in flight per thread
-    for (int i = threadIdx.x; i < G * (HD / 4); i += blockDim.x) {
-        const int h = i / (HD / 4), d4 = i - h * (HD / 4);
-        const float *ph = p0 + h * PR + 4 * d4;
-        float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
-        for (int c = 0; c < a.nsplit; c++) {
-            const float4 v = __ldcg(reinterpret_cast<const float4 *>(ph + c * pstride));
-            const float w = cw[h][c];
-            O.x = fmaf(v.x, w, O.x);
-            O.y = fmaf(v.y, w, O.y);
-            O.z = fmaf(v.z, w, O.z);
-            O.w = fmaf(v.w, w, O.w);
-        }
-        const int qh = kvh * G + h;
-        const float gsig = 1.0f / (1.0f + expf(-a.gate[(size_t)tok * a.ldgate + qh]));
-        float *dst = a.out + (size_t)tok * a.ldout + (size_t)qh * HD + 4 * d4;
-        dst[0] = (O.x / cl[h]) * gsig;
-        dst[1] = (O.y / cl[h]) * gsig;
-        dst[2] = (O.z / cl[h]) * gsig;
-        dst[3] = (O.w / cl[h]) * gsig;
-    }
-    if (threadIdx.x == 0) *ticket = 0u;
+    finish_splits<HD>(a, kvh, tok, G, pbase, pstride, cw, cl, &is_last);
 }
 
 // Rope K and store the K/V rows of ntok consecutive tokens: block t = token t.
@@ -334,6 +345,271 @@ __global__ void attn_store_kernel(const AttnArgs a) {
     }
 }
 
+
+// ===================================================== tensor-core decode ===
+// The same (token, KV head, split) grid for head_dim 256 over an f16 cache, with the
+// contractions on the tensor cores (mma.sync m16n8k16 f16 -> f32):
+//  * K and V rows of 64 positions per stage arrive by cp.async (16 bytes a thread,
+//    zero-filled past the split) into two slots of 544-byte rows (padded: no bank
+//    conflicts); each of the 4 warps takes 16 positions of a stage.
+//  * S^T = K q^T: K rows are the A operand (positions as rows; a thread's four k-slots
+//    are four consecutive dims, one 8-byte load), B holds the group's q heads as an
+//    f16 pair, hi in columns 0..3 and lo in 4..7, so one MMA per 16 dims gives ~22-bit
+//    scores; hi and lo meet by one shuffle.
+//  * the online softmax per head (model.rs:519-553 order of terms: s * scale, exp(s - m)),
+//    the lanes holding a head's scores also holding its O^T columns;
+//  * O^T += V^T P^T: V^T by ldmatrix.trans, P as an f16 pair again (hi / lo columns).
+// The token's own row (the SIMT kernel's exact f32 row) is masked in the tiles and
+// enters the CTA merge as a fifth, exact f32 term.
+constexpr int TC_WARPS = 4, TC_THREADS = TC_WARPS * 32;
+constexpr int TC_POS = 64;                       // positions per stage, 16 per warp
+constexpr int TC_RS = 256 * 2 + 32;              // shared-memory bytes per K or V row (padded)
+constexpr int TC_STAGE = TC_POS * TC_RS;         // bytes of K (or V) per stage
+constexpr size_t TC_SMEM = (size_t)2 * 2 * TC_STAGE;
+
+__device__ __forceinline__ void cp_async16(void *smem_dst, const void *src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(src),
+                 "r"(valid ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void *p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+
+__device__ __forceinline__ void mma_f16_tc(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                           uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// (x, y) as an f16 pair: the hi parts rn(x), rn(y), or the lo parts rn(x - hi), rn(y - hi).
+__device__ __forceinline__ uint32_t f16_pair(float x, float y, bool lo) {
+    const __half hx = __float2half_rn(x), hy = __float2half_rn(y);
+    const __half ox = lo ? __float2half_rn(x - __half2float(hx)) : hx;
+    const __half oy = lo ? __float2half_rn(y - __half2float(hy)) : hy;
+    return (uint32_t)__half_as_ushort(ox) | ((uint32_t)__half_as_ushort(oy) << 16);
+}
+
+template <int KT>
+__global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const AttnArgs a) {
+    constexpr int HD = 256, MG = ATT_MAX_GROUP, PR = HD + 4, NW = TC_WARPS + 1;
+    constexpr size_t RB = kv_row_bytes(KT, HD);
+    extern __shared__ __align__(16) uint8_t tsm[];
+    __shared__ float qs[MG][HD];
+    __shared__ float kn[HD], vn[HD];
+    __shared__ float wm[NW][MG], wl[NW][MG];
+    __shared__ float wo[NW][MG][HD];
+    __shared__ float pt[TC_WARPS][16][MG];
+    __shared__ float cw[MG][ATT_MAX_SPLIT];
+    __shared__ float cl[MG];
+    __shared__ int is_last;
+    pdl_trigger();
+    pdl_wait();
+    const int kvh = blockIdx.x, split = blockIdx.y, tok = blockIdx.z;
+    const int G = a.heads / a.kv_heads;
+    const int qd = a.heads * HD, kvd = a.kv_heads * HD;
+    const int pos = *a.pos + tok;
+    const int last = a.span > 0 ? *a.pos + a.span - 1 : pos;
+    const int start = a.full ? 0 : max(0, (a.span > 0 ? *a.pos : pos) + 1 - a.window);
+    const int n = last + 1 - start;
+    const int csz = max((n + a.nsplit - 1) / a.nsplit, 16);
+    const int c0 = start + split * csz, c1 = min(last + 1, c0 + csz);
+    const float *qrow = a.qkv + (size_t)tok * a.ldqkv;
+    const size_t pbase = ((size_t)tok * a.kv_heads + kvh) * a.nsplit;
+    const size_t pstride = (size_t)G * PR;
+    float *out = a.part + (pbase + split) * pstride;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, t = lane & 3;
+
+    for (int i = threadIdx.x; i < MG * HD; i += blockDim.x)
+        qs[i / HD][i % HD] = i / HD < G ? qrow[(size_t)(kvh * G + i / HD) * HD + i % HD] : 0.f;
+    for (int i = threadIdx.x; i < HD; i += blockDim.x) {
+        kn[i] = qrow[qd + (size_t)kvh * HD + i];
+        vn[i] = qrow[qd + kvd + (size_t)kvh * HD + i];
+    }
+    __syncthreads();
+    for (int h = 0; h < G; h++) rope_smem(qs[h], a.freq, a.pdim, pos);
+    rope_smem(kn, a.freq, a.pdim, pos);
+    __syncthreads();
+    if (a.store && c0 <= pos && pos < c1) {   // a single token's own row; nobody reads that slot now
+        const size_t o = ((size_t)kvh * a.slots + pos % a.slots) * RB;
+        store_row<KT>(kn, reinterpret_cast<uint8_t *>(a.kc) + o, HD);
+        store_row<KT>(vn, reinterpret_cast<uint8_t *>(a.vc) + o, HD);
+    }
+    const bool own = a.span == 0 && c0 <= pos && pos < c1;   // exact f32 own row: masked below
+    const float scale = 1.0f / sqrtf((float)HD);
+
+    // B fragments of q for the 16 k-steps: column g = head g & 3, hi (g < 4) or lo part
+    uint32_t qb[16][2];
+#pragma unroll
+    for (int ks = 0; ks < 16; ks++) {
+        const float *qh = qs[g & 3] + 16 * ks + 4 * t;
+        qb[ks][0] = f16_pair(qh[0], qh[1], g >= 4);
+        qb[ks][1] = f16_pair(qh[2], qh[3], g >= 4);
+    }
+    float o[16][4];
+#pragma unroll
+    for (int mt = 0; mt < 16; mt++) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+    float mA = -INFINITY, mB = -INFINITY, lA = 0.f, lB = 0.f;   // heads 2(t&1), 2(t&1)+1
+
+    const uint8_t *kbase = reinterpret_cast<const uint8_t *>(a.kc) + (size_t)kvh * a.slots * RB;
+    const uint8_t *vbase = reinterpret_cast<const uint8_t *>(a.vc) + (size_t)kvh * a.slots * RB;
+    const int nstage = c0 < c1 ? (c1 - c0 + TC_POS - 1) / TC_POS : 0;
+    auto issue = [&](int st, int slot) {
+        uint8_t *kd = tsm + (size_t)slot * 2 * TC_STAGE, *vd = kd + TC_STAGE;
+        const int js = c0 + st * TC_POS;
+        for (int i = threadIdx.x; i < TC_POS * 32; i += TC_THREADS) {   // 32 chunks of 16 bytes a row
+            const int r = i >> 5, c = i & 31, j = js + r;
+            const bool v = j < c1;
+            const size_t off = (size_t)((v ? j : c0) % a.slots) * RB + 16 * c;
+            cp_async16(kd + r * TC_RS + 16 * c, kbase + off, v);
+            cp_async16(vd + r * TC_RS + 16 * c, vbase + off, v);
+        }
+        cp_async_commit();
+    };
+    if (nstage > 0) issue(0, 0);
+    else cp_async_commit();
+    if (nstage > 1) issue(1, 1);
+    else cp_async_commit();
+    const int vpos = (lane & 7) + ((lane >> 4) << 3), vdim = ((lane >> 3) & 1) * 8;   // ldmatrix.trans rows
+    for (int st = 0; st < nstage; st++) {
+        cp_async_wait<1>();
+        __syncthreads();   // stage st landed for every thread
+        const uint8_t *kt = tsm + (size_t)(st & 1) * 2 * TC_STAGE, *vt = kt + TC_STAGE;
+        const int jw = c0 + st * TC_POS + 16 * warp;   // this warp's first position
+        if (jw < c1) {
+            float sc[4] = {0.f, 0.f, 0.f, 0.f};
+            const uint8_t *ra = kt + (size_t)(16 * warp + g) * TC_RS + 8 * t, *rb8 = ra + (size_t)8 * TC_RS;
+#pragma unroll
+            for (int ks = 0; ks < 16; ks++) {
+                const uint2 ka = *reinterpret_cast<const uint2 *>(ra + 32 * ks);
+                const uint2 kb = *reinterpret_cast<const uint2 *>(rb8 + 32 * ks);
+                mma_f16_tc(sc, ka.x, kb.x, ka.y, kb.y, qb[ks][0], qb[ks][1]);
+            }
+#pragma unroll
+            for (int e = 0; e < 4; e++) sc[e] += __shfl_xor_sync(0xffffffffu, sc[e], 2);   // hi + lo
+            const int p0 = jw + g, p1 = jw + g + 8;
+            const bool v0 = p0 < c1 && !(own && p0 == pos), v1 = p1 < c1 && !(own && p1 == pos);
+            const float s0 = v0 ? sc[0] * scale : -INFINITY, s1 = v0 ? sc[1] * scale : -INFINITY;
+            const float s2 = v1 ? sc[2] * scale : -INFINITY, s3 = v1 ? sc[3] * scale : -INFINITY;
+            float xA = fmaxf(s0, s2), xB = fmaxf(s1, s3);
+#pragma unroll
+            for (int off = 4; off < 32; off <<= 1) {
+                xA = fmaxf(xA, __shfl_xor_sync(0xffffffffu, xA, off));
+                xB = fmaxf(xB, __shfl_xor_sync(0xffffffffu, xB, off));
+            }
+            const float nA = fmaxf(mA, xA), nB = fmaxf(mB, xB);
+            const float cA = nA == -INFINITY ? 1.f : expf(mA - nA), cB = nB == -INFINITY ? 1.f : expf(mB - nB);
+            const float pA0 = v0 ? expf(s0 - nA) : 0.f, pB0 = v0 ? expf(s1 - nB) : 0.f;
+            const float pA1 = v1 ? expf(s2 - nA) : 0.f, pB1 = v1 ? expf(s3 - nB) : 0.f;
+            float sA = pA0 + pA1, sB = pB0 + pB1;
+#pragma unroll
+            for (int off = 4; off < 32; off <<= 1) {
+                sA += __shfl_xor_sync(0xffffffffu, sA, off);
+                sB += __shfl_xor_sync(0xffffffffu, sB, off);
+            }
+            lA = lA * cA + sA;
+            lB = lB * cB + sB;
+            mA = nA;
+            mB = nB;
+#pragma unroll
+            for (int mt = 0; mt < 16; mt++) {
+                o[mt][0] *= cA;
+                o[mt][1] *= cB;
+                o[mt][2] *= cA;
+                o[mt][3] *= cB;
+            }
+            // P^T as the B operand: row pos, column g (head g & 3, hi / lo), via shared memory
+            if (t < 2) {
+                pt[warp][g][2 * t] = pA0;
+                pt[warp][g][2 * t + 1] = pB0;
+                pt[warp][g + 8][2 * t] = pA1;
+                pt[warp][g + 8][2 * t + 1] = pB1;
+            }
+            __syncwarp();
+            const int hh = g & 3;
+            const uint32_t pb0 = f16_pair(pt[warp][2 * t][hh], pt[warp][2 * t + 1][hh], g >= 4);
+            const uint32_t pb1 = f16_pair(pt[warp][2 * t + 8][hh], pt[warp][2 * t + 9][hh], g >= 4);
+            __syncwarp();
+            const uint8_t *vr = vt + (size_t)(16 * warp + vpos) * TC_RS + 2 * vdim;
+#pragma unroll
+            for (int mt = 0; mt < 16; mt++) {
+                uint32_t av[4];
+                ldsm_x4_trans(av, vr + 32 * mt);
+                mma_f16_tc(o[mt], av[0], av[1], av[2], av[3], pb0, pb1);
+            }
+        }
+        __syncthreads();   // every warp is done with this slot
+        if (st + 2 < nstage) issue(st + 2, st & 1);
+        else cp_async_commit();
+    }
+    cp_async_wait<0>();
+
+    // this warp's (o, m, l) for the merge: O[h][dim] = O^T[dim][h] + O^T[dim][h + 4]
+#pragma unroll
+    for (int mt = 0; mt < 16; mt++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) o[mt][e] += __shfl_xor_sync(0xffffffffu, o[mt][e], 2);
+    const int hA = 2 * (t & 1), hB = hA + 1;
+    if (t < 2) {
+#pragma unroll
+        for (int mt = 0; mt < 16; mt++) {
+            wo[warp][hA][16 * mt + g] = o[mt][0];
+            wo[warp][hB][16 * mt + g] = o[mt][1];
+            wo[warp][hA][16 * mt + g + 8] = o[mt][2];
+            wo[warp][hB][16 * mt + g + 8] = o[mt][3];
+        }
+        if (g == 0) {
+            wm[warp][hA] = mA;
+            wm[warp][hB] = mB;
+            wl[warp][hA] = lA;
+            wl[warp][hB] = lB;
+        }
+    }
+    // the own row, exact in f32 (warp h: head h's score)
+    if (warp < MG) {
+        const int h = warp;
+        float sv = 0.f;
+        if (own && h < G)
+            for (int d = lane; d < HD; d += 32) sv = fmaf(qs[h][d], kn[d], sv);
+        sv = warp_sum(sv);
+        if (lane == 0) {
+            wm[TC_WARPS][h] = own && h < G ? sv * scale : -INFINITY;
+            wl[TC_WARPS][h] = own && h < G ? 1.f : 0.f;
+        }
+        for (int d = lane; d < HD; d += 32) wo[TC_WARPS][h][d] = own ? vn[d] : 0.f;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
+        const int h = i / HD, d = i % HD;
+        float M = -INFINITY;
+        for (int w = 0; w < NW; w++) M = fmaxf(M, wm[w][h]);
+        float L = 0.f, O = 0.f;
+        for (int w = 0; w < NW; w++) {
+            if (wm[w][h] == -INFINITY) continue;
+            const float e = expf(wm[w][h] - M);
+            L += wl[w][h] * e;
+            O += wo[w][h][d] * e;
+        }
+        out[h * PR + d] = O;
+        if (d == 0) {
+            out[h * PR + HD] = M;
+            out[h * PR + HD + 1] = L;
+        }
+    }
+    finish_splits<HD>(a, kvh, tok, G, pbase, pstride, cw, cl, &is_last);
+}
+
 }  // namespace
 
 int attn_decode(const AttnArgs &a, cudaStream_t s) {
@@ -347,6 +623,19 @@ int attn_decode(const AttnArgs &a, cudaStream_t s) {
     const bool longs = (span + a.nsplit - 1) / a.nsplit >= 64;
     if (a.hd != 256 && a.hd != 128) return set_error("attention: head_dim %d (128 or 256)", a.hd);
     if (a.kv_type < KV_F32 || a.kv_type > KV_Q8) return set_error("attention: cache type %d", a.kv_type);
+    if (a.hd == 256 && a.kv_type == KV_F16) {   // the tensor-core kernel
+        static int opted[64];
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (!opted[dev & 63]) {
+            cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<KV_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)TC_SMEM);
+            if (e != cudaSuccess) return cuda_fail("attention shared-memory opt-in", e);
+            opted[dev & 63] = 1;
+        }
+        const cudaError_t e = launch_pdl(attn_tc_kernel<KV_F16>, grid, dim3(TC_THREADS), TC_SMEM, s, a);
+        return e == cudaSuccess ? 0 : cuda_fail("attention launch", e);
+    }
     const int sel = (a.hd == 256 ? 0 : 6) + a.kv_type * 2 + (longs ? 1 : 0);
     void (*const ks[12])(const AttnArgs) = {
         attn_kernel<256, 0, 2>, attn_kernel<256, 0, 4>, attn_kernel<256, 1, 2>, attn_kernel<256, 1, 4>,

@@ -136,6 +136,53 @@ def test_attention_matches_reference(cuda, hd, heads, kvh, full, ntok, f16):
     assert ws.cpu().numpy()[:1024].max() == 0   # tickets reset
 
 
+@pytest.mark.parametrize("ntok,kv_type", [(1, 1), (8, 1), (1, 0), (3, 2)])
+@pytest.mark.parametrize("nsplit", [2, 3])
+def test_attention_long_splits(cuda, ntok, kv_type, nsplit):
+    """Splits of 200-300 positions (several 64-position stages of the tensor-core kernel,
+    a partial last stage, the own row inside a stage) at head_dim 256, full attention."""
+    import torch
+
+    import spk
+
+    L = spk.lib()
+    hd, heads, kvh = 256, 16, 4
+    rng = np.random.default_rng(31 + ntok + 7 * kv_type + nsplit)
+    slots, pos0, pdim = 640, 601 - ntok, hd // 4
+    freq = np.zeros(hd, np.float32)
+    freq[:pdim // 2] = (1.0 / np.power(np.float32(5e6), np.arange(pdim // 2, dtype=np.float32) * 2 / pdim)).astype(np.float32)
+    ld = (heads + 2 * kvh) * hd
+    qkv = rng.normal(0, 1, (ntok, ld)).astype(np.float32)
+    gate = rng.normal(0, 1, (ntok, heads)).astype(np.float32)
+    K, Kref = to_cache(rng.normal(0, 1, (kvh, slots, hd)), kv_type)
+    V, Vref = to_cache(rng.normal(0, 1, (kvh, slots, hd)), kv_type)
+    own = []
+    for t in range(ntok):
+        k = rope(qkv[t, heads * hd:(heads + kvh) * hd].reshape(kvh, hd).astype(np.float64), pos0 + t, freq, pdim)
+        v = qkv[t, (heads + kvh) * hd:].reshape(kvh, hd).astype(np.float64)
+        own.append((k, v))
+        Kref[:, pos0 + t] = to_cache(k.astype(np.float32), kv_type)[1]
+        Vref[:, pos0 + t] = to_cache(v.astype(np.float32), kv_type)[1]
+    want = reference(qkv, Kref, Vref, own, pos0, ntok, heads, kvh, hd, 1, 64, freq, pdim, gate)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+    t_qkv, t_gate, t_freq, t_k, t_v = dev(qkv), dev(gate), dev(freq), dev(K), dev(V)
+    t_pos = torch.tensor([pos0], dtype=torch.int32, device=cuda)
+    t_out = torch.zeros(ntok, heads * hd, device=cuda)
+    ws = torch.zeros(L.spk_attn_workspace_bytes(ntok, heads, kvh, hd, nsplit), dtype=torch.uint8, device=cuda)
+    a = AttnArgs(t_qkv.data_ptr(), ld, t_k.data_ptr(), t_v.data_ptr(), kv_type, slots, 1, 64, t_freq.data_ptr(),
+                 pdim, heads, kvh, hd, t_pos.data_ptr(), ntok, 1 if ntok == 1 else 0, nsplit, t_gate.data_ptr(),
+                 heads, t_out.data_ptr(), heads * hd, ws.data_ptr())
+    torch.cuda.synchronize()
+    if ntok > 1:
+        spk.check(L.spk_attn_store(C.byref(a), None))
+    for _ in range(2):
+        spk.check(L.spk_attn_decode(C.byref(a), None))
+        torch.cuda.synchronize()
+        got = t_out.cpu().numpy()
+        err = np.linalg.norm(got - want) / np.linalg.norm(want)
+        assert err < (1e-4 if kv_type == 2 else TOL), err
+
+
 def test_attention_rejects_bad_args(cuda):
     import spk
 
