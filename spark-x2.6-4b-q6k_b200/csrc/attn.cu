@@ -361,11 +361,21 @@ __global__ void attn_store_kernel(const AttnArgs a) {
 //  * O^T += V^T P^T: V^T by ldmatrix.trans, P as an f16 pair again (hi / lo columns).
 // The token's own row (the SIMT kernel's exact f32 row) is masked in the tiles and
 // enters the CTA merge as a fifth, exact f32 term.
+// q8_0 cache: K quants convert to f16 exactly at use, each 32-dim block's two k-steps
+// into a fresh accumulator scaled by that row's d; V quants are converted once per stage
+// into the padded f16 tile, and V's per-block scale multiplies P instead (one B operand
+// per 32-dim block), so every product stays exact.
 constexpr int TC_WARPS = 4, TC_THREADS = TC_WARPS * 32;
 constexpr int TC_POS = 64;                       // positions per stage, 16 per warp
-constexpr int TC_RS = 256 * 2 + 32;              // shared-memory bytes per K or V row (padded)
-constexpr int TC_STAGE = TC_POS * TC_RS;         // bytes of K (or V) per stage
-constexpr size_t TC_SMEM = (size_t)2 * 2 * TC_STAGE;
+constexpr int TC_RS = 256 * 2 + 32;              // shared-memory bytes of an f16 K or V row (padded)
+constexpr int TC_RS8 = 256 + 16;                 // a q8_0 row as cached (272 bytes: conflict-free as is)
+template <int KT>
+struct TcLayout {
+    static constexpr int KRS = KT == KV_Q8 ? TC_RS8 : TC_RS;   // K row stride in a slot
+    static constexpr int CH = KT == KV_Q8 ? TC_RS8 / 16 : 32;  // 16-byte chunks per cached row
+    static constexpr int SLOT = 2 * TC_POS * KRS;               // K then V rows as loaded
+    static constexpr size_t SMEM = (size_t)2 * SLOT + (KT == KV_Q8 ? (size_t)TC_POS * TC_RS : 0);   // + f16 V
+};
 
 __device__ __forceinline__ void cp_async16(void *smem_dst, const void *src, bool valid) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(src),
@@ -393,6 +403,18 @@ __device__ __forceinline__ void mma_f16_tc(float (&d)[4], uint32_t a0, uint32_t 
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// Four int8 of w as two exact f16 pairs (bytes 0,1 | bytes 2,3), low half first:
+// byte ^ 0x80 under the exponent of 1024 (0x64bb == 1024 + bb), minus 1152.
+__device__ __forceinline__ void s8x4_to_f16_exact(uint32_t w, uint32_t &lo, uint32_t &hi) {
+    const uint32_t b = w ^ 0x80808080u;
+    uint32_t l = __byte_perm(b, 0x64646464u, 0x5140u), h = __byte_perm(b, 0x64646464u, 0x7362u);
+    const __half2 bias = __half2half2(__ushort_as_half((unsigned short)0x6480u));
+    const __half2 lv = __hsub2(*reinterpret_cast<__half2 *>(&l), bias);
+    const __half2 hv = __hsub2(*reinterpret_cast<__half2 *>(&h), bias);
+    lo = *reinterpret_cast<const uint32_t *>(&lv);
+    hi = *reinterpret_cast<const uint32_t *>(&hv);
+}
+
 // (x, y) as an f16 pair: the hi parts rn(x), rn(y), or the lo parts rn(x - hi), rn(y - hi).
 __device__ __forceinline__ uint32_t f16_pair(float x, float y, bool lo) {
     const __half hx = __float2half_rn(x), hy = __float2half_rn(y);
@@ -405,6 +427,8 @@ template <int KT>
 __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const AttnArgs a) {
     constexpr int HD = 256, MG = ATT_MAX_GROUP, PR = HD + 4, NW = TC_WARPS + 1;
     constexpr size_t RB = kv_row_bytes(KT, HD);
+    using TL = TcLayout<KT>;
+    constexpr bool Q8 = KT == KV_Q8;
     extern __shared__ __align__(16) uint8_t tsm[];
     __shared__ float qs[MG][HD];
     __shared__ float kn[HD], vn[HD];
@@ -466,14 +490,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const AttnArgs a
     const uint8_t *vbase = reinterpret_cast<const uint8_t *>(a.vc) + (size_t)kvh * a.slots * RB;
     const int nstage = c0 < c1 ? (c1 - c0 + TC_POS - 1) / TC_POS : 0;
     auto issue = [&](int st, int slot) {
-        uint8_t *kd = tsm + (size_t)slot * 2 * TC_STAGE, *vd = kd + TC_STAGE;
+        uint8_t *kd = tsm + (size_t)slot * TL::SLOT, *vd = kd + TC_POS * TL::KRS;
         const int js = c0 + st * TC_POS;
-        for (int i = threadIdx.x; i < TC_POS * 32; i += TC_THREADS) {   // 32 chunks of 16 bytes a row
-            const int r = i >> 5, c = i & 31, j = js + r;
+        for (int i = threadIdx.x; i < TC_POS * TL::CH; i += TC_THREADS) {   // 16-byte chunks of the rows
+            const int r = i / TL::CH, c = i - r * TL::CH, j = js + r;
             const bool v = j < c1;
             const size_t off = (size_t)((v ? j : c0) % a.slots) * RB + 16 * c;
-            cp_async16(kd + r * TC_RS + 16 * c, kbase + off, v);
-            cp_async16(vd + r * TC_RS + 16 * c, vbase + off, v);
+            cp_async16(kd + r * TL::KRS + 16 * c, kbase + off, v);
+            cp_async16(vd + r * TL::KRS + 16 * c, vbase + off, v);
         }
         cp_async_commit();
     };
@@ -485,16 +509,50 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const AttnArgs a
     for (int st = 0; st < nstage; st++) {
         cp_async_wait<1>();
         __syncthreads();   // stage st landed for every thread
-        const uint8_t *kt = tsm + (size_t)(st & 1) * 2 * TC_STAGE, *vt = kt + TC_STAGE;
+        const uint8_t *kt = tsm + (size_t)(st & 1) * TL::SLOT, *vraw = kt + TC_POS * TL::KRS;
+        const uint8_t *vt = vraw;   // the f16 V tile ldmatrix reads
+        if constexpr (Q8) {   // V quants -> the f16 tile (exact); the scales stay in the raw rows
+            uint8_t *v16 = tsm + (size_t)2 * TL::SLOT;
+            for (int i = threadIdx.x; i < TC_POS * (HD / 4); i += TC_THREADS) {
+                const int r = i / (HD / 4), w = i - r * (HD / 4);
+                uint32_t lo, hi;
+                s8x4_to_f16_exact(*reinterpret_cast<const uint32_t *>(vraw + (size_t)r * TL::KRS + 4 * w), lo, hi);
+                *reinterpret_cast<uint2 *>(v16 + (size_t)r * TC_RS + 8 * w) = make_uint2(lo, hi);
+            }
+            __syncthreads();
+            vt = v16;
+        }
         const int jw = c0 + st * TC_POS + 16 * warp;   // this warp's first position
         if (jw < c1) {
             float sc[4] = {0.f, 0.f, 0.f, 0.f};
-            const uint8_t *ra = kt + (size_t)(16 * warp + g) * TC_RS + 8 * t, *rb8 = ra + (size_t)8 * TC_RS;
+            if constexpr (Q8) {
+                const uint8_t *ra = kt + (size_t)(16 * warp + g) * TL::KRS, *rb8 = ra + (size_t)8 * TL::KRS;
 #pragma unroll
-            for (int ks = 0; ks < 16; ks++) {
-                const uint2 ka = *reinterpret_cast<const uint2 *>(ra + 32 * ks);
-                const uint2 kb = *reinterpret_cast<const uint2 *>(rb8 + 32 * ks);
-                mma_f16_tc(sc, ka.x, kb.x, ka.y, kb.y, qb[ks][0], qb[ks][1]);
+                for (int b = 0; b < HD / 32; b++) {
+                    float sb[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                    for (int kk = 0; kk < 2; kk++) {
+                        const int ks = 2 * b + kk;
+                        uint32_t a0, a1, a2, a3;
+                        s8x4_to_f16_exact(*reinterpret_cast<const uint32_t *>(ra + 16 * ks + 4 * t), a0, a2);
+                        s8x4_to_f16_exact(*reinterpret_cast<const uint32_t *>(rb8 + 16 * ks + 4 * t), a1, a3);
+                        mma_f16_tc(sb, a0, a1, a2, a3, qb[ks][0], qb[ks][1]);
+                    }
+                    const float da = __half2float(reinterpret_cast<const __half *>(ra + HD)[b]);
+                    const float db = __half2float(reinterpret_cast<const __half *>(rb8 + HD)[b]);
+                    sc[0] = fmaf(da, sb[0], sc[0]);
+                    sc[1] = fmaf(da, sb[1], sc[1]);
+                    sc[2] = fmaf(db, sb[2], sc[2]);
+                    sc[3] = fmaf(db, sb[3], sc[3]);
+                }
+            } else {
+                const uint8_t *ra = kt + (size_t)(16 * warp + g) * TC_RS + 8 * t, *rb8 = ra + (size_t)8 * TC_RS;
+#pragma unroll
+                for (int ks = 0; ks < 16; ks++) {
+                    const uint2 ka = *reinterpret_cast<const uint2 *>(ra + 32 * ks);
+                    const uint2 kb = *reinterpret_cast<const uint2 *>(rb8 + 32 * ks);
+                    mma_f16_tc(sc, ka.x, kb.x, ka.y, kb.y, qb[ks][0], qb[ks][1]);
+                }
             }
 #pragma unroll
             for (int e = 0; e < 4; e++) sc[e] += __shfl_xor_sync(0xffffffffu, sc[e], 2);   // hi + lo
@@ -538,15 +596,34 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const AttnArgs a
             }
             __syncwarp();
             const int hh = g & 3;
-            const uint32_t pb0 = f16_pair(pt[warp][2 * t][hh], pt[warp][2 * t + 1][hh], g >= 4);
-            const uint32_t pb1 = f16_pair(pt[warp][2 * t + 8][hh], pt[warp][2 * t + 9][hh], g >= 4);
+            const float q0 = pt[warp][2 * t][hh], q1 = pt[warp][2 * t + 1][hh];
+            const float q2 = pt[warp][2 * t + 8][hh], q3 = pt[warp][2 * t + 9][hh];
             __syncwarp();
             const uint8_t *vr = vt + (size_t)(16 * warp + vpos) * TC_RS + 2 * vdim;
+            if constexpr (Q8) {   // per 32-dim block b: B = (P * d_b) as an f16 pair
+                const __half *dr = reinterpret_cast<const __half *>(vraw + (size_t)(16 * warp + 2 * t) * TL::KRS + HD);
+                const size_t rs = TL::KRS / 2;   // row stride in halves
 #pragma unroll
-            for (int mt = 0; mt < 16; mt++) {
-                uint32_t av[4];
-                ldsm_x4_trans(av, vr + 32 * mt);
-                mma_f16_tc(o[mt], av[0], av[1], av[2], av[3], pb0, pb1);
+                for (int b = 0; b < HD / 32; b++) {
+                    const float d0 = __half2float(dr[b]), d1 = __half2float(dr[rs + b]);
+                    const float d8 = __half2float(dr[8 * rs + b]), d9 = __half2float(dr[9 * rs + b]);
+                    const uint32_t pb0 = f16_pair(q0 * d0, q1 * d1, g >= 4);
+                    const uint32_t pb1 = f16_pair(q2 * d8, q3 * d9, g >= 4);
+#pragma unroll
+                    for (int mt = 2 * b; mt < 2 * b + 2; mt++) {
+                        uint32_t av[4];
+                        ldsm_x4_trans(av, vr + 32 * mt);
+                        mma_f16_tc(o[mt], av[0], av[1], av[2], av[3], pb0, pb1);
+                    }
+                }
+            } else {
+                const uint32_t pb0 = f16_pair(q0, q1, g >= 4), pb1 = f16_pair(q2, q3, g >= 4);
+#pragma unroll
+                for (int mt = 0; mt < 16; mt++) {
+                    uint32_t av[4];
+                    ldsm_x4_trans(av, vr + 32 * mt);
+                    mma_f16_tc(o[mt], av[0], av[1], av[2], av[3], pb0, pb1);
+                }
             }
         }
         __syncthreads();   // every warp is done with this slot
@@ -623,17 +700,19 @@ int attn_decode(const AttnArgs &a, cudaStream_t s) {
     const bool longs = (span + a.nsplit - 1) / a.nsplit >= 64;
     if (a.hd != 256 && a.hd != 128) return set_error("attention: head_dim %d (128 or 256)", a.hd);
     if (a.kv_type < KV_F32 || a.kv_type > KV_Q8) return set_error("attention: cache type %d", a.kv_type);
-    if (a.hd == 256 && a.kv_type == KV_F16) {   // the tensor-core kernel
-        static int opted[64];
+    if (a.hd == 256 && (a.kv_type == KV_F16 || a.kv_type == KV_Q8)) {   // the tensor-core kernel
+        static int opted[2][64];
         int dev = 0;
         cudaGetDevice(&dev);
-        if (!opted[dev & 63]) {
-            cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<KV_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 (int)TC_SMEM);
+        const int q8 = a.kv_type == KV_Q8;
+        auto k = q8 ? attn_tc_kernel<KV_Q8> : attn_tc_kernel<KV_F16>;
+        const size_t sm = q8 ? TcLayout<KV_Q8>::SMEM : TcLayout<KV_F16>::SMEM;
+        if (!opted[q8][dev & 63]) {
+            cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
             if (e != cudaSuccess) return cuda_fail("attention shared-memory opt-in", e);
-            opted[dev & 63] = 1;
+            opted[q8][dev & 63] = 1;
         }
-        const cudaError_t e = launch_pdl(attn_tc_kernel<KV_F16>, grid, dim3(TC_THREADS), TC_SMEM, s, a);
+        const cudaError_t e = launch_pdl(k, grid, dim3(TC_THREADS), sm, s, a);
         return e == cudaSuccess ? 0 : cuda_fail("attention launch", e);
     }
     const int sel = (a.hd == 256 ? 0 : 6) + a.kv_type * 2 + (longs ? 1 : 0);

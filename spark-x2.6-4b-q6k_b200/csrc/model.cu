@@ -292,6 +292,8 @@ int enqueue_verify(spk_model *m, int ntok) {
             return -1;
         AttnArgs a = attn_args(m, li, ntok);
         a.store = 0;
+        // ntok times a decode step's CTAs: fewer splits keep the grid near one wave
+        a.nsplit = std::max(1, std::min(a.nsplit, (sm_count() + m->kvl * ntok - 1) / (m->kvl * ntok)));
         if (attn_store_batch(a, s) || attn_decode(a, s)) return -1;
         if (vq_batch(L.m[2], ntok, m->attn, m->q_dim, nullptr, 0.f, tp ? m->pbuf : m->h, H, tp ? 0 : 1, s)) return -1;
         if (tp && tp_sum(m->tpv, m->pbuf, m->h, ntok * H, s)) return -1;
