@@ -351,7 +351,8 @@ __global__ void attn_store_kernel(const AttnArgs a) {
 // contractions on the tensor cores (mma.sync m16n8k16 f16 -> f32):
 //  * K and V rows of 64 positions per stage arrive by cp.async (16 bytes a thread,
 //    zero-filled past the split) into two slots of 544-byte rows (padded: no bank
-//    conflicts); each of the 4 warps takes 16 positions of a stage.
+//    conflicts); each 16-position tile of a stage goes to a pair of warps, which both
+//    form its scores and softmax and split the PV product's 256 dims (8 warps a CTA).
 //  * S^T = K q^T: K rows are the A operand (positions as rows; a thread's four k-slots
 //    are four consecutive dims, one 8-byte load), B holds the group's q heads as an
 //    f16 pair, hi in columns 0..3 and lo in 4..7, so one MMA per 16 dims gives ~22-bit
@@ -365,8 +366,9 @@ __global__ void attn_store_kernel(const AttnArgs a) {
 // into a fresh accumulator scaled by that row's d; V quants are converted once per stage
 // into the padded f16 tile, and V's per-block scale multiplies P instead (one B operand
 // per 32-dim block), so every product stays exact.
-constexpr int TC_WARPS = 4, TC_THREADS = TC_WARPS * 32;
-constexpr int TC_POS = 64;                       // positions per stage, 16 per warp
+constexpr int TC_WARPS = 8, TC_THREADS = TC_WARPS * 32;
+constexpr int TC_POS = 64;                       // positions per stage
+constexpr int TC_TILES = TC_POS / 16;            // 16-position tiles per stage, two warps each
 constexpr int TC_RS = 256 * 2 + 32;              // shared-memory bytes of an f16 K or V row (padded)
 constexpr int TC_RS8 = 256 + 16;                 // a q8_0 row as cached (272 bytes: conflict-free as is)
 template <int KT>
@@ -425,7 +427,7 @@ __device__ __forceinline__ uint32_t f16_pair(float x, float y, bool lo) {
 
 template <int KT>
 __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const AttnArgs a) {
-    constexpr int HD = 256, MG = ATT_MAX_GROUP, PR = HD + 4, NW = TC_WARPS + 1;
+    constexpr int HD = 256, MG = ATT_MAX_GROUP, PR = HD + 4, NW = TC_TILES + 1;
     constexpr size_t RB = kv_row_bytes(KT, HD);
     using TL = TcLayout<KT>;
     constexpr bool Q8 = KT == KV_Q8;
@@ -434,7 +436,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const AttnArgs a
     __shared__ float kn[HD], vn[HD];
     __shared__ float wm[NW][MG], wl[NW][MG];
     __shared__ float wo[NW][MG][HD];
-    __shared__ float pt[TC_WARPS][16][MG];
+    __shared__ float pt[TC_WARPS][16][MG];   // each warp's P, transposed for the B operand
     __shared__ float cw[MG][ATT_MAX_SPLIT];
     __shared__ float cl[MG];
     __shared__ int is_last;
@@ -454,6 +456,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const AttnArgs a
     const size_t pstride = (size_t)G * PR;
     float *out = a.part + (pbase + split) * pstride;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, t = lane & 3;
+    const int tw = warp % TC_TILES, dh = warp / TC_TILES;   // the warp's tile of a stage and its PV dims half
 
     for (int i = threadIdx.x; i < MG * HD; i += blockDim.x)
         qs[i / HD][i % HD] = i / HD < G ? qrow[(size_t)(kvh * G + i / HD) * HD + i % HD] : 0.f;
@@ -481,9 +484,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const AttnArgs a
         qb[ks][0] = f16_pair(qh[0], qh[1], g >= 4);
         qb[ks][1] = f16_pair(qh[2], qh[3], g >= 4);
     }
-    float o[16][4];
+    float o[8][4];   // O^T for dims 128 dh .. 128 dh + 127: m-tiles 8 dh + i
 #pragma unroll
-    for (int mt = 0; mt < 16; mt++) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+    for (int i = 0; i < 8; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
     float mA = -INFINITY, mB = -INFINITY, lA = 0.f, lB = 0.f;   // heads 2(t&1), 2(t&1)+1
 
     const uint8_t *kbase = reinterpret_cast<const uint8_t *>(a.kc) + (size_t)kvh * a.slots * RB;
@@ -522,11 +525,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const AttnArgs a
             __syncthreads();
             vt = v16;
         }
-        const int jw = c0 + st * TC_POS + 16 * warp;   // this warp's first position
+        const int jw = c0 + st * TC_POS + 16 * tw;   // this warp's first position
         if (jw < c1) {
             float sc[4] = {0.f, 0.f, 0.f, 0.f};
             if constexpr (Q8) {
-                const uint8_t *ra = kt + (size_t)(16 * warp + g) * TL::KRS, *rb8 = ra + (size_t)8 * TL::KRS;
+                const uint8_t *ra = kt + (size_t)(16 * tw + g) * TL::KRS, *rb8 = ra + (size_t)8 * TL::KRS;
 #pragma unroll
                 for (int b = 0; b < HD / 32; b++) {
                     float sb[4] = {0.f, 0.f, 0.f, 0.f};
@@ -546,7 +549,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const AttnArgs a
                     sc[3] = fmaf(db, sb[3], sc[3]);
                 }
             } else {
-                const uint8_t *ra = kt + (size_t)(16 * warp + g) * TC_RS + 8 * t, *rb8 = ra + (size_t)8 * TC_RS;
+                const uint8_t *ra = kt + (size_t)(16 * tw + g) * TC_RS + 8 * t, *rb8 = ra + (size_t)8 * TC_RS;
 #pragma unroll
                 for (int ks = 0; ks < 16; ks++) {
                     const uint2 ka = *reinterpret_cast<const uint2 *>(ra + 32 * ks);
@@ -581,11 +584,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const AttnArgs a
             mA = nA;
             mB = nB;
 #pragma unroll
-            for (int mt = 0; mt < 16; mt++) {
-                o[mt][0] *= cA;
-                o[mt][1] *= cB;
-                o[mt][2] *= cA;
-                o[mt][3] *= cB;
+            for (int i = 0; i < 8; i++) {
+                o[i][0] *= cA;
+                o[i][1] *= cB;
+                o[i][2] *= cA;
+                o[i][3] *= cB;
             }
             // P^T as the B operand: row pos, column g (head g & 3, hi / lo), via shared memory
             if (t < 2) {
@@ -599,30 +602,31 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const AttnArgs a
             const float q0 = pt[warp][2 * t][hh], q1 = pt[warp][2 * t + 1][hh];
             const float q2 = pt[warp][2 * t + 8][hh], q3 = pt[warp][2 * t + 9][hh];
             __syncwarp();
-            const uint8_t *vr = vt + (size_t)(16 * warp + vpos) * TC_RS + 2 * vdim;
+            const uint8_t *vr = vt + (size_t)(16 * tw + vpos) * TC_RS + 2 * vdim + 256 * dh;
             if constexpr (Q8) {   // per 32-dim block b: B = (P * d_b) as an f16 pair
-                const __half *dr = reinterpret_cast<const __half *>(vraw + (size_t)(16 * warp + 2 * t) * TL::KRS + HD);
+                const __half *dr = reinterpret_cast<const __half *>(vraw + (size_t)(16 * tw + 2 * t) * TL::KRS + HD);
                 const size_t rs = TL::KRS / 2;   // row stride in halves
 #pragma unroll
-                for (int b = 0; b < HD / 32; b++) {
+                for (int bb = 0; bb < 4; bb++) {
+                    const int b = 4 * dh + bb;
                     const float d0 = __half2float(dr[b]), d1 = __half2float(dr[rs + b]);
                     const float d8 = __half2float(dr[8 * rs + b]), d9 = __half2float(dr[9 * rs + b]);
                     const uint32_t pb0 = f16_pair(q0 * d0, q1 * d1, g >= 4);
                     const uint32_t pb1 = f16_pair(q2 * d8, q3 * d9, g >= 4);
 #pragma unroll
-                    for (int mt = 2 * b; mt < 2 * b + 2; mt++) {
+                    for (int i = 2 * bb; i < 2 * bb + 2; i++) {
                         uint32_t av[4];
-                        ldsm_x4_trans(av, vr + 32 * mt);
-                        mma_f16_tc(o[mt], av[0], av[1], av[2], av[3], pb0, pb1);
+                        ldsm_x4_trans(av, vr + 32 * i);
+                        mma_f16_tc(o[i], av[0], av[1], av[2], av[3], pb0, pb1);
                     }
                 }
             } else {
                 const uint32_t pb0 = f16_pair(q0, q1, g >= 4), pb1 = f16_pair(q2, q3, g >= 4);
 #pragma unroll
-                for (int mt = 0; mt < 16; mt++) {
+                for (int i = 0; i < 8; i++) {
                     uint32_t av[4];
-                    ldsm_x4_trans(av, vr + 32 * mt);
-                    mma_f16_tc(o[mt], av[0], av[1], av[2], av[3], pb0, pb1);
+                    ldsm_x4_trans(av, vr + 32 * i);
+                    mma_f16_tc(o[i], av[0], av[1], av[2], av[3], pb0, pb1);
                 }
             }
         }
@@ -634,23 +638,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const AttnArgs a
 
     // this warp's (o, m, l) for the merge: O[h][dim] = O^T[dim][h] + O^T[dim][h + 4]
 #pragma unroll
-    for (int mt = 0; mt < 16; mt++)
+    for (int i = 0; i < 8; i++)
 #pragma unroll
-        for (int e = 0; e < 4; e++) o[mt][e] += __shfl_xor_sync(0xffffffffu, o[mt][e], 2);
+        for (int e = 0; e < 4; e++) o[i][e] += __shfl_xor_sync(0xffffffffu, o[i][e], 2);
     const int hA = 2 * (t & 1), hB = hA + 1;
-    if (t < 2) {
+    if (t < 2) {   // the pair's m, l agree (same scores, same code); each writes its dims half
 #pragma unroll
-        for (int mt = 0; mt < 16; mt++) {
-            wo[warp][hA][16 * mt + g] = o[mt][0];
-            wo[warp][hB][16 * mt + g] = o[mt][1];
-            wo[warp][hA][16 * mt + g + 8] = o[mt][2];
-            wo[warp][hB][16 * mt + g + 8] = o[mt][3];
+        for (int i = 0; i < 8; i++) {
+            const int d0 = 128 * dh + 16 * i + g;
+            wo[tw][hA][d0] = o[i][0];
+            wo[tw][hB][d0] = o[i][1];
+            wo[tw][hA][d0 + 8] = o[i][2];
+            wo[tw][hB][d0 + 8] = o[i][3];
         }
-        if (g == 0) {
-            wm[warp][hA] = mA;
-            wm[warp][hB] = mB;
-            wl[warp][hA] = lA;
-            wl[warp][hB] = lB;
+        if (g == 0 && dh == 0) {
+            wm[tw][hA] = mA;
+            wm[tw][hB] = mB;
+            wl[tw][hA] = lA;
+            wl[tw][hB] = lB;
         }
     }
     // the own row, exact in f32 (warp h: head h's score)
@@ -661,10 +666,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const AttnArgs a
             for (int d = lane; d < HD; d += 32) sv = fmaf(qs[h][d], kn[d], sv);
         sv = warp_sum(sv);
         if (lane == 0) {
-            wm[TC_WARPS][h] = own && h < G ? sv * scale : -INFINITY;
-            wl[TC_WARPS][h] = own && h < G ? 1.f : 0.f;
+            wm[TC_TILES][h] = own && h < G ? sv * scale : -INFINITY;
+            wl[TC_TILES][h] = own && h < G ? 1.f : 0.f;
         }
-        for (int d = lane; d < HD; d += 32) wo[TC_WARPS][h][d] = own ? vn[d] : 0.f;
+        for (int d = lane; d < HD; d += 32) wo[TC_TILES][h][d] = own ? vn[d] : 0.f;
     }
     __syncthreads();
     for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
