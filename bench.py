@@ -367,6 +367,7 @@ def run_spec(args) -> None:
     d = DeviceDraft(dcfg, DW, max_ctx=max_ctx, device=dev, stream=m.stream)
     del DW
     m.enable_capture(dcfg.target_layers)
+    d.use_target_head(m)
     caps, stride = m.captures()
     m.advance_len(ctx)   # a zeroed KV cache at the context length (the attention reads the same bytes)
     d.encode_features(caps, stride, ctx - dcfg.swa_window - 1, ctx)   # the draft's window before pos0

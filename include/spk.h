@@ -278,6 +278,9 @@ void *spk_model_tp_mailbox(spk_model *m);
  * capture off. Rollback needs no action: later positions are rewritten when revisited. */
 int spk_model_enable_capture(spk_model *m, const int *layers, int n);
 const float *spk_model_captures(spk_model *m, size_t *slot_stride);
+/* The head's table re-laid for the tensor-core head (spk_q80_tile layout; this rank's
+ * vocabulary rows), made by spk_model_set_head; NULL when the geometry is not tiled. */
+const void *spk_model_head_tiled(spk_model *m);
 
 /* ------------------------------------------------ DSpark draft (row D) ---
  * The draft executor of tools/dspark/src/draft.rs (encode_features 567-628,
@@ -335,8 +338,25 @@ int spk_draft_encode(spk_draft *d, const float *caps, size_t slot_stride, int p0
  * The injected window before pos0 must be encoded. Synchronizes the draft's stream. */
 int spk_draft_block(spk_draft *d, const void *embed, int vocab, int anchor, int pos0, int n_draft, int *ids,
                     float *conf);
+/* The block's head from the target's tiled table (spk_model_head_tiled, all vocabulary rows)
+ * instead of the ggml blocks; NULL reverts. */
+int spk_draft_set_head_tiled(spk_draft *d, const void *tiled);
 /* The last block's biased logits, [n_block][vocab] f32 on device. */
 const float *spk_draft_logits(const spk_draft *d);
+
+/* The tied Q8_0 head in a tensor-core tile layout (no counterpart in the reference; it
+ * replaces the reference's per-row head GEMV over the same ggml blocks). spk_q80_tile
+ * re-lays a ggml Q8_0 matrix into [rows/16][cols/32] tile-blocks of 544 bytes (the 16 rows'
+ * 32 int8 in mma.sync fragment order, then their 16 f16 scales) in spk_q80_tile_bytes bytes;
+ * spk_q80_tile_head computes logits[n*ldl + r] = (W RMSNorm?(x[n*ldx ..]))[r] for ntok <= 8
+ * rows and, when amax is not NULL, the first-max argmax per row. rows % 16 == 0, cols a
+ * multiple of 32 in [256, 4096]; scratch is spk_q80_tile_scratch_bytes() device bytes, zeroed
+ * once and left zeroed; calls sharing a scratch must not overlap on the GPU. */
+size_t spk_q80_tile_bytes(int rows, int cols);
+int spk_q80_tile(const void *w, int rows, int cols, void *dst, void *stream);
+size_t spk_q80_tile_scratch_bytes(void);
+int spk_q80_tile_head(const void *wt, int rows, int cols, int ntok, const float *x, int ldx, const float *norm_w,
+                      float eps, float *logits, int ldl, int *amax, void *scratch, void *stream);
 
 /* The draft's skinny BF16 GEMM (dspark-gpu.h:897-907 draft_gemm): y[n*ldy + r] (=, or +=)
  * (W x[n*ldx ..])[r] for n < ntok <= 8; W bf16 [rows][cols], 16-byte aligned, cols % 32 == 0. */

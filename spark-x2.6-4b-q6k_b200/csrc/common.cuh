@@ -87,6 +87,15 @@ int q80_head_batch_launch(const void *w, int rows, int cols, int ntok, const flo
                           float eps, float *logits, int ldl, int *amax, unsigned long long *partial,
                           unsigned int *counter, cudaStream_t s);
 
+// The tied Q8_0 head in the tensor-core tile layout (q8t.cu): bytes of the tiled table,
+// the re-lay from ggml blocks, its scratch (zeroed once), and the head for ntok <= 8 rows
+// (1 launched, 0 geometry not taken, -1 error).
+size_t q8t_bytes(int rows, int cols);
+size_t q8t_scratch();
+int q8t_pack(const void *w, int rows, int cols, void *dst, cudaStream_t s);
+int q8t_head_launch(const void *wt, int rows, int cols, int ntok, const float *x, int ldx, const float *norm_w,
+                    float eps, float *logits, int ldl, int *amax, void *scratch, cudaStream_t s);
+
 // Q8_0 head (logits + argmax) with caller-owned scratch (ggml.cu).
 int q80_head_launch(const void *w, int rows, int cols, const float *x, const float *norm_w, float eps, float *logits,
                     int *argmax_out, unsigned long long *partial, unsigned int *counter, cudaStream_t s);

@@ -468,6 +468,8 @@ struct spk_draft {
     float *host_conf = nullptr;
     cudaStream_t stream = nullptr;
     int vocab_target = 0;
+    const void *head_tiled = nullptr;   // optional: the target head's tiled table (q8t.cu)
+    void *qt_scratch = nullptr;
 };
 
 namespace {
@@ -606,6 +608,7 @@ void spk_draft_destroy(spk_draft *d) {
                     d->head_partial, d->head_counter, d->mk_partial, d->mk_counter};
     for (void *b : bufs)
         if (b) cudaFree(b);
+    if (d->qt_scratch) cudaFree(d->qt_scratch);
     if (d->host_ids) cudaFreeHost(d->host_ids);
     if (d->host_conf) cudaFreeHost(d->host_conf);
     delete d;
@@ -742,9 +745,14 @@ int spk_draft_block(spk_draft *d, const void *embed, int vocab, int anchor, int 
         }
     }
     if (rms_rows(d->x, H, 0, d->g.out_norm, 0, d->hid, H, 0, H, 1, nb, c.eps, 0, 0.f, s)) return -1;
-    // the target's tied head over all rows in one pass, else row by row
-    const int hb = q80_head_batch_launch(embed, vocab, H, nb, d->hid, H, nullptr, c.eps, d->logits, vocab, d->amax,
-                                         d->head_partial, d->head_counter, s);
+    // the target's tied head over all rows in one pass (its tiled table when the target shares
+    // it, else the ggml blocks), else row by row
+    int hb = d->head_tiled ? q8t_head_launch(d->head_tiled, vocab, H, nb, d->hid, H, nullptr, c.eps, d->logits, vocab,
+                                             d->amax, d->qt_scratch, s)
+                           : 0;
+    if (hb == 0)
+        hb = q80_head_batch_launch(embed, vocab, H, nb, d->hid, H, nullptr, c.eps, d->logits, vocab, d->amax,
+                                   d->head_partial, d->head_counter, s);
     if (hb < 0) return -1;
     if (hb == 0)
         for (int i = 0; i < nb; i++)
@@ -791,6 +799,19 @@ int spk_draft_block(spk_draft *d, const void *embed, int vocab, int anchor, int 
     if (conf)   // NaN where the reference leaves it (no Markov or no confidence head)
         for (int i = 0; i < nb; i++) conf[i] = markov && d->g.conf_proj ? d->host_conf[i] : NAN;
     return nb;
+}
+
+/* Read the block's logits from the target head's tiled table (spk_model_head_tiled: the same
+ * embedding in the q8t layout, all vocabulary rows) instead of the ggml blocks; NULL reverts. */
+int spk_draft_set_head_tiled(spk_draft *d, const void *tiled) {
+    if (!d) return set_error("draft is null");
+    if (tiled && !d->qt_scratch) {
+        if (dalloc(&d->qt_scratch, q8t_scratch())) return -1;
+        if (cudaMemset(d->qt_scratch, 0, q8t_scratch()) != cudaSuccess)
+            return cuda_fail("clear draft head scratch", cudaGetLastError());
+    }
+    d->head_tiled = tiled;
+    return 0;
 }
 
 /* The last block's biased logits, [n_block][vocab] f32 on device. */

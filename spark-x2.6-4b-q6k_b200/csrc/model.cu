@@ -111,6 +111,8 @@ struct spk_model {
     DevCtl *host_ctl = nullptr;   // pinned staging for it
     unsigned long long *head_partial = nullptr;
     unsigned int *head_counter = nullptr;
+    void *head_tiled = nullptr;   // this rank's head rows re-laid for the tensor-core head (q8t.cu)
+    void *head_tiled_scratch = nullptr;
     unsigned long long *vhead_partial = nullptr;   // the verify batch's head
     unsigned int *vhead_counter = nullptr;
     int *host_io = nullptr;       // pinned: pos, token, argmax; [8..16) verify tokens, [16..24) verify ids
@@ -234,9 +236,15 @@ int enqueue_step(spk_model *m) {
         }
     }
     const uint8_t *head_rows = (const uint8_t *)m->embed + (size_t)m->row0 * (c.hidden / 32) * 34;
-    if (q80_head_launch(head_rows, m->vocab_l, c.hidden, m->h, m->final_norm, c.eps, m->logits, tp ? amax_l : amax,
-                        m->head_partial, m->head_counter, s) || mark(m))
+    const int ht = m->head_tiled ? q8t_head_launch(m->head_tiled, m->vocab_l, c.hidden, 1, m->h, c.hidden,
+                                                   m->final_norm, c.eps, m->logits, m->vocab_l, tp ? amax_l : amax,
+                                                   m->head_tiled_scratch, s)
+                                 : 0;
+    if (ht < 0) return -1;
+    if (ht == 0 && q80_head_launch(head_rows, m->vocab_l, c.hidden, m->h, m->final_norm, c.eps, m->logits,
+                                   tp ? amax_l : amax, m->head_partial, m->head_counter, s))
         return -1;
+    if (mark(m)) return -1;
     if (tp && (tp_argmax(m->tpv, m->logits, m->vocab_l, amax_l, m->row0, amax, 1, s) || mark(m))) return -1;
     cudaError_t e = launch_pdl(advance_kernel, dim3(1), dim3(1), 0, s, pos, token, (const int *)amax,
                                (const DevCtl *)m->ctl, m->state + 3);
@@ -302,9 +310,13 @@ int enqueue_verify(spk_model *m, int ntok) {
         if (tp && tp_sum(m->tpv, m->pbuf, m->h, ntok * H, s)) return -1;
     }
     const uint8_t *head_rows = (const uint8_t *)m->embed + (size_t)m->row0 * (H / 32) * 34;
-    // all rows in one pass over the table (head_batch.cu), else row by row
-    const int hb = q80_head_batch_launch(head_rows, m->vocab_l, H, ntok, m->h, H, m->final_norm, c.eps, m->logits,
-                                         m->vocab_l, tp ? vam_l : vam, m->vhead_partial, m->vhead_counter, s);
+    // all rows in one pass over the table: the tiled head (q8t.cu), else head_batch.cu, else row by row
+    int hb = m->head_tiled ? q8t_head_launch(m->head_tiled, m->vocab_l, H, ntok, m->h, H, m->final_norm, c.eps,
+                                             m->logits, m->vocab_l, tp ? vam_l : vam, m->head_tiled_scratch, s)
+                           : 0;
+    if (hb == 0)
+        hb = q80_head_batch_launch(head_rows, m->vocab_l, H, ntok, m->h, H, m->final_norm, c.eps, m->logits,
+                                   m->vocab_l, tp ? vam_l : vam, m->vhead_partial, m->vhead_counter, s);
     if (hb < 0) return -1;
     for (int t = 0; hb == 0 && t < ntok; t++)
         if (q80_head_launch(head_rows, m->vocab_l, H, m->h + (size_t)t * H, m->final_norm, c.eps,
@@ -513,6 +525,8 @@ spk_model *spk_model_create(const spk_model_config *cfg, void *stream) {
 void spk_model_destroy(spk_model *m) {
     if (!m) return;
     if (m->cap) cudaFree(m->cap);
+    if (m->head_tiled) cudaFree(m->head_tiled);
+    if (m->head_tiled_scratch) cudaFree(m->head_tiled_scratch);
     if (m->exec) cudaGraphExecDestroy(m->exec);
     if (m->graph) cudaGraphDestroy(m->graph);
     if (m->texec) cudaGraphExecDestroy(m->texec);
@@ -576,6 +590,22 @@ int spk_model_set_head(spk_model *m, const void *embed_q80, const float *final_n
     if (!m || !embed_q80 || !final_norm) return set_error("head weights are missing");
     m->embed = embed_q80;
     m->final_norm = final_norm;
+    // the head's rows (this rank's vocabulary shard) re-laid once for the tensor-core head;
+    // the embedding row gather keeps reading the ggml blocks
+    const int H = m->cfg.hidden;
+    if (!m->head_tiled && m->vocab_l % 16 == 0 && H % 32 == 0 && H >= 256 && H <= 4096) {
+        if (alloc(&m->head_tiled, q8t_bytes(m->vocab_l, H), "alloc tiled head") ||
+            alloc(&m->head_tiled_scratch, q8t_scratch(), "alloc tiled head scratch"))
+            return -1;
+        if (cudaMemset(m->head_tiled_scratch, 0, q8t_scratch()) != cudaSuccess)
+            return cuda_fail("clear tiled head scratch", cudaGetLastError());
+    }
+    if (m->head_tiled) {
+        const uint8_t *rows = (const uint8_t *)embed_q80 + (size_t)m->row0 * (H / 32) * 34;
+        if (q8t_pack(rows, m->vocab_l, H, m->head_tiled, m->stream)) return -1;
+        cudaError_t e = cudaStreamSynchronize(m->stream);
+        if (e != cudaSuccess) return cuda_fail("tile the head", e);
+    }
     return 0;
 }
 
@@ -721,6 +751,8 @@ int spk_model_enable_capture(spk_model *m, const int *layers, int n) {
 
 /* Model::captured (model.rs:345-348): the capture rows on device, slot k of position p at
  * [k * *slot_stride + p * hidden]. NULL while capture is off. */
+const void *spk_model_head_tiled(spk_model *m) { return m ? m->head_tiled : nullptr; }
+
 const float *spk_model_captures(spk_model *m, size_t *slot_stride) {
     if (!m || !m->ncap) return nullptr;
     if (slot_stride) *slot_stride = (size_t)m->cfg.max_ctx * m->cfg.hidden;

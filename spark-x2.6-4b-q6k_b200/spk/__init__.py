@@ -93,7 +93,13 @@ _PROTOS = {
     "spk_draft_encode": ([_vp, _vp, C.c_size_t, _i, _i], _i),
     "spk_draft_block": ([_vp, _vp, _i, _i, _i, _i, _vp, _vp], _i),
     "spk_draft_logits": ([_vp], _vp),
+    "spk_draft_set_head_tiled": ([_vp, _vp], _i),
+    "spk_model_head_tiled": ([_vp], _vp),
     "spk_bf16_gemm": ([_vp, _i, _i, _i, _vp, _i, _vp, _i, _i, _vp], _i),
+    "spk_q80_tile_bytes": ([_i, _i], C.c_size_t),
+    "spk_q80_tile": ([_vp, _i, _i, _vp, _vp], _i),
+    "spk_q80_tile_scratch_bytes": ([], C.c_size_t),
+    "spk_q80_tile_head": ([_vp, _i, _i, _i, _vp, _i, _vp, _f, _vp, _i, _vp, _vp, _vp], _i),
     "spk_bf16_gemm_pair": ([_vp, _vp, _i, _i, _i, _vp, _i, _vp, _i, _i, _vp], _i),
 }
 

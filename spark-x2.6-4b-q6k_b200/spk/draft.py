@@ -244,6 +244,13 @@ class DeviceDraft:
             self.weight_bytes += t.numel() * 2
         return t.data_ptr()
 
+    def use_target_head(self, target) -> bool:
+        """Read the block's logits from the target's tiled head table when it has one (the
+        same Q8_0 embedding, re-laid for the tensor-core head; one GPU only)."""
+        p = lib().spk_model_head_tiled(target.h) if target.tp[1] == 1 else None
+        check(lib().spk_draft_set_head_tiled(self.h, C.c_void_p(p) if p else None), "draft head")
+        return bool(p)
+
     def encode_features(self, caps_ptr: int, slot_stride: int, p0: int, p1: int):
         """encode_features for the committed positions [p0, p1) (caps: the target's device
         captures, spk_model_captures)."""

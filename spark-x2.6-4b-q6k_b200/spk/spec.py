@@ -28,6 +28,7 @@ class SpecResult:
 def prepare(target, draft) -> None:
     """Model::enable_capture with the draft's target layers (spec.rs:141)."""
     target.enable_capture(draft.cfg.target_layers)
+    draft.use_target_head(target)
 
 
 def run(target, draft, ids: list, gen: int, n_max: int | None = None, acceptor=None) -> SpecResult:
