@@ -231,16 +231,35 @@ def run_ours(args) -> None:
     rows_l = m.mats[0]["gate"].rows
     act = torch.zeros(rows_l, device=dev)
     launches = []
+    # the model runs the pair through the table kernel (vq_lut.cu) at >= 8192 rows, when it
+    # takes the geometry: time that one, on index words re-laid here the way the model does
+    lut_n = L.spk_vq_lut_bytes(4, 4096, rows_l, cfg.hidden, 1) if rows_l >= 8192 else 0
+    luts = []
     for li in range(cfg.layers):
         g, u = m.mats[li]["gate"], m.mats[li]["up"]
-        st = (C.c_void_p * 4)(g.stages[0], g.stages[1], u.stages[0], u.stages[1])
-        launches.append((st, m.norms[li][1]))
+        stp = [g.stages[0], g.stages[1], u.stages[0], u.stages[1]]
+        st = (C.c_void_p * 4)(*stp)
+        lt = None
+        if lut_n:
+            ws = [torch.empty(lut_n, dtype=torch.uint8, device=dev) for _ in range(4)]
+            for p_, w_ in zip(stp, ws):
+                spk.check(L.spk_vq_lut_pack(C.c_void_p(p_), 4, 4096, rows_l, cfg.hidden, 1, w_.data_ptr(), None))
+            luts.append(ws)
+            lt = (C.c_void_p * 4)(*[w_.data_ptr() for w_ in ws])
+        launches.append((st, lt, m.norms[li][1]))
+    scr = (torch.empty(L.spk_vq_lut_scratch_bytes(2, 4, 4096, rows_l, cfg.hidden, 1), dtype=torch.uint8, device=dev)
+           if lut_n else None)
+    torch.cuda.synchronize(dev)
     sp = C.c_void_p(m.stream.cuda_stream)
 
     def gateup(k):
-        st, nw = launches[k % cfg.layers]
-        spk.check(L.spk_vq_gemv(st, 2, 2, 4, 4096, rows_l, cfg.hidden, 1, x.data_ptr(), nw.data_ptr(), cfg.eps,
-                                act.data_ptr(), 0, sp))
+        st, lt, nw = launches[k % cfg.layers]
+        if lt is not None:
+            spk.check(L.spk_vq_lut_gemv(st, lt, 2, 2, 4, 4096, rows_l, cfg.hidden, 1, x.data_ptr(), nw.data_ptr(),
+                                        cfg.eps, act.data_ptr(), 0, scr.data_ptr(), sp))
+        else:
+            spk.check(L.spk_vq_gemv(st, 2, 2, 4, 4096, rows_l, cfg.hidden, 1, x.data_ptr(), nw.data_ptr(), cfg.eps,
+                                    act.data_ptr(), 0, sp))
 
     for k in range(cfg.layers):
         gateup(k)
@@ -257,7 +276,9 @@ def run_ours(args) -> None:
     alg_bytes = 2 * 2 * stage + 2 * cfg.hidden * 4 + rows_l * 4
     peak, peak_kind = hbm_peak()
     achieved = alg_bytes / t_kernel / 1e9
-    traffic = traffic_from_profiles("vq_gate_up_gemv_10240x2560x2") if world == 1 else None
+    traffic = (traffic_from_profiles("vq_lut_gate_up_10240x2560x2" if lut_n else "vq_gate_up_gemv_10240x2560x2")
+               if world == 1 else None)
+    del luts
 
     # end to end through the C-ABI with host buffers: token up, next id down, every step
     e2e_n = min(args.steps, 64)
@@ -284,6 +305,7 @@ def run_ours(args) -> None:
     row = {"f32": cfg.head_dim * 4, "f16": cfg.head_dim * 2, "q8": cfg.head_dim + cfg.head_dim // 16}[args.kv]
     kv_bytes = sum((args.ctx if f else cfg.window) for f in cfg.full) * kv_heads_l * row * 2
     cb = cpu_baseline(args.ctx) if (rank == 0 and world == 1 and not args.no_cpu) else None
+    step_launches = L.spk_model_step_launches(C.c_void_p(m.h))
     m.close()
     if rank == 0:
         line = {
@@ -302,12 +324,13 @@ def run_ours(args) -> None:
                        "step_hbm_gbs_per_gpu": (bytes_per_token + kv_bytes) * args.steps / dt / 1e9,
                        "step_trace_rank0": trace},
             "roofline": {"bound": "hbm",
-                         "kernel": f"vq_fast_kernel gate+up pair {rows_l}x2560 x2 stages (RMSNorm, GELU), rank 0",
+                         "kernel": (("vq_lut_kernel + vq_lut_finish_kernel" if lut_n else "vq_fast_kernel") +
+                                    f" gate+up pair {rows_l}x2560 x2 stages (RMSNorm, GELU), rank 0"),
                          "achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "alg_bytes_per_launch": alg_bytes,
                          "us_per_launch": t_kernel * 1e6},
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4},
-            "gpu_launches": args.steps * (3 + 5 * cfg.layers + (2 * cfg.layers + 1 if world > 1 else 0)),
+            "gpu_launches": args.steps * step_launches,
             "clocks": clk.summary(),
         }
         if cb:

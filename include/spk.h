@@ -98,6 +98,23 @@ int vqg_prefill_launch_tile(const void *payload, int dim, int nc, int rows, int 
  * (replaces rmsnorm_kernel, vq-model-gpu.cu:364-377). */
 int spk_vq_gemv(const void *const *stages, int nstages, int ngroups, int dim, int nc, int rows, int cols, int v3,
                 const float *x, const float *norm_w, float eps, float *y, int accumulate, void *stream);
+/* The same GEMV as shared-memory table look-ups (the decode step's kernel for DQV3 dim 4,
+ * 4096 codes, 12-bit indices; replaces the same per-stage loop as spk_vq_gemv). Each stage's
+ * index stream is re-laid once, slice-major (spk_vq_lut_pack into spk_vq_lut_bytes device
+ * bytes, 0 = geometry not taken); spk_vq_lut_gemv then takes spk_vq_gemv's arguments plus
+ * the re-laid words (group-major like stages) and spk_vq_lut_scratch_bytes of device
+ * scratch, and runs two launches (the table kernel, then the per-row sum and epilogue). */
+size_t spk_vq_lut_bytes(int dim, int nc, int rows, int cols, int v3);
+int spk_vq_lut_pack(const void *stage, int dim, int nc, int rows, int cols, int v3, void *dst, void *stream);
+size_t spk_vq_lut_scratch_bytes(int ngroups, int dim, int nc, int rows, int cols, int v3);
+int spk_vq_lut_gemv(const void *const *stages, const void *const *luts, int nstages, int ngroups, int dim, int nc,
+                    int rows, int cols, int v3, const float *x, const float *norm_w, float eps, float *y,
+                    int accumulate, void *scratch, void *stream);
+/* The same with the table kernel's block size chosen: threads 512 or 1024 (0 = default),
+ * as vqg_gemv_t takes one (decode-gpu.cu:800-807). */
+int spk_vq_lut_gemv_t(const void *const *stages, const void *const *luts, int nstages, int ngroups, int dim, int nc,
+                      int rows, int cols, int v3, const float *x, const float *norm_w, float eps, float *y,
+                      int accumulate, void *scratch, int threads, void *stream);
 /* 1 if spk_vq_gemv runs the persistent TMA kernel for this geometry, 0 if the generic one. */
 int spk_vq_gemv_fast_ok(int nstages, int ngroups, int dim, int nc, int rows, int cols, int v3);
 /* Bit-exact stage decode on a stream: out += decoded stage (vqg_dequant without timing). */
@@ -281,6 +298,9 @@ const float *spk_model_captures(spk_model *m, size_t *slot_stride);
 /* The head's table re-laid for the tensor-core head (spk_q80_tile layout; this rank's
  * vocabulary rows), made by spk_model_set_head; NULL when the geometry is not tiled. */
 const void *spk_model_head_tiled(spk_model *m);
+/* Kernels one decode step launches (known after the first spk_model_forward / run step;
+ * 0 before it). */
+int spk_model_step_launches(const spk_model *m);
 
 /* ------------------------------------------------ DSpark draft (row D) ---
  * The draft executor of tools/dspark/src/draft.rs (encode_features 567-628,

@@ -87,6 +87,18 @@ int q80_head_batch_launch(const void *w, int rows, int cols, int ntok, const flo
                           float eps, float *logits, int ldl, int *amax, unsigned long long *partial,
                           unsigned int *counter, cudaStream_t s);
 
+// The decode GEMV as shared-memory table look-ups (vq_lut.cu): DQV3 dim 4, 4096 codes.
+// lut_ok: the kernel takes the geometry; lut_bytes: one stage's re-laid index words;
+// lut_part_bytes: the partial-sum scratch; lut_gemv: spk_vq_gemv's contract (plus an
+// optional small extra matrix of the same input, g_proj) in two launches.
+bool lut_ok(const Layout &L, int ns, int ng);
+size_t lut_bytes(const Layout &L);
+size_t lut_part_bytes(const Layout &L, int ng);
+int lut_pack(const void *stage, const Layout &L, void *dst, cudaStream_t s);
+int lut_gemv(const void *const *stages, const void *const *luts, int ns, int ng, const Layout &L, const float *x,
+             const float *norm_w, float eps, float *y, int accumulate, float *part, const void *const *xst,
+             const Layout *XL, float *xy, cudaStream_t s, int threads = 0);
+
 // The tied Q8_0 head in the tensor-core tile layout (q8t.cu): bytes of the tiled table,
 // the re-lay from ggml blocks, its scratch (zeroed once), and the head for ntok <= 8 rows
 // (1 launched, 0 geometry not taken, -1 error).

@@ -80,6 +80,10 @@ struct spk_model {
         spk_vq_matrix m[6];   // qkv, attn_gate, out, gate, up, down
         const float *in_norm = nullptr, *post_norm = nullptr;
         bool set = false;
+        // the stages' index streams re-laid for the decode step's table kernel (vq_lut.cu),
+        // one allocation per matrix; null: the matrix runs the code-word kernel (vq.cu)
+        void *lut_mem[6] = {};
+        const void *lut[6][4] = {};
     };
     std::vector<Layer> layers;
     const void *embed = nullptr;
@@ -111,6 +115,9 @@ struct spk_model {
     DevCtl *host_ctl = nullptr;   // pinned staging for it
     unsigned long long *head_partial = nullptr;
     unsigned int *head_counter = nullptr;
+    int step_launches = 0;        // kernels one decode step launches (counted while enqueuing it)
+    float *lut_part = nullptr;    // the table kernel's per-slice partial sums (vq_lut.cu)
+    size_t lut_part_size = 0;
     void *head_tiled = nullptr;   // this rank's head rows re-laid for the tensor-core head (q8t.cu)
     void *head_tiled_scratch = nullptr;
     unsigned long long *vhead_partial = nullptr;   // the verify batch's head
@@ -155,6 +162,27 @@ int qkv_gate(const spk_model::Layer &L, const float *h, float eps, float *qkv, f
     return vq_call(G, 1, nullptr, h, L.in_norm, eps, gate, 0, s);
 }
 
+
+// Layer matrix mi (with mi2, the up_proj of a pair) through the table kernel when it
+// was re-laid for it: 0 launched, 1 not taken, -1 error. For q_k_v_proj, g_proj rides
+// along in the finishing kernel.
+int lut_call(spk_model *m, const spk_model::Layer &L, int mi, int mi2, const float *x, const float *norm_w, float eps,
+             float *y, int accumulate, float *xy, cudaStream_t s) {
+    const spk_vq_matrix &M = L.m[mi];
+    if (!L.lut[mi][0] || (mi2 >= 0 && !L.lut[mi2][0])) return 1;
+    const void *st[8], *lt[8];
+    for (int q = 0; q < M.nstages; q++) st[q] = M.stages[q], lt[q] = L.lut[mi][q];
+    if (mi2 >= 0)
+        for (int q = 0; q < M.nstages; q++) st[M.nstages + q] = L.m[mi2].stages[q], lt[M.nstages + q] = L.lut[mi2][q];
+    const Layout LM = make_layout(M.dim, M.nc, M.rows, M.cols, M.v3);
+    const spk_vq_matrix &G = L.m[1];
+    Layout LG;
+    const bool extra = xy && G.nstages == M.nstages && G.dim == M.dim && G.nc == M.nc && G.v3 == M.v3 && G.rows <= 64;
+    if (xy && !extra) return 1;
+    if (extra) LG = make_layout(G.dim, G.nc, G.rows, G.cols, G.v3);
+    return lut_gemv(st, lt, M.nstages, mi2 >= 0 ? 2 : 1, LM, x, norm_w, eps, y, accumulate, m->lut_part,
+                    extra ? G.stages : nullptr, extra ? &LG : nullptr, extra ? xy : nullptr, s) ? -1 : 0;
+}
 
 // The attention arguments of layer li for a batch of ntok tokens starting at the
 // device position (buffers [ntok][...]: qkv, gate, attn).
@@ -214,26 +242,34 @@ int enqueue_step(spk_model *m) {
     int *pos = m->state, *token = m->state + 1, *amax = m->state + 2, *amax_l = m->state + 4;
     const bool tp = m->tp_world > 1;
     if (mark(m) || spk_q80_row(m->embed, c.vocab, c.hidden, 0, token, m->h, s) || mark(m)) return -1;
+    // embedding row, head, advance; per layer attention plus one launch per code-word GEMV or
+    // two per table GEMV; per tensor-parallel exchange one, plus the vocabulary argmax
+    int nl = 3 + (tp ? 1 : 0);
     for (int li = 0; li < c.layers; li++) {
         const spk_model::Layer &L = m->layers[li];
         if (capture_rows(m, li, 1, s)) return -1;
-        if (qkv_gate(L, m->h, c.eps, m->qkv, m->gate, s) || mark(m)) return -1;
+        nl += (m->ncap && m->cap_slot[li] >= 0) + 1 + (tp ? 2 : 0);
+        int lr = lut_call(m, L, 0, -1, m->h, L.in_norm, c.eps, m->qkv, 0, m->gate, s);
+        if (lr < 0 || (lr == 1 && qkv_gate(L, m->h, c.eps, m->qkv, m->gate, s)) || mark(m)) return -1;
+        nl += lr == 0 ? 2 : 1;
         AttnArgs a = attn_args(m, li, 1);
         a.store = 1;
         if (attn_decode(a, s) || mark(m)) return -1;
-        if (tp) {
-            if (vq_call(L.m[2], 1, nullptr, m->attn, nullptr, 0.f, m->pbuf, 0, s) || mark(m)) return -1;
-            if (tp_sum(m->tpv, m->pbuf, m->h, c.hidden, s) || mark(m)) return -1;
-        } else if (vq_call(L.m[2], 1, nullptr, m->attn, nullptr, 0.f, m->h, 1, s) || mark(m)) {
+        float *const ro = tp ? m->pbuf : m->h;   // out_proj / down_proj: rank partial, or the residual
+        lr = lut_call(m, L, 2, -1, m->attn, nullptr, 0.f, ro, tp ? 0 : 1, nullptr, s);
+        if (lr < 0 || (lr == 1 && vq_call(L.m[2], 1, nullptr, m->attn, nullptr, 0.f, ro, tp ? 0 : 1, s)) || mark(m))
             return -1;
-        }
-        if (vq_call(L.m[3], 2, &L.m[4], m->h, L.post_norm, c.eps, m->act, 0, s) || mark(m)) return -1;
-        if (tp) {
-            if (vq_call(L.m[5], 1, nullptr, m->act, nullptr, 0.f, m->pbuf, 0, s) || mark(m)) return -1;
-            if (tp_sum(m->tpv, m->pbuf, m->h, c.hidden, s) || mark(m)) return -1;
-        } else if (vq_call(L.m[5], 1, nullptr, m->act, nullptr, 0.f, m->h, 1, s) || mark(m)) {
+        nl += lr == 0 ? 2 : 1;
+        if (tp && (tp_sum(m->tpv, m->pbuf, m->h, c.hidden, s) || mark(m))) return -1;
+        lr = lut_call(m, L, 3, 4, m->h, L.post_norm, c.eps, m->act, 0, nullptr, s);
+        if (lr < 0 || (lr == 1 && vq_call(L.m[3], 2, &L.m[4], m->h, L.post_norm, c.eps, m->act, 0, s)) || mark(m))
             return -1;
-        }
+        nl += lr == 0 ? 2 : 1;
+        lr = lut_call(m, L, 5, -1, m->act, nullptr, 0.f, ro, tp ? 0 : 1, nullptr, s);
+        if (lr < 0 || (lr == 1 && vq_call(L.m[5], 1, nullptr, m->act, nullptr, 0.f, ro, tp ? 0 : 1, s)) || mark(m))
+            return -1;
+        nl += lr == 0 ? 2 : 1;
+        if (tp && (tp_sum(m->tpv, m->pbuf, m->h, c.hidden, s) || mark(m))) return -1;
     }
     const uint8_t *head_rows = (const uint8_t *)m->embed + (size_t)m->row0 * (c.hidden / 32) * 34;
     const int ht = m->head_tiled ? q8t_head_launch(m->head_tiled, m->vocab_l, c.hidden, 1, m->h, c.hidden,
@@ -249,6 +285,7 @@ int enqueue_step(spk_model *m) {
     cudaError_t e = launch_pdl(advance_kernel, dim3(1), dim3(1), 0, s, pos, token, (const int *)amax,
                                (const DevCtl *)m->ctl, m->state + 3);
     if (e != cudaSuccess) return cuda_fail("decode step launch", e);
+    m->step_launches = nl;
     return mark(m);
 }
 
@@ -527,6 +564,10 @@ void spk_model_destroy(spk_model *m) {
     if (m->cap) cudaFree(m->cap);
     if (m->head_tiled) cudaFree(m->head_tiled);
     if (m->head_tiled_scratch) cudaFree(m->head_tiled_scratch);
+    for (auto &L : m->layers)
+        for (void *p : L.lut_mem)
+            if (p) cudaFree(p);
+    if (m->lut_part) cudaFree(m->lut_part);
     if (m->exec) cudaGraphExecDestroy(m->exec);
     if (m->graph) cudaGraphDestroy(m->graph);
     if (m->texec) cudaGraphExecDestroy(m->texec);
@@ -546,6 +587,52 @@ void spk_model_destroy(spk_model *m) {
     if (m->host_io) cudaFreeHost(m->host_io);
     if (m->host_ctl) cudaFreeHost(m->host_ctl);
     delete m;
+}
+
+// The matrices the decode step runs through the table kernel (vq_lut.cu): those it takes
+// with at least LUT_MIN_ROWS rows (a slice's table costs 4096 x 8 entries, so it pays back
+// only over many rows: measured faster than vq.cu for the 10240-row gate/up pair, slower
+// at 6144 and 2560 rows), the gate/up pair only together. Their index streams are re-laid once
+// here (the payloads stay: the verify batch and g_proj read them).
+constexpr int LUT_MIN_ROWS = 8192;
+
+static int relay_layer(spk_model *m, spk_model::Layer &L) {
+    for (int mi = 0; mi < 6; mi++) {
+        if (L.lut_mem[mi]) cudaFree(L.lut_mem[mi]);
+        L.lut_mem[mi] = nullptr;
+        for (int q = 0; q < 4; q++) L.lut[mi][q] = nullptr;
+    }
+    const int ng_of[6] = {1, 0, 1, 2, 2, 1};
+    bool take[6] = {};
+    for (int mi = 0; mi < 6; mi++) {
+        const spk_vq_matrix &M = L.m[mi];
+        const Layout LM = make_layout(M.dim, M.nc, M.rows, M.cols, M.v3);
+        take[mi] = ng_of[mi] && M.rows >= LUT_MIN_ROWS && lut_ok(LM, M.nstages, ng_of[mi]);
+        for (int q = 0; take[mi] && q < M.nstages; q++)
+            if (((uintptr_t)M.stages[q] + LM.cb_off) & 7) take[mi] = false;
+    }
+    take[3] = take[4] = take[3] && take[4];
+    for (int mi = 0; mi < 6; mi++) {
+        if (!take[mi]) continue;
+        const spk_vq_matrix &M = L.m[mi];
+        const Layout LM = make_layout(M.dim, M.nc, M.rows, M.cols, M.v3);
+        const size_t per = lut_bytes(LM);
+        if (alloc(&L.lut_mem[mi], per * M.nstages, "alloc vq table words")) return -1;
+        for (int q = 0; q < M.nstages; q++) {
+            L.lut[mi][q] = (const uint8_t *)L.lut_mem[mi] + per * q;
+            if (lut_pack(M.stages[q], LM, (void *)L.lut[mi][q], m->stream)) return -1;
+        }
+        const size_t need = lut_part_bytes(LM, ng_of[mi]);
+        if (need > m->lut_part_size) {
+            if (m->lut_part) cudaFree(m->lut_part);
+            m->lut_part = nullptr;
+            m->lut_part_size = 0;
+            if (alloc((void **)&m->lut_part, need, "alloc vq table partials")) return -1;
+            m->lut_part_size = need;
+        }
+    }
+    cudaError_t e = cudaStreamSynchronize(m->stream);
+    return e == cudaSuccess ? 0 : cuda_fail("re-lay the index streams", e);
 }
 
 static int check_mat(const spk_vq_matrix *M, int rows, int cols, const char *name) {
@@ -581,6 +668,7 @@ int spk_model_set_layer(spk_model *m, int layer, const spk_vq_matrix *qkv, const
     L.m[5] = *down;
     L.in_norm = in_norm;
     L.post_norm = post_norm;
+    if (relay_layer(m, L)) return -1;
     L.set = true;
     return 0;
 }
@@ -751,6 +839,8 @@ int spk_model_enable_capture(spk_model *m, const int *layers, int n) {
 
 /* Model::captured (model.rs:345-348): the capture rows on device, slot k of position p at
  * [k * *slot_stride + p * hidden]. NULL while capture is off. */
+int spk_model_step_launches(const spk_model *m) { return m ? m->step_launches : -1; }
+
 const void *spk_model_head_tiled(spk_model *m) { return m ? m->head_tiled : nullptr; }
 
 const float *spk_model_captures(spk_model *m, size_t *slot_stride) {

@@ -52,6 +52,11 @@ _PROTOS = {
     "vqg_prefill_launch": ([_vp, _i, _i, _i, _i, _i, _vp, _i, _vp, _i], _i),
     "vqg_prefill_launch_tile": ([_vp, _i, _i, _i, _i, _i, _vp, _i, _vp, _i, _i, _i], _i),
     "spk_vq_gemv": ([_vp, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _f, _vp, _i, _vp], _i),
+    "spk_vq_lut_bytes": ([_i, _i, _i, _i, _i], C.c_size_t),
+    "spk_vq_lut_pack": ([_vp, _i, _i, _i, _i, _i, _vp, _vp], _i),
+    "spk_vq_lut_scratch_bytes": ([_i, _i, _i, _i, _i, _i], C.c_size_t),
+    "spk_vq_lut_gemv": ([_vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _f, _vp, _i, _vp, _vp], _i),
+    "spk_vq_lut_gemv_t": ([_vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _f, _vp, _i, _vp, _i, _vp], _i),
     "spk_vq_gemv_fast_ok": ([_i] * 7, _i),
     "spk_vq_dequant": ([_vp, _i, _i, _i, _i, _i, _vp, _vp], _i),
     "spk_q6k_gemv": ([_vp, _i, _i, _vp, _vp, _f, _vp, _i, _vp], _i),
@@ -95,6 +100,7 @@ _PROTOS = {
     "spk_draft_logits": ([_vp], _vp),
     "spk_draft_set_head_tiled": ([_vp, _vp], _i),
     "spk_model_head_tiled": ([_vp], _vp),
+    "spk_model_step_launches": ([_vp], _i),
     "spk_bf16_gemm": ([_vp, _i, _i, _i, _vp, _i, _vp, _i, _i, _vp], _i),
     "spk_q80_tile_bytes": ([_i, _i], C.c_size_t),
     "spk_q80_tile": ([_vp, _i, _i, _vp, _vp], _i),
