@@ -480,10 +480,11 @@ spk_model *spk_model_create(const spk_model_config *cfg, void *stream) {
     m->pdim_full = pdim(c.rope_partial_full);
     m->pdim_slide = pdim(c.rope_partial_slide);
     // as many splits as SMs per KV head (the attention is latency-bound: every CTA's
-    // row loads in flight at once), with at least 16 positions per split
+    // row loads in flight at once), with at least 64 positions (one tensor-core stage) per
+    // split: a 512-position window measured 11.9 us at 8 splits, 12.8 us at 32
     const int per_head = std::min(ATT_MAX_SPLIT, sm_count() / m->kvl > 0 ? sm_count() / m->kvl : 1);
-    m->nsplit_full = std::max(1, std::min(per_head, (c.max_ctx + 15) / 16));
-    m->nsplit_slide = std::max(1, std::min(per_head, (std::min(c.window, c.max_ctx) + 15) / 16));
+    m->nsplit_full = std::max(1, std::min(per_head, (c.max_ctx + 63) / 64));
+    m->nsplit_slide = std::max(1, std::min(per_head, (std::min(c.window, c.max_ctx) + 63) / 64));
     if (c.kv_type < KV_F32 || c.kv_type > KV_Q8) {
         set_error("KV cache type %d (0 f32, 1 f16, 2 q8_0)", c.kv_type);
         delete m;

@@ -38,7 +38,7 @@ constexpr int LGC = 8;           // column groups per slice
 constexpr int LNC = 4096;        // codes
 constexpr int LMAXS = 2;         // stages
 constexpr int FR = 32;           // rows per CTA of the finishing kernel
-constexpr int FT = 256;          // threads of the finishing kernel
+constexpr int FT = 512;          // threads of the finishing kernel
 constexpr int FQ = FT / FR;      // slice lanes per row there
 constexpr int GX_MAX = 64;       // g_proj rows the finishing kernel takes
 constexpr int LMAXSEG = 8;       // segments a CTA of the table kernel may walk
@@ -175,25 +175,26 @@ __global__ void __launch_bounds__(NT, 1) vq_lut_kernel(const LutArgs a) {
     float *xs = srow + a.srow_cap;                       // [LMAXSEG][32] each segment's activations
     double *red = reinterpret_cast<double *>(xs + LMAXSEG * 32);   // [NT / 32]
     const int tid = threadIdx.x;
+    // unit indices (group, slice, row) fit in 32 bits (the host checks), so no 64-bit division
     const int R = a.rows, nsl = a.nsl;
-    const long long per_g = (long long)nsl * R, W = per_g * a.ng;
-    const long long u0 = W * blockIdx.x / gridDim.x, u1 = W * (blockIdx.x + 1) / gridDim.x;
+    const int per_g = nsl * R, W = per_g * a.ng;
+    const int u0 = (int)((long long)W * blockIdx.x / gridDim.x), u1 = (int)((long long)W * (blockIdx.x + 1) / gridDim.x);
     pdl_trigger();
     if (u0 < u1) {   // weights: before the wait
-        prefetch_cb<NT>(cbs, a.cb[(int)(u0 / per_g)][0]);
+        prefetch_cb<NT>(cbs, a.cb[u0 / per_g][0]);
         if (tid == 0) {
-            const long long r0 = u0 % per_g;
-            const int sl0 = (int)(r0 / R), ra0 = (int)(r0 % R);
-            prefetch_phase(a, (int)(u0 / per_g), 0, sl0, ra0, (int)min((long long)R, ra0 + (u1 - u0)));
+            const int r0 = u0 % per_g;
+            const int sl0 = r0 / R, ra0 = r0 % R;
+            prefetch_phase(a, u0 / per_g, 0, sl0, ra0, min(R, ra0 + (u1 - u0)));
         }
     }
     bool have_x = false;
     float inv = 1.0f;
-    for (long long u = u0, seg = 0; u < u1; seg++) {
-        const int g = (int)(u / per_g);
-        const long long rem = u - (long long)g * per_g;
-        const int sl = (int)(rem / R), ra = (int)(rem - (long long)sl * R);
-        const int rb = (int)min((long long)R, (long long)ra + (u1 - u));
+    for (int u = u0, seg = 0; u < u1; seg++) {
+        const int g = u / per_g;
+        const int rem = u - g * per_g;
+        const int sl = rem / R, ra = rem - sl * R;
+        const int rb = min(R, ra + (u1 - u));
         const int nr = rb - ra;
         const int nk = nr > tid ? (nr - tid + NT - 1) / NT : 0;   // this thread's rows ra + tid + k NT
         for (int s = 0; s < a.ns; s++) {
@@ -207,15 +208,10 @@ __global__ void __launch_bounds__(NT, 1) vq_lut_kernel(const LutArgs a) {
                 pdl_wait();
                 if (a.norm_w) inv = rms_inv(a.x, a.cols, a.eps, red);
                 if (tid < LMAXSEG * 32) {
-                    long long v = u0;
-                    int k = 0;
-                    while (v < u1 && k < tid / 32) {
-                        const long long rv = v % per_g;
-                        v += min((long long)R - rv % R, u1 - v);
-                        k++;
-                    }
+                    int v = u0;
+                    for (int k = 0; v < u1 && k < tid / 32; k++) v += min(R - v % per_g % R, u1 - v);
                     if (v < u1) {
-                        const int c = 32 * (int)((v % per_g) / R) + (tid & 31);
+                        const int c = 32 * (v % per_g / R) + (tid & 31);
                         float xv = a.x[c];
                         if (a.norm_w) xv = __fmul_rn(__fmul_rn(xv, inv), a.norm_w[c]);
                         xs[tid] = xv;
@@ -227,21 +223,17 @@ __global__ void __launch_bounds__(NT, 1) vq_lut_kernel(const LutArgs a) {
             __syncthreads();   // the previous table's readers are done; xs and the code words are in
             {
                 const float4 *x4 = reinterpret_cast<const float4 *>(xs + 32 * seg);
+                float4 xv[LGC];
 #pragma unroll
-                for (int h = 0; h < LGC; h += 4) {
-                    float4 xv[4];
+                for (int jj = 0; jj < LGC; jj++) xv[jj] = x4[jj];
+#pragma unroll 2
+                for (int c = tid; c < LNC; c += NT) {
+                    const uint2 q = cbs[c];
+                    const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&q.x));
+                    const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&q.y));
 #pragma unroll
-                    for (int jj = 0; jj < 4; jj++) xv[jj] = x4[h + jj];
-#pragma unroll
-                    for (int c = tid; c < LNC; c += NT) {
-                        const uint2 q = cbs[c];
-                        const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&q.x));
-                        const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&q.y));
-#pragma unroll
-                        for (int jj = 0; jj < 4; jj++)
-                            T[(h + jj) * LNC + c] = fmaf(hi.y, xv[jj].w,
-                                                         fmaf(hi.x, xv[jj].z, fmaf(lo.y, xv[jj].y, lo.x * xv[jj].x)));
-                    }
+                    for (int jj = 0; jj < LGC; jj++)
+                        T[jj * LNC + c] = fmaf(hi.y, xv[jj].w, fmaf(hi.x, xv[jj].z, fmaf(lo.y, xv[jj].y, lo.x * xv[jj].x)));
                 }
             }
             __syncthreads();
@@ -250,12 +242,12 @@ __global__ void __launch_bounds__(NT, 1) vq_lut_kernel(const LutArgs a) {
                 prefetch_cb<NT>(cbs, a.cb[g][s + 1]);
                 if (tid == 0) prefetch_phase(a, g, s + 1, sl, ra, rb);
             } else if (u + nr < u1) {
-                const long long un = u + nr, rn = un % per_g;
-                const int gn2 = (int)(un / per_g), sln = (int)(rn / R), ran = (int)(rn % R);
+                const int un = u + nr, rn = un % per_g;
+                const int gn2 = un / per_g, sln = rn / R, ran = rn % R;
                 prefetch_cb<NT>(cbs, a.cb[gn2][0]);
-                if (tid == 0) prefetch_phase(a, gn2, 0, sln, ran, (int)min((long long)R, ran + (u1 - un)));
+                if (tid == 0) prefetch_phase(a, gn2, 0, sln, ran, min(R, ran + (u1 - un)));
             }
-            float *pout = a.part + ((size_t)g * nsl + sl) * R;
+            float *pout = a.part + (size_t)(g * nsl + sl) * R;
             const bool last = s + 1 == a.ns;
             for (int k0 = 0; k0 < nk; k0 += CH) {
                 uint4 wn[CH];
@@ -338,15 +330,18 @@ __global__ void __launch_bounds__(FT) vq_lut_finish_kernel(const FinArgs a) {
     }
     const int ri = threadIdx.x % FR, q = threadIdx.x / FR;
     const int r = blockIdx.x * FR + ri;
-    for (int g = 0; g < a.ng; g++) {
-        float s = 0.f;
-        if (r < a.rows) {
-            const float *p = a.part + (size_t)g * a.nsl * a.rows + r;
-#pragma unroll 8
-            for (int sl = q; sl < a.nsl; sl += FQ) s += p[(size_t)sl * a.rows];
+    float s0 = 0.f, s1 = 0.f;   // both groups' loads in flight together
+    if (r < a.rows) {
+        const float *p = a.part + r;
+        const size_t gs = (size_t)a.nsl * a.rows;
+#pragma unroll 4
+        for (int sl = q; sl < a.nsl; sl += FQ) {
+            s0 += p[(size_t)sl * a.rows];
+            if (a.ng == 2) s1 += p[gs + (size_t)sl * a.rows];
         }
-        red[g][q][ri] = s;
     }
+    red[0][q][ri] = s0;
+    red[1][q][ri] = s1;
     __syncthreads();
     if (q == 0 && r < a.rows) {
         float t[2] = {0.f, 0.f};
@@ -401,6 +396,7 @@ int lut_srow_cap(const Layout &L, int ns, int ng) {
 }  // namespace
 
 bool lut_ok(const Layout &L, int ns, int ng) {
+    if ((long long)ng * (long long)L.nidx_row * L.rows >= (1LL << 31)) return false;   // 32-bit unit indices
     if (!(L.v3 && L.dim == 4 && L.nc == LNC && L.nbit == 12 && L.prow == 0 && L.nidx_row % LGC == 0)) return false;
     if (ns < 1 || ns > LMAXS || ng < 1 || ng > 2 || L.mrow * 2 != L.nidx_row * 3) return false;
     return lut_segments_ok(L, ng) && lut_smem(lut_srow_cap(L, ns, ng)) <= smem_optin_max();
