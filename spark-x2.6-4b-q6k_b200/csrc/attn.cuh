@@ -33,6 +33,7 @@ struct AttnArgs {
     int ntok;                  // grid.z
     int store;                 // 1: the kernel writes each token's K/V row itself (ntok 1)
     int span;                  // 0: causal rows; > 0: every row reads [pos0 + 1 - window, pos0 + span - 1]
+    int cached_before;         // 1: every cache row but the own one was written by an earlier graph launch
                                // (a non-causal draft block whose rows sit at pos0 .. pos0 + span - 1)
     int nsplit;                // grid.y: sequence splits
     float *part;               // [ntok][kv_heads][nsplit][group][hd + 4]: o, m, l (+2 pad) per split

@@ -129,6 +129,7 @@ struct spk_model {
     // spk_model_trace: a second capture of the step with a timing event after every launch
     std::vector<cudaEvent_t> tev;
     int tracing = 0, nmark = 0;
+    int capturing = 0;            // enqueue_step is being captured into a step graph
     cudaGraph_t tgraph = nullptr;
     cudaGraphExec_t texec = nullptr;
     int eager_steps = 0;
@@ -254,6 +255,7 @@ int enqueue_step(spk_model *m) {
         nl += lr == 0 ? 2 : 1;
         AttnArgs a = attn_args(m, li, 1);
         a.store = 1;
+        a.cached_before = m->capturing;   // a graph replay: every earlier step has completed
         if (attn_decode(a, s) || mark(m)) return -1;
         float *const ro = tp ? m->pbuf : m->h;   // out_proj / down_proj: rank partial, or the residual
         lr = lut_call(m, L, 2, -1, m->attn, nullptr, 0.f, ro, tp ? 0 : 1, nullptr, s);
@@ -383,7 +385,9 @@ int run_step(spk_model *m) {
     if (!m->exec) {
         cudaError_t e = cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal);
         if (e != cudaSuccess) return cuda_fail("begin step capture", e);
+        m->capturing = 1;
         const int rc = enqueue_step(m);
+        m->capturing = 0;
         cudaGraph_t g = nullptr;
         e = cudaStreamEndCapture(m->stream, &g);
         if (rc) {
@@ -894,9 +898,11 @@ int spk_model_trace(spk_model *m, float *us, int cap) {
         cudaError_t e = cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal);
         if (e != cudaSuccess) return cuda_fail("begin trace capture", e);
         m->tracing = 1;
+        m->capturing = 1;
         m->nmark = 0;
         const int rc = enqueue_step(m);
         m->tracing = 0;
+        m->capturing = 0;
         cudaGraph_t g = nullptr;
         e = cudaStreamEndCapture(m->stream, &g);
         if (rc || e != cudaSuccess) {
