@@ -23,6 +23,7 @@ cannot be built here; its restatement stands in for it).
 from __future__ import annotations
 
 import argparse
+import hashlib
 import json
 import os
 import re
@@ -150,18 +151,53 @@ def dist_env():
 
 def run_reference(args) -> None:
     """--impl reference: the reference's CPU implementation of the path (its Rust runtime is not
-    buildable without cargo; the C restatement in oracle/ stands in), rank 0 only."""
+    buildable without cargo; the C restatement of model.rs::forward in oracle/ stands in), rank 0
+    only. A step is one whole decode token: all 36 layers and the tied head over f32 weights
+    expanded at load (as Weights::from_vq does), all host threads, at positions ctx, ctx + 1, ...
+    over a KV cache holding ctx seeded positions (the prompt itself is not run on the CPU: the
+    decode token reads the same cache bytes). W untimed tokens, then exactly K timed tokens."""
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    cb = cpu_baseline(args.ctx, tokens=3)
-    v = cb["value"]
+    import oracle
+    from spk.model import ModelConfig, synth_weights
+
+    threads = os.cpu_count() or 1
+    cfg = ModelConfig()
+    t_setup = time.perf_counter()
+    W = synth_weights(cfg, seed=1234)
+    layers = [{"in_norm": L["in_norm"], "post_norm": L["post_norm"],
+               **{n: oracle.decode(L[n]) for n in ("qkv", "attn_gate", "out", "gate", "up", "down")}}
+              for L in W["layers"]]
+    embed = oracle.q80_dequant(W["embed"], cfg.vocab, cfg.hidden)
+    m = oracle.Model(cfg.as_oracle(), layers, embed, W["norm"], args.ctx + args.warmup + args.steps + 1,
+                     threads=threads)
+    m.fill_kv(args.ctx, 7)
+    del W
+    t_setup = time.perf_counter() - t_setup
+    tok, pos = 1, args.ctx
+    for _ in range(args.warmup):
+        tok = oracle.argmax(m.forward(tok, pos))
+        pos += 1
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        tok = oracle.argmax(m.forward(tok, pos))
+        pos += 1
+    dt = time.perf_counter() - t0
+    m.close()
+    v = args.steps / dt
+    sample = (f"model.rs forward restated in C (oracle/), all 36 layers + tied head, {threads} threads, "
+              f"{args.steps} timed tokens at positions {args.ctx}..{pos - 1} after {args.warmup} untimed, "
+              f"over a seeded {args.ctx}-position f32 KV cache; load + f32 expansion {t_setup:.0f} s untimed")
+    cb = {"value": v, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample}
     line = {"metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": 1e3 / v, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init weights, seeded prompt)",
-            "impl": "reference", "config": {"workload": f"config2 decode step, 36-layer VQ decoder, ctx {args.ctx}",
-                                            "model": "spark-x2.6-4b (random-init)", "global_batch": 1,
-                                            "seq_len": args.ctx, "parallelism": "cpu"},
+            "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded random-init weights, seeded KV cache)",
+            "impl": "reference", "config": {"workload": f"config2: 36-layer VQ decoder batch-1 greedy decode at ctx "
+                                                        f"{args.ctx} (CPU, f32 KV)",
+                                            "model": "spark-x2.6-4b geometry (random-init), f32 weights",
+                                            "global_batch": 1, "seq_len": args.ctx, "parallelism": "cpu"},
             "cpu_baseline": cb, "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -224,6 +260,16 @@ def run_ours(args) -> None:
     m.advance_len(args.warmup + args.steps)
     pos = m.len
     value = args.steps / dt
+    # the greedy ids of the warm-up and timed steps: the same on every rank, and at every N
+    # (tensor parallelism changes only the summation order of the logits)
+    gen = ids.cpu().numpy().astype("<i4")
+    greedy = {"n": int(gen.size), "sha1": hashlib.sha1(gen.tobytes()).hexdigest(), "first8": gen[:8].tolist()}
+    if pg:
+        h = torch.tensor(np.frombuffer(hashlib.sha1(gen.tobytes()).digest()[:8], dtype="<i8").copy(), device=dev)
+        hmax, hmin = h.clone(), h.clone()
+        pg.all_reduce(hmax, op=pg.ReduceOp.MAX)
+        pg.all_reduce(hmin, op=pg.ReduceOp.MIN)
+        greedy["ranks_agree"] = bool(hmax.item() == hmin.item())
 
     # the dominant kernel, timed live: the fused gate+up VQ GEMV over every layer's weights
     L = spk.lib()
@@ -331,6 +377,7 @@ def run_ours(args) -> None:
                          "us_per_launch": t_kernel * 1e6},
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4},
             "gpu_launches": args.steps * step_launches,
+            "greedy_ids": greedy,
             "clocks": clk.summary(),
         }
         if cb:

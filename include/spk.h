@@ -262,6 +262,12 @@ int spk_model_reset(spk_model *m);
 /* Positions cached; and the host-side length bump after spk_model_run. */
 int spk_model_len(spk_model *m);
 int spk_model_advance_len(spk_model *m, int n);
+/* Cache rows given as values (no counterpart in the reference, whose Model fills its cache
+ * only through forward): positions pos0 .. pos0 + n - 1 of `layer` from device f32 rows
+ * k, v [n][kv_heads * head_dim] (keys already roped), stored in the cache's type; a
+ * tensor-parallel rank keeps its own KV heads. Asynchronous; record the positions with
+ * spk_model_advance_len. */
+int spk_model_write_kv(spk_model *m, int layer, int pos0, int n, const float *k, const float *v);
 
 /* Per-launch device times of one decode step (no counterpart in the reference): runs
  * one step from the device state, as spk_model_run does, from a second captured graph

@@ -57,6 +57,8 @@ def lib():
         L.orc_model_forward.argtypes = [C.c_void_p, C.c_uint32, C.c_int, _f32p]
         L.orc_model_forward.restype = C.c_int
         L.orc_model_fill_kv.argtypes = [C.c_void_p, C.c_int, C.c_uint64]
+        L.orc_model_kv.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]
+        L.orc_model_kv.restype = C.c_int
         L.orc_model_capture.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]
         L.orc_model_capture.restype = C.c_int
         L.orc_draft_new.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int]
@@ -213,6 +215,7 @@ class Model:
         self.norm = np.ascontiguousarray(norm, np.float32)
         self.vocab = cfg["vocab"]
         self.hidden, self.max_ctx = cfg["hidden"], max_ctx
+        self.kv_dim = cfg["kv_heads"] * cfg["head_dim"]
         self._keep += [c, arr]
         self.h = lib().orc_model_new(C.byref(c), arr, self.embed, self.norm, max_ctx, threads or threads_default())
         if not self.h:
@@ -236,6 +239,15 @@ class Model:
     def fill_kv(self, n: int, seed: int = 0):
         """Seeded K/V for the first n positions (CPU-baseline samples at long context)."""
         lib().orc_model_fill_kv(self.h, n, seed)
+
+    def kv(self, layer: int) -> tuple[np.ndarray, np.ndarray]:
+        """Views of layer's K and V caches, [max_ctx][kv_heads * head_dim] f32 (no copy)."""
+        k, v = C.POINTER(C.c_float)(), C.POINTER(C.c_float)()
+        if lib().orc_model_kv(self.h, layer, C.byref(k), C.byref(v)):
+            raise ValueError(f"layer {layer} outside the model")
+        n = self.max_ctx * self.kv_dim
+        return (np.ctypeslib.as_array(k, (n,)).reshape(self.max_ctx, self.kv_dim),
+                np.ctypeslib.as_array(v, (n,)).reshape(self.max_ctx, self.kv_dim))
 
     def close(self):
         if self.h:

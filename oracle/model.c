@@ -214,6 +214,16 @@ int orc_model_capture(orc_model *m, const int *layers, int n, float *dst) {
 
 int orc_model_rollback(orc_model *m, int pos) { return (pos < 0 || pos > m->max_ctx) ? -1 : 0; }
 
+/* The K and V caches of one layer, [max_ctx][kv_dim] f32 each (position-major, as
+ * model.rs:398-412 keeps them), for tests that give a device cache the same rows. */
+int orc_model_kv(orc_model *m, int layer, float **k, float **v) {
+    if (layer < 0 || layer >= m->c.layers) return -1;
+    const size_t kvd = (size_t)m->c.kv_heads * m->c.head_dim;
+    *k = m->kv_k + (size_t)layer * m->max_ctx * kvd;
+    *v = m->kv_v + (size_t)layer * m->max_ctx * kvd;
+    return 0;
+}
+
 /* The hidden state entering the final norm, for debugging parity. */
 const float *orc_model_hidden(const orc_model *m) { return m->h; }
 

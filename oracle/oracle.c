@@ -133,10 +133,13 @@ uint32_t orc_stage_index(const orc_stage *st, size_t row, size_t i) {
 
 float orc_stage_gain(const orc_stage *st, size_t row) { return orc_f16(u16le(st->gains, row * 2)); }
 
-/* lib.rs:197-212 */
+/* lib.rs:197-212 (rows are independent: spread over the host threads, same arithmetic per element) */
 void orc_stage_add_into(const orc_stage *st, float *out) {
     const size_t nidx_row = (size_t)(st->cols / st->dim);
-    for (size_t r = 0; r < (size_t)st->rows; r++) {
+    long rr;
+#pragma omp parallel for schedule(static)
+    for (rr = 0; rr < (long)st->rows; rr++) {
+        const size_t r = (size_t)rr;
         const float g = orc_stage_gain(st, r);
         float *o = out + r * (size_t)st->cols;
         for (size_t i = 0; i < nidx_row; i++) {
@@ -230,7 +233,9 @@ int orc_container_info(const uint8_t *buf, size_t n, int *dim, int *nc, int *sta
 int orc_container_decode(const uint8_t *buf, size_t n, float *out, char *err, int errn) {
     orc_cont c;
     if (cont_parse(buf, n, &c, err, errn)) return -1;
-    memset(out, 0, (size_t)c.rows * (size_t)c.cols * sizeof(float));
+    long rr;
+#pragma omp parallel for schedule(static)
+    for (rr = 0; rr < (long)c.rows; rr++) memset(out + (size_t)rr * c.cols, 0, (size_t)c.cols * sizeof(float));
     for (int s = 0; s < c.nstages; s++) {
         orc_stage st;
         if (cont_stage(buf, &c, s, &st, err, errn)) return -1;

@@ -34,6 +34,7 @@ int orc_model_capture(orc_model *m, const int *layers, int n, float *dst);
 int orc_rope_dim(const orc_cfg *c, int layer);
 const float *orc_model_hidden(const orc_model *m);
 void orc_model_fill_kv(orc_model *m, int n, uint64_t seed);
+int orc_model_kv(orc_model *m, int layer, float **k, float **v);
 
 #ifdef __cplusplus
 }

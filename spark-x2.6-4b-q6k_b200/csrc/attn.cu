@@ -528,8 +528,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const AttnArgs a
     for (int st = 0; st < nstage; st++) {
         cp_async_wait<1>();
         __syncthreads();   // stage st landed for every thread
-        const uint8_t *kt = tsm + (size_t)(st & 1) * TL::SLOT, *vraw = kt + TC_POS * TL::KRS;
+        uint8_t *kt = tsm + (size_t)(st & 1) * TL::SLOT, *vraw = kt + TC_POS * TL::KRS;
         const uint8_t *vt = vraw;   // the f16 V tile ldmatrix reads
+        // The token's own row enters the merge exactly (below) and its score is masked, but the
+        // tile may hold what the slot held before this step's store (a row from before a rollback,
+        // possibly an overflowed f16): its V values (f16) or V scales (q8_0) are zeroed here so
+        // the masked P = 0 never meets an Inf or NaN in the PV product.
+        const int jo = own ? pos - (c0 + st * TC_POS) : -1;
+        const bool zown = jo >= 0 && jo < TC_POS;   // the same for every thread of the CTA
         if constexpr (Q8) {   // V quants -> the f16 tile (exact); the scales stay in the raw rows
             uint8_t *v16 = tsm + (size_t)2 * TL::SLOT;
             for (int i = threadIdx.x; i < TC_POS * (HD / 4); i += TC_THREADS) {
@@ -538,8 +544,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const AttnArgs a
                 s8x4_to_f16_exact(*reinterpret_cast<const uint32_t *>(vraw + (size_t)r * TL::KRS + 4 * w), lo, hi);
                 *reinterpret_cast<uint2 *>(v16 + (size_t)r * TC_RS + 8 * w) = make_uint2(lo, hi);
             }
+            if (zown && threadIdx.x < HD / 32)
+                reinterpret_cast<__half *>(vraw + (size_t)jo * TL::KRS + HD)[threadIdx.x] = __ushort_as_half(0);
             __syncthreads();
             vt = v16;
+        } else if (zown) {
+            if (threadIdx.x < HD / 8)
+                *reinterpret_cast<uint4 *>(vraw + (size_t)jo * TL::KRS + 16 * threadIdx.x) = make_uint4(0, 0, 0, 0);
+            __syncthreads();
         }
         const int jw = c0 + st * TC_POS + 16 * tw;   // this warp's first position
         if (jw < c1) {
@@ -751,6 +763,28 @@ int attn_store_batch(const AttnArgs &a, cudaStream_t s) {
     void (*const ks[3])(const AttnArgs) = {attn_store_kernel<0>, attn_store_kernel<1>, attn_store_kernel<2>};
     cudaError_t e = launch_pdl(ks[a.kv_type], dim3(a.ntok), dim3(256), sm, s, a);
     return e == cudaSuccess ? 0 : cuda_fail("attention K/V store launch", e);
+}
+
+// Cache rows written from given f32 values: CTA (position, head) stores K and V of that head.
+template <int KT>
+__global__ void kv_write_kernel(uint8_t *kc, uint8_t *vc, int slots, int hd, int pos0, int head0, const float *k,
+                                const float *v, int ld) {
+    const int t = blockIdx.x, h = blockIdx.y;
+    const size_t o = ((size_t)h * slots + (size_t)(pos0 + t) % slots) * kv_row_bytes(KT, hd);
+    const size_t src = (size_t)t * ld + (size_t)(head0 + h) * hd;
+    store_row<KT>(k + src, kc + o, hd);
+    store_row<KT>(v + src, vc + o, hd);
+}
+
+int kv_write(void *kc, void *vc, int kv_type, int slots, int kv_heads, int head0, int hd, int pos0, int n,
+             const float *k, const float *v, int ld, cudaStream_t s) {
+    if (kv_type < KV_F32 || kv_type > KV_Q8) return set_error("cache write: cache type %d", kv_type);
+    if (n <= 0) return 0;
+    void (*const ks[3])(uint8_t *, uint8_t *, int, int, int, int, const float *, const float *, int) = {
+        kv_write_kernel<0>, kv_write_kernel<1>, kv_write_kernel<2>};
+    ks[kv_type]<<<dim3(n, kv_heads), dim3(128), 0, s>>>((uint8_t *)kc, (uint8_t *)vc, slots, hd, pos0, head0, k, v, ld);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_fail("cache write launch", e);
 }
 
 }  // namespace spk

@@ -51,4 +51,10 @@ int attn_decode(const AttnArgs &a, cudaStream_t s);
 // Rope K and store K/V rows of a batch of ntok tokens (before attn_decode with store 0).
 int attn_store_batch(const AttnArgs &a, cudaStream_t s);
 
+// Store the rows of positions pos0 .. pos0 + n - 1 for cache heads 0 .. kv_heads - 1, read
+// from f32 rows k / v [n][ld] at head offsets (head0 + h) * hd (already roped keys), by
+// the cache type's rule.
+int kv_write(void *kc, void *vc, int kv_type, int slots, int kv_heads, int head0, int hd, int pos0, int n,
+             const float *k, const float *v, int ld, cudaStream_t s);
+
 }  // namespace spk

@@ -63,6 +63,31 @@ inline size_t stage_bytes(const Layout &L) {
     return L.stream_off + idx;
 }
 
+// ----------------------------------------------------------- index read ---
+// lib.rs:162-190 / decode-gpu.cu:82-121. Byte reads: a payload's row stream
+// need not be word aligned for the generic path. The 4-byte window may read
+// up to 3 bytes past the last index, inside the caller's 8 zeroed slack bytes.
+__device__ __forceinline__ uint32_t rd_idx(const uint8_t *st, const Layout &L, size_t r, size_t i) {
+    if (!L.v3) {
+        const size_t gi = r * L.nidx_row + i;
+        if (L.nbit == 8) return st[gi];
+        const size_t bit = gi * (size_t)L.nbit;
+        const uint8_t *q = st + (bit >> 3);
+        const uint32_t w = (uint32_t)q[0] | ((uint32_t)q[1] << 8) | ((uint32_t)q[2] << 16);
+        return (w >> (bit & 7)) & L.mask;
+    }
+    const uint32_t mb = L.nbit > 12 ? 12u : (uint32_t)L.nbit;
+    const size_t bit = i * mb;
+    const uint8_t *q = st + r * L.mrow + (bit >> 3);
+    const uint32_t w = (uint32_t)q[0] | ((uint32_t)q[1] << 8) | ((uint32_t)q[2] << 16) | ((uint32_t)q[3] << 24);
+    uint32_t v = (w >> (bit & 7)) & ((1u << mb) - 1u);
+    if (L.prow) {
+        const uint8_t *pl = st + L.mrow * (size_t)L.rows + r * L.prow;
+        v |= (uint32_t)((pl[i >> 3] >> (i & 7)) & 1u) << 12;
+    }
+    return v;
+}
+
 // A DQV3 width above 13 bits would decode truncated indices silently
 // (decode-gpu.cu:66-80), so every entry point refuses it.
 inline bool v3_width_ok(int nc) {

@@ -613,7 +613,7 @@ int spk_q80_head(const void *w, int rows, int cols, const float *x, const float 
     if (!argmax_out) return set_error("argmax output pointer is null");
     int dev = 0;
     cudaGetDevice(&dev);
-    const int grid = 2 * sm_count();
+    const int grid = 2 * sm_count() < 1024 ? 2 * sm_count() : 1024;   // the partial buffer holds 1024 slots
     if (!g_head_counter[dev & 63]) {
         void *c = nullptr, *p = nullptr;
         cudaError_t e = cudaMalloc(&c, sizeof(unsigned int));

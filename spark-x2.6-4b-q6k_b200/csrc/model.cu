@@ -868,6 +868,23 @@ int spk_model_reset(spk_model *m) { return spk_model_rollback(m, 0); }
 /* Positions cached (Model::len). */
 int spk_model_len(spk_model *m) { return m ? m->len : -1; }
 
+/* Cache rows given as values: positions pos0 .. pos0 + n - 1 of `layer` take K and V from
+ * device f32 rows k, v [n][kv_heads * head_dim] (every KV head of the model, keys already
+ * roped, as the attention stores them; a tensor-parallel rank keeps its own heads), stored
+ * in the cache's type. Asynchronous on the model's stream; the host length is not changed
+ * (spk_model_advance_len records the positions). */
+int spk_model_write_kv(spk_model *m, int layer, int pos0, int n, const float *k, const float *v) {
+    if (!m) return set_error("model is null");
+    const spk_model_config &c = m->cfg;
+    if (layer < 0 || layer >= c.layers || pos0 < 0 || n < 0 || (long long)pos0 + n > c.max_ctx)
+        return set_error("cache write: layer %d, positions %d + %d outside the model", layer, pos0, n);
+    if (n > 0 && (!k || !v)) return set_error("cache write: null rows");
+    const int head0 = m->tp_rank * m->hl * c.kv_heads / c.heads;
+    return kv_write((uint8_t *)m->kc + m->kv_off[layer], (uint8_t *)m->vc + m->kv_off[layer], c.kv_type,
+                    m->kv_slots[layer], m->kvl, head0, c.head_dim, pos0, n, k, v, c.kv_heads * c.head_dim,
+                    m->stream);
+}
+
 /* Record that `n` device-run steps extended the cache (spk_model_run does not
  * sync, so the host view is advanced explicitly). */
 int spk_model_advance_len(spk_model *m, int n) {

@@ -17,27 +17,6 @@ using namespace spk;
 
 namespace {
 
-__device__ __forceinline__ uint32_t rd_idx_p(const uint8_t *st, const Layout &L, size_t r, size_t i) {
-    if (!L.v3) {
-        const size_t gi = r * L.nidx_row + i;
-        if (L.nbit == 8) return st[gi];
-        const size_t bit = gi * (size_t)L.nbit;
-        const uint8_t *q = st + (bit >> 3);
-        const uint32_t w = (uint32_t)q[0] | ((uint32_t)q[1] << 8) | ((uint32_t)q[2] << 16);
-        return (w >> (bit & 7)) & L.mask;
-    }
-    const uint32_t mb = L.nbit > 12 ? 12u : (uint32_t)L.nbit;
-    const size_t bit = i * mb;
-    const uint8_t *q = st + r * L.mrow + (bit >> 3);
-    const uint32_t w = (uint32_t)q[0] | ((uint32_t)q[1] << 8) | ((uint32_t)q[2] << 16) | ((uint32_t)q[3] << 24);
-    uint32_t v = (w >> (bit & 7)) & ((1u << mb) - 1u);
-    if (L.prow) {
-        const uint8_t *pl = st + L.mrow * (size_t)L.rows + r * L.prow;
-        v |= (uint32_t)((pl[i >> 3] >> (i & 7)) & 1u) << 12;
-    }
-    return v;
-}
-
 constexpr int TOK = 8;
 
 __global__ void vq_prefill_kernel(const uint8_t *p, const Layout L, const float *xT, int ntok, float *y) {
@@ -53,7 +32,7 @@ __global__ void vq_prefill_kernel(const uint8_t *p, const Layout L, const float 
 #pragma unroll
         for (int t = 0; t < TOK; t++) acc[t] = 0.f;
         for (size_t i = lane; i < L.nidx_row; i += 32) {
-            const uint32_t v = min(rd_idx_p(st, L, (size_t)r, i), (uint32_t)L.nc - 1u);
+            const uint32_t v = min(rd_idx(st, L, (size_t)r, i), (uint32_t)L.nc - 1u);
             const __half *c = cb + (size_t)v * L.dim;
             for (int d = 0; d < L.dim; d++) {
                 const float cw = __half2float(c[d]);

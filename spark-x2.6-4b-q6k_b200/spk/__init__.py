@@ -83,6 +83,7 @@ _PROTOS = {
     "spk_model_reset": ([_vp], _i),
     "spk_model_len": ([_vp], _i),
     "spk_model_advance_len": ([_vp, _i], _i),
+    "spk_model_write_kv": ([_vp, _i, _i, _i, _vp, _vp], _i),
     "spk_model_verify": ([_vp, _vp, _i, _i, _vp, _vp], _i),
     "spk_model_trace": ([_vp, _vp, _i], _i),
     "spk_model_tp_handle": ([_vp, _vp, _i], _i),

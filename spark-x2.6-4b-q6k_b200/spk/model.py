@@ -23,7 +23,7 @@ from . import formats as F
 
 @dataclass
 class ModelConfig:
-    """tools/vq-runtime/src/config.rs:16-30 (values from SURVEY §0.1 / models/quantize.log)."""
+    """tools/vq-runtime/src/config.rs:16-30 (values from models/quantize.log:19-35)."""
 
     hidden: int = 2560
     layers: int = 36
@@ -323,6 +323,12 @@ class DeviceModel:
 
     def advance_len(self, n: int):
         check(lib().spk_model_advance_len(self.h, n), "advance_len")
+
+    def write_kv(self, layer: int, pos0: int, k, v):
+        """Cache rows of `layer` at pos0.. from f32 device tensors k, v [n][kv_heads * head_dim]
+        (keys already roped), stored in the cache's type; the host length is not changed."""
+        n = int(k.shape[0])
+        check(lib().spk_model_write_kv(self.h, layer, pos0, n, k.data_ptr(), v.data_ptr()), "write_kv")
 
     @property
     def len(self) -> int:

@@ -191,3 +191,62 @@ def test_bad_inputs(small):
     with pytest.raises(Exception):
         dev.forward(0, 8)
     dev.close()
+
+
+@pytest.fixture(scope="module")
+def config2(cuda):
+    """The benchmarked geometry: 36 layers (27 sliding-512 + 9 full), hidden 2560, GQA 16/4 x 256,
+    FFN 10240, vocabulary 131072, VQ 4x4096x2 trunk and Q8_0 tied head."""
+    cfg = ModelConfig()
+    W = synth_weights(cfg, seed=21)
+    return cfg, W
+
+
+def test_config2_36_layers_ctx4096(config2, cuda):
+    """The full 36-layer model at the benchmarked context: every layer's cache holds the same 4096
+    seeded positions in the oracle and on the device (f32 KV, the parity type), so the full layers
+    attend over 4096+ positions and the sliding ones over a full 512 window; then 64 greedy steps.
+    The same token sequence then runs on an f16-KV model (the type the benchmark times), checked
+    against the same oracle logits at the f16 cache's tolerance."""
+    import torch
+
+    cfg, W = config2
+    P, S = 4096, 64
+    ref = oracle_model(cfg, W, max_ctx=P + S + 1)
+    ref.fill_kv(P, seed=9)
+    dev = DeviceModel(cfg, W, max_ctx=P + S + 1, kv_f16=False)
+    for li in range(cfg.layers):
+        k, v = ref.kv(li)
+        dev.write_kv(li, 0, torch.from_numpy(k[:P].copy()).to(cuda), torch.from_numpy(v[:P].copy()).to(cuda))
+    dev.advance_len(P)
+    tok, worst, tie, toks, wants = 4242, 0.0, 0, [], []
+    for pos in range(P, P + S):
+        want = ref.forward(tok, pos)
+        nxt, got = dev.forward(tok, pos)
+        worst = max(worst, rel(got, want))
+        o_id = oracle.argmax(want)
+        if nxt != o_id:
+            assert margin(want) <= EPS_MARGIN * max(1.0, abs(float(want.max()))), f"pos {pos}: id {nxt} vs {o_id}"
+            tie += 1
+        toks.append(tok)
+        wants.append(want)
+        tok = o_id
+    dev.close()
+    ref.close()
+    print(f"36 layers, ctx {P}: worst logits relL2 {worst:.3g} over {S} steps, near-tie steps {tie}")
+    assert worst < LOGIT_TOL
+
+    ref16 = oracle_model(cfg, W, max_ctx=P + 1)
+    ref16.fill_kv(P, seed=9)
+    d16 = DeviceModel(cfg, W, max_ctx=P + S + 1, kv_f16=True)
+    for li in range(cfg.layers):
+        k, v = ref16.kv(li)
+        d16.write_kv(li, 0, torch.from_numpy(k[:P].copy()).to(cuda), torch.from_numpy(v[:P].copy()).to(cuda))
+    ref16.close()
+    d16.advance_len(P)
+    w16 = 0.0
+    for i, t in enumerate(toks[:16]):
+        w16 = max(w16, rel(d16.forward(t, P + i)[1], wants[i]))
+    d16.close()
+    print(f"f16 KV: worst logits relL2 {w16:.3g} over 16 steps")
+    assert w16 < 2e-2

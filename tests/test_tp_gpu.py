@@ -1,8 +1,9 @@
 """Tensor-parallel decode on the GPU.
 
-* Two ranks (one process per GPU, needs 2 GPUs): the sharded small model's greedy
-  tokens and gathered logits against the CPU oracle (model.rs::forward in C) and
-  against each other; the device-resident loop against the host loop.
+* 2, 4 and 8 ranks (one process per GPU, as many GPUs as ranks): the sharded small
+  model's greedy tokens and gathered logits against the CPU oracle (model.rs::forward
+  in C) and against each other; the device-resident loop against the host loop. At 4
+  and 8 ranks the model's 2 KV heads are replicated over the ranks of each head.
 * One GPU: a rank whose peer never arrives. Its exchange waits give up after the
   wait limit, the forward reports the peer timeout, and the context stays usable.
 """
@@ -70,18 +71,19 @@ def _rank_main(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_tp2_matches_oracle(cuda):
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_matches_oracle(cuda, world):
     import torch
     import torch.multiprocessing as mp
 
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    ps = [ctx.Process(target=_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    ps = [ctx.Process(target=_rank_main, args=(r, world, port, q)) for r in range(world)]
     for p in ps:
         p.start()
     res = {}
@@ -90,11 +92,12 @@ def test_tp2_matches_oracle(cuda):
         res[r[0]] = r
     for p in ps:
         p.join(timeout=120)
-    for r in (0, 1):
+    for r in range(world):
         assert res[r][4] is None, res[r][4]
     toks0, logits, (dev0, tgt0) = res[0][1], res[0][2], res[0][3]
-    assert toks0 == res[1][1], "ranks disagree on the greedy ids"
-    assert (dev0, tgt0) == res[1][3]
+    for r in range(1, world):
+        assert toks0 == res[r][1], f"rank {r} disagrees on the greedy ids"
+        assert (dev0, tgt0) == res[r][3]
     p0 = len(PROMPT) - 1
     assert tgt0 == toks0[p0:p0 + 8], "the verify batch disagrees with the sequential steps"
 

@@ -63,6 +63,35 @@ def test_verify_gemm_matches_oracle(cuda, geom, ntok):
             assert rel(got[n], want) < GEMM_TOL, (geom, ntok, norm, n, rel(got[n], want))
 
 
+# the config-3 verify batch's matrices at their full size, M = 8 (qkv, out, gate/up, down)
+FULL = [(6144, 2560), (2560, 4096), (10240, 2560), (2560, 10240)]
+
+
+@pytest.mark.parametrize("rows,cols", FULL)
+def test_verify_gemm_full_shapes_m8(cuda, rows, cols):
+    import torch
+
+    import spk
+
+    buf = F.random_rvq_fast(rows, cols, 4, 4096, 2, seed=rows * 7 + cols)
+    c = F.parse_container(buf)
+    W = oracle.decode(buf).reshape(rows, cols).astype(np.float64)
+    rng = np.random.default_rng(rows + cols)
+    X = rng.normal(0, 1, (8, cols)).astype(np.float32)
+    keep = [spk.dev_bytes(buf[c.stage_offset(s):c.stage_offset(s) + c.stage_bytes], cuda) for s in range(2)]
+    st = (C.c_void_p * 2)(*[t.data_ptr() for t in keep])
+    x = torch.from_numpy(X).to(cuda)
+    y = torch.zeros(8, rows, device=cuda)
+    L = spk.lib()
+    spk.check(L.spk_verify_gemm(st, 2, 4, 4096, rows, cols, 1, 8, x.data_ptr(), cols, None, 0.0, y.data_ptr(), rows,
+                                0, None))
+    torch.cuda.synchronize()
+    got = y.cpu().numpy()
+    want = X.astype(np.float64) @ W.T
+    for n in range(8):
+        assert rel(got[n], want[n]) < GEMM_TOL, (rows, cols, n, rel(got[n], want[n]))
+
+
 def test_verify_gemm_rejects_bad_arguments(cuda):
     import spk
 

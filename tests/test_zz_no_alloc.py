@@ -5,12 +5,13 @@ real-time loops that must not stall on an allocation, host frameworks that own a
 device memory — and keeps its scratch in a fixed array inside the library. Its output
 must equal the allocating entry point's (spk_q80_head) on the same inputs, within the
 GEMV tolerance these tests use, on two calls in a row (the second call reuses the
-array the first one left behind). This file sorts last so a stop-at-first-failure run
+array the first one left behind), and match the CPU oracle's GEMV and first-max argmax. This file sorts last so a stop-at-first-failure run
 has already run every other test; it also passes alone in a fresh process.
 """
 import numpy as np
 import pytest
 
+import oracle
 import spk
 from spk import formats as F
 
@@ -41,6 +42,9 @@ def test_noalloc_head_matches_allocating_head_twice(cuda, rows, cols):
                              ref_arg.data_ptr(), None), "allocating head")
     torch.cuda.synchronize()
     want, want_arg = ref_logits.cpu().numpy(), int(ref_arg.item())
+    # the CPU oracle's GEMV (ggml's dequantize_row_q8_0 restated) and first-max argmax, directly
+    xn = oracle.rms_norm(x.cpu().numpy(), nw.cpu().numpy(), 1e-6)
+    o_logits = oracle.q80_gemv(blocks, rows, cols, xn)
 
     for call in range(2):
         logits = torch.zeros(rows, device=cuda)
@@ -49,8 +53,13 @@ def test_noalloc_head_matches_allocating_head_twice(cuda, rows, cols):
                                          logits.data_ptr(), arg.data_ptr(), None), f"no-alloc head, call {call}")
         torch.cuda.synchronize()
         spk.check(L.spk_check_device_error(), "device error")
-        assert rel(logits.cpu().numpy(), want) < TOL, call
+        got = logits.cpu().numpy()
+        assert rel(got, want) < TOL, call
         assert int(arg.item()) == want_arg, call
+        assert rel(got, o_logits) < TOL, call
+        assert int(arg.item()) == oracle.argmax(got), call
+        if np.sort(o_logits)[-2] < o_logits.max() - 1e-3 * max(1.0, abs(float(o_logits.max()))):
+            assert int(arg.item()) == oracle.argmax(o_logits), call
 
 
 def test_noalloc_head_rejects_bad_arguments(cuda):
