@@ -232,11 +232,15 @@ def run_ours(args) -> None:
         m.tp_connect()
     # the synthetic prompt, fed through the host API (teacher-forced)
     prompt = np.random.default_rng(7).integers(0, cfg.vocab, args.ctx)
+    prompt_s = None
     if args.fill_kv:
         m.advance_len(args.ctx)
-    else:
-        for p, t in enumerate(prompt):
-            m.forward(int(t), p, want_logits=False)
+    else:   # the prompt through the chunked tensor-core path (spk_model_prefill), wall clock with its syncs
+        if pg:
+            pg.barrier()
+        t0 = time.perf_counter()
+        m.prefill(prompt.tolist(), 0, want_logits=False)
+        prompt_s = time.perf_counter() - t0
     ids = torch.zeros(args.warmup + args.steps, dtype=torch.int32, device=dev)
     m.begin(int(prompt[-1]), args.ctx, ids, args.warmup + args.steps)
     m.run(args.warmup)
@@ -293,7 +297,7 @@ def run_ours(args) -> None:
             luts.append(ws)
             lt = (C.c_void_p * 4)(*[w_.data_ptr() for w_ in ws])
         launches.append((st, lt, m.norms[li][1]))
-    scr = (torch.empty(L.spk_vq_lut_scratch_bytes(2, 4, 4096, rows_l, cfg.hidden, 1), dtype=torch.uint8, device=dev)
+    scr = (torch.zeros(L.spk_vq_lut_scratch_bytes(2, 4, 4096, rows_l, cfg.hidden, 1), dtype=torch.uint8, device=dev)
            if lut_n else None)
     torch.cuda.synchronize(dev)
     sp = C.c_void_p(m.stream.cuda_stream)
@@ -366,6 +370,7 @@ def run_ours(args) -> None:
                        "model": f"spark-x2.6-4b geometry, VQ 4x4096x2 trunk, Q8_0 tied head, {args.kv} KV",
                        "global_batch": 1, "seq_len": args.ctx,
                        "parallelism": f"tp{world}" if world > 1 else "single", "l2": "weights 3.2 GB > L2, no flush",
+                       "prompt_tok_s": args.ctx / prompt_s if prompt_s else None,
                        "step_bytes_per_gpu": bytes_per_token + kv_bytes,
                        "step_hbm_gbs_per_gpu": (bytes_per_token + kv_bytes) * args.steps / dt / 1e9,
                        "step_trace_rank0": trace},

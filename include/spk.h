@@ -99,22 +99,36 @@ int vqg_prefill_launch_tile(const void *payload, int dim, int nc, int rows, int 
 int spk_vq_gemv(const void *const *stages, int nstages, int ngroups, int dim, int nc, int rows, int cols, int v3,
                 const float *x, const float *norm_w, float eps, float *y, int accumulate, void *stream);
 /* The same GEMV as shared-memory table look-ups (the decode step's kernel for DQV3 dim 4,
- * 4096 codes, 12-bit indices; replaces the same per-stage loop as spk_vq_gemv). Each stage's
- * index stream is re-laid once, slice-major (spk_vq_lut_pack into spk_vq_lut_bytes device
- * bytes, 0 = geometry not taken); spk_vq_lut_gemv then takes spk_vq_gemv's arguments plus
- * the re-laid words (group-major like stages) and spk_vq_lut_scratch_bytes of device
- * scratch, and runs two launches (the table kernel, then the per-row sum and epilogue). */
+ * 4096 codes, 12-bit indices; replaces the same per-stage loop as spk_vq_gemv). Each stage is
+ * re-laid once into self-contained words (spk_vq_lut_pack into spk_vq_lut_bytes device bytes,
+ * 16-byte aligned; 0 = geometry not taken): its code words, its gains, and its index stream
+ * slice-major, the same bytes as the payload's. spk_vq_lut_gemv then takes spk_vq_gemv's
+ * arguments plus the re-laid words (group-major like stages; stages themselves may be NULL)
+ * and spk_vq_lut_scratch_bytes of device scratch, zeroed before its first use (its first
+ * 256 bytes are a grid barrier the kernel leaves as it found them; calls sharing a scratch
+ * must not overlap on the GPU). One launch, no sync. */
 size_t spk_vq_lut_bytes(int dim, int nc, int rows, int cols, int v3);
 int spk_vq_lut_pack(const void *stage, int dim, int nc, int rows, int cols, int v3, void *dst, void *stream);
 size_t spk_vq_lut_scratch_bytes(int ngroups, int dim, int nc, int rows, int cols, int v3);
 int spk_vq_lut_gemv(const void *const *stages, const void *const *luts, int nstages, int ngroups, int dim, int nc,
                     int rows, int cols, int v3, const float *x, const float *norm_w, float eps, float *y,
                     int accumulate, void *scratch, void *stream);
-/* The same with the table kernel's block size chosen: threads 512 or 1024 (0 = default),
- * as vqg_gemv_t takes one (decode-gpu.cu:800-807). */
+/* The same with the table kernel's consumer thread count stated (0 = default; the kernel runs
+ * 512 consumer threads and a producer warp), as vqg_gemv_t takes one (decode-gpu.cu:800-807). */
 int spk_vq_lut_gemv_t(const void *const *stages, const void *const *luts, int nstages, int ngroups, int dim, int nc,
                       int rows, int cols, int v3, const float *x, const float *norm_w, float eps, float *y,
                       int accumulate, void *scratch, int threads, void *stream);
+/* The VQ GEMM of a token batch on the tcgen05 tensor cores, from the same re-laid words:
+ * for n < ntok <= 128, Y[n] (=|+=) sum_s gain_s W_s RMSNorm?(X[n]) (DQV3 dim 4, 4096 codes,
+ * 12-bit, 1-2 stages, cols a multiple of 32; replaces forward_batch's gemm_tiled_kernel
+ * launches, vq-model-gpu.cu:858-943, decode-gpu.cu:359-501, and the verify batch's GEMMs).
+ * X rows stride ldx floats, Y rows ldy; scratch: spk_vq_lut_gemm_scratch_bytes device bytes,
+ * zeroed before the first call (calls leave it reusable; calls sharing one must not overlap
+ * on the GPU). Two launches, no sync. */
+size_t spk_vq_lut_gemm_scratch_bytes(int rows, int cols, int ntok);
+int spk_vq_lut_gemm(const void *const *luts, int nstages, int dim, int nc, int rows, int cols, int v3, int ntok,
+                    const float *x, int ldx, const float *norm_w, float eps, float *y, int ldy, int accumulate,
+                    void *scratch, void *stream);
 /* 1 if spk_vq_gemv runs the persistent TMA kernel for this geometry, 0 if the generic one. */
 int spk_vq_gemv_fast_ok(int nstages, int ngroups, int dim, int nc, int rows, int cols, int v3);
 /* Bit-exact stage decode on a stream: out += decoded stage (vqg_dequant without timing). */
@@ -249,6 +263,11 @@ int spk_model_forward(spk_model *m, int token, int pos, float *logits_host, int 
  * keep the accepted prefix with spk_model_rollback(m, pos + k + 1) as spec.rs:241 does.
  * Synchronizes. */
 int spk_model_verify(spk_model *m, const int *tokens, int ntok, int pos, int *next_host, float *logits_host);
+/* The prompt in chunks of up to 128 tokens on the tensor cores (forward_batch + its chunk loop,
+ * vq-model-gpu.cu:858-943, 1164-1168): tokens[0..n) at positions pos.., every K/V row stored;
+ * the last token's greedy next id and logits (vocab floats, may be NULL) come back as
+ * spk_model_forward's would. Synchronizes. */
+int spk_model_prefill(spk_model *m, const int *tokens, int n, int pos, int *next_host, float *logits_host);
 /* Device-resident greedy loop: set the start (token, pos) and a device int buffer
  * for the generated ids; spk_model_run then replays the captured step `steps` times
  * with no host round trip (asynchronous on the model's stream). */

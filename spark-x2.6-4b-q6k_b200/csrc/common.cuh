@@ -124,6 +124,14 @@ int lut_gemv(const void *const *stages, const void *const *luts, int ns, int ng,
              const float *norm_w, float eps, float *y, int accumulate, float *part, const void *const *xst,
              const Layout *XL, float *xy, cudaStream_t s, int threads = 0);
 
+// The VQ GEMM of a token batch on the tcgen05 tensor cores (vq_tc.cu), over the table
+// kernel's re-laid stage words: 1 launched, 0 geometry not taken, -1 error.
+//   mode 0: Y[n][r] = (accumulate ? Y[n][r] : 0) + (W RMSNorm?(X[n]))[r]
+//   mode 1: Y[n][r] = gelu_erf(AUX[n][r]) * (W RMSNorm?(X[n]))[r]
+size_t tc_scratch_bytes(int rows, int cols, int ntok);
+int tc_gemm(const void *const *luts, int ns, const Layout &L, int ntok, const float *x, int ldx, const float *norm_w,
+            float eps, float *y, int ldy, int accumulate, int mode, const float *aux, void *scratch, cudaStream_t s);
+
 // The tied Q8_0 head in the tensor-core tile layout (q8t.cu): bytes of the tiled table,
 // the re-lay from ggml blocks, its scratch (zeroed once), and the head for ntok <= 8 rows
 // (1 launched, 0 geometry not taken, -1 error).

@@ -84,6 +84,7 @@ struct spk_model {
         // one allocation per matrix; null: the matrix runs the code-word kernel (vq.cu)
         void *lut_mem[6] = {};
         const void *lut[6][4] = {};
+        bool dec[6] = {};     // the decode step runs this matrix through the table kernel
     };
     std::vector<Layer> layers;
     const void *embed = nullptr;
@@ -118,6 +119,13 @@ struct spk_model {
     int step_launches = 0;        // kernels one decode step launches (counted while enqueuing it)
     float *lut_part = nullptr;    // the table kernel's per-slice partial sums (vq_lut.cu)
     size_t lut_part_size = 0;
+    void *tc_scr = nullptr;       // the batched tensor-core GEMM's scratch (vq_tc.cu), zeroed once
+    size_t tc_scr_size = 0;
+    // the prompt path (spk_model_prefill): rows for a chunk of up to PF_MAX tokens, made on first use
+    float *pf_h = nullptr, *pf_qkv = nullptr, *pf_gate = nullptr, *pf_attn = nullptr, *pf_act = nullptr,
+          *pf_g = nullptr;
+    int *pf_tok = nullptr, *pf_pos = nullptr, *pf_host = nullptr;
+    void *pf_scr = nullptr;
     void *head_tiled = nullptr;   // this rank's head rows re-laid for the tensor-core head (q8t.cu)
     void *head_tiled_scratch = nullptr;
     unsigned long long *vhead_partial = nullptr;   // the verify batch's head
@@ -170,7 +178,7 @@ int qkv_gate(const spk_model::Layer &L, const float *h, float eps, float *qkv, f
 int lut_call(spk_model *m, const spk_model::Layer &L, int mi, int mi2, const float *x, const float *norm_w, float eps,
              float *y, int accumulate, float *xy, cudaStream_t s) {
     const spk_vq_matrix &M = L.m[mi];
-    if (!L.lut[mi][0] || (mi2 >= 0 && !L.lut[mi2][0])) return 1;
+    if (!L.dec[mi] || (mi2 >= 0 && !L.dec[mi2])) return 1;
     const void *st[8], *lt[8];
     for (int q = 0; q < M.nstages; q++) st[q] = M.stages[q], lt[q] = L.lut[mi][q];
     if (mi2 >= 0)
@@ -219,12 +227,12 @@ AttnArgs attn_args(spk_model *m, int li, int ntok) {
 
 // Layer li's input rows into its capture slot, when capture is on (no trace mark: the
 // copy is counted with the launch after it).
-int capture_rows(spk_model *m, int li, int ntok, cudaStream_t s) {
+int capture_rows(spk_model *m, int li, int ntok, cudaStream_t s, const float *h = nullptr, const int *pos = nullptr) {
     if (!m->ncap || m->cap_slot[li] < 0) return 0;
     const int H = m->cfg.hidden;
     float *dst = m->cap + (size_t)m->cap_slot[li] * m->cfg.max_ctx * H;
-    cudaError_t e = launch_pdl(capture_kernel, dim3((ntok * H + 255) / 256), dim3(256), 0, s, (const float *)m->h, H,
-                               ntok, (const int *)m->state, dst);
+    cudaError_t e = launch_pdl(capture_kernel, dim3((ntok * H + 255) / 256), dim3(256), 0, s, h ? h : (const float *)m->h,
+                               H, ntok, pos ? pos : (const int *)m->state, dst);
     return e == cudaSuccess ? 0 : cuda_fail("layer capture launch", e);
 }
 
@@ -292,17 +300,46 @@ int enqueue_step(spk_model *m) {
 }
 
 // ---------------------------------------------------------- verify batch ---
-// y[n] (=|+=) W RMSNorm?(x[n]) for a batch of ntok token rows.
-int vq_batch(const spk_vq_matrix &M, int ntok, const float *x, int ldx, const float *norm_w, float eps, float *y,
-             int ldy, int accumulate, cudaStream_t s) {
+// Layer matrix mi for a batch of ntok token rows on the tcgen05 GEMM over its re-laid words
+// (vq_tc.cu): 0 launched, 1 not taken, -1 error.
+int tc_call(spk_model *m, const spk_model::Layer &L, int mi, int ntok, const float *x, int ldx, const float *norm_w,
+            float eps, float *y, int ldy, int accumulate, int mode, const float *aux, cudaStream_t s) {
+    const spk_vq_matrix &M = L.m[mi];
+    if (!L.lut[mi][0] || !m->tc_scr) return 1;
+    const Layout LM = make_layout(M.dim, M.nc, M.rows, M.cols, M.v3);
+    const int rc = tc_gemm(L.lut[mi], M.nstages, LM, ntok, x, ldx, norm_w, eps, y, ldy, accumulate, mode, aux,
+                           m->tc_scr, s);
+    return rc < 0 ? -1 : rc == 1 ? 0 : 1;
+}
+
+// y[n] (=|+=) W RMSNorm?(x[n]) for a batch of ntok token rows: the tcgen05 GEMM, else the
+// mma.sync kernel (vq_mma.cu) through spk_verify_gemm.
+// (The verify batch, ntok <= 8, is bound by the code-word gathers either way; the tcgen05 GEMM
+// is the faster of the two for rows of 8192 columns and more, measured at 58 vs 72 us for
+// down_proj 2560 x 10240 at 8 tokens, and slower for the shorter rows.)
+int vq_batch(spk_model *m, const spk_model::Layer &L, int mi, int ntok, const float *x, int ldx, const float *norm_w,
+             float eps, float *y, int ldy, int accumulate, cudaStream_t s) {
+    if (L.m[mi].cols >= 8192) {
+        const int rc = tc_call(m, L, mi, ntok, x, ldx, norm_w, eps, y, ldy, accumulate, 0, nullptr, s);
+        if (rc <= 0) return rc;
+    }
+    const spk_vq_matrix &M = L.m[mi];
     return spk_verify_gemm(M.stages, M.nstages, M.dim, M.nc, M.rows, M.cols, M.v3, ntok, x, ldx, norm_w, eps, y, ldy,
                            accumulate, s);
 }
 
 // act[n] = gelu_erf(W_gate xn) * (W_up xn) for the batch: gate into g, then up with the
-// GELU epilogue on the tensor-core kernel; else the SIMT pair token by token.
-int ffn_batch(const spk_model::Layer &L, int ntok, const float *h, int ldh, float eps, float *g, float *act, int ld,
-              cudaStream_t s) {
+// GELU epilogue on a tensor-core kernel; else the SIMT pair token by token.
+int ffn_batch(spk_model *m, const spk_model::Layer &L, int ntok, const float *h, int ldh, float eps, float *g,
+              float *act, int ld, cudaStream_t s) {
+    if (L.lut[3][0] && L.lut[4][0] && m->tc_scr && L.m[3].cols >= 8192) {
+        int rc = tc_call(m, L, 3, ntok, h, ldh, L.post_norm, eps, g, ld, 0, 0, nullptr, s);
+        if (rc < 0) return -1;
+        if (rc == 0) {
+            rc = tc_call(m, L, 4, ntok, h, ldh, L.post_norm, eps, act, ld, 0, 1, g, s);
+            if (rc <= 0) return rc;
+        }
+    }
     const spk_vq_matrix &Gm = L.m[3], &U = L.m[4];
     if (Gm.nstages <= 2 && Gm.nstages == U.nstages) {
         const Layout LG = make_layout(Gm.dim, Gm.nc, Gm.rows, Gm.cols, Gm.v3);
@@ -334,18 +371,20 @@ int enqueue_verify(spk_model *m, int ntok) {
     for (int li = 0; li < c.layers; li++) {
         const spk_model::Layer &L = m->layers[li];
         if (capture_rows(m, li, ntok, s)) return -1;
-        if (vq_batch(L.m[0], ntok, m->h, H, L.in_norm, c.eps, m->qkv, ldqkv, 0, s) ||
-            vq_batch(L.m[1], ntok, m->h, H, L.in_norm, c.eps, m->gate, m->hl, 0, s))
+        if (vq_batch(m, L, 0, ntok, m->h, H, L.in_norm, c.eps, m->qkv, ldqkv, 0, s) ||
+            vq_batch(m, L, 1, ntok, m->h, H, L.in_norm, c.eps, m->gate, m->hl, 0, s))
             return -1;
         AttnArgs a = attn_args(m, li, ntok);
         a.store = 0;
         // ntok times a decode step's CTAs: fewer splits keep the grid near one wave
         a.nsplit = std::max(1, std::min(a.nsplit, (sm_count() + m->kvl * ntok - 1) / (m->kvl * ntok)));
         if (attn_store_batch(a, s) || attn_decode(a, s)) return -1;
-        if (vq_batch(L.m[2], ntok, m->attn, m->q_dim, nullptr, 0.f, tp ? m->pbuf : m->h, H, tp ? 0 : 1, s)) return -1;
+        if (vq_batch(m, L, 2, ntok, m->attn, m->q_dim, nullptr, 0.f, tp ? m->pbuf : m->h, H, tp ? 0 : 1, s))
+            return -1;
         if (tp && tp_sum(m->tpv, m->pbuf, m->h, ntok * H, s)) return -1;
-        if (ffn_batch(L, ntok, m->h, H, c.eps, m->gbuf, m->act, m->inter_l, s)) return -1;
-        if (vq_batch(L.m[5], ntok, m->act, m->inter_l, nullptr, 0.f, tp ? m->pbuf : m->h, H, tp ? 0 : 1, s)) return -1;
+        if (ffn_batch(m, L, ntok, m->h, H, c.eps, m->gbuf, m->act, m->inter_l, s)) return -1;
+        if (vq_batch(m, L, 5, ntok, m->act, m->inter_l, nullptr, 0.f, tp ? m->pbuf : m->h, H, tp ? 0 : 1, s))
+            return -1;
         if (tp && tp_sum(m->tpv, m->pbuf, m->h, ntok * H, s)) return -1;
     }
     const uint8_t *head_rows = (const uint8_t *)m->embed + (size_t)m->row0 * (H / 32) * 34;
@@ -364,6 +403,89 @@ int enqueue_verify(spk_model *m, int ntok) {
             return -1;
     if (tp && tp_argmax(m->tpv, m->logits, m->vocab_l, vam_l, m->row0, vam, ntok, s)) return -1;
     return 0;
+}
+
+// ------------------------------------------------------------- prompt path ---
+int alloc(void **p, size_t bytes, const char *what);
+constexpr int PF_MAX = 128;   // tokens per prompt chunk (the batched GEMM's widest batch)
+
+// The forward of n <= PF_MAX prompt tokens (device m->pf_tok) at positions pf_pos[0] + t
+// (pf_pos[b] = pf_pos[0] + 8 b): every token's K/V row is stored, each token attends the
+// positions up to its own (8 tokens per attention launch, in order), and the last token's
+// logits and greedy id come out (forward_batch + tail_logits, vq-model-gpu.cu:858-949).
+// All GEMMs run on the tensor-core kernel over the re-laid words (vq_tc.cu).
+int enqueue_prefill(spk_model *m, int n) {
+    const spk_model_config &c = m->cfg;
+    cudaStream_t s = m->stream;
+    const int H = c.hidden, ldqkv = m->q_dim + 2 * m->kv_dim;
+    auto gemm = [&](const spk_model::Layer &L, int mi, const float *x, int ldx, const float *nw, float *y, int ldy,
+                    int acc, int mode, const float *aux) -> int {
+        const spk_vq_matrix &M = L.m[mi];
+        if (!L.lut[mi][0]) return set_error("prompt path: matrix %d was not re-laid (geometry not taken)", mi);
+        const Layout LM = make_layout(M.dim, M.nc, M.rows, M.cols, M.v3);
+        const int rc = tc_gemm(L.lut[mi], M.nstages, LM, n, x, ldx, nw, c.eps, y, ldy, acc, mode, aux, m->pf_scr, s);
+        return rc == 1 ? 0 : rc < 0 ? -1 : set_error("prompt path: the batched GEMM does not take matrix %d", mi);
+    };
+    for (int t = 0; t < n; t++)
+        if (spk_q80_row(m->embed, c.vocab, H, 0, m->pf_tok + t, m->pf_h + (size_t)t * H, s)) return -1;
+    for (int li = 0; li < c.layers; li++) {
+        const spk_model::Layer &L = m->layers[li];
+        if (capture_rows(m, li, n, s, m->pf_h, m->pf_pos)) return -1;
+        if (gemm(L, 0, m->pf_h, H, L.in_norm, m->pf_qkv, ldqkv, 0, 0, nullptr) ||
+            gemm(L, 1, m->pf_h, H, L.in_norm, m->pf_gate, m->hl, 0, 0, nullptr))
+            return -1;
+        for (int b = 0; 8 * b < n; b++) {
+            const int nb = std::min(8, n - 8 * b);
+            AttnArgs a = attn_args(m, li, nb);
+            a.qkv = m->pf_qkv + (size_t)8 * b * ldqkv;
+            a.gate = m->pf_gate + (size_t)8 * b * m->hl;
+            a.out = m->pf_attn + (size_t)8 * b * m->q_dim;
+            a.pos = m->pf_pos + b;
+            a.store = 0;
+            a.nsplit = std::max(1, std::min(a.nsplit, (sm_count() + m->kvl * nb - 1) / (m->kvl * nb)));
+            if (attn_store_batch(a, s) || attn_decode(a, s)) return -1;
+        }
+        if (gemm(L, 2, m->pf_attn, m->q_dim, nullptr, m->pf_h, H, 1, 0, nullptr) ||
+            gemm(L, 3, m->pf_h, H, L.post_norm, m->pf_g, m->inter_l, 0, 0, nullptr) ||
+            gemm(L, 4, m->pf_h, H, L.post_norm, m->pf_act, m->inter_l, 0, 1, m->pf_g) ||
+            gemm(L, 5, m->pf_act, m->inter_l, nullptr, m->pf_h, H, 1, 0, nullptr))
+            return -1;
+    }
+    const float *last = m->pf_h + (size_t)(n - 1) * H;
+    int *amax = m->state + 2;
+    const int ht = m->head_tiled ? q8t_head_launch(m->head_tiled, m->vocab_l, H, 1, last, H, m->final_norm, c.eps,
+                                                   m->logits, m->vocab_l, amax, m->head_tiled_scratch, s)
+                                 : 0;
+    if (ht < 0) return -1;
+    if (ht == 0 && q80_head_launch(m->embed, m->vocab_l, H, last, m->final_norm, c.eps, m->logits, amax,
+                                   m->head_partial, m->head_counter, s))
+        return -1;
+    return 0;
+}
+
+// The prompt buffers and the batched GEMM's scratch for PF_MAX tokens, on first use.
+int prefill_buffers(spk_model *m) {
+    if (m->pf_h) return 0;
+    const spk_model_config &c = m->cfg;
+    const size_t R = PF_MAX;
+    size_t scr = 0;
+    for (const auto &L : m->layers)
+        for (int mi = 0; mi < 6; mi++)
+            if (L.lut[mi][0]) scr = std::max(scr, tc_scratch_bytes(L.m[mi].rows, L.m[mi].cols, PF_MAX));
+    if (!scr) return set_error("prompt path: no matrix was re-laid for the batched GEMM");
+    if (alloc((void **)&m->pf_h, R * c.hidden * 4, "alloc prompt rows") ||
+        alloc((void **)&m->pf_qkv, R * (m->q_dim + 2 * m->kv_dim) * 4, "alloc prompt qkv") ||
+        alloc((void **)&m->pf_gate, R * m->hl * 4, "alloc prompt gate") ||
+        alloc((void **)&m->pf_attn, R * m->q_dim * 4, "alloc prompt attention") ||
+        alloc((void **)&m->pf_act, R * m->inter_l * 4, "alloc prompt act") ||
+        alloc((void **)&m->pf_g, R * m->inter_l * 4, "alloc prompt gate act") ||
+        alloc((void **)&m->pf_tok, R * sizeof(int), "alloc prompt tokens") ||
+        alloc((void **)&m->pf_pos, R / 8 * sizeof(int), "alloc prompt positions") || alloc(&m->pf_scr, scr, "alloc prompt scratch"))
+        return -1;
+    if (cudaMallocHost((void **)&m->pf_host, (R + R / 8) * sizeof(int)) != cudaSuccess)
+        return set_error("prompt staging allocation failed");
+    cudaError_t e = cudaMemset(m->pf_scr, 0, scr);   // the batched GEMM's tile tickets start at zero
+    return e == cudaSuccess ? 0 : cuda_fail("zero the prompt scratch", e);
 }
 
 bool ready(const spk_model *m) {
@@ -573,6 +695,11 @@ void spk_model_destroy(spk_model *m) {
         for (void *p : L.lut_mem)
             if (p) cudaFree(p);
     if (m->lut_part) cudaFree(m->lut_part);
+    if (m->tc_scr) cudaFree(m->tc_scr);
+    for (void *p : {(void *)m->pf_h, (void *)m->pf_qkv, (void *)m->pf_gate, (void *)m->pf_attn, (void *)m->pf_act,
+                    (void *)m->pf_g, (void *)m->pf_tok, (void *)m->pf_pos, m->pf_scr})
+        if (p) cudaFree(p);
+    if (m->pf_host) cudaFreeHost(m->pf_host);
     if (m->exec) cudaGraphExecDestroy(m->exec);
     if (m->graph) cudaGraphDestroy(m->graph);
     if (m->texec) cudaGraphExecDestroy(m->texec);
@@ -594,48 +721,64 @@ void spk_model_destroy(spk_model *m) {
     delete m;
 }
 
-// The matrices the decode step runs through the table kernel (vq_lut.cu): those it takes
-// with at least LUT_MIN_ROWS rows (a slice's table costs 4096 x 8 entries, so it pays back
-// only over many rows: measured faster than vq.cu for the 10240-row gate/up pair, slower
-// at 6144 and 2560 rows), the gate/up pair only together. Their index streams are re-laid once
-// here (the payloads stay: the verify batch and g_proj read them).
+// Every layer matrix the table layout takes (DQV3 dim 4, 4096 codes, 12-bit) is re-laid once
+// here (vq_lut.cu's words: code words, gains, slice-major index records): the batched GEMM of
+// the verify batch runs on those words (vq_tc.cu). The decode step runs a matrix through the
+// table kernel when it has at least LUT_MIN_ROWS rows (a slice's table costs 4096 x 8 entries,
+// so it pays back only over many rows), the gate/up pair only together; the others through
+// the code-word kernel (vq.cu) over the payloads, which stay (g_proj reads them too).
 constexpr int LUT_MIN_ROWS = 8192;
 
 static int relay_layer(spk_model *m, spk_model::Layer &L) {
     for (int mi = 0; mi < 6; mi++) {
         if (L.lut_mem[mi]) cudaFree(L.lut_mem[mi]);
         L.lut_mem[mi] = nullptr;
+        L.dec[mi] = false;
         for (int q = 0; q < 4; q++) L.lut[mi][q] = nullptr;
     }
-    const int ng_of[6] = {1, 0, 1, 2, 2, 1};
-    bool take[6] = {};
+    const int ng_of[6] = {1, 1, 1, 2, 2, 1};
     for (int mi = 0; mi < 6; mi++) {
         const spk_vq_matrix &M = L.m[mi];
         const Layout LM = make_layout(M.dim, M.nc, M.rows, M.cols, M.v3);
-        take[mi] = ng_of[mi] && M.rows >= LUT_MIN_ROWS && lut_ok(LM, M.nstages, ng_of[mi]);
-        for (int q = 0; take[mi] && q < M.nstages; q++)
-            if (((uintptr_t)M.stages[q] + LM.cb_off) & 7) take[mi] = false;
-    }
-    take[3] = take[4] = take[3] && take[4];
-    for (int mi = 0; mi < 6; mi++) {
-        if (!take[mi]) continue;
-        const spk_vq_matrix &M = L.m[mi];
-        const Layout LM = make_layout(M.dim, M.nc, M.rows, M.cols, M.v3);
+        if (!lut_ok(LM, M.nstages, 1)) continue;
         const size_t per = lut_bytes(LM);
         if (alloc(&L.lut_mem[mi], per * M.nstages, "alloc vq table words")) return -1;
         for (int q = 0; q < M.nstages; q++) {
             L.lut[mi][q] = (const uint8_t *)L.lut_mem[mi] + per * q;
             if (lut_pack(M.stages[q], LM, (void *)L.lut[mi][q], m->stream)) return -1;
         }
-        const size_t need = lut_part_bytes(LM, ng_of[mi]);
-        if (need > m->lut_part_size) {
+        L.dec[mi] = mi != 1 && M.rows >= LUT_MIN_ROWS && lut_ok(LM, M.nstages, ng_of[mi]);
+        const size_t need = std::max(lut_part_bytes(LM, ng_of[mi]), (size_t)0);
+        if (L.dec[mi] && need > m->lut_part_size) {
             if (m->lut_part) cudaFree(m->lut_part);
+    if (m->tc_scr) cudaFree(m->tc_scr);
+    for (void *p : {(void *)m->pf_h, (void *)m->pf_qkv, (void *)m->pf_gate, (void *)m->pf_attn, (void *)m->pf_act,
+                    (void *)m->pf_g, (void *)m->pf_tok, (void *)m->pf_pos, m->pf_scr})
+        if (p) cudaFree(p);
+    if (m->pf_host) cudaFreeHost(m->pf_host);
             m->lut_part = nullptr;
             m->lut_part_size = 0;
             if (alloc((void **)&m->lut_part, need, "alloc vq table partials")) return -1;
             m->lut_part_size = need;
+            cudaError_t e = cudaMemset(m->lut_part, 0, need);   // the grid-barrier words start at zero
+            if (e != cudaSuccess) return cuda_fail("zero the vq table scratch", e);
+        }
+        const size_t tneed = M.cols % 32 == 0 ? tc_scratch_bytes(M.rows, M.cols, ATT_MAX_TOK) : 0;
+        if (tneed > m->tc_scr_size) {
+            if (m->tc_scr) cudaFree(m->tc_scr);
+    for (void *p : {(void *)m->pf_h, (void *)m->pf_qkv, (void *)m->pf_gate, (void *)m->pf_attn, (void *)m->pf_act,
+                    (void *)m->pf_g, (void *)m->pf_tok, (void *)m->pf_pos, m->pf_scr})
+        if (p) cudaFree(p);
+    if (m->pf_host) cudaFreeHost(m->pf_host);
+            m->tc_scr = nullptr;
+            m->tc_scr_size = 0;
+            if (alloc(&m->tc_scr, tneed, "alloc batched gemm scratch")) return -1;
+            m->tc_scr_size = tneed;
+            cudaError_t e = cudaMemset(m->tc_scr, 0, tneed);   // the tile tickets start at zero
+            if (e != cudaSuccess) return cuda_fail("zero the batched gemm scratch", e);
         }
     }
+    L.dec[3] = L.dec[4] = L.dec[3] && L.dec[4];
     cudaError_t e = cudaStreamSynchronize(m->stream);
     return e == cudaSuccess ? 0 : cuda_fail("re-lay the index streams", e);
 }
@@ -772,6 +915,66 @@ int spk_model_verify(spk_model *m, const int *tokens, int ntok, int pos, int *ne
     if (next_host)
         for (int t = 0; t < ntok; t++) next_host[t] = m->host_io[16 + t];
     m->len = pos + ntok;
+    return 0;
+}
+
+/* The prompt: tokens[0..n) at positions pos .. pos + n - 1 through the model in chunks of up to
+ * 128 tokens (the reference's chunked prefill, forward_batch, vq-model-gpu.cu:858-943, and its
+ * loop at :1164-1168), every GEMM on the tensor cores (tcgen05); every position's K/V row is
+ * stored, and the last token's greedy next id (*next_host) and logits (logits_host, vocab
+ * floats) come back as spk_model_forward's would. Tensor-parallel models take the prompt in
+ * verify batches of 8. Synchronizes. */
+int spk_model_prefill(spk_model *m, const int *tokens, int n, int pos, int *next_host, float *logits_host) {
+    if (!m) return set_error("model is null");
+    if (!ready(m)) return set_error("model weights are not all set");
+    if (!tokens || n < 1) return set_error("prefill needs at least one token");
+    for (int t = 0; t < n; t++)
+        if (tokens[t] < 0 || tokens[t] >= m->cfg.vocab) return set_error("token %d is outside the vocabulary", tokens[t]);
+    if (pos < 0 || (long long)pos + n > m->cfg.max_ctx)
+        return set_error("positions %d..%d exceed the %d-token cache", pos, pos + n - 1, m->cfg.max_ctx);
+    if (pos > m->len) return set_error("position %d skips cached positions (%d cached)", pos, m->len);
+    if (m->tp_world > 1) {   // verify batches: the exchanges hold 8 rows
+        for (int t0 = 0; t0 < n; t0 += ATT_MAX_TOK) {
+            const int nb = std::min(ATT_MAX_TOK, n - t0);
+            int ids[ATT_MAX_TOK];
+            const bool last = t0 + nb == n;
+            if (spk_model_verify(m, tokens + t0, nb, pos + t0, ids, nullptr)) return -1;
+            if (last) {
+                if (next_host) *next_host = ids[nb - 1];
+                if (logits_host) {   // the verify batch left every row's logits; the last is wanted
+                    std::vector<float> all((size_t)nb * m->cfg.vocab);
+                    if (spk_model_verify(m, tokens + t0, nb, pos + t0, ids, all.data())) return -1;
+                    memcpy(logits_host, all.data() + (size_t)(nb - 1) * m->cfg.vocab, (size_t)m->cfg.vocab * 4);
+                }
+            }
+        }
+        return 0;
+    }
+    if (prefill_buffers(m)) return -1;
+    cudaError_t e = cudaSuccess;
+    for (int t0 = 0; t0 < n; t0 += PF_MAX) {
+        const int nb = std::min(PF_MAX, n - t0);
+        for (int t = 0; t < nb; t++) m->pf_host[t] = tokens[t0 + t];
+        for (int b = 0; b < PF_MAX / 8; b++) m->pf_host[PF_MAX + b] = pos + t0 + 8 * b;
+        e = cudaMemcpyAsync(m->pf_tok, m->pf_host, nb * sizeof(int), cudaMemcpyHostToDevice, m->stream);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(m->pf_pos, m->pf_host + PF_MAX, PF_MAX / 8 * sizeof(int), cudaMemcpyHostToDevice, m->stream);
+        if (e != cudaSuccess) return cuda_fail("prefill upload", e);
+        if (enqueue_prefill(m, nb)) return -1;
+        // the staging is rewritten for the next chunk: its copies must have left
+        e = cudaStreamSynchronize(m->stream);
+        if (e != cudaSuccess) return cuda_fail("prefill", e);
+    }
+    m->host_io[0] = pos + n;
+    e = cudaMemcpyAsync(m->state, m->host_io, sizeof(int), cudaMemcpyHostToDevice, m->stream);   // the next position
+    if (e == cudaSuccess) e = cudaMemcpyAsync(m->host_io + 2, m->state + 2, sizeof(int), cudaMemcpyDeviceToHost, m->stream);
+    if (e == cudaSuccess && logits_host)
+        e = cudaMemcpyAsync(logits_host, m->logits, (size_t)m->cfg.vocab * 4, cudaMemcpyDeviceToHost, m->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+    if (e != cudaSuccess) return cuda_fail("prefill", e);
+    if (check_device_error("prefill")) return -1;
+    if (next_host) *next_host = m->host_io[2];
+    m->len = pos + n;
     return 0;
 }
 

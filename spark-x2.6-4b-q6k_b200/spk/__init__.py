@@ -57,6 +57,8 @@ _PROTOS = {
     "spk_vq_lut_scratch_bytes": ([_i, _i, _i, _i, _i, _i], C.c_size_t),
     "spk_vq_lut_gemv": ([_vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _f, _vp, _i, _vp, _vp], _i),
     "spk_vq_lut_gemv_t": ([_vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _f, _vp, _i, _vp, _i, _vp], _i),
+    "spk_vq_lut_gemm_scratch_bytes": ([_i, _i, _i], C.c_size_t),
+    "spk_vq_lut_gemm": ([_vp, _i, _i, _i, _i, _i, _i, _i, _vp, _i, _vp, _f, _vp, _i, _i, _vp, _vp], _i),
     "spk_vq_gemv_fast_ok": ([_i] * 7, _i),
     "spk_vq_dequant": ([_vp, _i, _i, _i, _i, _i, _vp, _vp], _i),
     "spk_q6k_gemv": ([_vp, _i, _i, _vp, _vp, _f, _vp, _i, _vp], _i),
@@ -85,6 +87,7 @@ _PROTOS = {
     "spk_model_advance_len": ([_vp, _i], _i),
     "spk_model_write_kv": ([_vp, _i, _i, _i, _vp, _vp], _i),
     "spk_model_verify": ([_vp, _vp, _i, _i, _vp, _vp], _i),
+    "spk_model_prefill": ([_vp, _vp, _i, _i, _vp, _vp], _i),
     "spk_model_trace": ([_vp, _vp, _i], _i),
     "spk_model_tp_handle": ([_vp, _vp, _i], _i),
     "spk_model_tp_attach": ([_vp, _vp, _i, _i], _i),

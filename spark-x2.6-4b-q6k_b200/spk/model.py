@@ -262,6 +262,18 @@ class DeviceModel:
               f"verify({n} tokens at {pos})")
         return list(nxt), lg
 
+    def prefill(self, tokens, pos: int = 0, want_logits: bool = True):
+        """The prompt (forward_batch in chunks of up to 128 tokens on the tensor cores): tokens at
+        positions pos.., every K/V row stored. Returns (the last token's greedy next id, its logits
+        or None); afterwards len = pos + len(tokens)."""
+        n = len(tokens)
+        tk = (C.c_int * n)(*[int(t) for t in tokens])
+        nxt = C.c_int()
+        lg = np.empty(self.cfg.vocab, np.float32) if want_logits else None
+        check(lib().spk_model_prefill(self.h, tk, n, pos, C.byref(nxt), lg.ctypes.data_as(C.c_void_p) if lg is not None
+                                      else None), f"prefill({n} tokens at {pos})")
+        return int(nxt.value), lg
+
     def spec_round(self, anchor: int, proposals, pos0: int):
         """One verify round of spec.rs:177-245: returns (accepted proposals k, the target's
         token after them, the ids) and leaves the cache at pos0 + k + 1 positions."""

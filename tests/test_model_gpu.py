@@ -250,3 +250,51 @@ def test_config2_36_layers_ctx4096(config2, cuda):
     d16.close()
     print(f"f16 KV: worst logits relL2 {w16:.3g} over 16 steps")
     assert w16 < 2e-2
+
+
+@pytest.mark.parametrize("n", [7, 64, 130, 512])
+def test_prefill_matches_oracle(small, n):
+    """spk_model_prefill (the prompt in chunks of up to 128 tokens on the tcgen05 GEMM, attention
+    8 tokens at a time) against the oracle run token by token: the last token's logits and
+    greedy id, then 8 decode steps over the cache the prompt left (every K/V row it stored)."""
+    cfg, W = small
+    rng = np.random.default_rng(n)
+    prompt = rng.integers(0, cfg.vocab, n).tolist()
+    ref = oracle_model(cfg, W, max_ctx=n + 9)
+    for p, t in enumerate(prompt):
+        want = ref.forward(t, p)
+    dev = DeviceModel(cfg, W, max_ctx=n + 9, kv_f16=False)
+    nxt, got = dev.prefill(prompt, 0)
+    assert rel(got, want) < LOGIT_TOL, rel(got, want)
+    if margin(want) > EPS_MARGIN * max(1.0, abs(float(want.max()))):
+        assert nxt == oracle.argmax(want)
+    tok, worst = oracle.argmax(want), 0.0
+    for p in range(n, n + 8):
+        want = ref.forward(tok, p)
+        nx, got = dev.forward(tok, p)
+        worst = max(worst, rel(got, want))
+        tok = oracle.argmax(want)
+    dev.close()
+    ref.close()
+    assert worst < LOGIT_TOL, worst
+
+
+def test_prefill_full_width_512(cuda):
+    """Config-2 geometry, 4 layers (3 sliding-512 + 1 full): a 600-token prompt through the
+    prompt path (5 chunks, past the sliding window) against the oracle token by token."""
+    cfg = ModelConfig(layers=4, full=[False, False, False, True])
+    W = synth_weights(cfg, seed=6)
+    n = 600
+    prompt = np.random.default_rng(3).integers(0, cfg.vocab, n).tolist()
+    ref = oracle_model(cfg, W, max_ctx=n + 4)
+    for p, t in enumerate(prompt):
+        want = ref.forward(t, p)
+    dev = DeviceModel(cfg, W, max_ctx=n + 4, kv_f16=False)
+    nxt, got = dev.prefill(prompt, 0)
+    e0 = rel(got, want)
+    tok = oracle.argmax(want)
+    want2 = ref.forward(tok, n)
+    _, got2 = dev.forward(tok, n)
+    dev.close()
+    ref.close()
+    assert e0 < LOGIT_TOL and rel(got2, want2) < LOGIT_TOL, (e0, rel(got2, want2))

@@ -1,7 +1,7 @@
 """The table look-up VQ GEMV (vq_lut.cu, spk_vq_lut_*) against the CPU oracle.
 
-* CPU: a numpy restatement of the slice-major re-lay (the 8 indices at bytes [12 sl, 12 sl + 12)
-  of a DQV3 row stream as one 16-byte word at [sl][row] of u16 offsets 4 * idx) and of the
+* CPU: a numpy restatement of the re-lay (code words, gains, then the 8 indices at bytes
+  [12 sl, 12 sl + 12) of each DQV3 row stream as a 12-byte record at [sl][row]) and of the
   look-up sum
   (T[jj][c] = cb[c] . x[4(8 sl + jj) ..]) gives oracle.gemv_fused's result.
 * GPU: spk_vq_lut_pack is bit-exact against that re-lay; spk_vq_lut_gemv matches the oracle
@@ -26,15 +26,34 @@ def rel(a, b):
 
 
 def np_pack(buf: bytes, c: F.Container, s: int) -> np.ndarray:
-    """Stage s's index stream re-laid as [nsl][rows][8] u16: index 8 sl + jj of a row (bits
-    [12 (8 sl + jj), +12) of its little-endian DQV3 row stream) as the byte offset 4 * idx."""
+    """Stage s re-laid for the table kernel: its code words (32 KB) in the table builder's order
+    (u32 word (block, t, g) = the f16 pair (cb[16 block + g][t], cb[16 block + g + 8][t])), the
+    code words in their own order (32 KB), its gains (rows padded to a multiple of 8 with zeros, then to 16 bytes), then the index stream
+    slice-major: record [sl][row] = bytes [12 sl, 12 sl + 12) of the row's DQV3 stream (rows
+    padded with zeros)."""
     rows, nidx = c.rows, c.cols // 4
-    mrow = nidx * 3 // 2
-    o = c.stage_offset(s) + 24 + c.nc * 4 * 2 + rows * 2
-    b = np.frombuffer(buf, np.uint8, rows * mrow, o).reshape(rows, nidx // 2, 3).astype(np.uint32)
+    rows8, nsl, mrow = (rows + 7) // 8 * 8, nidx // 8, nidx * 3 // 2
+    o = c.stage_offset(s) + 24
+    cb = np.frombuffer(buf, np.uint16, c.nc * 4, o).reshape(c.nc // 16, 2, 8, 4)   # [block][half][g][t]
+    cw = (cb[:, 0].astype(np.uint32) | (cb[:, 1].astype(np.uint32) << 16)).transpose(0, 2, 1)   # [block][t][g]
+    gains = np.zeros((rows8 * 2 + 15) // 16 * 16, np.uint8)
+    gains[:rows * 2] = np.frombuffer(buf, np.uint8, rows * 2, o + c.nc * 8)
+    st = np.frombuffer(buf, np.uint8, rows * mrow, o + c.nc * 8 + rows * 2).reshape(rows, nsl, 12)
+    rec = np.zeros((nsl, rows8, 12), np.uint8)
+    rec[:, :rows] = st.transpose(1, 0, 2)
+    cbn = np.frombuffer(buf, np.uint8, c.nc * 8, o)
+    return np.concatenate([np.ascontiguousarray(cw).view(np.uint8).reshape(-1), cbn, gains, rec.reshape(-1)])
+
+
+def np_indices(buf: bytes, c: F.Container, s: int) -> np.ndarray:
+    """[nsl][rows][8] indices from the re-laid records (12-bit little-endian fields)."""
+    rows, nsl = c.rows, c.cols // 32
+    rows8 = (rows + 7) // 8 * 8
+    w = np_pack(buf, c, s)
+    off = 2 * c.nc * 8 + (rows8 * 2 + 15) // 16 * 16
+    b = w[off:].reshape(nsl, rows8, 4, 3).astype(np.uint32)[:, :rows]
     trip = b[..., 0] | (b[..., 1] << 8) | (b[..., 2] << 16)            # two indices per 3 bytes
-    idx = np.stack([trip & 0xFFF, trip >> 12], axis=-1).reshape(rows, nidx)
-    return np.ascontiguousarray((idx * 4).astype(np.uint16).reshape(rows, nidx // 8, 8).transpose(1, 0, 2))
+    return np.stack([trip & 0xFFF, trip >> 12], axis=-1).reshape(nsl, rows, 8)
 
 
 def np_lut_gemv(buf: bytes, c: F.Container, x: np.ndarray) -> np.ndarray:
@@ -44,7 +63,7 @@ def np_lut_gemv(buf: bytes, c: F.Container, x: np.ndarray) -> np.ndarray:
         o = c.stage_offset(s) + 24
         cb = np.frombuffer(buf, np.float16, c.nc * 4, o).astype(np.float64).reshape(c.nc, 4)
         gain = np.frombuffer(buf, np.float16, rows, o + c.nc * 8).astype(np.float64)
-        W = np_pack(buf, c, s).astype(np.int64) // 4
+        W = np_indices(buf, c, s).astype(np.int64)
         for sl in range(nsl):
             T = cb @ x[32 * sl:32 * sl + 32].astype(np.float64).reshape(8, 4).T   # [code][jj]
             for jj in range(8):
@@ -73,7 +92,8 @@ def _packed(bufs, c, cuda):
 
     L = spk.lib()
     n = L.spk_vq_lut_bytes(4, c.nc, c.rows, c.cols, 1)
-    assert n == c.rows * c.cols // 4 * 2
+    rows8 = (c.rows + 7) // 8 * 8
+    assert n == 2 * c.nc * 8 + (rows8 * 2 + 15) // 16 * 16 + c.cols // 32 * rows8 * 12
     out = []
     for b in bufs:
         t = torch.zeros(n, dtype=torch.uint8, device=cuda)
@@ -93,8 +113,9 @@ def test_lut_pack_is_bit_exact(cuda):
     packed = _packed(bufs, c, cuda)
     torch.cuda.synchronize()
     for s in range(2):
-        got = packed[s].cpu().numpy().view(np.uint16).reshape(cols // 32, rows, 8)
-        assert np.array_equal(got, np_pack(buf, c, s))
+        want = np_pack(buf, c, s)
+        got = packed[s].cpu().numpy()
+        assert got.size == want.size and np.array_equal(got, want)
 
 
 def _run(cuda, bufs, packed, ns, ng, rows, cols, x, w, y0, acc):
@@ -173,10 +194,12 @@ def test_lut_refuses_other_geometries(cuda):
     assert L.spk_vq_lut_bytes(4, 4096, 17, 200, 1) == 0      # 50 index groups: not whole slices
     assert L.spk_vq_lut_bytes(4, 512, 37, 96, 0) == 0        # DQVQ
     assert L.spk_vq_lut_gemv(None, None, 2, 1, 4, 4096, 64, 256, 1, None, None, 0.0, None, 0, None, None) == -1
+    st = (C.c_void_p * 2)(None, None)
+    assert L.spk_vq_lut_gemv_t(st, st, 2, 1, 4, 4096, 64, 256, 1, None, None, 0.0, None, 0, None, 1024, None) == -1
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("threads", [512, 1024])
+@pytest.mark.parametrize("threads", [0, 512])
 def test_lut_gemv_block_sizes(cuda, threads):
     import torch
 
