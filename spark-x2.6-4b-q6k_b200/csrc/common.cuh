@@ -124,6 +124,18 @@ int lut_gemv(const void *const *stages, const void *const *luts, int ns, int ng,
              const float *norm_w, float eps, float *y, int accumulate, float *part, const void *const *xst,
              const Layout *XL, float *xy, cudaStream_t s, int threads = 0);
 
+// The decode step's gate/up pair as table look-ups over 16-byte u16-offset words (vq_lut16.cu):
+// the same contract as lut_* over its own re-lay.
+namespace w16 {
+bool ok(const Layout &L, int ns, int ng);
+size_t bytes(const Layout &L);
+size_t part_bytes(const Layout &L, int ng);
+int pack(const void *stage, const Layout &L, void *dst, cudaStream_t s);
+int gemv(const void *const *stages, const void *const *luts, int ns, int ng, const Layout &L, const float *x,
+         const float *norm_w, float eps, float *y, int accumulate, float *part, const void *const *xst,
+         const Layout *XL, float *xy, cudaStream_t s, int threads = 0);
+}  // namespace w16
+
 // The VQ GEMM of a token batch on the tcgen05 tensor cores (vq_tc.cu), over the table
 // kernel's re-laid stage words: 1 launched, 0 geometry not taken, -1 error.
 //   mode 0: Y[n][r] = (accumulate ? Y[n][r] : 0) + (W RMSNorm?(X[n]))[r]

@@ -23,6 +23,7 @@
 // write a partial residual that tp_sum (tp.cu) reduces over all ranks into the
 // replicated h, and tp_argmax picks the greedy id over the vocabulary shards.
 #include <math.h>
+#include <stdio.h>
 #include <stdlib.h>
 
 #include <vector>
@@ -36,6 +37,19 @@
 using namespace spk;
 
 namespace {
+
+// With SPK_TRACE_ERRORS set, the first model entry point that finds a CUDA error pending
+// (one an earlier call left behind without reporting it) says where; a diagnostic only.
+void trace_pending(const char *where) {
+    static const bool on = getenv("SPK_TRACE_ERRORS") != nullptr;
+    static bool said = false;
+    if (!on || said) return;
+    const cudaError_t e = cudaPeekAtLastError();
+    if (e != cudaSuccess) {
+        fprintf(stderr, "[spk] CUDA error pending at %s: %s\n", where, cudaGetErrorString(e));
+        said = true;
+    }
+}
 
 // End of a step: record the generated id, feed it back as the next token, advance.
 struct DevCtl {
@@ -85,6 +99,8 @@ struct spk_model {
         void *lut_mem[6] = {};
         const void *lut[6][4] = {};
         bool dec[6] = {};     // the decode step runs this matrix through the table kernel
+        void *w16_mem[6] = {};   // its index streams re-laid for that kernel (vq_lut16.cu)
+        const void *w16[6][4] = {};
     };
     std::vector<Layer> layers;
     const void *embed = nullptr;
@@ -117,7 +133,7 @@ struct spk_model {
     unsigned long long *head_partial = nullptr;
     unsigned int *head_counter = nullptr;
     int step_launches = 0;        // kernels one decode step launches (counted while enqueuing it)
-    float *lut_part = nullptr;    // the table kernel's per-slice partial sums (vq_lut.cu)
+    float *lut_part = nullptr;    // the decode table kernel's per-slice partial sums (vq_lut16.cu)
     size_t lut_part_size = 0;
     void *tc_scr = nullptr;       // the batched tensor-core GEMM's scratch (vq_tc.cu), zeroed once
     size_t tc_scr_size = 0;
@@ -180,16 +196,16 @@ int lut_call(spk_model *m, const spk_model::Layer &L, int mi, int mi2, const flo
     const spk_vq_matrix &M = L.m[mi];
     if (!L.dec[mi] || (mi2 >= 0 && !L.dec[mi2])) return 1;
     const void *st[8], *lt[8];
-    for (int q = 0; q < M.nstages; q++) st[q] = M.stages[q], lt[q] = L.lut[mi][q];
+    for (int q = 0; q < M.nstages; q++) st[q] = M.stages[q], lt[q] = L.w16[mi][q];
     if (mi2 >= 0)
-        for (int q = 0; q < M.nstages; q++) st[M.nstages + q] = L.m[mi2].stages[q], lt[M.nstages + q] = L.lut[mi2][q];
+        for (int q = 0; q < M.nstages; q++) st[M.nstages + q] = L.m[mi2].stages[q], lt[M.nstages + q] = L.w16[mi2][q];
     const Layout LM = make_layout(M.dim, M.nc, M.rows, M.cols, M.v3);
     const spk_vq_matrix &G = L.m[1];
     Layout LG;
     const bool extra = xy && G.nstages == M.nstages && G.dim == M.dim && G.nc == M.nc && G.v3 == M.v3 && G.rows <= 64;
     if (xy && !extra) return 1;
     if (extra) LG = make_layout(G.dim, G.nc, G.rows, G.cols, G.v3);
-    return lut_gemv(st, lt, M.nstages, mi2 >= 0 ? 2 : 1, LM, x, norm_w, eps, y, accumulate, m->lut_part,
+    return w16::gemv(st, lt, M.nstages, mi2 >= 0 ? 2 : 1, LM, x, norm_w, eps, y, accumulate, m->lut_part,
                     extra ? G.stages : nullptr, extra ? &LG : nullptr, extra ? xy : nullptr, s) ? -1 : 0;
 }
 
@@ -564,6 +580,7 @@ extern "C" {
 /* vq_runtime::model::Model::new (model.rs:294-320) plus the device state the
  * reference GPU runtime allocates in alloc_model (vq-model-gpu.cu:662-705). */
 spk_model *spk_model_create(const spk_model_config *cfg, void *stream) {
+    trace_pending("spk_model_create (entry)");
     if (!cfg || !cfg->full) {
         set_error("model config is missing");
         return nullptr;
@@ -687,13 +704,17 @@ spk_model *spk_model_create(const spk_model_config *cfg, void *stream) {
 }
 
 void spk_model_destroy(spk_model *m) {
+    trace_pending("spk_model_destroy (entry)");
     if (!m) return;
     if (m->cap) cudaFree(m->cap);
     if (m->head_tiled) cudaFree(m->head_tiled);
     if (m->head_tiled_scratch) cudaFree(m->head_tiled_scratch);
-    for (auto &L : m->layers)
+    for (auto &L : m->layers) {
         for (void *p : L.lut_mem)
             if (p) cudaFree(p);
+        for (void *p : L.w16_mem)
+            if (p) cudaFree(p);
+    }
     if (m->lut_part) cudaFree(m->lut_part);
     if (m->tc_scr) cudaFree(m->tc_scr);
     for (void *p : {(void *)m->pf_h, (void *)m->pf_qkv, (void *)m->pf_gate, (void *)m->pf_attn, (void *)m->pf_act,
@@ -719,6 +740,7 @@ void spk_model_destroy(spk_model *m) {
     if (m->host_io) cudaFreeHost(m->host_io);
     if (m->host_ctl) cudaFreeHost(m->host_ctl);
     delete m;
+    trace_pending("spk_model_destroy (exit)");
 }
 
 // Every layer matrix the table layout takes (DQV3 dim 4, 4096 codes, 12-bit) is re-laid once
@@ -732,9 +754,10 @@ constexpr int LUT_MIN_ROWS = 8192;
 static int relay_layer(spk_model *m, spk_model::Layer &L) {
     for (int mi = 0; mi < 6; mi++) {
         if (L.lut_mem[mi]) cudaFree(L.lut_mem[mi]);
-        L.lut_mem[mi] = nullptr;
+        if (L.w16_mem[mi]) cudaFree(L.w16_mem[mi]);
+        L.lut_mem[mi] = L.w16_mem[mi] = nullptr;
         L.dec[mi] = false;
-        for (int q = 0; q < 4; q++) L.lut[mi][q] = nullptr;
+        for (int q = 0; q < 4; q++) L.lut[mi][q] = L.w16[mi][q] = nullptr;
     }
     const int ng_of[6] = {1, 1, 1, 2, 2, 1};
     for (int mi = 0; mi < 6; mi++) {
@@ -747,8 +770,18 @@ static int relay_layer(spk_model *m, spk_model::Layer &L) {
             L.lut[mi][q] = (const uint8_t *)L.lut_mem[mi] + per * q;
             if (lut_pack(M.stages[q], LM, (void *)L.lut[mi][q], m->stream)) return -1;
         }
-        L.dec[mi] = mi != 1 && M.rows >= LUT_MIN_ROWS && lut_ok(LM, M.nstages, ng_of[mi]);
-        const size_t need = std::max(lut_part_bytes(LM, ng_of[mi]), (size_t)0);
+        L.dec[mi] = mi != 1 && M.rows >= LUT_MIN_ROWS && w16::ok(LM, M.nstages, ng_of[mi]);
+        for (int q = 0; L.dec[mi] && q < M.nstages; q++)
+            if (((uintptr_t)M.stages[q] + LM.cb_off) & 7) L.dec[mi] = false;
+        if (L.dec[mi]) {
+            const size_t pw = w16::bytes(LM);
+            if (alloc(&L.w16_mem[mi], pw * M.nstages, "alloc vq table words")) return -1;
+            for (int q = 0; q < M.nstages; q++) {
+                L.w16[mi][q] = (const uint8_t *)L.w16_mem[mi] + pw * q;
+                if (w16::pack(M.stages[q], LM, (void *)L.w16[mi][q], m->stream)) return -1;
+            }
+        }
+        const size_t need = w16::part_bytes(LM, ng_of[mi]);
         if (L.dec[mi] && need > m->lut_part_size) {
             if (m->lut_part) cudaFree(m->lut_part);
     if (m->tc_scr) cudaFree(m->tc_scr);
@@ -760,8 +793,6 @@ static int relay_layer(spk_model *m, spk_model::Layer &L) {
             m->lut_part_size = 0;
             if (alloc((void **)&m->lut_part, need, "alloc vq table partials")) return -1;
             m->lut_part_size = need;
-            cudaError_t e = cudaMemset(m->lut_part, 0, need);   // the grid-barrier words start at zero
-            if (e != cudaSuccess) return cuda_fail("zero the vq table scratch", e);
         }
         const size_t tneed = M.cols % 32 == 0 ? tc_scratch_bytes(M.rows, M.cols, ATT_MAX_TOK) : 0;
         if (tneed > m->tc_scr_size) {
@@ -778,7 +809,12 @@ static int relay_layer(spk_model *m, spk_model::Layer &L) {
             if (e != cudaSuccess) return cuda_fail("zero the batched gemm scratch", e);
         }
     }
-    L.dec[3] = L.dec[4] = L.dec[3] && L.dec[4];
+    if (!(L.dec[3] && L.dec[4]))   // the pair only together
+        for (int mi : {3, 4}) {
+            if (L.w16_mem[mi]) cudaFree(L.w16_mem[mi]);
+            L.w16_mem[mi] = nullptr;
+            L.dec[mi] = false;
+        }
     cudaError_t e = cudaStreamSynchronize(m->stream);
     return e == cudaSuccess ? 0 : cuda_fail("re-lay the index streams", e);
 }
@@ -797,6 +833,7 @@ static int check_mat(const spk_vq_matrix *M, int rows, int cols, const char *nam
 int spk_model_set_layer(spk_model *m, int layer, const spk_vq_matrix *qkv, const spk_vq_matrix *attn_gate,
                         const spk_vq_matrix *out, const spk_vq_matrix *gate, const spk_vq_matrix *up,
                         const spk_vq_matrix *down, const float *in_norm, const float *post_norm) {
+    trace_pending("spk_model_set_layer (entry)");
     if (!m) return set_error("model is null");
     if (layer < 0 || layer >= m->cfg.layers) return set_error("layer %d is outside the %d layers", layer, m->cfg.layers);
     const spk_model_config &c = m->cfg;
@@ -823,6 +860,7 @@ int spk_model_set_layer(spk_model *m, int layer, const spk_vq_matrix *qkv, const
 
 /* The tied embedding / LM head as Q8_0 blocks [vocab][hidden] and the final norm. */
 int spk_model_set_head(spk_model *m, const void *embed_q80, const float *final_norm) {
+    trace_pending("spk_model_set_head (entry)");
     if (!m || !embed_q80 || !final_norm) return set_error("head weights are missing");
     m->embed = embed_q80;
     m->final_norm = final_norm;
@@ -849,6 +887,7 @@ int spk_model_set_head(spk_model *m, const void *embed_q80, const float *final_n
  * goes up, the greedy next id (and, if logits_host is not NULL, the vocab-wide
  * logits) come back; synchronizes the model's stream. */
 int spk_model_forward(spk_model *m, int token, int pos, float *logits_host, int *next_host) {
+    trace_pending("spk_model_forward (entry)");
     if (!m) return set_error("model is null");
     if (token < 0 || token >= m->cfg.vocab) return set_error("token %d is outside the vocabulary", token);
     if (pos < 0 || pos >= m->cfg.max_ctx) return set_error("position %d exceeds the %d-token cache", pos, m->cfg.max_ctx);
@@ -884,6 +923,7 @@ int spk_model_forward(spk_model *m, int token, int pos, float *logits_host, int 
  * (optional) the [ntok][vocab] logits. Afterwards len = pos + ntok; the caller keeps
  * the accepted prefix with spk_model_rollback, as spec.rs:241 does. Synchronizes. */
 int spk_model_verify(spk_model *m, const int *tokens, int ntok, int pos, int *next_host, float *logits_host) {
+    trace_pending("spk_model_verify (entry)");
     if (!m) return set_error("model is null");
     if (!ready(m)) return set_error("model weights are not all set");
     if (!tokens || ntok < 1 || ntok > ATT_MAX_TOK) return set_error("verify takes 1..%d tokens, not %d", ATT_MAX_TOK, ntok);
@@ -925,6 +965,7 @@ int spk_model_verify(spk_model *m, const int *tokens, int ntok, int pos, int *ne
  * floats) come back as spk_model_forward's would. Tensor-parallel models take the prompt in
  * verify batches of 8. Synchronizes. */
 int spk_model_prefill(spk_model *m, const int *tokens, int n, int pos, int *next_host, float *logits_host) {
+    trace_pending("spk_model_prefill (entry)");
     if (!m) return set_error("model is null");
     if (!ready(m)) return set_error("model weights are not all set");
     if (!tokens || n < 1) return set_error("prefill needs at least one token");
@@ -981,6 +1022,7 @@ int spk_model_prefill(spk_model *m, const int *tokens, int n, int pos, int *next
 /* Device-resident greedy decoding: set (pos, token) and the device id buffer
  * that spk_model_run fills, one id per step. */
 int spk_model_begin(spk_model *m, int token, int pos, int *ids_dev, int ids_cap) {
+    trace_pending("spk_model_begin (entry)");
     if (!m) return set_error("model is null");
     if (token < 0 || token >= m->cfg.vocab || pos < 0 || pos > m->len) return set_error("bad start token/position");
     cudaError_t e = cudaStreamSynchronize(m->stream);   // the pinned staging may still be in flight
@@ -996,6 +1038,7 @@ int spk_model_begin(spk_model *m, int token, int pos, int *ids_dev, int ids_cap)
 
 /* Run `steps` greedy decode steps from the device state, no host round trip. */
 int spk_model_run(spk_model *m, int steps) {
+    trace_pending("spk_model_run (entry)");
     if (!m) return set_error("model is null");
     for (int i = 0; i < steps; i++)
         if (run_step(m)) return -1;
@@ -1059,6 +1102,7 @@ const float *spk_model_captures(spk_model *m, size_t *slot_stride) {
 
 /* Model::rollback (model.rs:361-382): keep the first `pos` cached positions. */
 int spk_model_rollback(spk_model *m, int pos) {
+    trace_pending("spk_model_rollback (entry)");
     if (!m) return set_error("model is null");
     if (pos < 0 || pos > m->len) return set_error("rollback to %d exceeds the %d cached positions", pos, m->len);
     m->len = pos;

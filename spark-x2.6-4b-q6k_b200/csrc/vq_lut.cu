@@ -509,6 +509,8 @@ int lut_pack(const void *stage, const Layout &L, void *dst, cudaStream_t s) {
     if (((uintptr_t)dst & 15) != 0) return set_error("vq table pack: the destination must be 16-byte aligned");
     const size_t n = (L.nidx_row / LGC) * (size_t)rows8_of(L);
     const int blocks = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
+    const cudaError_t before = cudaGetLastError();   // an earlier call's error: not this launch's
+    if (before != cudaSuccess) return cuda_fail("vq table pack: an earlier CUDA call had failed", before);
     vq_lut_pack_kernel<<<blocks > 128 ? blocks : 128, 256, 0, s>>>((const uint8_t *)stage, L, rows8_of(L),
                                                                   rec_off_of(L), (uint8_t *)dst);
     cudaError_t e = cudaGetLastError();

@@ -37,7 +37,7 @@ namespace {
 
 constexpr int TC_M = 128;          // rows per tile (tensor-memory lanes)
 constexpr int TC_KB = 32;          // columns per slice (one k-block: two K = 16 MMAs)
-constexpr int TC_NAMAX = 8;        // operand slots at most (A tiles of both stages + B block + records)
+constexpr int TC_NAMAX = 3;        // operand slots (A tiles of both stages + B block + records): more measured slower
 constexpr int TC_GW = 8;           // gather warps
 constexpr int TC_THREADS = (2 + TC_GW) * 32;   // producer, MMA issuer, gather / epilogue warps
 constexpr int TC_MAXSEG = 8;       // segments a CTA may walk
@@ -183,16 +183,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) vq_tc_kernel(const TcArgs a) {
             // the stages' natural-order code words, once (weights: before the wait)
             mbar_arrive_expect_tx(cb_full, a.ns * LUT_CB);
             for (int s = 0; s < a.ns; s++) bulk_g2s(cbn + s * LUT_CB, a.lut[s] + a.cbn_off, LUT_CB, cb_full);
-            for (int j = 0; j < nseg; j++) {   // every record this CTA reads: into L2 (a hint)
-                const Seg sg = segs[j];
-                const int r0 = sg.tile * TC_M, nr = min(TC_M, a.rows8 - r0);
-                for (int kb = sg.kb0; kb < sg.kb1; kb++)
-                    for (int s = 0; s < a.ns; s++)
-                        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(
-                                         a.lut[s] + a.rec_off + ((size_t)kb * a.rows8 + r0) * 12),
-                                     "r"((uint32_t)nr * 12)
-                                     : "memory");
-            }
             pdl_wait();   // the activation blocks are the previous kernel's output
             int k = 0;
             for (int j = 0; j < nseg; j++) {
@@ -412,10 +402,12 @@ int tc_gemm(const void *const *luts, int ns, const Layout &L, int ntok, const fl
     for (int q = 0; q < ns; q++)
         if (!luts[q] || ((uintptr_t)luts[q] & 15)) return 0;
     const int ntok8 = (ntok + 7) & ~7, N = 2 * ntok8, nsl = L.cols / TC_KB, tiles = (L.rows + TC_M - 1) / TC_M;
+    // the kernel's static shared memory (2 ints, padded by the compiler) counts against the same limit
+    const size_t limit = smem_optin_max() > 2048 ? smem_optin_max() - 2048 : 0;
     int na = TC_NAMAX;
-    while (na > 2 && tc_smem(N, na) > smem_optin_max()) na--;
+    while (na > 2 && tc_smem(N, na) > limit) na--;
     const size_t smem = tc_smem(N, na);
-    if (smem > smem_optin_max()) return 0;
+    if (smem > limit) return 0;
     const long long U = (long long)tiles * nsl;
     const int G = (int)(U < sm_count() ? U : sm_count());   // every CTA has work
     if ((U + G - 1) / G / nsl + 2 > TC_MAXSEG) return 0;

@@ -252,7 +252,7 @@ def test_config2_36_layers_ctx4096(config2, cuda):
     assert w16 < 2e-2
 
 
-@pytest.mark.parametrize("n", [7, 64, 130, 512])
+@pytest.mark.parametrize("n", [7, 64, 130, 512, 4096])
 def test_prefill_matches_oracle(small, n):
     """spk_model_prefill (the prompt in chunks of up to 128 tokens on the tcgen05 GEMM, attention
     8 tokens at a time) against the oracle run token by token: the last token's logits and
