@@ -281,9 +281,9 @@ def run_ours(args) -> None:
     rows_l = m.mats[0]["gate"].rows
     act = torch.zeros(rows_l, device=dev)
     launches = []
-    # the model runs the pair through the table kernel (vq_lut.cu) at >= 8192 rows, when it
-    # takes the geometry: time that one, on index words re-laid here the way the model does
-    lut_n = L.spk_vq_lut_bytes(4, 4096, rows_l, cfg.hidden, 1) if rows_l >= 8192 else 0
+    # the model runs the pair through the 16-byte-word table kernel (vq_lut16.cu) at >= 8192 rows,
+    # when it takes the geometry: time that one, on index words re-laid here the way the model does
+    lut_n = L.spk_vq_lut16_bytes(4, 4096, rows_l, cfg.hidden, 1) if rows_l >= 8192 else 0
     luts = []
     for li in range(cfg.layers):
         g, u = m.mats[li]["gate"], m.mats[li]["up"]
@@ -293,11 +293,11 @@ def run_ours(args) -> None:
         if lut_n:
             ws = [torch.empty(lut_n, dtype=torch.uint8, device=dev) for _ in range(4)]
             for p_, w_ in zip(stp, ws):
-                spk.check(L.spk_vq_lut_pack(C.c_void_p(p_), 4, 4096, rows_l, cfg.hidden, 1, w_.data_ptr(), None))
+                spk.check(L.spk_vq_lut16_pack(C.c_void_p(p_), 4, 4096, rows_l, cfg.hidden, 1, w_.data_ptr(), None))
             luts.append(ws)
             lt = (C.c_void_p * 4)(*[w_.data_ptr() for w_ in ws])
         launches.append((st, lt, m.norms[li][1]))
-    scr = (torch.zeros(L.spk_vq_lut_scratch_bytes(2, 4, 4096, rows_l, cfg.hidden, 1), dtype=torch.uint8, device=dev)
+    scr = (torch.zeros(L.spk_vq_lut16_scratch_bytes(2, 4, 4096, rows_l, cfg.hidden, 1), dtype=torch.uint8, device=dev)
            if lut_n else None)
     torch.cuda.synchronize(dev)
     sp = C.c_void_p(m.stream.cuda_stream)
@@ -305,8 +305,8 @@ def run_ours(args) -> None:
     def gateup(k):
         st, lt, nw = launches[k % cfg.layers]
         if lt is not None:
-            spk.check(L.spk_vq_lut_gemv(st, lt, 2, 2, 4, 4096, rows_l, cfg.hidden, 1, x.data_ptr(), nw.data_ptr(),
-                                        cfg.eps, act.data_ptr(), 0, scr.data_ptr(), sp))
+            spk.check(L.spk_vq_lut16_gemv(st, lt, 2, 2, 4, 4096, rows_l, cfg.hidden, 1, x.data_ptr(), nw.data_ptr(),
+                                          cfg.eps, act.data_ptr(), 0, scr.data_ptr(), sp))
         else:
             spk.check(L.spk_vq_gemv(st, 2, 2, 4, 4096, rows_l, cfg.hidden, 1, x.data_ptr(), nw.data_ptr(), cfg.eps,
                                     act.data_ptr(), 0, sp))
@@ -375,7 +375,7 @@ def run_ours(args) -> None:
                        "step_hbm_gbs_per_gpu": (bytes_per_token + kv_bytes) * args.steps / dt / 1e9,
                        "step_trace_rank0": trace},
             "roofline": {"bound": "hbm",
-                         "kernel": (("vq_lut_kernel + vq_lut_finish_kernel" if lut_n else "vq_fast_kernel") +
+                         "kernel": (("vq_lut16.cu vq_lut_kernel + vq_lut_finish_kernel" if lut_n else "vq_fast_kernel") +
                                     f" gate+up pair {rows_l}x2560 x2 stages (RMSNorm, GELU), rank 0"),
                          "achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "alg_bytes_per_launch": alg_bytes,
@@ -734,7 +734,7 @@ def run_ggml(args) -> None:
     head = len(mats) - 1
     line = _gemv_line(args, "config1: Q6_K trunk shapes + Q8_0 131072x2560 head, batch 1", alg / t / 1e9,
                       mats[head]["alg"], per[head], "blk_fast_kernel Q8_0 131072x2560",
-                      traffic_from_profiles("q80_gemv_131072x2560"),
+                      traffic_from_profiles("ggml_gemv_trunk_and_head"),
                       {"matrices": detail, "l2": "each matrix rotates over copies totalling > 256 MB"},
                       e2e, sum(4 * m["cols"] for m in mats), sum(4 * m["rows"] for m in mats), cb, clk,
                       args.steps * len(mats))

@@ -118,7 +118,18 @@ int spk_vq_lut_gemv(const void *const *stages, const void *const *luts, int nsta
 int spk_vq_lut_gemv_t(const void *const *stages, const void *const *luts, int nstages, int ngroups, int dim, int nc,
                       int rows, int cols, int v3, const float *x, const float *norm_w, float eps, float *y,
                       int accumulate, void *scratch, int threads, void *stream);
-/* The VQ GEMM of a token batch on the tcgen05 tensor cores, from the same re-laid words:
+/* The decode step's gate/up-pair kernel (the same contract, table look-ups over each stage's
+ * index stream re-laid as 16-byte words of u16 table offsets, one per row and 8-group slice;
+ * code words and gains read from the payloads): re-lay once with spk_vq_lut16_pack into
+ * spk_vq_lut16_bytes device bytes, then spk_vq_lut16_gemv with spk_vq_lut16_scratch_bytes of
+ * scratch. Two launches, no sync. */
+size_t spk_vq_lut16_bytes(int dim, int nc, int rows, int cols, int v3);
+int spk_vq_lut16_pack(const void *stage, int dim, int nc, int rows, int cols, int v3, void *dst, void *stream);
+size_t spk_vq_lut16_scratch_bytes(int ngroups, int dim, int nc, int rows, int cols, int v3);
+int spk_vq_lut16_gemv(const void *const *stages, const void *const *luts, int nstages, int ngroups, int dim, int nc,
+                      int rows, int cols, int v3, const float *x, const float *norm_w, float eps, float *y,
+                      int accumulate, void *scratch, void *stream);
+/* The VQ GEMM of a token batch on the tcgen05 tensor cores, from spk_vq_lut_pack's words:
  * for n < ntok <= 128, Y[n] (=|+=) sum_s gain_s W_s RMSNorm?(X[n]) (DQV3 dim 4, 4096 codes,
  * 12-bit, 1-2 stages, cols a multiple of 32; replaces forward_batch's gemm_tiled_kernel
  * launches, vq-model-gpu.cu:858-943, decode-gpu.cu:359-501, and the verify batch's GEMMs).

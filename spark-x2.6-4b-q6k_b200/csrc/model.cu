@@ -40,14 +40,14 @@ namespace {
 
 // With SPK_TRACE_ERRORS set, the first model entry point that finds a CUDA error pending
 // (one an earlier call left behind without reporting it) says where; a diagnostic only.
-void trace_pending(const char *where) {
+void trace_pending(const char *where, int arg = -1) {
     static const bool on = getenv("SPK_TRACE_ERRORS") != nullptr;
-    static bool said = false;
-    if (!on || said) return;
+    static int said = 0;
+    if (!on || said >= 3) return;
     const cudaError_t e = cudaPeekAtLastError();
     if (e != cudaSuccess) {
-        fprintf(stderr, "[spk] CUDA error pending at %s: %s\n", where, cudaGetErrorString(e));
-        said = true;
+        fprintf(stderr, "[spk] CUDA error pending at %s (%d): %s\n", where, arg, cudaGetErrorString(e));
+        said++;
     }
 }
 
@@ -752,14 +752,19 @@ void spk_model_destroy(spk_model *m) {
 constexpr int LUT_MIN_ROWS = 8192;
 
 static int relay_layer(spk_model *m, spk_model::Layer &L) {
+    auto release = [](void *&p, const char *what) -> int {
+        if (!p) return 0;
+        const cudaError_t e = cudaFree(p);
+        p = nullptr;
+        return e == cudaSuccess ? 0 : cuda_fail(what, e);
+    };
     for (int mi = 0; mi < 6; mi++) {
-        if (L.lut_mem[mi]) cudaFree(L.lut_mem[mi]);
-        if (L.w16_mem[mi]) cudaFree(L.w16_mem[mi]);
-        L.lut_mem[mi] = L.w16_mem[mi] = nullptr;
+        if (release(L.lut_mem[mi], "free vq table words") || release(L.w16_mem[mi], "free vq table words")) return -1;
         L.dec[mi] = false;
         for (int q = 0; q < 4; q++) L.lut[mi][q] = L.w16[mi][q] = nullptr;
     }
     const int ng_of[6] = {1, 1, 1, 2, 2, 1};
+    size_t part_need = 0, tc_need = 0;
     for (int mi = 0; mi < 6; mi++) {
         const spk_vq_matrix &M = L.m[mi];
         const Layout LM = make_layout(M.dim, M.nc, M.rows, M.cols, M.v3);
@@ -780,41 +785,33 @@ static int relay_layer(spk_model *m, spk_model::Layer &L) {
                 L.w16[mi][q] = (const uint8_t *)L.w16_mem[mi] + pw * q;
                 if (w16::pack(M.stages[q], LM, (void *)L.w16[mi][q], m->stream)) return -1;
             }
+            part_need = std::max(part_need, w16::part_bytes(LM, ng_of[mi]));
         }
-        const size_t need = w16::part_bytes(LM, ng_of[mi]);
-        if (L.dec[mi] && need > m->lut_part_size) {
-            if (m->lut_part) cudaFree(m->lut_part);
-    if (m->tc_scr) cudaFree(m->tc_scr);
-    for (void *p : {(void *)m->pf_h, (void *)m->pf_qkv, (void *)m->pf_gate, (void *)m->pf_attn, (void *)m->pf_act,
-                    (void *)m->pf_g, (void *)m->pf_tok, (void *)m->pf_pos, m->pf_scr})
-        if (p) cudaFree(p);
-    if (m->pf_host) cudaFreeHost(m->pf_host);
-            m->lut_part = nullptr;
-            m->lut_part_size = 0;
-            if (alloc((void **)&m->lut_part, need, "alloc vq table partials")) return -1;
-            m->lut_part_size = need;
-        }
-        const size_t tneed = M.cols % 32 == 0 ? tc_scratch_bytes(M.rows, M.cols, ATT_MAX_TOK) : 0;
-        if (tneed > m->tc_scr_size) {
-            if (m->tc_scr) cudaFree(m->tc_scr);
-    for (void *p : {(void *)m->pf_h, (void *)m->pf_qkv, (void *)m->pf_gate, (void *)m->pf_attn, (void *)m->pf_act,
-                    (void *)m->pf_g, (void *)m->pf_tok, (void *)m->pf_pos, m->pf_scr})
-        if (p) cudaFree(p);
-    if (m->pf_host) cudaFreeHost(m->pf_host);
-            m->tc_scr = nullptr;
-            m->tc_scr_size = 0;
-            if (alloc(&m->tc_scr, tneed, "alloc batched gemm scratch")) return -1;
-            m->tc_scr_size = tneed;
-            cudaError_t e = cudaMemset(m->tc_scr, 0, tneed);   // the tile tickets start at zero
-            if (e != cudaSuccess) return cuda_fail("zero the batched gemm scratch", e);
-        }
+        if (M.cols % 32 == 0) tc_need = std::max(tc_need, tc_scratch_bytes(M.rows, M.cols, ATT_MAX_TOK));
     }
     if (!(L.dec[3] && L.dec[4]))   // the pair only together
         for (int mi : {3, 4}) {
-            if (L.w16_mem[mi]) cudaFree(L.w16_mem[mi]);
-            L.w16_mem[mi] = nullptr;
+            if (release(L.w16_mem[mi], "free vq table words")) return -1;
             L.dec[mi] = false;
         }
+    // the scratches, grown (once) to the largest need of any layer
+    if (part_need > m->lut_part_size) {
+        void *p = m->lut_part;
+        if (release(p, "free vq table partials")) return -1;
+        m->lut_part = nullptr;
+        m->lut_part_size = 0;
+        if (alloc((void **)&m->lut_part, part_need, "alloc vq table partials")) return -1;
+        m->lut_part_size = part_need;
+    }
+    if (tc_need > m->tc_scr_size) {
+        if (release(m->tc_scr, "free batched gemm scratch")) return -1;
+        m->tc_scr_size = 0;
+        if (alloc(&m->tc_scr, tc_need, "alloc batched gemm scratch")) return -1;
+        m->tc_scr_size = tc_need;
+        cudaError_t e = cudaMemset(m->tc_scr, 0, tc_need);   // the tile tickets start at zero
+        if (e != cudaSuccess) return cuda_fail("zero the batched gemm scratch", e);
+    }
+    trace_pending("relay: exit");
     cudaError_t e = cudaStreamSynchronize(m->stream);
     return e == cudaSuccess ? 0 : cuda_fail("re-lay the index streams", e);
 }

@@ -495,3 +495,43 @@ int gemv(const void *const *stages, const void *const *luts, int ns, int ng, con
 
 }  // namespace w16
 }  // namespace spk
+
+using namespace spk;
+
+extern "C" {
+
+/* Bytes of one stage's index stream re-laid for spk_vq_lut16_gemv (16-byte words of u16 table
+ * offsets, one per row and slice of 8 index groups); 0 when the kernel does not take the
+ * geometry (DQV3, dim 4, 4096 codes, 12-bit, whole slices). */
+size_t spk_vq_lut16_bytes(int dim, int nc, int rows, int cols, int v3) {
+    if (dim <= 0 || nc <= 0 || rows <= 0 || cols <= 0 || cols % dim) return 0;
+    const Layout L = make_layout(dim, nc, rows, cols, v3);
+    return w16::ok(L, 1, 1) ? w16::bytes(L) : 0;
+}
+
+/* Re-lay one stage's index stream (device DQV3 payload) into dst (device, 16-byte aligned). */
+int spk_vq_lut16_pack(const void *stage, int dim, int nc, int rows, int cols, int v3, void *dst, void *stream) {
+    if (!spk_vq_lut16_bytes(dim, nc, rows, cols, v3)) return set_error("vq table kernel: geometry not taken");
+    return w16::pack(stage, make_layout(dim, nc, rows, cols, v3), dst, (cudaStream_t)stream);
+}
+
+/* Device scratch spk_vq_lut16_gemv needs for the per-slice partial sums. */
+size_t spk_vq_lut16_scratch_bytes(int ngroups, int dim, int nc, int rows, int cols, int v3) {
+    if (!spk_vq_lut16_bytes(dim, nc, rows, cols, v3) || ngroups < 1 || ngroups > 2) return 0;
+    return w16::part_bytes(make_layout(dim, nc, rows, cols, v3), ngroups);
+}
+
+/* spk_vq_gemv's contract through the decode step's gate/up-pair table kernel: stages are the
+ * DQV3 payloads (code words and gains are read there), luts their spk_vq_lut16_pack words, both
+ * group-major; scratch is spk_vq_lut16_scratch_bytes device bytes. Two launches, no sync. */
+int spk_vq_lut16_gemv(const void *const *stages, const void *const *luts, int nstages, int ngroups, int dim, int nc,
+                      int rows, int cols, int v3, const float *x, const float *norm_w, float eps, float *y,
+                      int accumulate, void *scratch, void *stream) {
+    if (!stages || !luts) return set_error("vq table kernel: null stage list");
+    if (!spk_vq_lut16_bytes(dim, nc, rows, cols, v3)) return set_error("vq table kernel: geometry not taken");
+    const Layout L = make_layout(dim, nc, rows, cols, v3);
+    return w16::gemv(stages, luts, nstages, ngroups, L, x, norm_w, eps, y, accumulate, (float *)scratch, nullptr,
+                     nullptr, nullptr, (cudaStream_t)stream, 0);
+}
+
+}  // extern "C"
