@@ -281,32 +281,32 @@ def run_ours(args) -> None:
     rows_l = m.mats[0]["gate"].rows
     act = torch.zeros(rows_l, device=dev)
     launches = []
-    # the model runs the pair through the 16-byte-word table kernel (vq_lut16.cu) at >= 8192 rows,
+    # the model runs the pair through the bank-scheduled table kernel (vq_tab.cu) at >= 8192 rows,
     # when it takes the geometry: time that one, on index words re-laid here the way the model does
-    lut_n = L.spk_vq_lut16_bytes(4, 4096, rows_l, cfg.hidden, 1) if rows_l >= 8192 else 0
-    luts = []
+    tab_n = L.spk_vq_tab_bytes(4, 4096, rows_l, cfg.hidden, 1) if rows_l >= 8192 else 0
+    tabs = []
     for li in range(cfg.layers):
         g, u = m.mats[li]["gate"], m.mats[li]["up"]
         stp = [g.stages[0], g.stages[1], u.stages[0], u.stages[1]]
         st = (C.c_void_p * 4)(*stp)
         lt = None
-        if lut_n:
-            ws = [torch.empty(lut_n, dtype=torch.uint8, device=dev) for _ in range(4)]
+        if tab_n:
+            ws = [torch.empty(tab_n, dtype=torch.uint8, device=dev) for _ in range(4)]
             for p_, w_ in zip(stp, ws):
-                spk.check(L.spk_vq_lut16_pack(C.c_void_p(p_), 4, 4096, rows_l, cfg.hidden, 1, w_.data_ptr(), None))
-            luts.append(ws)
+                spk.check(L.spk_vq_tab_pack(C.c_void_p(p_), 4, 4096, rows_l, cfg.hidden, 1, w_.data_ptr(), None))
+            tabs.append(ws)
             lt = (C.c_void_p * 4)(*[w_.data_ptr() for w_ in ws])
         launches.append((st, lt, m.norms[li][1]))
-    scr = (torch.zeros(L.spk_vq_lut16_scratch_bytes(2, 4, 4096, rows_l, cfg.hidden, 1), dtype=torch.uint8, device=dev)
-           if lut_n else None)
+    scr = (torch.zeros(L.spk_vq_tab_scratch_bytes(2, 4, 4096, rows_l, cfg.hidden, 1), dtype=torch.uint8, device=dev)
+           if tab_n else None)
     torch.cuda.synchronize(dev)
     sp = C.c_void_p(m.stream.cuda_stream)
 
     def gateup(k):
         st, lt, nw = launches[k % cfg.layers]
         if lt is not None:
-            spk.check(L.spk_vq_lut16_gemv(st, lt, 2, 2, 4, 4096, rows_l, cfg.hidden, 1, x.data_ptr(), nw.data_ptr(),
-                                          cfg.eps, act.data_ptr(), 0, scr.data_ptr(), sp))
+            spk.check(L.spk_vq_tab_gemv(st, lt, 2, 2, 4, 4096, rows_l, cfg.hidden, 1, x.data_ptr(), nw.data_ptr(),
+                                        cfg.eps, act.data_ptr(), 0, scr.data_ptr(), sp))
         else:
             spk.check(L.spk_vq_gemv(st, 2, 2, 4, 4096, rows_l, cfg.hidden, 1, x.data_ptr(), nw.data_ptr(), cfg.eps,
                                     act.data_ptr(), 0, sp))
@@ -326,9 +326,9 @@ def run_ours(args) -> None:
     alg_bytes = 2 * 2 * stage + 2 * cfg.hidden * 4 + rows_l * 4
     peak, peak_kind = hbm_peak()
     achieved = alg_bytes / t_kernel / 1e9
-    traffic = (traffic_from_profiles("vq_lut_gate_up_10240x2560x2" if lut_n else "vq_gate_up_gemv_10240x2560x2")
+    traffic = (traffic_from_profiles("vq_tab_gate_up_10240x2560x2" if tab_n else "vq_gate_up_gemv_10240x2560x2")
                if world == 1 else None)
-    del luts
+    del tabs
 
     # end to end through the C-ABI with host buffers: token up, next id down, every step
     e2e_n = min(args.steps, 64)
@@ -375,7 +375,7 @@ def run_ours(args) -> None:
                        "step_hbm_gbs_per_gpu": (bytes_per_token + kv_bytes) * args.steps / dt / 1e9,
                        "step_trace_rank0": trace},
             "roofline": {"bound": "hbm",
-                         "kernel": (("vq_lut16.cu vq_lut_kernel + vq_lut_finish_kernel" if lut_n else "vq_fast_kernel") +
+                         "kernel": (("vq_tab.cu vq_tab_kernel" if tab_n else "vq_fast_kernel") +
                                     f" gate+up pair {rows_l}x2560 x2 stages (RMSNorm, GELU), rank 0"),
                          "achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "alg_bytes_per_launch": alg_bytes,

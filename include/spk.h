@@ -118,17 +118,23 @@ int spk_vq_lut_gemv(const void *const *stages, const void *const *luts, int nsta
 int spk_vq_lut_gemv_t(const void *const *stages, const void *const *luts, int nstages, int ngroups, int dim, int nc,
                       int rows, int cols, int v3, const float *x, const float *norm_w, float eps, float *y,
                       int accumulate, void *scratch, int threads, void *stream);
-/* The decode step's gate/up-pair kernel (the same contract, table look-ups over each stage's
- * index stream re-laid as 16-byte words of u16 table offsets, one per row and 8-group slice;
- * code words and gains read from the payloads): re-lay once with spk_vq_lut16_pack into
- * spk_vq_lut16_bytes device bytes, then spk_vq_lut16_gemv with spk_vq_lut16_scratch_bytes of
- * scratch. Two launches, no sync. */
-size_t spk_vq_lut16_bytes(int dim, int nc, int rows, int cols, int v3);
-int spk_vq_lut16_pack(const void *stage, int dim, int nc, int rows, int cols, int v3, void *dst, void *stream);
-size_t spk_vq_lut16_scratch_bytes(int ngroups, int dim, int nc, int rows, int cols, int v3);
-int spk_vq_lut16_gemv(const void *const *stages, const void *const *luts, int nstages, int ngroups, int dim, int nc,
-                      int rows, int cols, int v3, const float *x, const float *norm_w, float eps, float *y,
-                      int accumulate, void *scratch, void *stream);
+/* The decode step's VQ GEMV (the same contract as spk_vq_gemv, replacing the same per-stage
+ * loop, vq-model-gpu.cu:651-660 over decode-gpu.cu:267-301) as shared-memory table look-ups
+ * over index words whose look-up order is scheduled for the shared-memory banks: DQV3, dim 4,
+ * 4096 codes, 12-bit, 1-2 stages, 1-2 groups, rows a multiple of 32 up to 10240, cols a
+ * multiple of 32. Re-lay each stage once with spk_vq_tab_pack into spk_vq_tab_bytes device
+ * bytes (16-byte aligned; 0 = geometry not taken): per (8-group slice, row) one 16-byte word of
+ * 8 u16 table offsets. spk_vq_tab_gemv reads the code words and gains from the payloads and
+ * takes spk_vq_tab_scratch_bytes of device scratch (for the device current at the call),
+ * zeroed before its first use and kept for later calls: its first 256 bytes hold a grid
+ * barrier's count, which every call advances; calls sharing a scratch must not overlap on the
+ * GPU. One launch (the cross-CTA sums and the epilogue inside it), no sync. */
+size_t spk_vq_tab_bytes(int dim, int nc, int rows, int cols, int v3);
+int spk_vq_tab_pack(const void *stage, int dim, int nc, int rows, int cols, int v3, void *dst, void *stream);
+size_t spk_vq_tab_scratch_bytes(int ngroups, int dim, int nc, int rows, int cols, int v3);
+int spk_vq_tab_gemv(const void *const *stages, const void *const *words, int nstages, int ngroups, int dim, int nc,
+                    int rows, int cols, int v3, const float *x, const float *norm_w, float eps, float *y,
+                    int accumulate, void *scratch, void *stream);
 /* The VQ GEMM of a token batch on the tcgen05 tensor cores, from spk_vq_lut_pack's words:
  * for n < ntok <= 128, Y[n] (=|+=) sum_s gain_s W_s RMSNorm?(X[n]) (DQV3 dim 4, 4096 codes,
  * 12-bit, 1-2 stages, cols a multiple of 32; replaces forward_batch's gemm_tiled_kernel

@@ -124,17 +124,19 @@ int lut_gemv(const void *const *stages, const void *const *luts, int ns, int ng,
              const float *norm_w, float eps, float *y, int accumulate, float *part, const void *const *xst,
              const Layout *XL, float *xy, cudaStream_t s, int threads = 0);
 
-// The decode step's gate/up pair as table look-ups over 16-byte u16-offset words (vq_lut16.cu):
-// the same contract as lut_* over its own re-lay.
-namespace w16 {
+// The decode step's VQ GEMVs as table look-ups over bank-scheduled u16-offset words, the
+// cross-CTA sums and the epilogue in the same launch (vq_tab.cu). scratch: scratch_bytes,
+// zeroed once (a grid barrier's count, then the per-CTA partials). An optional small matrix of
+// the same input (g_proj, <= 64 rows) rides along.
+namespace tab {
 bool ok(const Layout &L, int ns, int ng);
 size_t bytes(const Layout &L);
-size_t part_bytes(const Layout &L, int ng);
+size_t scratch_bytes(const Layout &L, int ng);
 int pack(const void *stage, const Layout &L, void *dst, cudaStream_t s);
-int gemv(const void *const *stages, const void *const *luts, int ns, int ng, const Layout &L, const float *x,
-         const float *norm_w, float eps, float *y, int accumulate, float *part, const void *const *xst,
-         const Layout *XL, float *xy, cudaStream_t s, int threads = 0);
-}  // namespace w16
+int gemv(const void *const *stages, const void *const *words, int ns, int ng, const Layout &L, const float *x,
+         const float *norm_w, float eps, float *y, int accumulate, void *scratch, const void *const *xst,
+         const Layout *XL, float *xy, cudaStream_t s);
+}  // namespace tab
 
 // The VQ GEMM of a token batch on the tcgen05 tensor cores (vq_tc.cu), over the table
 // kernel's re-laid stage words: 1 launched, 0 geometry not taken, -1 error.

@@ -99,8 +99,8 @@ struct spk_model {
         void *lut_mem[6] = {};
         const void *lut[6][4] = {};
         bool dec[6] = {};     // the decode step runs this matrix through the table kernel
-        void *w16_mem[6] = {};   // its index streams re-laid for that kernel (vq_lut16.cu)
-        const void *w16[6][4] = {};
+        void *tab_mem[6] = {};   // its index streams re-laid for that kernel (vq_tab.cu)
+        const void *tab[6][4] = {};
     };
     std::vector<Layer> layers;
     const void *embed = nullptr;
@@ -133,8 +133,8 @@ struct spk_model {
     unsigned long long *head_partial = nullptr;
     unsigned int *head_counter = nullptr;
     int step_launches = 0;        // kernels one decode step launches (counted while enqueuing it)
-    float *lut_part = nullptr;    // the decode table kernel's per-slice partial sums (vq_lut16.cu)
-    size_t lut_part_size = 0;
+    void *tab_scr = nullptr;      // the decode table kernel's grid-barrier count and per-CTA partials (vq_tab.cu)
+    size_t tab_scr_size = 0;
     void *tc_scr = nullptr;       // the batched tensor-core GEMM's scratch (vq_tc.cu), zeroed once
     size_t tc_scr_size = 0;
     // the prompt path (spk_model_prefill): rows for a chunk of up to PF_MAX tokens, made on first use
@@ -190,22 +190,22 @@ int qkv_gate(const spk_model::Layer &L, const float *h, float eps, float *qkv, f
 
 // Layer matrix mi (with mi2, the up_proj of a pair) through the table kernel when it
 // was re-laid for it: 0 launched, 1 not taken, -1 error. For q_k_v_proj, g_proj rides
-// along in the finishing kernel.
+// along (the kernel's last CTAs).
 int lut_call(spk_model *m, const spk_model::Layer &L, int mi, int mi2, const float *x, const float *norm_w, float eps,
              float *y, int accumulate, float *xy, cudaStream_t s) {
     const spk_vq_matrix &M = L.m[mi];
     if (!L.dec[mi] || (mi2 >= 0 && !L.dec[mi2])) return 1;
     const void *st[8], *lt[8];
-    for (int q = 0; q < M.nstages; q++) st[q] = M.stages[q], lt[q] = L.w16[mi][q];
+    for (int q = 0; q < M.nstages; q++) st[q] = M.stages[q], lt[q] = L.tab[mi][q];
     if (mi2 >= 0)
-        for (int q = 0; q < M.nstages; q++) st[M.nstages + q] = L.m[mi2].stages[q], lt[M.nstages + q] = L.w16[mi2][q];
+        for (int q = 0; q < M.nstages; q++) st[M.nstages + q] = L.m[mi2].stages[q], lt[M.nstages + q] = L.tab[mi2][q];
     const Layout LM = make_layout(M.dim, M.nc, M.rows, M.cols, M.v3);
     const spk_vq_matrix &G = L.m[1];
     Layout LG;
     const bool extra = xy && G.nstages == M.nstages && G.dim == M.dim && G.nc == M.nc && G.v3 == M.v3 && G.rows <= 64;
     if (xy && !extra) return 1;
     if (extra) LG = make_layout(G.dim, G.nc, G.rows, G.cols, G.v3);
-    return w16::gemv(st, lt, M.nstages, mi2 >= 0 ? 2 : 1, LM, x, norm_w, eps, y, accumulate, m->lut_part,
+    return tab::gemv(st, lt, M.nstages, mi2 >= 0 ? 2 : 1, LM, x, norm_w, eps, y, accumulate, m->tab_scr,
                     extra ? G.stages : nullptr, extra ? &LG : nullptr, extra ? xy : nullptr, s) ? -1 : 0;
 }
 
@@ -267,8 +267,8 @@ int enqueue_step(spk_model *m) {
     int *pos = m->state, *token = m->state + 1, *amax = m->state + 2, *amax_l = m->state + 4;
     const bool tp = m->tp_world > 1;
     if (mark(m) || spk_q80_row(m->embed, c.vocab, c.hidden, 0, token, m->h, s) || mark(m)) return -1;
-    // embedding row, head, advance; per layer attention plus one launch per code-word GEMV or
-    // two per table GEMV; per tensor-parallel exchange one, plus the vocabulary argmax
+    // embedding row, head, advance; per layer attention plus one launch per GEMV; per
+    // tensor-parallel exchange one, plus the vocabulary argmax
     int nl = 3 + (tp ? 1 : 0);
     for (int li = 0; li < c.layers; li++) {
         const spk_model::Layer &L = m->layers[li];
@@ -276,7 +276,7 @@ int enqueue_step(spk_model *m) {
         nl += (m->ncap && m->cap_slot[li] >= 0) + 1 + (tp ? 2 : 0);
         int lr = lut_call(m, L, 0, -1, m->h, L.in_norm, c.eps, m->qkv, 0, m->gate, s);
         if (lr < 0 || (lr == 1 && qkv_gate(L, m->h, c.eps, m->qkv, m->gate, s)) || mark(m)) return -1;
-        nl += lr == 0 ? 2 : 1;
+        nl += 1;
         AttnArgs a = attn_args(m, li, 1);
         a.store = 1;
         a.cached_before = m->capturing;   // a graph replay: every earlier step has completed
@@ -285,16 +285,16 @@ int enqueue_step(spk_model *m) {
         lr = lut_call(m, L, 2, -1, m->attn, nullptr, 0.f, ro, tp ? 0 : 1, nullptr, s);
         if (lr < 0 || (lr == 1 && vq_call(L.m[2], 1, nullptr, m->attn, nullptr, 0.f, ro, tp ? 0 : 1, s)) || mark(m))
             return -1;
-        nl += lr == 0 ? 2 : 1;
+        nl += 1;
         if (tp && (tp_sum(m->tpv, m->pbuf, m->h, c.hidden, s) || mark(m))) return -1;
         lr = lut_call(m, L, 3, 4, m->h, L.post_norm, c.eps, m->act, 0, nullptr, s);
         if (lr < 0 || (lr == 1 && vq_call(L.m[3], 2, &L.m[4], m->h, L.post_norm, c.eps, m->act, 0, s)) || mark(m))
             return -1;
-        nl += lr == 0 ? 2 : 1;
+        nl += 1;
         lr = lut_call(m, L, 5, -1, m->act, nullptr, 0.f, ro, tp ? 0 : 1, nullptr, s);
         if (lr < 0 || (lr == 1 && vq_call(L.m[5], 1, nullptr, m->act, nullptr, 0.f, ro, tp ? 0 : 1, s)) || mark(m))
             return -1;
-        nl += lr == 0 ? 2 : 1;
+        nl += 1;
         if (tp && (tp_sum(m->tpv, m->pbuf, m->h, c.hidden, s) || mark(m))) return -1;
     }
     const uint8_t *head_rows = (const uint8_t *)m->embed + (size_t)m->row0 * (c.hidden / 32) * 34;
@@ -712,10 +712,10 @@ void spk_model_destroy(spk_model *m) {
     for (auto &L : m->layers) {
         for (void *p : L.lut_mem)
             if (p) cudaFree(p);
-        for (void *p : L.w16_mem)
+        for (void *p : L.tab_mem)
             if (p) cudaFree(p);
     }
-    if (m->lut_part) cudaFree(m->lut_part);
+    if (m->tab_scr) cudaFree(m->tab_scr);
     if (m->tc_scr) cudaFree(m->tc_scr);
     for (void *p : {(void *)m->pf_h, (void *)m->pf_qkv, (void *)m->pf_gate, (void *)m->pf_attn, (void *)m->pf_act,
                     (void *)m->pf_g, (void *)m->pf_tok, (void *)m->pf_pos, m->pf_scr})
@@ -759,9 +759,9 @@ static int relay_layer(spk_model *m, spk_model::Layer &L) {
         return e == cudaSuccess ? 0 : cuda_fail(what, e);
     };
     for (int mi = 0; mi < 6; mi++) {
-        if (release(L.lut_mem[mi], "free vq table words") || release(L.w16_mem[mi], "free vq table words")) return -1;
+        if (release(L.lut_mem[mi], "free vq table words") || release(L.tab_mem[mi], "free vq table words")) return -1;
         L.dec[mi] = false;
-        for (int q = 0; q < 4; q++) L.lut[mi][q] = L.w16[mi][q] = nullptr;
+        for (int q = 0; q < 4; q++) L.lut[mi][q] = L.tab[mi][q] = nullptr;
     }
     const int ng_of[6] = {1, 1, 1, 2, 2, 1};
     size_t part_need = 0, tc_need = 0;
@@ -775,33 +775,33 @@ static int relay_layer(spk_model *m, spk_model::Layer &L) {
             L.lut[mi][q] = (const uint8_t *)L.lut_mem[mi] + per * q;
             if (lut_pack(M.stages[q], LM, (void *)L.lut[mi][q], m->stream)) return -1;
         }
-        L.dec[mi] = mi != 1 && M.rows >= LUT_MIN_ROWS && w16::ok(LM, M.nstages, ng_of[mi]);
+        L.dec[mi] = mi != 1 && M.rows >= LUT_MIN_ROWS && tab::ok(LM, M.nstages, ng_of[mi]);
         for (int q = 0; L.dec[mi] && q < M.nstages; q++)
             if (((uintptr_t)M.stages[q] + LM.cb_off) & 7) L.dec[mi] = false;
         if (L.dec[mi]) {
-            const size_t pw = w16::bytes(LM);
-            if (alloc(&L.w16_mem[mi], pw * M.nstages, "alloc vq table words")) return -1;
+            const size_t pw = tab::bytes(LM);
+            if (alloc(&L.tab_mem[mi], pw * M.nstages, "alloc vq table words")) return -1;
             for (int q = 0; q < M.nstages; q++) {
-                L.w16[mi][q] = (const uint8_t *)L.w16_mem[mi] + pw * q;
-                if (w16::pack(M.stages[q], LM, (void *)L.w16[mi][q], m->stream)) return -1;
+                L.tab[mi][q] = (const uint8_t *)L.tab_mem[mi] + pw * q;
+                if (tab::pack(M.stages[q], LM, (void *)L.tab[mi][q], m->stream)) return -1;
             }
-            part_need = std::max(part_need, w16::part_bytes(LM, ng_of[mi]));
+            part_need = std::max(part_need, tab::scratch_bytes(LM, ng_of[mi]));
         }
         if (M.cols % 32 == 0) tc_need = std::max(tc_need, tc_scratch_bytes(M.rows, M.cols, ATT_MAX_TOK));
     }
     if (!(L.dec[3] && L.dec[4]))   // the pair only together
         for (int mi : {3, 4}) {
-            if (release(L.w16_mem[mi], "free vq table words")) return -1;
+            if (release(L.tab_mem[mi], "free vq table words")) return -1;
             L.dec[mi] = false;
         }
     // the scratches, grown (once) to the largest need of any layer
-    if (part_need > m->lut_part_size) {
-        void *p = m->lut_part;
-        if (release(p, "free vq table partials")) return -1;
-        m->lut_part = nullptr;
-        m->lut_part_size = 0;
-        if (alloc((void **)&m->lut_part, part_need, "alloc vq table partials")) return -1;
-        m->lut_part_size = part_need;
+    if (part_need > m->tab_scr_size) {
+        if (release(m->tab_scr, "free vq table scratch")) return -1;
+        m->tab_scr_size = 0;
+        if (alloc(&m->tab_scr, part_need, "alloc vq table scratch")) return -1;
+        m->tab_scr_size = part_need;
+        cudaError_t e = cudaMemset(m->tab_scr, 0, part_need);   // the grid barrier's count starts at zero
+        if (e != cudaSuccess) return cuda_fail("zero the vq table scratch", e);
     }
     if (tc_need > m->tc_scr_size) {
         if (release(m->tc_scr, "free batched gemm scratch")) return -1;

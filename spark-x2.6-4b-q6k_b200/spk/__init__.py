@@ -57,10 +57,10 @@ _PROTOS = {
     "spk_vq_lut_scratch_bytes": ([_i, _i, _i, _i, _i, _i], C.c_size_t),
     "spk_vq_lut_gemv": ([_vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _f, _vp, _i, _vp, _vp], _i),
     "spk_vq_lut_gemv_t": ([_vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _f, _vp, _i, _vp, _i, _vp], _i),
-    "spk_vq_lut16_bytes": ([_i, _i, _i, _i, _i], C.c_size_t),
-    "spk_vq_lut16_pack": ([_vp, _i, _i, _i, _i, _i, _vp, _vp], _i),
-    "spk_vq_lut16_scratch_bytes": ([_i, _i, _i, _i, _i, _i], C.c_size_t),
-    "spk_vq_lut16_gemv": ([_vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _f, _vp, _i, _vp, _vp], _i),
+    "spk_vq_tab_bytes": ([_i, _i, _i, _i, _i], C.c_size_t),
+    "spk_vq_tab_pack": ([_vp, _i, _i, _i, _i, _i, _vp, _vp], _i),
+    "spk_vq_tab_scratch_bytes": ([_i, _i, _i, _i, _i, _i], C.c_size_t),
+    "spk_vq_tab_gemv": ([_vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _f, _vp, _i, _vp, _vp], _i),
     "spk_vq_lut_gemm_scratch_bytes": ([_i, _i, _i], C.c_size_t),
     "spk_vq_lut_gemm": ([_vp, _i, _i, _i, _i, _i, _i, _i, _vp, _i, _vp, _f, _vp, _i, _i, _vp, _vp], _i),
     "spk_vq_gemv_fast_ok": ([_i] * 7, _i),
