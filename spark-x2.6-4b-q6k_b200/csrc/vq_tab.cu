@@ -66,7 +66,8 @@ constexpr size_t SM_T = 0, SM_CB = SM_T + T_BYTES, SM_ACC = SM_CB + CB_BYTES;
 constexpr size_t SM_X = SM_ACC + (size_t)MAXS * NT * 4;
 constexpr size_t SM_RED = SM_X + (size_t)MAXSEG * GC * 4 * 8, SM_FRED = SM_RED + NW * 8;
 constexpr size_t SM_BND = SM_FRED + MAXST * NW * 4;
-constexpr size_t SM_END = SM_BND + (MAXCTA + 1) * 4;
+constexpr size_t SM_Y = SM_BND + (MAXCTA + 1) * 4;   // the finishing rows' residual (accumulate)
+constexpr size_t SM_END = SM_Y + 128 * 4;
 
 struct TabArgs {
     const uint4 *w[MAXG][MAXST];        // re-laid words [nsl][rows]
@@ -330,6 +331,8 @@ __global__ void __launch_bounds__(NT, 1) vq_tab_kernel(const TabArgs a) {
     bool have_x = false;
     float inv = 1.0f;
     unsigned long long seen = 0;   // the barrier count after the wait (thread 0)
+    const int r0 = R * k / G, r1 = R * (k + 1) / G, nr = r1 - r0;   // this CTA's finishing rows
+    float *ys = reinterpret_cast<float *>(smem + SM_Y);
 
     int seg = 0;
     for (int u = u0; u < u1; seg++) {
@@ -362,6 +365,7 @@ __global__ void __launch_bounds__(NT, 1) vq_tab_kernel(const TabArgs a) {
             if (!have_x) {   // weights only so far: the activations after the wait
                 pdl_wait();
                 if (tid == 0) seen = ld_relaxed(a.bar);
+                if (a.mode == 1 && tid < nr) ys[tid] = a.y[r0 + tid];   // the residual they add to, early
                 // this thread's slice activation (segment tid / 32), loaded with the norm's
                 const int v0 = u0 / nch, nseg = min((u1 - 1) / nch - v0 + 1, MAXSEG);
                 const bool mine = tid < nseg * 32;
@@ -415,6 +419,7 @@ __global__ void __launch_bounds__(NT, 1) vq_tab_kernel(const TabArgs a) {
     if (!have_x) {   // a CTA with no units still meets the barrier (and may take a g_proj row)
         pdl_wait();
         if (tid == 0) seen = ld_relaxed(a.bar);
+        if (a.mode == 1 && tid < nr) ys[tid] = a.y[r0 + tid];
         if (a.norm_w) inv = rms_inv(a.x, a.cols, a.eps, red);
     }
     if (u0 < u1) {
@@ -428,24 +433,26 @@ __global__ void __launch_bounds__(NT, 1) vq_tab_kernel(const TabArgs a) {
     // ---- the finishing share: rows [r0, r1), summed over the CTAs that wrote them. A CTA that
     // holds unit (g, sl, c) for any slice sl wrote a partial for every row of chunk c of group
     // g; the rows' sums run over those CTAs in CTA order.
-    const int r0 = R * k / G, r1 = R * (k + 1) / G, nr = r1 - r0;
     if (nr > 0) {
         const int c0 = r0 >> 5, nck = ((r1 - 1) >> 5) - c0 + 1, ntask = a.ng * nck;   // task: (group, chunk)
-        int *lst = reinterpret_cast<int *>(smem);        // [ntask][G] covering CTAs, in order
-        int *len = lst + ntask * G;                      // [ntask]
-        float *Q = reinterpret_cast<float *>(len + ntask);   // [ntask][P][32] partial sums
+        uint8_t *flag = smem;                                              // [ntask][G]
+        int *lst = reinterpret_cast<int *>(smem + MAXG * MAXCH * MAXCTA);  // [ntask][G] covering CTAs, in order
+        int *len = lst + MAXG * MAXCH * MAXCTA;                            // [ntask]
+        float *Q = reinterpret_cast<float *>(len + MAXG * MAXCH);          // [parts][32]
+        for (int e = tid; e < ntask * G; e += NT) {
+            const int task = e / G, kk = e - task * G;
+            const int base = (task / nck) * per_g + c0 + task % nck;   // unit (g, sl = 0, c)
+            const int v0 = bs[kk], v1 = bs[kk + 1], lo = max(v0, base);
+            const int sl0 = (lo - base + nch - 1) / nch;   // the first unit of chunk c at or after the range start
+            flag[e] = sl0 < nsl && base + sl0 * nch < v1;
+        }
+        __syncthreads();
         const uint32_t lt = (1u << lane) - 1u;
         for (int task = warp; task < ntask; task += NW) {
-            const int g = task / nck, base = g * per_g + c0 + task % nck;
             int n = 0;
             for (int k0 = 0; k0 < G; k0 += 32) {
                 const int kk = k0 + lane;
-                bool f = false;
-                if (kk < G) {   // the first unit of chunk c at or after the range start, inside the range?
-                    const int v0 = bs[kk], v1 = bs[kk + 1];
-                    const int sl0 = v0 > base ? (v0 - base + nch - 1) / nch : 0;
-                    f = sl0 < nsl && base + sl0 * nch < v1;
-                }
+                const bool f = kk < G && flag[task * G + kk];
                 const uint32_t m = __ballot_sync(0xffffffffu, f);
                 if (f) lst[task * G + n + __popc(m & lt)] = kk;
                 n += __popc(m);
@@ -453,12 +460,12 @@ __global__ void __launch_bounds__(NT, 1) vq_tab_kernel(const TabArgs a) {
             if (lane == 0) len[task] = n;
         }
         __syncthreads();
-        // P warps per task split its list; each sums its share in list order, all loads in flight
+        // P warps per task split its list; each sums its share in list order, 16 loads in flight
         const int P = max(1, NW / ntask);
         for (int w2 = warp; w2 < ntask * P; w2 += NW) {
-            const int task = w2 / P, p = w2 % P, g = task / nck;
+            const int task = w2 / P, pp = w2 % P, g = task / nck;
             const int row = 32 * (c0 + task % nck) + lane, n = len[task];
-            const int i0 = n * p / P, i1 = n * (p + 1) / P;
+            const int i0 = n * pp / P, i1 = n * (pp + 1) / P;
             float t = 0.f;
             if (row >= r0 && row < r1) {
                 const float *src = a.part + (size_t)g * G * R + row;
@@ -473,7 +480,7 @@ __global__ void __launch_bounds__(NT, 1) vq_tab_kernel(const TabArgs a) {
                 }
                 for (; i < i1; i++) t += __ldcg(src + (size_t)l[i] * R);
             }
-            Q[(task * P + p) * 32 + lane] = t;
+            Q[(task * P + pp) * 32 + lane] = t;
         }
         __syncthreads();
         for (int ri = tid; ri < nr; ri += NT) {
@@ -483,13 +490,13 @@ __global__ void __launch_bounds__(NT, 1) vq_tab_kernel(const TabArgs a) {
             for (int g = 0; g < MAXG; g++) {
                 float t = 0.f;
                 if (g < a.ng)
-                    for (int p = 0; p < P; p++) t += Q[((g * nck + cc) * P + p) * 32 + (r & 31)];
+                    for (int pp = 0; pp < P; pp++) t += Q[((g * nck + cc) * P + pp) * 32 + (r & 31)];
                 sg[g] = t;
             }
             if (a.mode == 2)
                 a.y[r] = __fmul_rn(gelu_erf(sg[0]), sg[1]);
             else if (a.mode == 1)
-                a.y[r] = __fadd_rn(a.y[r], sg[0]);
+                a.y[r] = __fadd_rn(ys[ri], sg[0]);
             else
                 a.y[r] = sg[0];
         }
@@ -682,8 +689,9 @@ bool ok(const Layout &L, int ns, int ng) {
     const long long nr = (L.rows + G - 1) / G;
     if ((nr + 31) / 32 + 1 > MAXCH) return false;
     // the finishing stage: partials [ng][G][nrp] and covering flags [ng][G][chunks] in the table's space
-    const size_t ntask = (size_t)ng * MAXCH;
-    if ((ntask * G + ntask) * 4 + ntask * NW * 32 * 4 > SM_X) return false;
+    if ((size_t)MAXG * MAXCH * MAXCTA * 5 + MAXG * MAXCH * 4 + (size_t)MAXG * MAXCH * ((G + 31) / 32) * 32 * 4 > SM_X)
+        return false;
+    if (nr > 128) return false;   // the residual rows held for the epilogue
     return SM_END <= smem_optin_max();
 }
 
