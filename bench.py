@@ -535,10 +535,12 @@ def _gemv_line(args, workload: str, value: float, alg: int, t_launch: float, ker
 def run_vq_gemv(args) -> None:
     """Config 0: one VQ decode-GEMV, W 10240x2560 as DQV3 4x4096x2 (seeded codebooks and
     indices), x ~ N(0,1) seed 1, y fp32 [10240]. A step is the whole GEMV (both stages, one
-    launch). Eight copies of the container (158 MB > L2) rotate, so every step reads HBM.
-    `--workload vq-pair` runs the decode step's dominant kernel instead: the FFN gate and up
-    matrices (two such containers) in one launch with the RMSNorm prologue and the
-    gelu(gate)*up epilogue."""
+    launch) through the bank-scheduled table kernel (spk_vq_tab_gemv, the decode step's kernel
+    for matrices of 8192 rows and more; its index words re-laid once at load by
+    spk_vq_tab_pack, outside the timed region). Eight copies of the container (158 MB > L2)
+    rotate, so every step reads HBM. `--workload vq-pair` runs the decode step's dominant
+    launch instead: the FFN gate and up matrices (two such containers) in one launch with the
+    RMSNorm prologue and the gelu(gate)*up epilogue."""
     import ctypes as C
 
     import torch
@@ -554,10 +556,16 @@ def run_vq_gemv(args) -> None:
     L = spk.lib()
     bufs = [F.random_rvq_fast(rows, cols, 4, 4096, 2, seed=g) for g in range(ng)]
     c = F.parse_container(bufs[0])
+    nw_bytes = L.spk_vq_tab_bytes(4, 4096, rows, cols, 1)
     copies = []
     for _ in range(ncopy):
         ts = [spk.dev_bytes(b[c.stage_offset(s):c.stage_offset(s) + c.stage_bytes], dev) for b in bufs for s in range(2)]
-        copies.append(((C.c_void_p * len(ts))(*[t.data_ptr() for t in ts]), ts))
+        ws = [torch.empty(nw_bytes, dtype=torch.uint8, device=dev) for _ in ts]
+        for t, w in zip(ts, ws):
+            spk.check(L.spk_vq_tab_pack(t.data_ptr(), 4, 4096, rows, cols, 1, w.data_ptr(), None))
+        copies.append(((C.c_void_p * len(ts))(*[t.data_ptr() for t in ts]), ts,
+                       (C.c_void_p * len(ws))(*[w.data_ptr() for w in ws]), ws))
+    scr = torch.zeros(L.spk_vq_tab_scratch_bytes(ng, 4, 4096, rows, cols, 1), dtype=torch.uint8, device=dev)
     rng = np.random.default_rng(1)
     x_host = rng.normal(0, 1, cols).astype(np.float32)
     x = torch.from_numpy(x_host).to(dev)
@@ -569,8 +577,9 @@ def run_vq_gemv(args) -> None:
     alg = sum(len(b) for b in bufs) + cols * 4 + rows * 4 + (cols * 4 if pair else 0)
 
     def step(k, stream):
-        spk.check(L.spk_vq_gemv(copies[k % ncopy][0], 2, ng, 4, 4096, rows, cols, 1, x.data_ptr(),
-                                nw.data_ptr() if pair else None, 1e-6, y.data_ptr(), 0, stream))
+        cp = copies[k % ncopy]
+        spk.check(L.spk_vq_tab_gemv(cp[0], cp[2], 2, ng, 4, 4096, rows, cols, 1, x.data_ptr(),
+                                    nw.data_ptr() if pair else None, 1e-6, y.data_ptr(), 0, scr.data_ptr(), stream))
 
     for k in range(args.warmup):
         step(k, sp)
@@ -622,10 +631,10 @@ def run_vq_gemv(args) -> None:
                         f"{reps} reps, {tc * 1e3:.1f} ms each"}
     if pair:
         workload = "decode-step FFN gate+up: two VQ 10240x2560 DQV3 4x4096x2 matrices, RMSNorm in, gelu(g)*u out"
-        kernel, prof = "vq_fast_kernel<2,2,20,0> gate+up 10240x2560 x2 stages", "vq_gate_up_gemv_10240x2560x2"
+        kernel, prof = "vq_tab_kernel gate+up 10240x2560 x2 stages", "vq_tab_gate_up_10240x2560x2"
     else:
         workload = "config0: VQ decode-GEMV 10240x2560, DQV3 dim 4, K 4096, 2 stages, batch 1"
-        kernel, prof = "vq_fast_kernel<2,1,20,0> 10240x2560 x2 stages", "vq_gemv_10240x2560x2"
+        kernel, prof = "vq_tab_kernel 10240x2560 x2 stages", "vq_tab_10240x2560x2"
     line = _gemv_line(args, workload, alg / t / 1e9, alg, t, kernel, traffic_from_profiles(prof),
                       {"rows": rows, "cols": cols, "container_bytes": [len(b) for b in bufs],
                        "l2": f"{ncopy} rotating copies, {ncopy * alg / 1e6:.0f} MB > L2"},
