@@ -10,6 +10,8 @@
 // each (token, KV head) to finish — an atomic ticket — merges all splits in a
 // fixed order and applies the per-head sigmoid gate (model.rs:538-550). The
 // ticket is reset by that CTA, so a captured graph replays without a memset.
+#include <cooperative_groups.h>
+
 #include "attn.cuh"
 #include "spk.h"
 
@@ -425,7 +427,11 @@ __device__ __forceinline__ uint32_t f16_pair(float x, float y, bool lo) {
     return (uint32_t)__half_as_ushort(ox) | ((uint32_t)__half_as_ushort(oy) << 16);
 }
 
-template <int KT>
+// CL: the splits of a (token, KV head) run as one thread-block cluster (grid.y = nsplit <= 8 =
+// the cluster's size): each CTA leaves its (o, m, l) in its own shared memory and, after a
+// cluster barrier, merges its slice of the output dims from every split's shared memory
+// (distributed shared memory), so the merge costs no global round trip and no ticket.
+template <int KT, bool CL>
 __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const AttnArgs a) {
     constexpr int HD = 256, MG = ATT_MAX_GROUP, PR = HD + 4, NW = TC_TILES + 1;
     constexpr size_t RB = kv_row_bytes(KT, HD);
@@ -437,9 +443,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const AttnArgs a
     __shared__ float wm[NW][MG], wl[NW][MG];
     __shared__ float wo[NW][MG][HD];
     __shared__ float pt[TC_WARPS][16][MG];   // each warp's P, transposed for the B operand
-    __shared__ float cw[MG][ATT_MAX_SPLIT];
+    __shared__ float cw[MG][CL ? 1 : ATT_MAX_SPLIT];
     __shared__ float cl[MG];
     __shared__ int is_last;
+    __shared__ float cpm[CL ? MG : 1][CL ? PR : 1];   // CL: this split's o, m, l
+    __shared__ float gs[MG];                          // CL: the heads' sigmoid gates
     pdl_trigger();
     // The model's decode step (one token storing its own row, cached_before set) reads only
     // cache rows written by earlier graph launches, which run one after another, plus its own
@@ -493,6 +501,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const AttnArgs a
         kn[i] = qrow[qd + (size_t)kvh * HD + i];
         vn[i] = qrow[qd + kvd + (size_t)kvh * HD + i];
     }
+    if (CL && threadIdx.x < G)   // the heads' gates (model.rs:538-550), loaded with q
+        gs[threadIdx.x] = 1.0f / (1.0f + expf(-a.gate[(size_t)tok * a.ldgate + kvh * G + threadIdx.x]));
     __syncthreads();
     for (int h = 0; h < G; h++) rope_smem(qs[h], a.freq, a.pdim, pos);
     rope_smem(kn, a.freq, a.pdim, pos);
@@ -711,13 +721,36 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const AttnArgs a
             L += wl[w][h] * e;
             O += wo[w][h][d] * e;
         }
-        out[h * PR + d] = O;
+        float *dst = CL ? &cpm[h][0] : out + h * PR;
+        dst[d] = O;
         if (d == 0) {
-            out[h * PR + HD] = M;
-            out[h * PR + HD + 1] = L;
+            dst[HD] = M;
+            dst[HD + 1] = L;
         }
     }
-    finish_splits<HD>(a, kvh, tok, G, pbase, pstride, cw, cl, &is_last);
+    if constexpr (CL) {
+        namespace cg = cooperative_groups;
+        cg::cluster_group cluster = cg::this_cluster();
+        cluster.sync();   // every split's (o, m, l) is in its CTA's shared memory
+        const int ns = a.nsplit, r = (int)cluster.block_rank(), dpc = HD / ns;
+        for (int i = threadIdx.x; i < G * dpc; i += blockDim.x) {   // this CTA's dims, every head
+            const int h = i / dpc, d = r * dpc + i % dpc;
+            float M = -INFINITY;
+            for (int c = 0; c < ns; c++) M = fmaxf(M, cluster.map_shared_rank(&cpm[h][HD], c)[0]);
+            float L = 0.f, O = 0.f;
+            for (int c = 0; c < ns; c++) {   // the same order as the ticket merge: split 0 first
+                const float *pc = cluster.map_shared_rank(&cpm[h][0], c);
+                const float mc = pc[HD];
+                const float e = mc == -INFINITY ? 0.f : expf(mc - M);
+                L += pc[HD + 1] * e;
+                O = fmaf(pc[d], e, O);
+            }
+            a.out[(size_t)tok * a.ldout + (size_t)(kvh * G + h) * HD + d] = (O / L) * gs[h];
+        }
+        cluster.sync();   // no CTA leaves while another still reads its shared memory
+    } else {
+        finish_splits<HD>(a, kvh, tok, G, pbase, pstride, cw, cl, &is_last);
+    }
 }
 
 }  // namespace
@@ -734,18 +767,40 @@ int attn_decode(const AttnArgs &a, cudaStream_t s) {
     if (a.hd != 256 && a.hd != 128) return set_error("attention: head_dim %d (128 or 256)", a.hd);
     if (a.kv_type < KV_F32 || a.kv_type > KV_Q8) return set_error("attention: cache type %d", a.kv_type);
     if (a.hd == 256 && (a.kv_type == KV_F16 || a.kv_type == KV_Q8)) {   // the tensor-core kernel
-        static int opted[2][64];
+        static int opted[4][64];
         int dev = 0;
         cudaGetDevice(&dev);
         const int q8 = a.kv_type == KV_Q8;
-        auto k = q8 ? attn_tc_kernel<KV_Q8> : attn_tc_kernel<KV_F16>;
+        // up to 8 splits: one cluster per (token, KV head), the merge in distributed shared memory
+        const bool cl = a.nsplit <= 8 && (a.hd % a.nsplit) == 0;
+        auto k = q8 ? (cl ? attn_tc_kernel<KV_Q8, true> : attn_tc_kernel<KV_Q8, false>)
+                    : (cl ? attn_tc_kernel<KV_F16, true> : attn_tc_kernel<KV_F16, false>);
         const size_t sm = q8 ? TcLayout<KV_Q8>::SMEM : TcLayout<KV_F16>::SMEM;
-        if (!opted[q8][dev & 63]) {
+        if (!opted[q8 * 2 + cl][dev & 63]) {
             cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
             if (e != cudaSuccess) return cuda_fail("attention shared-memory opt-in", e);
-            opted[q8][dev & 63] = 1;
+            opted[q8 * 2 + cl][dev & 63] = 1;
         }
-        const cudaError_t e = launch_pdl(k, grid, dim3(TC_THREADS), sm, s, a);
+        cudaError_t e;
+        if (cl) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = grid;
+            cfg.blockDim = dim3(TC_THREADS);
+            cfg.dynamicSmemBytes = sm;
+            cfg.stream = s;
+            cudaLaunchAttribute at[2];
+            at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            at[0].val.programmaticStreamSerializationAllowed = 1;
+            at[1].id = cudaLaunchAttributeClusterDimension;
+            at[1].val.clusterDim.x = 1;
+            at[1].val.clusterDim.y = a.nsplit;
+            at[1].val.clusterDim.z = 1;
+            cfg.attrs = at;
+            cfg.numAttrs = 2;
+            e = cudaLaunchKernelEx(&cfg, k, a);
+        } else {
+            e = launch_pdl(k, grid, dim3(TC_THREADS), sm, s, a);
+        }
         return e == cudaSuccess ? 0 : cuda_fail("attention launch", e);
     }
     const int sel = (a.hd == 256 ? 0 : 6) + a.kv_type * 2 + (longs ? 1 : 0);
