@@ -202,6 +202,107 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_reference_gemv(args) -> None:
+    """--impl reference for configs 0 (`vq`) and the gate+up pair (`vq-pair`): the reference's CPU
+    implementation of the GEMV (Stage::dot_row per stage, restated in C in oracle/, "port"), all
+    host threads, K timed whole GEMVs over the same seeded matrices and x as our arm. When the
+    reference's own GPU kernel file was built here for sm_100a (oracle/_ref/libvqg_ref.so, from
+    tools/vq/gpu/decode-gpu.cu by `make -C oracle ref`), its GEMV is timed too, the way the
+    reference's runtime runs it (vq-model-gpu.cu:651-660: y zeroed, then one vqg_gemv_launch per
+    stage, the DQV3 block kernel chosen by variant 0), over 8 rotating copies with CUDA events,
+    and reported as `reference_gpu` beside the CPU line."""
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    import ctypes as C
+
+    import oracle
+    from spk import formats as F
+
+    pair = args.workload == "vq-pair"
+    ng = 2 if pair else 1
+    rows, cols, ncopy = 10240, 2560, 8
+    bufs = [F.random_rvq_fast(rows, cols, 4, 4096, 2, seed=g) for g in range(ng)]
+    rng = np.random.default_rng(1)
+    x = rng.normal(0, 1, cols).astype(np.float32)
+    alg = sum(len(b) for b in bufs) + cols * 4 + rows * 4 + (cols * 4 if pair else 0)
+    threads = os.cpu_count() or 1
+    for _ in range(args.warmup):
+        for b in bufs:
+            oracle.gemv_fused(b, x, threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        for b in bufs:
+            oracle.gemv_fused(b, x, threads)
+    dt = (time.perf_counter() - t0) / args.steps
+    v = alg / dt / 1e9
+    sample = (f"Stage::dot_row GEMV restated in C (oracle/), {ng} matrix(es) 10240x2560 DQV3 4x4096x2, {threads} "
+              f"threads, {args.steps} timed GEMVs after {args.warmup} untimed")
+    ref_gpu = None
+    so = os.path.join(ROOT, "oracle", "_ref", "libvqg_ref.so")
+    try:
+        import torch
+
+        if os.path.exists(so) and torch.cuda.is_available():
+            R = C.CDLL(so)
+            R.vqg_gemv_launch.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p,
+                                          C.c_void_p, C.c_int]
+            R.vqg_gemv_launch.restype = C.c_int
+            dev = torch.device("cuda", 0)
+            c = F.parse_container(bufs[0])
+            copies = []
+            for _ in range(ncopy):   # every stage its own buffer with the 8 zeroed slack bytes
+                ts = []
+                for b in bufs:
+                    for q in range(2):
+                        t = torch.zeros(c.stage_bytes + 8, dtype=torch.uint8, device=dev)
+                        t[:c.stage_bytes].copy_(torch.frombuffer(bytearray(b[c.stage_offset(q):c.stage_offset(q) +
+                                                                             c.stage_bytes]), dtype=torch.uint8))
+                        ts.append(t)
+                copies.append(ts)
+            xd = torch.from_numpy(x).to(dev)
+            ys = [torch.zeros(rows, device=dev) for _ in range(ng)]
+
+            def step(k):
+                ts = copies[k % ncopy]
+                for gi in range(ng):
+                    ys[gi].zero_()
+                    for q in range(2):
+                        if R.vqg_gemv_launch(ts[2 * gi + q].data_ptr(), 4, 4096, rows, cols, 1, xd.data_ptr(),
+                                             ys[gi].data_ptr(), 0) != 0:
+                            raise RuntimeError("reference vqg_gemv_launch failed")
+
+            for k in range(max(args.warmup, ncopy)):
+                step(k)
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for k in range(args.steps):
+                step(k)
+            e1.record()
+            e1.synchronize()
+            tg = e0.elapsed_time(e1) / 1e3 / args.steps
+            want = oracle.gemv_fused(bufs[0], x, threads)
+            got = ys[0].cpu().numpy()   # every copy holds the same matrices
+            ref_gpu = {"value": alg / tg / 1e9, "unit": "GB/s", "us_per_step": tg * 1e6,
+                       "kernel": "the reference's gemv_v3blk_kernel (tools/vq/gpu/decode-gpu.cu:267-301) built for "
+                                 "sm_100a, one launch per stage (+ a y memset per matrix), as vq-model-gpu.cu runs it",
+                       "check_relL2_vs_oracle": float(np.linalg.norm(got - want) / np.linalg.norm(want))}
+    except Exception as e:   # the comparison point is optional; the CPU line stands on its own
+        ref_gpu = {"unavailable": f"{type(e).__name__}: {e}"}
+    cb = {"value": v, "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample}
+    line = {"metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded weights in the reference's formats, x ~ N(0,1))",
+            "impl": "reference",
+            "config": {"workload": ("decode-step FFN gate+up: two VQ 10240x2560 DQV3 4x4096x2 matrices" if pair else
+                                    "config0: VQ decode-GEMV 10240x2560, DQV3 dim 4, K 4096, 2 stages, batch 1"),
+                       "rows": rows, "cols": cols},
+            "cpu_baseline": cb, "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "reference_gpu": ref_gpu}
+    print(json.dumps(line), flush=True)
+
+
 def run_ours(args) -> None:
     import ctypes as C
 
@@ -281,9 +382,9 @@ def run_ours(args) -> None:
     rows_l = m.mats[0]["gate"].rows
     act = torch.zeros(rows_l, device=dev)
     launches = []
-    # the model runs the pair through the bank-scheduled table kernel (vq_tab.cu) at >= 8192 rows,
+    # the model runs the pair through the bank-scheduled table kernel (vq_tab.cu) at >= 4096 rows,
     # when it takes the geometry: time that one, on index words re-laid here the way the model does
-    tab_n = L.spk_vq_tab_bytes(4, 4096, rows_l, cfg.hidden, 1) if rows_l >= 8192 else 0
+    tab_n = L.spk_vq_tab_bytes(4, 4096, rows_l, cfg.hidden, 1) if rows_l >= 4096 else 0
     tabs = []
     for li in range(cfg.layers):
         g, u = m.mats[li]["gate"], m.mats[li]["up"]
@@ -649,7 +750,7 @@ GGML_SHAPES = [("q6k", "q", 4096, 2560), ("q6k", "k", 1024, 2560), ("q6k", "v", 
 
 def run_ggml(args) -> None:
     """Config 1: the Q6_K dequant-GEMV over every trunk shape and the Q8_0 GEMV over the
-    131072x2560 tied head, batch 1, W ~ N(0, 0.02^2) quantized with the block rules (Q6_K by
+    131072x2560 tied head (the tensor-core head the decode step runs, with its argmax), batch 1, W ~ N(0, 0.02^2) quantized with the block rules (Q6_K by
     the package's encoder, Q8_0 by ggml's d = max|w|/127 statistics), x ~ N(0,1). A step is
     one pass over the eight matrices; value = their bytes over the sum of their per-launch times."""
     import ctypes as C
@@ -673,17 +774,30 @@ def run_ggml(args) -> None:
         mats.append({"fmt": fmt, "name": name, "rows": rows, "cols": cols, "blob": blob,
                      "w": spk.dev_bytes(blob, dev), "x_host": x_host, "x": torch.from_numpy(x_host).to(dev),
                      "y": torch.zeros(rows, device=dev), "alg": len(blob) + 4 * cols + 4 * rows})
-    # each matrix rotates over copies totalling > 2x L2, so back-to-back launches read HBM
+    # each matrix rotates over copies totalling > 2x L2, so back-to-back launches read HBM. The Q8_0
+    # head runs as the decode step runs it: its blocks re-laid once (outside the timed region) into
+    # the tensor-core tile layout (spk_q80_tile), then spk_q80_tile_head over those tiles.
     for m in mats:
-        m["copies"] = [m["w"]] + [m["w"].clone() for _ in range(-(-256_000_000 // len(m["blob"])) - 1)]
+        if m["fmt"] == "q80":
+            t = torch.zeros(L.spk_q80_tile_bytes(m["rows"], m["cols"]), dtype=torch.uint8, device=dev)
+            spk.check(L.spk_q80_tile(m["w"].data_ptr(), m["rows"], m["cols"], t.data_ptr(), None))
+            m["w"] = t
+            m["scratch"] = torch.zeros(L.spk_q80_tile_scratch_bytes(), dtype=torch.uint8, device=dev)
+            m["amax"] = torch.zeros(1, dtype=torch.int32, device=dev)
+        m["copies"] = [m["w"]] + [m["w"].clone() for _ in range(-(-256_000_000 // m["w"].numel()) - 1)]
     torch.cuda.synchronize(dev)
     s = torch.cuda.Stream(dev)
     sp = C.c_void_p(s.cuda_stream)
 
     def launch(m, k=0, stream=sp):
-        fn = L.spk_q6k_gemv if m["fmt"] == "q6k" else L.spk_q80_gemv
         w = m["copies"][k % len(m["copies"])]
-        spk.check(fn(w.data_ptr(), m["rows"], m["cols"], m["x"].data_ptr(), None, 0.0, m["y"].data_ptr(), 0, stream))
+        if m["fmt"] == "q6k":
+            spk.check(L.spk_q6k_gemv(w.data_ptr(), m["rows"], m["cols"], m["x"].data_ptr(), None, 0.0,
+                                     m["y"].data_ptr(), 0, stream))
+        else:
+            spk.check(L.spk_q80_tile_head(w.data_ptr(), m["rows"], m["cols"], 1, m["x"].data_ptr(), m["cols"], None,
+                                          0.0, m["y"].data_ptr(), m["rows"], m["amax"].data_ptr(),
+                                          m["scratch"].data_ptr(), stream))
 
     for k in range(args.warmup):
         for m in mats:
@@ -742,8 +856,8 @@ def run_ggml(args) -> None:
               for i, m in enumerate(mats)}
     head = len(mats) - 1
     line = _gemv_line(args, "config1: Q6_K trunk shapes + Q8_0 131072x2560 head, batch 1", alg / t / 1e9,
-                      mats[head]["alg"], per[head], "blk_fast_kernel Q8_0 131072x2560",
-                      traffic_from_profiles("ggml_gemv_trunk_and_head"),
+                      mats[head]["alg"], per[head], "q8t_head_kernel Q8_0 131072x2560 (tensor-core tile layout, fused argmax)",
+                      traffic_from_profiles("q8t_head_131072x2560"),
                       {"matrices": detail, "l2": "each matrix rotates over copies totalling > 256 MB"},
                       e2e, sum(4 * m["cols"] for m in mats), sum(4 * m["rows"] for m in mats), cb, clk,
                       args.steps * len(mats))
@@ -782,7 +896,9 @@ def main():
         args.ctx = 8192
     if args.warmup < 3:
         ap.error("at least 3 warm-up steps")
-    if args.impl == "reference":
+    if args.impl == "reference" and args.workload in ("vq", "vq-pair"):
+        run_reference_gemv(args)
+    elif args.impl == "reference":
         run_reference(args)
     elif args.workload in ("vq", "vq-pair"):
         run_vq_gemv(args)

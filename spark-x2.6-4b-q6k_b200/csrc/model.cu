@@ -745,11 +745,13 @@ void spk_model_destroy(spk_model *m) {
 
 // Every layer matrix the table layout takes (DQV3 dim 4, 4096 codes, 12-bit) is re-laid once
 // here (vq_lut.cu's words: code words, gains, slice-major index records): the batched GEMM of
-// the verify batch runs on those words (vq_tc.cu). The decode step runs a matrix through the
-// table kernel when it has at least LUT_MIN_ROWS rows (a slice's table costs 4096 x 8 entries,
-// so it pays back only over many rows), the gate/up pair only together; the others through
-// the code-word kernel (vq.cu) over the payloads, which stay (g_proj reads them too).
-constexpr int LUT_MIN_ROWS = 8192;
+// the verify batch runs on those words (vq_tc.cu). The decode step runs the gate/up pair through
+// the bank-scheduled table kernel (vq_tab.cu) when its shard has at least PAIR_TAB_MIN_ROWS rows
+// (measured on B200: 35 vs 43 us at 5120 rows, even at 2560, slower below: a table of 4096 x 8
+// entries pays back only over many rows, and the kernel has a fixed cost of its own); every
+// other matrix through the code-word kernel (vq.cu) over the payloads, which stay (g_proj reads
+// them too), and which measured faster for q_k_v_proj, out_proj and down_proj at every shard.
+constexpr int PAIR_TAB_MIN_ROWS = 4096;
 
 static int relay_layer(spk_model *m, spk_model::Layer &L) {
     auto release = [](void *&p, const char *what) -> int {
@@ -775,7 +777,7 @@ static int relay_layer(spk_model *m, spk_model::Layer &L) {
             L.lut[mi][q] = (const uint8_t *)L.lut_mem[mi] + per * q;
             if (lut_pack(M.stages[q], LM, (void *)L.lut[mi][q], m->stream)) return -1;
         }
-        L.dec[mi] = mi != 1 && M.rows >= LUT_MIN_ROWS && tab::ok(LM, M.nstages, ng_of[mi]);
+        L.dec[mi] = (mi == 3 || mi == 4) && M.rows >= PAIR_TAB_MIN_ROWS && tab::ok(LM, M.nstages, ng_of[mi]);
         for (int q = 0; L.dec[mi] && q < M.nstages; q++)
             if (((uintptr_t)M.stages[q] + LM.cb_off) & 7) L.dec[mi] = false;
         if (L.dec[mi]) {
