@@ -153,6 +153,7 @@ struct spk_model {
     // spk_model_trace: a second capture of the step with a timing event after every launch
     std::vector<cudaEvent_t> tev;
     int tracing = 0, nmark = 0;
+    int nmark_all = 0, step_marks = 0;   // marks an enqueued step makes (counted traced or not)
     int capturing = 0;            // enqueue_step is being captured into a step graph
     cudaGraph_t tgraph = nullptr;
     cudaGraphExec_t texec = nullptr;
@@ -254,10 +255,39 @@ int capture_rows(spk_model *m, int li, int ntok, cudaStream_t s, const float *h 
 
 // Under spk_model_trace's capture: an event after the launch just enqueued.
 int mark(spk_model *m) {
+    m->nmark_all++;
     if (!m->tracing) return 0;
     if (m->nmark >= (int)m->tev.size()) return set_error("trace: more launches than events");
     cudaError_t e = cudaEventRecordWithFlags(m->tev[m->nmark++], m->stream, cudaEventRecordExternal);
     return e == cudaSuccess ? 0 : cuda_fail("trace event", e);
+}
+
+// out_proj / down_proj (matrix mi) into the residual: at N = 1 accumulated into h; under
+// tensor parallelism the code-word kernel with the residual exchange fused in (one launch,
+// vq_gemv_tp), else this rank's partial into pbuf and tp_sum. *nl counts the launches.
+int residual_gemv(spk_model *m, const spk_model::Layer &L, int mi, const float *x, cudaStream_t s, int *nl) {
+    const spk_model_config &c = m->cfg;
+    const bool tp = m->tp_world > 1;
+    if (tp) {
+        const spk_vq_matrix &M = L.m[mi];
+        const Layout LM = make_layout(M.dim, M.nc, M.rows, M.cols, M.v3);
+        const int rc = vq_gemv_tp(M.stages, M.nstages, LM, x, m->h, m->tpv, s);
+        if (rc < 0) return -1;
+        if (rc == 0) {
+            *nl += 1;
+            return mark(m);
+        }
+    }
+    float *const ro = tp ? m->pbuf : m->h;   // rank partial, or the residual
+    const int lr = lut_call(m, L, mi, -1, x, nullptr, 0.f, ro, tp ? 0 : 1, nullptr, s);
+    if (lr < 0 || (lr == 1 && vq_call(L.m[mi], 1, nullptr, x, nullptr, 0.f, ro, tp ? 0 : 1, s)) || mark(m))
+        return -1;
+    *nl += 1;
+    if (tp) {
+        if (tp_sum(m->tpv, m->pbuf, m->h, c.hidden, s) || mark(m)) return -1;
+        *nl += 1;
+    }
+    return 0;
 }
 
 // Enqueue one decode step on m->stream: reads pos/token from m->state.
@@ -266,14 +296,16 @@ int enqueue_step(spk_model *m) {
     cudaStream_t s = m->stream;
     int *pos = m->state, *token = m->state + 1, *amax = m->state + 2, *amax_l = m->state + 4;
     const bool tp = m->tp_world > 1;
+    m->nmark_all = 0;
     if (mark(m) || spk_q80_row(m->embed, c.vocab, c.hidden, 0, token, m->h, s) || mark(m)) return -1;
-    // embedding row, head, advance; per layer attention plus one launch per GEMV; per
-    // tensor-parallel exchange one, plus the vocabulary argmax
+    // embedding row, head, advance; per layer attention plus one launch per GEMV (and a
+    // tensor-parallel exchange launch where it is not fused into the GEMV), plus the
+    // vocabulary argmax
     int nl = 3 + (tp ? 1 : 0);
     for (int li = 0; li < c.layers; li++) {
         const spk_model::Layer &L = m->layers[li];
         if (capture_rows(m, li, 1, s)) return -1;
-        nl += (m->ncap && m->cap_slot[li] >= 0) + 1 + (tp ? 2 : 0);
+        nl += (m->ncap && m->cap_slot[li] >= 0) + 1;
         int lr = lut_call(m, L, 0, -1, m->h, L.in_norm, c.eps, m->qkv, 0, m->gate, s);
         if (lr < 0 || (lr == 1 && qkv_gate(L, m->h, c.eps, m->qkv, m->gate, s)) || mark(m)) return -1;
         nl += 1;
@@ -281,21 +313,12 @@ int enqueue_step(spk_model *m) {
         a.store = 1;
         a.cached_before = m->capturing;   // a graph replay: every earlier step has completed
         if (attn_decode(a, s) || mark(m)) return -1;
-        float *const ro = tp ? m->pbuf : m->h;   // out_proj / down_proj: rank partial, or the residual
-        lr = lut_call(m, L, 2, -1, m->attn, nullptr, 0.f, ro, tp ? 0 : 1, nullptr, s);
-        if (lr < 0 || (lr == 1 && vq_call(L.m[2], 1, nullptr, m->attn, nullptr, 0.f, ro, tp ? 0 : 1, s)) || mark(m))
-            return -1;
-        nl += 1;
-        if (tp && (tp_sum(m->tpv, m->pbuf, m->h, c.hidden, s) || mark(m))) return -1;
+        if (residual_gemv(m, L, 2, m->attn, s, &nl)) return -1;
         lr = lut_call(m, L, 3, 4, m->h, L.post_norm, c.eps, m->act, 0, nullptr, s);
         if (lr < 0 || (lr == 1 && vq_call(L.m[3], 2, &L.m[4], m->h, L.post_norm, c.eps, m->act, 0, s)) || mark(m))
             return -1;
         nl += 1;
-        lr = lut_call(m, L, 5, -1, m->act, nullptr, 0.f, ro, tp ? 0 : 1, nullptr, s);
-        if (lr < 0 || (lr == 1 && vq_call(L.m[5], 1, nullptr, m->act, nullptr, 0.f, ro, tp ? 0 : 1, s)) || mark(m))
-            return -1;
-        nl += 1;
-        if (tp && (tp_sum(m->tpv, m->pbuf, m->h, c.hidden, s) || mark(m))) return -1;
+        if (residual_gemv(m, L, 5, m->act, s, &nl)) return -1;
     }
     const uint8_t *head_rows = (const uint8_t *)m->embed + (size_t)m->row0 * (c.hidden / 32) * 34;
     const int ht = m->head_tiled ? q8t_head_launch(m->head_tiled, m->vocab_l, c.hidden, 1, m->h, c.hidden,
@@ -312,7 +335,9 @@ int enqueue_step(spk_model *m) {
                                (const DevCtl *)m->ctl, m->state + 3);
     if (e != cudaSuccess) return cuda_fail("decode step launch", e);
     m->step_launches = nl;
-    return mark(m);
+    if (mark(m)) return -1;
+    m->step_marks = m->nmark_all;
+    return 0;
 }
 
 // ---------------------------------------------------------- verify batch ---
@@ -1149,8 +1174,7 @@ int spk_model_trace(spk_model *m, float *us, int cap) {
     if (!m) return set_error("model is null");
     if (!ready(m)) return set_error("model weights are not all set");
     if (!m->eager_steps) return set_error("trace needs one step run first");
-    const int tp = m->tp_world > 1 ? 1 : 0;
-    const int n = 1 + 1 + m->cfg.layers * (5 + 2 * tp) + 1 + tp + 1;   // marks, the first one before any launch
+    const int n = m->step_marks;   // marks of a step (the first one before any launch), as the last enqueue made
     if (!us || cap < n - 1) return set_error("trace needs room for %d launches", n - 1);
     if (!m->texec) {
         for (int i = 0; i < n; i++) {

@@ -15,21 +15,9 @@ namespace {
 
 constexpr int TP_THREADS = 128;
 
-__device__ __forceinline__ unsigned long long globaltimer_ns() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-
-__device__ __forceinline__ void st_pair(uint2 *p, uint32_t value, uint32_t seq) {
-    asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(value), "r"(seq) : "memory");
-}
-
-__device__ __forceinline__ uint2 ld_pair(const uint2 *p) {
-    uint2 v;
-    asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
-    return v;
-}
+__device__ __forceinline__ unsigned long long globaltimer_ns() { return tp_time_ns(); }
+__device__ __forceinline__ void st_pair(uint2 *p, uint32_t value, uint32_t seq) { tp_st_pair(p, value, seq); }
+__device__ __forceinline__ uint2 ld_pair(const uint2 *p) { return tp_ld_pair(p); }
 
 // The residual reduction, low-latency form: every value travels as an 8-byte
 // (value, sequence number) pair — one single-copy-atomic store — so a receiver
@@ -55,26 +43,7 @@ __global__ void __launch_bounds__(TP_THREADS) tp_sum_kernel(const TpView v, cons
         const uint32_t x = __float_as_uint(part[i]);
         for (int q = 0; q < v.world; q++) st_pair(reinterpret_cast<uint2 *>(v.mail[q]) + mine_row + i, x, seq);
     }
-    const uint2 *mail = reinterpret_cast<const uint2 *>(v.mail[v.rank]) + (size_t)slot * v.world * prow;
-    bool give_up = *reinterpret_cast<volatile int *>(v.err) == DEV_PEER_TIMEOUT;
-    const unsigned long long t0 = globaltimer_ns();
-    for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
-        float acc = 0.f;
-        for (int r = 0; r < v.world; r++) {
-            uint2 pr = ld_pair(mail + (size_t)r * prow + i);
-            for (unsigned int it = 0; pr.y != seq && !give_up; it++) {
-                if (it > (1u << 30) || globaltimer_ns() - t0 > v.wait_ns) {
-                    give_up = true;
-                    atomicExch(v.err, DEV_PEER_TIMEOUT);
-                    break;
-                }
-                pr = ld_pair(mail + (size_t)r * prow + i);
-            }
-            const float x = __uint_as_float(pr.x);
-            acc = r == 0 ? x : acc + x;
-        }
-        h[i] = h[i] + acc;
-    }
+    tp_reduce_rows(v, seq, i0, i1, h);
     // the last CTA to finish advances the counter (every CTA has read it by then)
     __syncthreads();
     if (threadIdx.x == 0) s_last = atomicAdd(&v.seq[1], 1u) == gridDim.x - 1;

@@ -22,6 +22,7 @@
 // exact index semantics. Dequant kernels are bit-exact: one f32 multiply and
 // one f32 add per element, no contraction.
 #include "common.cuh"
+#include "tp.cuh"
 #include "spk.h"
 #include "stream.cuh"
 
@@ -82,6 +83,12 @@ struct FastArgs {
     const uint8_t *xst[MAXQ];
     Layout XL;
     float *xy;
+    // Tensor parallel (NG 1, no second matrix): the rows are this rank's partial of a residual
+    // update; a CTA sends its rows to every rank's mailbox as (value, sequence) pairs instead
+    // of writing y, then adds the rank-ordered sum of every rank's rows into h (tp.cuh).
+    int tp;
+    TpView tpv;
+    float *h;
 };
 
 template <int F>
@@ -221,7 +228,22 @@ __global__ void __launch_bounds__(Warps<F>::W * 32, 1) vq_fast_kernel(const Fast
         const int ln = c / (4 * F);   // global lane index = ks * 32 + lane
         xs[(size_t)ln * XS + (c - ln * 4 * F)] = v;
     }
+    __shared__ unsigned int s_tp_seq;
+    __shared__ int s_tp_last;
+    if (NG == 1 && a.tp && tid == 0) s_tp_seq = a.tpv.seq[0] + 1u;   // this exchange's number
     __syncthreads();
+    // A finished row: y, or under tensor parallelism this rank's pair in every rank's mailbox.
+    auto emit = [&](int rr, float o) {
+        if (NG == 1 && a.tp) {
+            const unsigned int seq = s_tp_seq;
+            const size_t prow = (size_t)a.tpv.stride / 2;
+            const size_t mine = ((size_t)(seq & 1u) * a.tpv.world + a.tpv.rank) * prow + rr;
+            for (int q = 0; q < a.tpv.world; q++)
+                tp_st_pair(reinterpret_cast<uint2 *>(a.tpv.mail[q]) + mine, __float_as_uint(o), seq);
+        } else {
+            yout[rr] = o;
+        }
+    };
     float xr[4 * F];
     {
         const float4 *xp = reinterpret_cast<const float4 *>(xs + (size_t)(ks * 32 + lane) * XS);
@@ -287,7 +309,7 @@ __global__ void __launch_bounds__(Warps<F>::W * 32, 1) vq_fast_kernel(const Fast
                     float o = yold;
 #pragma unroll
                     for (int s = 0; s < NSTG; s++) o = __fadd_rn(o, __fmul_rn(acc[s], gain[s]));
-                    yout[r] = o;
+                    emit(r, o);
                 } else {
 #pragma unroll
                     for (int s = 0; s < NSTG; s++) pt[((rw * NG + g) * ks_n + ks) * NSTG + s] = acc[s];
@@ -317,9 +339,23 @@ __global__ void __launch_bounds__(Warps<F>::W * 32, 1) vq_fast_kernel(const Fast
                 outv[gg] = o;
             }
             if (NG == 1)
-                yout[rr] = outv[0];
+                emit(rr, outv[0]);
             else
                 yout[rr] = __fmul_rn(gelu_erf(outv[0]), outv[NG - 1]);
+        }
+    }
+    if (NG == 1 && a.tp) {
+        // every row of this CTA is sent; add every rank's rows, in rank order, into h
+        __syncthreads();
+        const unsigned int seq = s_tp_seq;
+        tp_reduce_rows(a.tpv, seq, rb, re, a.h);
+        // the last CTA to finish advances the exchange counter (every CTA has read it by then)
+        __syncthreads();
+        if (tid == 0) s_tp_last = atomicAdd(&a.tpv.seq[1], 1u) == gridDim.x - 1;
+        __syncthreads();
+        if (s_tp_last && tid == 0) {
+            a.tpv.seq[1] = 0u;
+            a.tpv.seq[0] = seq;
         }
     }
 }
@@ -623,6 +659,29 @@ int spk::vq_gemv_with_extra(const void *const *stages, int nstg, const Layout &L
         return launch_fast(P, nstg, 1, s);
     }
     return 1;
+}
+
+int spk::vq_gemv_tp(const void *const *stages, int nstg, const Layout &L, const float *x, float *h, const TpView &v,
+                    cudaStream_t s) {
+    const uint8_t *st[MAXQ];
+    if (nstg < 1 || nstg > 2) return 1;
+    for (int q = 0; q < nstg; q++) {
+        if (!stages[q]) return set_error("stage %d payload pointer is null", q);
+        st[q] = (const uint8_t *)stages[q];
+    }
+    if (!x || !h) return set_error("gemv needs x and h");
+    if (check_geometry(L.dim, L.nc, L.rows, L.cols, L.v3)) return -1;
+    FastPlan P;
+    if (!fast_plan(st, nstg, 1, L, &P)) return 1;
+    if ((size_t)v.stride < 2 * (size_t)L.rows) return set_error("tensor-parallel mailbox rows hold %d floats, %d needed", v.stride, 2 * L.rows);
+    P.args.x = x;
+    P.args.y = h;   // not written: the rows travel as pairs
+    P.args.accumulate = 0;
+    P.args.err = device_error_ptr();
+    P.args.tp = 1;
+    P.args.tpv = v;
+    P.args.h = h;
+    return launch_fast(P, nstg, 1, s) ? -1 : 0;
 }
 
 namespace {

@@ -300,16 +300,25 @@ class DeviceModel:
 
     def trace(self) -> list:
         """One decode step (as run() does) with every launch's device time: [(name, us), ...]
-        in enqueue order (spk_model_trace). All tensor-parallel ranks trace together."""
+        in enqueue order (spk_model_trace). All tensor-parallel ranks trace together. Under
+        tensor parallelism out_proj and down_proj carry the residual exchange themselves where
+        the code-word kernel takes the matrix; otherwise a tp_sum launch follows each."""
         tp = self.tp[1] > 1
-        layer = ["qkv_g", "attention", "out"] + (["tp_sum"] if tp else []) + ["gate_up", "down"] + \
-                (["tp_sum"] if tp else [])
-        names = ["embed"] + layer * self.cfg.layers + ["head"] + (["tp_argmax"] if tp else []) + ["advance"]
-        buf = (C.c_float * len(names))()
-        n = lib().spk_model_trace(self.h, buf, len(names))
-        if n != len(names):
+
+        def names_for(fused: bool) -> list:
+            ex = ["tp_sum"] if tp and not fused else []
+            layer = ["qkv_g", "attention", "out"] + ex + ["gate_up", "down"] + ex
+            return ["embed"] + layer * self.cfg.layers + ["head"] + (["tp_argmax"] if tp else []) + ["advance"]
+
+        full = names_for(False)
+        buf = (C.c_float * len(full))()
+        n = lib().spk_model_trace(self.h, buf, len(full))
+        if n < 0:
             raise SpkError(f"trace: {lib().spk_last_error().decode()}")
-        return list(zip(names, [float(v) for v in buf]))
+        for names in (names_for(True), full):
+            if len(names) == n:
+                return list(zip(names, [float(v) for v in buf[:n]]))
+        raise SpkError(f"trace: {n} launches in a step, neither the fused nor the separate exchange layout")
 
     def forward(self, token: int, pos: int, want_logits: bool = True):
         """Model::forward: returns (next_id, logits or None) through host buffers."""
