@@ -34,6 +34,23 @@ __device__ void rope_smem(float *x, const float *freq, int pdim, int pos) {
     }
 }
 
+// The same rotation on the G query heads and the key of one token at once: the angle of a
+// dims pair depends only on the pair, so its cosine and sine are computed once for all G + 1
+// vectors (each element's arithmetic is rope_smem's).
+__device__ void rope_group(float (*q)[256], int G, float *k, const float *freq, int pdim, int pos) {
+    const int half = pdim / 2;
+    for (int i = threadIdx.x; i < half; i += blockDim.x) {
+        const float ang = __fmul_rn((float)pos, freq[i]);
+        const float c = cosf(ang), s = sinf(ang);
+        for (int h = 0; h <= G; h++) {
+            float *x = h < G ? q[h] : k;
+            const float a = x[i], b = x[i + half];
+            x[i] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+            x[i + half] = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
+        }
+    }
+}
+
 // This lane's DPL dims (lane*DPL ..) of one cache row of HD values, as f32.
 template <int HD, int DPL, int KT>
 __device__ __forceinline__ void load_row(const uint8_t *row, int lane, float (&r)[DPL]) {
@@ -448,6 +465,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const AttnArgs a
     __shared__ int is_last;
     __shared__ float cpm[CL ? MG : 1][CL ? PR : 1];   // CL: this split's o, m, l
     __shared__ float gs[MG];                          // CL: the heads' sigmoid gates
+    __shared__ float we[NW][MG], wml[MG][2];          // the merge's per-(tile, head) weights, per-head (M, L)
+    __shared__ float cwt[CL ? 8 : 1][MG];             // CL: the splits' per-head weights
     pdl_trigger();
     // The model's decode step (one token storing its own row, cached_before set) reads only
     // cache rows written by earlier graph launches, which run one after another, plus its own
@@ -504,8 +523,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const AttnArgs a
     if (CL && threadIdx.x < G)   // the heads' gates (model.rs:538-550), loaded with q
         gs[threadIdx.x] = 1.0f / (1.0f + expf(-a.gate[(size_t)tok * a.ldgate + kvh * G + threadIdx.x]));
     __syncthreads();
-    for (int h = 0; h < G; h++) rope_smem(qs[h], a.freq, a.pdim, pos);
-    rope_smem(kn, a.freq, a.pdim, pos);
+    rope_group(qs, G, kn, a.freq, a.pdim, pos);
     __syncthreads();
     if (a.store && c0 <= pos && pos < c1) {   // a single token's own row; nobody reads that slot now
         const size_t o = ((size_t)kvh * a.slots + pos % a.slots) * RB;
@@ -710,16 +728,27 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const AttnArgs a
         for (int d = lane; d < HD; d += 32) wo[TC_TILES][h][d] = own ? vn[d] : 0.f;
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
-        const int h = i / HD, d = i % HD;
+    if (threadIdx.x < G) {   // per head: the running max, the tiles' weights e^{m_w - M}, the sum L
+        const int h = threadIdx.x;
         float M = -INFINITY;
         for (int w = 0; w < NW; w++) M = fmaxf(M, wm[w][h]);
-        float L = 0.f, O = 0.f;
+        float L = 0.f;
+        for (int w = 0; w < NW; w++) {
+            const float e = wm[w][h] == -INFINITY ? 0.f : expf(wm[w][h] - M);
+            if (wm[w][h] != -INFINITY) L += wl[w][h] * e;
+            we[w][h] = e;
+        }
+        wml[h][0] = M;
+        wml[h][1] = L;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
+        const int h = i / HD, d = i % HD;
+        const float M = wml[h][0], L = wml[h][1];
+        float O = 0.f;
         for (int w = 0; w < NW; w++) {
             if (wm[w][h] == -INFINITY) continue;
-            const float e = expf(wm[w][h] - M);
-            L += wl[w][h] * e;
-            O += wo[w][h][d] * e;
+            O += wo[w][h][d] * we[w][h];
         }
         float *dst = CL ? &cpm[h][0] : out + h * PR;
         dst[d] = O;
@@ -733,19 +762,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const AttnArgs a
         cg::cluster_group cluster = cg::this_cluster();
         cluster.sync();   // every split's (o, m, l) is in its CTA's shared memory
         const int ns = a.nsplit, r = (int)cluster.block_rank(), dpc = HD / ns;
-        for (int i = threadIdx.x; i < G * dpc; i += blockDim.x) {   // this CTA's dims, every head
-            const int h = i / dpc, d = r * dpc + i % dpc;
+        if (threadIdx.x < G) {   // per head: the splits' weights e^{m_c - M} and the sum L, once
+            const int h = threadIdx.x;
             float M = -INFINITY;
             for (int c = 0; c < ns; c++) M = fmaxf(M, cluster.map_shared_rank(&cpm[h][HD], c)[0]);
-            float L = 0.f, O = 0.f;
+            float L = 0.f;
             for (int c = 0; c < ns; c++) {   // the same order as the ticket merge: split 0 first
                 const float *pc = cluster.map_shared_rank(&cpm[h][0], c);
                 const float mc = pc[HD];
                 const float e = mc == -INFINITY ? 0.f : expf(mc - M);
                 L += pc[HD + 1] * e;
-                O = fmaf(pc[d], e, O);
+                cwt[c][h] = e;
             }
-            a.out[(size_t)tok * a.ldout + (size_t)(kvh * G + h) * HD + d] = (O / L) * gs[h];
+            wml[h][1] = L;
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < G * dpc; i += blockDim.x) {   // this CTA's dims, every head
+            const int h = i / dpc, d = r * dpc + i % dpc;
+            float O = 0.f;
+            for (int c = 0; c < ns; c++) O = fmaf(cluster.map_shared_rank(&cpm[h][0], c)[d], cwt[c][h], O);
+            a.out[(size_t)tok * a.ldout + (size_t)(kvh * G + h) * HD + d] = (O / wml[h][1]) * gs[h];
         }
         cluster.sync();   // no CTA leaves while another still reads its shared memory
     } else {
