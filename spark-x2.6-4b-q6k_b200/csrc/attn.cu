@@ -36,11 +36,12 @@ __device__ void rope_smem(float *x, const float *freq, int pdim, int pos) {
 
 // The same rotation on the G query heads and the key of one token at once: the angle of a
 // dims pair depends only on the pair, so its cosine and sine are computed once for all G + 1
-// vectors (each element's arithmetic is rope_smem's).
-__device__ void rope_group(float (*q)[256], int G, float *k, const float *freq, int pdim, int pos) {
+// vectors (each element's arithmetic is rope_smem's). fi: freq[threadIdx.x], loaded by the
+// caller together with the vectors (its first pair), so its latency overlaps theirs.
+__device__ void rope_group(float (*q)[256], int G, float *k, const float *freq, float fi, int pdim, int pos) {
     const int half = pdim / 2;
     for (int i = threadIdx.x; i < half; i += blockDim.x) {
-        const float ang = __fmul_rn((float)pos, freq[i]);
+        const float ang = __fmul_rn((float)pos, i == (int)threadIdx.x ? fi : freq[i]);
         const float c = cosf(ang), s = sinf(ang);
         for (int h = 0; h <= G; h++) {
             float *x = h < G ? q[h] : k;
@@ -445,9 +446,11 @@ __device__ __forceinline__ uint32_t f16_pair(float x, float y, bool lo) {
 }
 
 // CL: the splits of a (token, KV head) run as one thread-block cluster (grid.y = nsplit <= 8 =
-// the cluster's size): each CTA leaves its (o, m, l) in its own shared memory and, after a
-// cluster barrier, merges its slice of the output dims from every split's shared memory
-// (distributed shared memory), so the merge costs no global round trip and no ticket.
+// the cluster's size) and CTA r owns output dims r * dpc .. (dpc = HD / nsplit): each split
+// stores its (o, m, l) for those dims straight into CTA r's shared memory (distributed shared
+// memory stores, which do not wait for an answer) and, after one cluster barrier, every CTA
+// merges its own dims from its own shared memory: no global round trip, no ticket, no remote
+// load.
 template <int KT, bool CL>
 __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const AttnArgs a) {
     constexpr int HD = 256, MG = ATT_MAX_GROUP, PR = HD + 4, NW = TC_TILES + 1;
@@ -463,11 +466,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const AttnArgs a
     __shared__ float cw[MG][CL ? 1 : ATT_MAX_SPLIT];
     __shared__ float cl[MG];
     __shared__ int is_last;
-    __shared__ float cpm[CL ? MG : 1][CL ? PR : 1];   // CL: this split's o, m, l
+    // CL: every split's (o for this CTA's dims, m, l) per head, [split][head][dpc + 2]
+    __shared__ float mrg[CL ? MG * (HD + 2 * 8) : 1];
     __shared__ float gs[MG];                          // CL: the heads' sigmoid gates
     __shared__ float we[NW][MG], wml[MG][2];          // the merge's per-(tile, head) weights, per-head (M, L)
     __shared__ float cwt[CL ? 8 : 1][MG];             // CL: the splits' per-head weights
     pdl_trigger();
+    if constexpr (CL)   // first half of the barrier that shows every CTA of the cluster runs
+        asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
     // The model's decode step (one token storing its own row, cached_before set) reads only
     // cache rows written by earlier graph launches, which run one after another, plus its own
     // row, which the score masks: its first K/V stages are issued before the wait for the
@@ -514,6 +520,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const AttnArgs a
         pdl_wait();
     }
 
+    const float fi = (int)threadIdx.x < a.pdim / 2 ? a.freq[threadIdx.x] : 0.f;
     for (int i = threadIdx.x; i < MG * HD; i += blockDim.x)
         qs[i / HD][i % HD] = i / HD < G ? qrow[(size_t)(kvh * G + i / HD) * HD + i % HD] : 0.f;
     for (int i = threadIdx.x; i < HD; i += blockDim.x) {
@@ -523,7 +530,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const AttnArgs a
     if (CL && threadIdx.x < G)   // the heads' gates (model.rs:538-550), loaded with q
         gs[threadIdx.x] = 1.0f / (1.0f + expf(-a.gate[(size_t)tok * a.ldgate + kvh * G + threadIdx.x]));
     __syncthreads();
-    rope_group(qs, G, kn, a.freq, a.pdim, pos);
+    rope_group(qs, G, kn, a.freq, fi, a.pdim, pos);
     __syncthreads();
     if (a.store && c0 <= pos && pos < c1) {   // a single token's own row; nobody reads that slot now
         const size_t o = ((size_t)kvh * a.slots + pos % a.slots) * RB;
@@ -742,6 +749,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const AttnArgs a
         wml[h][1] = L;
     }
     __syncthreads();
+    if constexpr (CL)   // the other half of the first barrier: every CTA of the cluster runs
+        asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
     for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
         const int h = i / HD, d = i % HD;
         const float M = wml[h][0], L = wml[h][1];
@@ -750,40 +759,50 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const AttnArgs a
             if (wm[w][h] == -INFINITY) continue;
             O += wo[w][h][d] * we[w][h];
         }
-        float *dst = CL ? &cpm[h][0] : out + h * PR;
-        dst[d] = O;
-        if (d == 0) {
-            dst[HD] = M;
-            dst[HD + 1] = L;
+        if constexpr (CL) {   // dim d goes to the CTA that owns it; m, l to every CTA (d < ns)
+            namespace cg = cooperative_groups;
+            cg::cluster_group cluster = cg::this_cluster();
+            const int ns = a.nsplit, dpc = HD / ns, me = (int)cluster.block_rank(), rr = d / dpc;
+            cluster.map_shared_rank(mrg, rr)[(me * G + h) * (dpc + 2) + d - rr * dpc] = O;
+            if (d < ns) {
+                float *dm = cluster.map_shared_rank(mrg, d) + (me * G + h) * (dpc + 2) + dpc;
+                dm[0] = M;
+                dm[1] = L;
+            }
+        } else {
+            float *dst = out + h * PR;
+            dst[d] = O;
+            if (d == 0) {
+                dst[HD] = M;
+                dst[HD + 1] = L;
+            }
         }
     }
     if constexpr (CL) {
         namespace cg = cooperative_groups;
         cg::cluster_group cluster = cg::this_cluster();
-        cluster.sync();   // every split's (o, m, l) is in its CTA's shared memory
+        cluster.sync();   // every split's stores are in; nothing touches another CTA's memory after it
         const int ns = a.nsplit, r = (int)cluster.block_rank(), dpc = HD / ns;
         if (threadIdx.x < G) {   // per head: the splits' weights e^{m_c - M} and the sum L, once
             const int h = threadIdx.x;
             float M = -INFINITY;
-            for (int c = 0; c < ns; c++) M = fmaxf(M, cluster.map_shared_rank(&cpm[h][HD], c)[0]);
+            for (int c = 0; c < ns; c++) M = fmaxf(M, mrg[(c * G + h) * (dpc + 2) + dpc]);
             float L = 0.f;
             for (int c = 0; c < ns; c++) {   // the same order as the ticket merge: split 0 first
-                const float *pc = cluster.map_shared_rank(&cpm[h][0], c);
-                const float mc = pc[HD];
+                const float mc = mrg[(c * G + h) * (dpc + 2) + dpc];
                 const float e = mc == -INFINITY ? 0.f : expf(mc - M);
-                L += pc[HD + 1] * e;
+                L += mrg[(c * G + h) * (dpc + 2) + dpc + 1] * e;
                 cwt[c][h] = e;
             }
             wml[h][1] = L;
         }
         __syncthreads();
         for (int i = threadIdx.x; i < G * dpc; i += blockDim.x) {   // this CTA's dims, every head
-            const int h = i / dpc, d = r * dpc + i % dpc;
+            const int h = i / dpc, dd = i - h * dpc;
             float O = 0.f;
-            for (int c = 0; c < ns; c++) O = fmaf(cluster.map_shared_rank(&cpm[h][0], c)[d], cwt[c][h], O);
-            a.out[(size_t)tok * a.ldout + (size_t)(kvh * G + h) * HD + d] = (O / wml[h][1]) * gs[h];
+            for (int c = 0; c < ns; c++) O = fmaf(mrg[(c * G + h) * (dpc + 2) + dd], cwt[c][h], O);
+            a.out[(size_t)tok * a.ldout + (size_t)(kvh * G + h) * HD + r * dpc + dd] = (O / wml[h][1]) * gs[h];
         }
-        cluster.sync();   // no CTA leaves while another still reads its shared memory
     } else {
         finish_splits<HD>(a, kvh, tok, G, pbase, pstride, cw, cl, &is_last);
     }

@@ -137,10 +137,12 @@ def test_attention_matches_reference(cuda, hd, heads, kvh, full, ntok, f16):
 
 
 @pytest.mark.parametrize("ntok,kv_type", [(1, 1), (8, 1), (1, 0), (3, 2)])
-@pytest.mark.parametrize("nsplit", [2, 3])
+@pytest.mark.parametrize("nsplit", [1, 2, 3, 4, 8, 37])
 def test_attention_long_splits(cuda, ntok, kv_type, nsplit):
-    """Splits of 200-300 positions (several 64-position stages of the tensor-core kernel,
-    a partial last stage, the own row inside a stage) at head_dim 256, full attention."""
+    """Splits of 16-600 positions (several 64-position stages of the tensor-core kernel,
+    a partial last stage, the own row inside a stage) at head_dim 256, full attention.
+    1, 2, 4 and 8 splits merge inside one thread-block cluster; 3 and 37 through the
+    workspace and the last split's ticket."""
     import torch
 
     import spk
