@@ -345,12 +345,11 @@ __device__ __forceinline__ float q80_unit_s(const uint8_t *row, int u, const flo
 }
 
 __device__ __forceinline__ void gf_issue(const GFArgs &a, uint8_t *slot, uint64_t *bar, int r0, int nr) {
-    BulkList bl;
-    bl.n = 0;
+    BulkList<1> bl;
     bl.tx = 0;
     const uintptr_t A = (uintptr_t)(a.w + (size_t)r0 * a.rb_bytes);
     const uintptr_t limit = (uintptr_t)(a.w + (size_t)a.rows * a.rb_bytes);   // no slack promised
-    bulk_plan(bl, slot, A, A + (size_t)nr * a.rb_bytes, limit);
+    bulk_plan(bl, 0, slot, A, A + (size_t)nr * a.rb_bytes, limit);
     bulk_issue(bl, bar);
 }
 

@@ -60,11 +60,10 @@ __device__ __forceinline__ uint2 q4_to_f16(const uint8_t *p) {
 }
 
 __device__ __forceinline__ void hb_issue(const HBArgs &a, uint8_t *slot, uint64_t *bar, int r0, int nr) {
-    BulkList bl;
-    bl.n = 0;
+    BulkList<1> bl;
     bl.tx = 0;
     const uintptr_t A = (uintptr_t)(a.w + (size_t)r0 * a.rb_bytes);
-    bulk_plan(bl, slot, A, A + (size_t)nr * a.rb_bytes, (uintptr_t)(a.w + (size_t)a.rows * a.rb_bytes));
+    bulk_plan(bl, 0, slot, A, A + (size_t)nr * a.rb_bytes, (uintptr_t)(a.w + (size_t)a.rows * a.rb_bytes));
     bulk_issue(bl, bar);
 }
 

@@ -13,52 +13,57 @@
 
 namespace spk {
 
+// The copies of one tile: range k of the tile in entry k (len 0: nothing to copy). Every
+// caller plans with compile-time k, so after unrolling the list lives in registers; a list
+// indexed by a running count would sit in local memory, and the producer's loads and stores
+// to it would queue behind the consumers' shared- and global-memory traffic.
+template <int N>
 struct BulkList {
-    const void *src[8];
-    void *dst[8];
-    uint32_t len[8];
-    int n;
+    const void *src[N];
+    void *dst[N];
+    uint32_t len[N];
     uint32_t tx;
 };
 
-__device__ __forceinline__ void bulk_plan(BulkList &bl, uint8_t *d, uintptr_t A, uintptr_t B, uintptr_t limit) {
+template <int N>
+__device__ __forceinline__ void bulk_plan(BulkList<N> &bl, int k, uint8_t *d, uintptr_t A, uintptr_t B, uintptr_t limit) {
+    bl.len[k] = 0;
     const uintptr_t Aal = A & ~(uintptr_t)15, Bup = (B + 15) & ~(uintptr_t)15;
     if (B <= A) return;
+    bl.src[k] = (const void *)Aal;
+    bl.dst[k] = d;
     if (Bup <= limit) {
-        bl.src[bl.n] = (const void *)Aal;
-        bl.dst[bl.n] = d;
-        bl.len[bl.n] = (uint32_t)(Bup - Aal);
-        bl.tx += bl.len[bl.n];
-        bl.n++;
+        bl.len[k] = (uint32_t)(Bup - Aal);
+        bl.tx += bl.len[k];
         return;
     }
     const uintptr_t Bfl = B & ~(uintptr_t)15;
     if (Bfl > Aal) {
-        bl.src[bl.n] = (const void *)Aal;
-        bl.dst[bl.n] = d;
-        bl.len[bl.n] = (uint32_t)(Bfl - Aal);
-        bl.tx += bl.len[bl.n];
-        bl.n++;
+        bl.len[k] = (uint32_t)(Bfl - Aal);
+        bl.tx += bl.len[k];
     }
     const uintptr_t t0 = Bfl > Aal ? Bfl : Aal;   // 2-byte aligned, B - t0 < 16
     const int nt = (int)((B - t0 + 1) >> 1);
     uint16_t tv[8];
 #pragma unroll
-    for (int k = 0; k < 8; k++)
-        if (k < nt) tv[k] = reinterpret_cast<const uint16_t *>(t0)[k];
+    for (int j = 0; j < 8; j++)
+        if (j < nt) tv[j] = reinterpret_cast<const uint16_t *>(t0)[j];
     uint16_t *dt = reinterpret_cast<uint16_t *>(d + (t0 - Aal));
 #pragma unroll
-    for (int k = 0; k < 8; k++)
-        if (k < nt) dt[k] = tv[k];
+    for (int j = 0; j < 8; j++)
+        if (j < nt) dt[j] = tv[j];
 }
 
 // Called by one thread after every bulk_plan of the tile: arrive on the
 // tile's mbarrier with its byte count (release: orders the register-tail stores
 // before the consumers' acquire), then start the copies.
-__device__ __forceinline__ void bulk_issue(const BulkList &bl, uint64_t *bar) {
+template <int N>
+__device__ __forceinline__ void bulk_issue(const BulkList<N> &bl, uint64_t *bar) {
     mbar_arrive_expect_tx(bar, bl.tx);
     fence_proxy_async();
-    for (int k = 0; k < bl.n; k++) bulk_g2s(bl.dst[k], bl.src[k], bl.len[k], bar);
+#pragma unroll
+    for (int k = 0; k < N; k++)
+        if (bl.len[k]) bulk_g2s(bl.dst[k], bl.src[k], bl.len[k], bar);
 }
 
 }  // namespace spk

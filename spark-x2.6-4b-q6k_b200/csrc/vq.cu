@@ -38,11 +38,10 @@ __device__ __forceinline__ float gelu_erf(float g) {
     return __fmul_rn(__fmul_rn(0.5f, g), __fadd_rn(1.0f, (float)e));
 }
 
-// Block-wide RMSNorm scale, sum of squares in f64 (model.rs:236-245). Every CTA
-// sums in the same order, so every CTA gets the same scale.
-__device__ float block_rms_inv(const float *x, int n, float eps, double *red) {
-    double s = 0.0;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) s += (double)x[i] * (double)x[i];
+// Block-wide RMSNorm scale from each thread's partial sum s of x[i]^2 over i = threadIdx.x,
+// threadIdx.x + blockDim.x, ... (in that order), the total in f64 (model.rs:236-245). Every
+// CTA sums in the same order, so every CTA gets the same scale.
+__device__ float block_rms_inv_from(double s, int n, float eps, double *red) {
     s = warp_sum_d(s);
     const int w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
     if ((threadIdx.x & 31) == 0) red[w] = s;
@@ -51,6 +50,12 @@ __device__ float block_rms_inv(const float *x, int n, float eps, double *red) {
     for (int k = 0; k < nw; k++) t += red[k];
     __syncthreads();
     return (float)(1.0 / sqrt(t / (double)n + (double)eps));
+}
+
+__device__ float block_rms_inv(const float *x, int n, float eps, double *red) {
+    double s = 0.0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) s += (double)x[i] * (double)x[i];
+    return block_rms_inv_from(s, n, eps, red);
 }
 
 // ============================================================ fast path ===
@@ -62,6 +67,11 @@ struct Warps {
     static constexpr int W = 16;
 };
 constexpr int FAST_NBUF = 3;
+
+// Shared-memory bytes of one stage's codebook region: nc 8-byte code words copied from the
+// 16-byte boundary at or below the codebook (the payload keeps it 8-byte aligned), so up to 8
+// leading and 15 trailing bytes ride along.
+__host__ __device__ constexpr size_t cb_region(int nc) { return ((size_t)nc * 8 + 16 + 15) & ~(size_t)15; }
 constexpr int MAXQ = 4;   // streams: groups x stages
 
 struct FastArgs {
@@ -143,20 +153,22 @@ __device__ __forceinline__ float row_chunk(const uint8_t *row, const uint8_t *pl
 // [r0, r0+nr) of every stream (stream.cuh). The contract gives every stage
 // payload 8 zeroed slack bytes, so a copy may round up to at most 8 bytes past
 // the payload end.
-__device__ __forceinline__ void issue_tile(const FastArgs &a, const uint8_t *const *stp, const Layout &L, int nq,
-                                           int ext, uint8_t *slot, uint64_t *bar, int r0, int nr) {
+template <int NQ, int EXT>
+__device__ __forceinline__ void issue_tile(const FastArgs &a, const uint8_t *const (&stp)[NQ], const Layout &L,
+                                           uint8_t *slot, uint64_t *bar, int r0, int nr) {
     const size_t payload = L.stream_off + (size_t)L.rows * (L.mrow + L.prow);
-    BulkList bl;
-    bl.n = 0;
+    BulkList<NQ * (1 + EXT)> bl;
     bl.tx = 0;
-    for (int q = 0; q < nq; q++) {
+#pragma unroll
+    for (int q = 0; q < NQ; q++) {
         const uintptr_t limit = (uintptr_t)(stp[q] + payload + 8);
-        for (int part = 0; part < 1 + ext; part++) {
+#pragma unroll
+        for (int part = 0; part < 1 + EXT; part++) {
             const uint8_t *base = stp[q] + L.stream_off +
                                   (part ? (size_t)L.rows * L.mrow + (size_t)r0 * L.prow : (size_t)r0 * L.mrow);
             const size_t bytes = (size_t)nr * (part ? L.prow : L.mrow);
-            uint8_t *d = slot + (part ? (nq * a.main_slot + q * a.plane_slot) : q * a.main_slot);
-            bulk_plan(bl, d, (uintptr_t)base, (uintptr_t)base + bytes, limit);
+            uint8_t *d = slot + (part ? (NQ * a.main_slot + q * a.plane_slot) : q * a.main_slot);
+            bulk_plan(bl, q * (1 + EXT) + part, d, (uintptr_t)base, (uintptr_t)base + bytes, limit);
         }
     }
     bulk_issue(bl, bar);
@@ -172,16 +184,19 @@ __global__ void __launch_bounds__(Warps<F>::W * 32, 1) vq_fast_kernel(const Fast
     extern __shared__ __align__(16) uint8_t smem[];
     const bool xt = NG == 1 && a.has_x && blockIdx.x == gridDim.x - 1;   // this CTA runs the second matrix
     const Layout &L = xt ? a.XL : a.L;
-    const uint8_t *const *stp = xt ? a.xst : a.st;
+    const uint8_t *stp[NQ];   // this CTA's stage payloads, in registers
+#pragma unroll
+    for (int q = 0; q < NQ; q++) stp[q] = xt ? a.xst[q] : a.st[q];
     float *const yout = xt ? a.xy : a.y;
     const int nc = L.nc;
     const int ks_n = a.ks, tr = a.tr, NB = a.nbuf;
-    uint2 *cb = reinterpret_cast<uint2 *>(smem);
-    float *xs = reinterpret_cast<float *>(smem + (((size_t)NQ * nc * 8 + 15) & ~(size_t)15));
+    const size_t CBR = cb_region(nc);
+    float *xs = reinterpret_cast<float *>(smem + NQ * CBR);
     uint8_t *ring = reinterpret_cast<uint8_t *>(xs + (size_t)ks_n * 32 * XS);
     uint64_t *full = reinterpret_cast<uint64_t *>(ring + (size_t)NB * a.slot_bytes);
     uint64_t *empty = full + NB;
-    float *part = reinterpret_cast<float *>(empty + NB);   // [2][tr][NG][ks][NSTG]
+    uint64_t *cbar = empty + NB;                            // the codebooks' copy
+    float *part = reinterpret_cast<float *>(cbar + 2);   // [2][tr][NG][ks][NSTG]
     double *red = reinterpret_cast<double *>(part + 2 * tr * NG * ks_n * NSTG);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -200,33 +215,54 @@ __global__ void __launch_bounds__(Warps<F>::W * 32, 1) vq_fast_kernel(const Fast
             mbar_init(&full[b], 1);
             mbar_init(&empty[b], FAST_WARPS);
         }
+        mbar_init(cbar, 1);
         fence_mbar_init();
     }
     __syncthreads();
     if (tid == 0) {
+        // Codebooks: NQ x nc code words of 8 bytes, one bulk copy per stage ahead of the
+        // first tiles (a few large copies load the hot lines every CTA shares better than
+        // thousands of 8-byte ones).
+        uint32_t tx = 0;
+        for (int q = 0; q < NQ; q++) {
+            const uintptr_t A = (uintptr_t)(stp[q] + L.cb_off);
+            tx += (uint32_t)((((A + (size_t)nc * 8) + 15) & ~(uintptr_t)15) - (A & ~(uintptr_t)15));
+        }
+        mbar_arrive_expect_tx(cbar, tx);
+        for (int q = 0; q < NQ; q++) {
+            const uintptr_t A = (uintptr_t)(stp[q] + L.cb_off), Aal = A & ~(uintptr_t)15;
+            bulk_g2s(smem + q * CBR, (const void *)Aal, (uint32_t)((((A + (size_t)nc * 8) + 15) & ~(uintptr_t)15) - Aal), cbar);
+        }
         for (int t = 0; t < NB - 1 && t < ntile; t++) {
             const int r0 = rb + t * tr;
-            issue_tile(a, stp, L, NQ, EXT, ring + (size_t)t * a.slot_bytes, &full[t], r0, min(tr, re - r0));
+            issue_tile<NQ, EXT>(a, stp, L, ring + (size_t)t * a.slot_bytes, &full[t], r0, min(tr, re - r0));
         }
-    }
-    // Codebooks: NQ x nc code words of 8 bytes (the payload keeps them 8-byte aligned).
-    for (int q = 0; q < NQ; q++) {
-        const uint2 *src = reinterpret_cast<const uint2 *>(stp[q] + L.cb_off);
-        for (int v = tid; v < nc; v += FAST_THREADS) cb[q * nc + v] = __ldg(src + v);
     }
     // Everything above read weights only; x (and y, when accumulating) come from
     // the preceding kernels.
     pdl_wait();
-    // Activations: coalesced loads (with the optional RMSNorm folded in) into a
-    // per-lane padded layout, then each lane takes its 4F values with 16-byte
-    // shared loads that hit distinct banks.
-    float inv = 1.0f;
-    if (a.norm_w) inv = block_rms_inv(a.x, L.cols, a.eps, red);
-    for (int c = tid; c < L.cols; c += FAST_THREADS) {
-        float v = a.x[c];
-        if (a.norm_w) v = __fmul_rn(__fmul_rn(v, inv), a.norm_w[c]);
-        const int ln = c / (4 * F);   // global lane index = ks * 32 + lane
-        xs[(size_t)ln * XS + (c - ln * 4 * F)] = v;
+    // Activations: coalesced loads (one read of x; the optional RMSNorm's sum of squares
+    // taken on the way, then the scale applied in shared memory) into a per-lane padded
+    // layout, then each lane takes its 4F values with 16-byte shared loads that hit
+    // distinct banks.
+    {
+        double ss = 0.0;
+#pragma unroll 4
+        for (int c = tid; c < L.cols; c += FAST_THREADS) {
+            const float v = a.x[c];
+            ss += (double)v * (double)v;
+            const int ln = c / (4 * F);   // global lane index = ks * 32 + lane
+            xs[(size_t)ln * XS + (c - ln * 4 * F)] = v;
+        }
+        if (a.norm_w) {   // the block's common branch
+            const float inv = block_rms_inv_from(ss, L.cols, a.eps, red);
+#pragma unroll 4
+            for (int c = tid; c < L.cols; c += FAST_THREADS) {
+                const int ln = c / (4 * F);
+                float &v = xs[(size_t)ln * XS + (c - ln * 4 * F)];
+                v = __fmul_rn(__fmul_rn(v, inv), a.norm_w[c]);
+            }
+        }
     }
     __shared__ unsigned int s_tp_seq;
     __shared__ int s_tp_last;
@@ -258,6 +294,20 @@ __global__ void __launch_bounds__(Warps<F>::W * 32, 1) vq_fast_kernel(const Fast
     }
     const int i0 = ks * 32 * F + lane * F;
     const uint32_t bit0 = 12u * (uint32_t)i0, pbit0 = (uint32_t)i0;
+    const uint2 *cbq[NQ];   // each stage's code words in shared memory
+#pragma unroll
+    for (int q = 0; q < NQ; q++)
+        cbq[q] = reinterpret_cast<const uint2 *>(smem + q * CBR + ((uintptr_t)(stp[q] + L.cb_off) & 15));
+    // this warp's group's stages (selected once: a register array indexed by the warp's group
+    // inside the loop would go to local memory)
+    const uint8_t *wst[NSTG];
+    const uint2 *wcb[NSTG];
+#pragma unroll
+    for (int s = 0; s < NSTG; s++) {
+        wst[s] = (NG == 2 && g) ? stp[NSTG + s] : stp[s];
+        wcb[s] = (NG == 2 && g) ? cbq[NSTG + s] : cbq[s];
+    }
+    const bool cb_in = mbar_wait(cbar, 0u, a.err);   // a lost copy: the error is set, no look-ups
 
     for (int t = 0; t < ntile; t++) {
         const int slot = t % NB;
@@ -267,7 +317,7 @@ __global__ void __launch_bounds__(Warps<F>::W * 32, 1) vq_fast_kernel(const Fast
             const int tn = t + NB - 1, r0n = rb + tn * tr, sn = tn % NB;
             // the slot last held tile tn - NBUF: wait until every warp released it
             if (tn < NB || mbar_wait(&empty[sn], (uint32_t)(((tn / NB) - 1) & 1), a.err))
-                issue_tile(a, stp, L, NQ, EXT, ring + (size_t)sn * a.slot_bytes, &full[sn], r0n, min(tr, re - r0n));
+                issue_tile<NQ, EXT>(a, stp, L, ring + (size_t)sn * a.slot_bytes, &full[sn], r0n, min(tr, re - r0n));
         }
         const int r0 = rb + t * tr, nr = min(tr, re - r0);
         const int r = r0 + rw;
@@ -283,20 +333,20 @@ __global__ void __launch_bounds__(Warps<F>::W * 32, 1) vq_fast_kernel(const Fast
         float acc[NSTG];
 #pragma unroll
         for (int s = 0; s < NSTG; s++) acc[s] = 0.f;
-        if (rw < nr && have) {
+        if (rw < nr && have && cb_in) {
             const uint8_t *sb = ring + (size_t)slot * a.slot_bytes;
 #pragma unroll
             for (int s = 0; s < NSTG; s++) {
                 const int q = g * NSTG + s;
-                const uintptr_t A = (uintptr_t)(stp[q] + L.stream_off + (size_t)r0 * L.mrow);
+                const uintptr_t A = (uintptr_t)(wst[s] + L.stream_off + (size_t)r0 * L.mrow);
                 const uint8_t *row = sb + q * a.main_slot + (A & 15) + (size_t)rw * L.mrow;
                 const uint8_t *pl = nullptr;
                 if (EXT) {
-                    const uintptr_t P = (uintptr_t)(stp[q] + L.stream_off + (size_t)L.rows * L.mrow +
+                    const uintptr_t P = (uintptr_t)(wst[s] + L.stream_off + (size_t)L.rows * L.mrow +
                                                     (size_t)r0 * L.prow);
                     pl = sb + NQ * a.main_slot + q * a.plane_slot + (P & 15) + (size_t)rw * L.prow;
                 }
-                acc[s] = row_chunk<F, EXT>(row, pl, cb + (size_t)q * nc, xr, bit0, pbit0);
+                acc[s] = row_chunk<F, EXT>(row, pl, wcb[s], xr, bit0, pbit0);
             }
         }
         __syncwarp();
@@ -505,8 +555,8 @@ bool fast_plan(const uint8_t *const *st, int nstg, int ng, const Layout &L, Fast
     int nbuf = FAST_NBUF;
     size_t smem = 0;
     for (; nbuf >= 2; nbuf--) {
-        smem = (((size_t)nq * L.nc * 8 + 15) & ~(size_t)15) + (size_t)ks * 32 * (4 * (F + 1 + (F & 1))) * 4 + (size_t)nbuf * slot +
-               2 * (size_t)nbuf * 8 + (size_t)2 * tr * ng * ks * nstg * 4 + 32 * 8;
+        smem = (size_t)nq * cb_region(L.nc) + (size_t)ks * 32 * (4 * (F + 1 + (F & 1))) * 4 + (size_t)nbuf * slot +
+               (2 * (size_t)nbuf + 2) * 8 + (size_t)2 * tr * ng * ks * nstg * 4 + 32 * 8;
         if (smem <= smem_optin_max()) break;
     }
     if (nbuf < 2) return false;

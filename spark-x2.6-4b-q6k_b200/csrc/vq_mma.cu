@@ -40,21 +40,20 @@ struct MmaArgs {
 
 __device__ __forceinline__ float h2f_u16(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 
-__device__ __forceinline__ void mma_issue(const MmaArgs &a, int nq, uint8_t *slot, uint64_t *bar, int r0, int nr) {
+template <int NQ>
+__device__ __forceinline__ void mma_issue(const MmaArgs &a, uint8_t *slot, uint64_t *bar, int r0, int nr) {
     const Layout &L = a.L;
     const size_t payload = L.stream_off + (size_t)L.rows * (L.mrow + L.prow);
-    BulkList bl;
-    bl.n = 0;
+    BulkList<2 * NQ> bl;
     bl.tx = 0;
-    for (int q = 0; q < nq; q++) {
+#pragma unroll
+    for (int q = 0; q < NQ; q++) {
         const uintptr_t limit = (uintptr_t)(a.st[q] + payload + 8);
         const uint8_t *m = a.st[q] + L.stream_off + (size_t)r0 * L.mrow;
-        bulk_plan(bl, slot + q * a.main_slot, (uintptr_t)m, (uintptr_t)m + (size_t)nr * L.mrow, limit);
-        if (L.prow) {
-            const uint8_t *p = a.st[q] + L.stream_off + (size_t)L.rows * L.mrow + (size_t)r0 * L.prow;
-            bulk_plan(bl, slot + nq * a.main_slot + q * a.plane_slot, (uintptr_t)p, (uintptr_t)p + (size_t)nr * L.prow,
-                      limit);
-        }
+        bulk_plan(bl, 2 * q, slot + q * a.main_slot, (uintptr_t)m, (uintptr_t)m + (size_t)nr * L.mrow, limit);
+        const uint8_t *p = a.st[q] + L.stream_off + (size_t)L.rows * L.mrow + (size_t)r0 * L.prow;
+        bulk_plan(bl, 2 * q + 1, slot + NQ * a.main_slot + q * a.plane_slot, (uintptr_t)p,
+                  (uintptr_t)p + (size_t)nr * L.prow, limit);   // empty without a plane (prow 0)
     }
     bulk_issue(bl, bar);
 }
@@ -129,7 +128,7 @@ __global__ void __launch_bounds__(warps_for(S) * 32, 1) vq_mma_kernel(const MmaA
     if (tid == 0)
         for (int k = 0; k < NB - 1 && k < ntile; k++) {
             const int r0 = rb + k * TRR;
-            mma_issue(a, NSTG, ring + (size_t)k * a.slot_bytes, &full[k], r0, min(TRR, re - r0));
+            mma_issue<NSTG>(a, ring + (size_t)k * a.slot_bytes, &full[k], r0, min(TRR, re - r0));
         }
     for (int q = 0; q < NSTG; q++) {
         const uint2 *src = reinterpret_cast<const uint2 *>(a.st[q] + L.cb_off);
@@ -162,7 +161,7 @@ __global__ void __launch_bounds__(warps_for(S) * 32, 1) vq_mma_kernel(const MmaA
         if (tid == 0 && k + NB - 1 < ntile) {
             const int kn = k + NB - 1, r0n = rb + kn * TRR, sn = kn % NB;
             if (kn < NB || mbar_wait(&empty[sn], (uint32_t)(((kn / NB) - 1) & 1), a.err))
-                mma_issue(a, NSTG, ring + (size_t)sn * a.slot_bytes, &full[sn], r0n, min(TRR, re - r0n));
+                mma_issue<NSTG>(a, ring + (size_t)sn * a.slot_bytes, &full[sn], r0n, min(TRR, re - r0n));
         }
         const int r0 = rb + k * TRR, nr = min(TRR, re - r0);
         const bool have = mbar_wait(&full[slot], (uint32_t)((k / NB) & 1), a.err);
