@@ -34,7 +34,14 @@ __device__ __forceinline__ uint32_t ld_u32_unaligned(const uint8_t *p) {
 
 __device__ float block_rms_inv(const float *x, int n, float eps, double *red) {
     double s = 0.0;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) s += (double)x[i] * (double)x[i];
+    for (int i0 = threadIdx.x; i0 < n; i0 += 8 * blockDim.x) {   // 8 loads in flight, summed in index order
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[j] = i0 + j * (int)blockDim.x < n ? x[i0 + j * blockDim.x] : 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+            if (i0 + j * (int)blockDim.x < n) s += (double)v[j] * (double)v[j];
+    }
     s = warp_sum_d(s);
     const int w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
     if ((threadIdx.x & 31) == 0) red[w] = s;

@@ -54,7 +54,14 @@ __device__ float block_rms_inv_from(double s, int n, float eps, double *red) {
 
 __device__ float block_rms_inv(const float *x, int n, float eps, double *red) {
     double s = 0.0;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) s += (double)x[i] * (double)x[i];
+    for (int i0 = threadIdx.x; i0 < n; i0 += 8 * blockDim.x) {   // 8 loads in flight, summed in index order
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[j] = i0 + j * (int)blockDim.x < n ? x[i0 + j * blockDim.x] : 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+            if (i0 + j * (int)blockDim.x < n) s += (double)v[j] * (double)v[j];
+    }
     return block_rms_inv_from(s, n, eps, red);
 }
 
@@ -67,6 +74,8 @@ struct Warps {
     static constexpr int W = 16;
 };
 constexpr int FAST_NBUF = 3;
+constexpr int CB_PIECES = 8;   // bulk copies per stage codebook
+constexpr int X_BATCH = 20;    // activations a thread loads in one round trip
 
 // Shared-memory bytes of one stage's codebook region: nc 8-byte code words copied from the
 // 16-byte boundary at or below the codebook (the payload keeps it 8-byte aligned), so up to 8
@@ -219,33 +228,80 @@ __global__ void __launch_bounds__(Warps<F>::W * 32, 1) vq_fast_kernel(const Fast
         fence_mbar_init();
     }
     __syncthreads();
-    if (tid == 0) {
-        // Codebooks: NQ x nc code words of 8 bytes, one bulk copy per stage ahead of the
-        // first tiles (a few large copies load the hot lines every CTA shares better than
-        // thousands of 8-byte ones).
+    // Warp 0: lane 0 issues the first tile; then every lane takes codebook pieces (NQ x nc code
+    // words of 8 bytes as CB_PIECES bulk copies per stage), issued side by side rather than one
+    // after another; then lane 0 issues the other ring tiles. Every CTA reads the same codebook
+    // lines: each starts at its own piece (rotated by CTA), so at any moment the CTAs'
+    // requests spread over the L2 slices instead of queueing on the same lines.
+    if (warp == 0) {
+        if (lane == 0 && ntile > 0) issue_tile<NQ, EXT>(a, stp, L, ring, &full[0], rb, min(tr, re - rb));
         uint32_t tx = 0;
+        uintptr_t cba[NQ];
+        uint32_t cbn[NQ];
+#pragma unroll
         for (int q = 0; q < NQ; q++) {
             const uintptr_t A = (uintptr_t)(stp[q] + L.cb_off);
-            tx += (uint32_t)((((A + (size_t)nc * 8) + 15) & ~(uintptr_t)15) - (A & ~(uintptr_t)15));
+            cba[q] = A & ~(uintptr_t)15;
+            cbn[q] = (uint32_t)((((A + (size_t)nc * 8) + 15) & ~(uintptr_t)15) - cba[q]);
+            tx += cbn[q];
         }
-        mbar_arrive_expect_tx(cbar, tx);
+        if (lane == 0) mbar_arrive_expect_tx(cbar, tx);   // before any piece can complete
+        __syncwarp();
+#pragma unroll
         for (int q = 0; q < NQ; q++) {
-            const uintptr_t A = (uintptr_t)(stp[q] + L.cb_off), Aal = A & ~(uintptr_t)15;
-            bulk_g2s(smem + q * CBR, (const void *)Aal, (uint32_t)((((A + (size_t)nc * 8) + 15) & ~(uintptr_t)15) - Aal), cbar);
+            const uint32_t piece = ((cbn[q] / CB_PIECES) + 15) & ~15u;   // a multiple of 16 bytes
+            for (int k = lane; k < CB_PIECES; k += 32) {
+                const uint32_t o = (uint32_t)((k + blockIdx.x) % CB_PIECES) * piece;
+                if (o < cbn[q]) bulk_g2s(smem + q * CBR + o, (const void *)(cba[q] + o), min(piece, cbn[q] - o), cbar);
+            }
         }
-        for (int t = 0; t < NB - 1 && t < ntile; t++) {
-            const int r0 = rb + t * tr;
-            issue_tile<NQ, EXT>(a, stp, L, ring + (size_t)t * a.slot_bytes, &full[t], r0, min(tr, re - r0));
+        if (lane == 0) {
+            for (int t = 1; t < NB - 1 && t < ntile; t++) {
+                const int r0 = rb + t * tr;
+                issue_tile<NQ, EXT>(a, stp, L, ring + (size_t)t * a.slot_bytes, &full[t], r0, min(tr, re - r0));
+            }
+        }
+    }
+    // The RMSNorm weights (when x fits one batch of X_BATCH loads per thread) are weights too.
+    const bool xone = L.cols <= X_BATCH * FAST_THREADS;
+    float nwv[X_BATCH];
+    if (xone && a.norm_w) {
+#pragma unroll
+        for (int j = 0; j < X_BATCH; j++) {
+            const int c = tid + j * FAST_THREADS;
+            nwv[j] = c < L.cols ? a.norm_w[c] : 0.f;
         }
     }
     // Everything above read weights only; x (and y, when accumulating) come from
     // the preceding kernels.
     pdl_wait();
     // Activations: coalesced loads (one read of x; the optional RMSNorm's sum of squares
-    // taken on the way, then the scale applied in shared memory) into a per-lane padded
-    // layout, then each lane takes its 4F values with 16-byte shared loads that hit
-    // distinct banks.
-    {
+    // taken on the way) into a per-lane padded layout, then each lane takes its 4F values
+    // with 16-byte shared loads that hit distinct banks. Up to X_BATCH * FAST_THREADS
+    // values: all of a thread's loads in flight at once, scaled in registers.
+    if (xone) {
+        float v[X_BATCH];
+#pragma unroll
+        for (int j = 0; j < X_BATCH; j++) {
+            const int c = tid + j * FAST_THREADS;
+            v[j] = c < L.cols ? a.x[c] : 0.f;
+        }
+        if (a.norm_w) {   // the block's common branch
+            double ss = 0.0;   // this thread's values in index order: block_rms_inv's sum
+#pragma unroll
+            for (int j = 0; j < X_BATCH; j++)
+                if (tid + j * FAST_THREADS < L.cols) ss += (double)v[j] * (double)v[j];
+            const float inv = block_rms_inv_from(ss, L.cols, a.eps, red);
+#pragma unroll
+            for (int j = 0; j < X_BATCH; j++) v[j] = __fmul_rn(__fmul_rn(v[j], inv), nwv[j]);
+        }
+#pragma unroll
+        for (int j = 0; j < X_BATCH; j++) {
+            const int c = tid + j * FAST_THREADS;
+            const int ln = c / (4 * F);   // global lane index = ks * 32 + lane
+            if (c < L.cols) xs[(size_t)ln * XS + (c - ln * 4 * F)] = v[j];
+        }
+    } else {
         double ss = 0.0;
 #pragma unroll 4
         for (int c = tid; c < L.cols; c += FAST_THREADS) {

@@ -102,7 +102,14 @@ __device__ __forceinline__ float gelu_erf(float g) {
 // same order and gets the same scale.
 __device__ float rms_inv(const float *x, int n, float eps, double *red) {
     double s = 0.0;
-    for (int i = threadIdx.x; i < n; i += NT) s += (double)x[i] * (double)x[i];
+    for (int i0 = threadIdx.x; i0 < n; i0 += 8 * NT) {   // 8 loads in flight, summed in index order
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[j] = i0 + j * NT < n ? x[i0 + j * NT] : 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+            if (i0 + j * NT < n) s += (double)v[j] * (double)v[j];
+    }
     s = warp_sum_d(s);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
     __syncthreads();
@@ -324,6 +331,11 @@ __global__ void __launch_bounds__(NT, 1) vq_tab_kernel(const TabArgs a) {
         fetch_cb(cbs, a.cb[u0 / per_g][0]);
         if (tid == 0) prefetch_phase(u0, 0);
     }
+    // this thread's slice activation (segment tid / 32) and its norm weight (a weight: early)
+    const int xv0 = u0 / nch, xnseg = min((u1 - 1) / nch - xv0 + 1, MAXSEG);
+    const bool xmine = u0 < u1 && tid < xnseg * 32;
+    const int xc = 32 * ((xv0 + tid / 32) % nsl) + (tid & 31);
+    const float wv = xmine && a.norm_w ? a.norm_w[xc] : 1.f;
 
     float *acc = reinterpret_cast<float *>(smem + SM_ACC) + tid;   // [MAXS][NT]: this thread's rows' running sums
     uint32_t touched = 0;
@@ -366,17 +378,10 @@ __global__ void __launch_bounds__(NT, 1) vq_tab_kernel(const TabArgs a) {
                 pdl_wait();
                 if (tid == 0) seen = ld_relaxed(a.bar);
                 if (a.mode == 1 && tid < nr) ys[tid] = a.y[r0 + tid];   // the residual they add to, early
-                // this thread's slice activation (segment tid / 32), loaded with the norm's
-                const int v0 = u0 / nch, nseg = min((u1 - 1) / nch - v0 + 1, MAXSEG);
-                const bool mine = tid < nseg * 32;
-                const int c = 32 * ((v0 + tid / 32) % nsl) + (tid & 31);
-                float xv = 0.f, wv = 1.f;
-                if (mine) {
-                    xv = a.x[c];
-                    if (a.norm_w) wv = a.norm_w[c];
-                }
+                // this thread's slice activation, loaded with the norm's
+                float xv = xmine ? a.x[xc] : 0.f;
                 if (a.norm_w) inv = rms_inv(a.x, a.cols, a.eps, red);
-                if (mine) {
+                if (xmine) {
                     if (a.norm_w) xv = __fmul_rn(__fmul_rn(xv, inv), wv);
                     xs2[tid] = f2(xv, xv);
                 }
