@@ -52,6 +52,18 @@ __device__ float block_rms_inv_from(double s, int n, float eps, double *red) {
     return (float)(1.0 / sqrt(t / (double)n + (double)eps));
 }
 
+// The same scale over the `nt` threads (whole warps, starting at warp w0) that meet on named
+// barrier `id`: each passes its partial sum over its own strided share of x in index order.
+__device__ float group_rms_inv_from(double s, int n, float eps, double *red, int id, int nt, int w0) {
+    s = warp_sum_d(s);
+    const int w = (int)(threadIdx.x >> 5) - w0, nw = nt >> 5;
+    if ((threadIdx.x & 31) == 0) red[w] = s;
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nt) : "memory");
+    double t = 0.0;
+    for (int k = 0; k < nw; k++) t += red[k];
+    return (float)(1.0 / sqrt(t / (double)n + (double)eps));
+}
+
 __device__ float block_rms_inv(const float *x, int n, float eps, double *red) {
     double s = 0.0;
     for (int i0 = threadIdx.x; i0 < n; i0 += 8 * blockDim.x) {   // 8 loads in flight, summed in index order
@@ -75,7 +87,8 @@ struct Warps {
 };
 constexpr int FAST_NBUF = 3;
 constexpr int CB_PIECES = 8;   // bulk copies per stage codebook
-constexpr int X_BATCH = 20;    // activations a thread loads in one round trip
+constexpr int X_BATCH = 22;    // activations a staging thread loads in one round trip
+constexpr int X_BAR = 15;      // named barrier of the staging warps (row barriers use 1 .. 8)
 
 // Shared-memory bytes of one stage's codebook region: nc 8-byte code words copied from the
 // 16-byte boundary at or below the codebook (the payload keeps it 8-byte aligned), so up to 8
@@ -262,63 +275,67 @@ __global__ void __launch_bounds__(Warps<F>::W * 32, 1) vq_fast_kernel(const Fast
             }
         }
     }
-    // The RMSNorm weights (when x fits one batch of X_BATCH loads per thread) are weights too.
-    const bool xone = L.cols <= X_BATCH * FAST_THREADS;
-    float nwv[X_BATCH];
-    if (xone && a.norm_w) {
+    // Warps 1 .. 15 stage the activations while warp 0 issues the copies above: coalesced loads
+    // (one read of x; the optional RMSNorm's sum of squares taken on the way, the scale applied
+    // in registers) into a per-lane padded layout, from which each lane later takes its 4F values
+    // with 16-byte shared loads that hit distinct banks. Up to X_BATCH values per staging thread
+    // are in flight at once (the RMSNorm weights, being weights, before the dependency wait).
+    constexpr int XT = FAST_THREADS - 32;   // staging threads
+    if (warp > 0) {
+        const int xt0 = tid - 32;
+        const bool xone = L.cols <= X_BATCH * XT;
+        float nwv[X_BATCH];
+        if (xone && a.norm_w) {
 #pragma unroll
-        for (int j = 0; j < X_BATCH; j++) {
-            const int c = tid + j * FAST_THREADS;
-            nwv[j] = c < L.cols ? a.norm_w[c] : 0.f;
-        }
-    }
-    // Everything above read weights only; x (and y, when accumulating) come from
-    // the preceding kernels.
-    pdl_wait();
-    // Activations: coalesced loads (one read of x; the optional RMSNorm's sum of squares
-    // taken on the way) into a per-lane padded layout, then each lane takes its 4F values
-    // with 16-byte shared loads that hit distinct banks. Up to X_BATCH * FAST_THREADS
-    // values: all of a thread's loads in flight at once, scaled in registers.
-    if (xone) {
-        float v[X_BATCH];
-#pragma unroll
-        for (int j = 0; j < X_BATCH; j++) {
-            const int c = tid + j * FAST_THREADS;
-            v[j] = c < L.cols ? a.x[c] : 0.f;
-        }
-        if (a.norm_w) {   // the block's common branch
-            double ss = 0.0;   // this thread's values in index order: block_rms_inv's sum
-#pragma unroll
-            for (int j = 0; j < X_BATCH; j++)
-                if (tid + j * FAST_THREADS < L.cols) ss += (double)v[j] * (double)v[j];
-            const float inv = block_rms_inv_from(ss, L.cols, a.eps, red);
-#pragma unroll
-            for (int j = 0; j < X_BATCH; j++) v[j] = __fmul_rn(__fmul_rn(v[j], inv), nwv[j]);
-        }
-#pragma unroll
-        for (int j = 0; j < X_BATCH; j++) {
-            const int c = tid + j * FAST_THREADS;
-            const int ln = c / (4 * F);   // global lane index = ks * 32 + lane
-            if (c < L.cols) xs[(size_t)ln * XS + (c - ln * 4 * F)] = v[j];
-        }
-    } else {
-        double ss = 0.0;
-#pragma unroll 4
-        for (int c = tid; c < L.cols; c += FAST_THREADS) {
-            const float v = a.x[c];
-            ss += (double)v * (double)v;
-            const int ln = c / (4 * F);   // global lane index = ks * 32 + lane
-            xs[(size_t)ln * XS + (c - ln * 4 * F)] = v;
-        }
-        if (a.norm_w) {   // the block's common branch
-            const float inv = block_rms_inv_from(ss, L.cols, a.eps, red);
-#pragma unroll 4
-            for (int c = tid; c < L.cols; c += FAST_THREADS) {
-                const int ln = c / (4 * F);
-                float &v = xs[(size_t)ln * XS + (c - ln * 4 * F)];
-                v = __fmul_rn(__fmul_rn(v, inv), a.norm_w[c]);
+            for (int j = 0; j < X_BATCH; j++) {
+                const int c = xt0 + j * XT;
+                nwv[j] = c < L.cols ? a.norm_w[c] : 0.f;
             }
         }
+        pdl_wait();   // everything above read weights only; x comes from the preceding kernels
+        if (xone) {
+            float v[X_BATCH];
+#pragma unroll
+            for (int j = 0; j < X_BATCH; j++) {
+                const int c = xt0 + j * XT;
+                v[j] = c < L.cols ? a.x[c] : 0.f;
+            }
+            if (a.norm_w) {   // the staging warps' common branch
+                double ss = 0.0;   // this thread's values in index order
+#pragma unroll
+                for (int j = 0; j < X_BATCH; j++)
+                    if (xt0 + j * XT < L.cols) ss += (double)v[j] * (double)v[j];
+                const float inv = group_rms_inv_from(ss, L.cols, a.eps, red, X_BAR, XT, 1);
+#pragma unroll
+                for (int j = 0; j < X_BATCH; j++) v[j] = __fmul_rn(__fmul_rn(v[j], inv), nwv[j]);
+            }
+#pragma unroll
+            for (int j = 0; j < X_BATCH; j++) {
+                const int c = xt0 + j * XT;
+                const int ln = c / (4 * F);   // global lane index = ks * 32 + lane
+                if (c < L.cols) xs[(size_t)ln * XS + (c - ln * 4 * F)] = v[j];
+            }
+        } else {
+            double ss = 0.0;
+#pragma unroll 4
+            for (int c = xt0; c < L.cols; c += XT) {
+                const float v = a.x[c];
+                ss += (double)v * (double)v;
+                const int ln = c / (4 * F);
+                xs[(size_t)ln * XS + (c - ln * 4 * F)] = v;
+            }
+            if (a.norm_w) {
+                const float inv = group_rms_inv_from(ss, L.cols, a.eps, red, X_BAR, XT, 1);
+#pragma unroll 4
+                for (int c = xt0; c < L.cols; c += XT) {
+                    const int ln = c / (4 * F);
+                    float &v = xs[(size_t)ln * XS + (c - ln * 4 * F)];
+                    v = __fmul_rn(__fmul_rn(v, inv), a.norm_w[c]);
+                }
+            }
+        }
+    } else {
+        pdl_wait();   // warp 0 reads and writes y (and the exchange counters) after the wait too
     }
     __shared__ unsigned int s_tp_seq;
     __shared__ int s_tp_last;
