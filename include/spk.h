@@ -312,6 +312,18 @@ int spk_model_write_kv(spk_model *m, int layer, int pos0, int n, const float *k,
  * [tp_sum], gate+up, down, [tp_sum]; head; [tp_argmax]; advance. Returns the launch
  * count or -1. Needs one step run before; with tp_world > 1 every rank traces together. */
 int spk_model_trace(spk_model *m, float *us, int cap);
+/* Apply a tuning profile the caller has trusted (spk_vqprof_trust == 0), per matrix
+ * geometry, as vq-model-gpu.cu:301-324 does: a gemv entry naming SPK_VARIANT_TABLE puts
+ * that geometry's matrices on the table kernel (the gate/up pair only both together), any
+ * other variant on the code-word kernel; an entry the kernel cannot run keeps the heuristic
+ * (a line on stderr says so); geometries without an entry keep it too. NULL restores the
+ * heuristic. Layers already set are re-laid and the captured step graphs are dropped (the
+ * next step captures again). The profile is copied. */
+int spk_model_use_profile(spk_model *m, const struct spk_vqprof *pf);
+/* Which kernel the decode step runs for a layer's matrix (0 q_k_v_proj, 1 g_proj, 2 out_proj,
+ * 3 gate_proj, 4 up_proj, 5 down_proj): SPK_VARIANT_TABLE for the table kernel, 3 for the
+ * code-word kernel (g_proj rides with q_k_v_proj), -1 on error. */
+int spk_model_kernel_of(spk_model *m, int layer, int matrix);
 
 /* Tensor-parallel wiring (no counterpart in the reference). Each rank's model owns a
  * mailbox in device memory; the residual reductions and the head's argmax store rows
@@ -427,6 +439,52 @@ int spk_bf16_gemm(const void *w, int rows, int cols, int ntok, const float *x, i
 /* The FFN pair y = act(G x) * (U x), act 0 = gelu (tanh form), 1 = silu (draft.rs:838-855). */
 int spk_bf16_gemm_pair(const void *gate, const void *up, int rows, int cols, int ntok, const float *x, int ldx,
                        float *y, int ldy, int act, void *stream);
+
+/* ------------------------------------------------------- tuning profiles */
+/* VQPROF 1 per-artifact tuning profiles (tools/vq/gpu/vq-profile.h:1-40, the format;
+ * tools/vq-tune/src/profile.rs, the writer; vq-model-gpu.cu:1094-1122 and :301-324, how the
+ * reference runtime trusts and applies one). Host memory throughout; no device work.
+ *
+ * GEMV variants a profile entry can name for this build's kernels: 0-3 as vqg_gemv takes
+ * them (the model runs them all as the code-word kernel, vq.cu, which falls back to the
+ * generic kernel where its geometry rules fail), and SPK_VARIANT_TABLE, the shared-memory
+ * table kernel over re-laid words (vq_tab.cu). `threads` and the prefill tile (bn, bk) are
+ * recorded and written back but this build's kernels fix their own launch shapes. */
+#define SPK_VQPROF_VERSION 1
+#define SPK_VQPROF_MAX 512
+#define SPK_VARIANT_TABLE 4
+typedef struct {
+    int kind;                   /* 0 = gemv, 1 = prefill */
+    int dim, nc, rows, cols, v3;
+    int variant;
+    int threads;                /* gemv */
+    int bn, bk;                 /* prefill */
+    double rate;                /* the trailing measured rate: GB/s (gemv), tok/s (prefill) */
+} spk_vqprof_entry;
+typedef struct spk_vqprof {
+    unsigned long long artifact;   /* the fingerprint the profile was tuned on */
+    char gpu[128];                 /* device name, matched literally */
+    char driver[64];
+    int version;                   /* the VQPROF line's number */
+    int n;
+    spk_vqprof_entry e[SPK_VQPROF_MAX];
+} spk_vqprof;
+/* vq-profile.h:114-140 (vqprof_artifact): FNV-1a 64 over dir/manifest.txt, then per matrix
+ * line `name rows cols stages bytes relL2` with stages > 0, in file order: the name, the size
+ * of dir/name.bin as 8 LE bytes, its first and last min(4096, size) bytes. */
+int spk_vqprof_fingerprint(const char *dir, unsigned long long *out);
+/* vq-profile.h:152-187 (vqprof_load): 0 when the file parsed and says VQPROF 1 (pf holds
+ * what was read either way), -1 otherwise. Unknown lines are skipped; at most
+ * SPK_VQPROF_MAX entries are kept. */
+int spk_vqprof_load(const char *path, spk_vqprof *pf);
+/* vq-profile.h:189-197 (vqprof_find): the index of the first entry of that kind and
+ * geometry, or -1. */
+int spk_vqprof_find(const spk_vqprof *pf, int kind, int dim, int nc, int rows, int cols, int v3);
+/* The runtime's gate (vq-model-gpu.cu:1101-1121): 0 = trusted; 1 = tuned on another
+ * artifact; 2 = tuned on another device (names compared literally); 3 = not version 1. */
+int spk_vqprof_trust(const spk_vqprof *pf, unsigned long long artifact, const char *device);
+/* profile.rs render + write_atomic: the text through path.tmp and a rename. */
+int spk_vqprof_write(const char *path, const spk_vqprof *pf);
 
 #ifdef __cplusplus
 }

@@ -18,7 +18,7 @@ OUT = os.path.join(HERE, "spk", "libspk.so")
 BUILD = os.path.join(HERE, "_build")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-SOURCES = ["common.cu", "vq.cu", "vq_mma.cu", "ggml.cu", "prefill.cu", "tp.cu", "attn.cu", "head_batch.cu", "q8t.cu", "vq_lut.cu", "vq_tab.cu", "vq_tc.cu", "draft.cu", "model.cu"]
+SOURCES = ["common.cu", "vq.cu", "vq_mma.cu", "ggml.cu", "prefill.cu", "tp.cu", "attn.cu", "head_batch.cu", "q8t.cu", "vq_lut.cu", "vq_tab.cu", "vq_tc.cu", "draft.cu", "model.cu", "vqprof.cu"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
          "-I", CSRC, "-I", os.path.join(ROOT, "include")]
 

@@ -160,6 +160,7 @@ struct spk_model {
     int eager_steps = 0;
     int len = 0;                  // positions cached (host view, for rollback checks)
     std::vector<int> cap_slot;    // per layer: capture slot or -1
+    std::vector<spk_vqprof_entry> prof;   // spk_model_use_profile's gemv entries (empty: heuristics)
     float *cap = nullptr;         // [ncap][max_ctx][hidden]
     int ncap = 0;
 };
@@ -268,7 +269,7 @@ int mark(spk_model *m) {
 int residual_gemv(spk_model *m, const spk_model::Layer &L, int mi, const float *x, cudaStream_t s, int *nl) {
     const spk_model_config &c = m->cfg;
     const bool tp = m->tp_world > 1;
-    if (tp) {
+    if (tp && !L.dec[mi]) {   // (a profile that puts this matrix on the table kernel: lut_call + tp_sum)
         const spk_vq_matrix &M = L.m[mi];
         const Layout LM = make_layout(M.dim, M.nc, M.rows, M.cols, M.v3);
         const int rc = vq_gemv_tp(M.stages, M.nstages, LM, x, m->h, m->tpv, s);
@@ -802,9 +803,26 @@ static int relay_layer(spk_model *m, spk_model::Layer &L) {
             L.lut[mi][q] = (const uint8_t *)L.lut_mem[mi] + per * q;
             if (lut_pack(M.stages[q], LM, (void *)L.lut[mi][q], m->stream)) return -1;
         }
-        L.dec[mi] = (mi == 3 || mi == 4) && M.rows >= PAIR_TAB_MIN_ROWS && tab::ok(LM, M.nstages, ng_of[mi]);
-        for (int q = 0; L.dec[mi] && q < M.nstages; q++)
-            if (((uintptr_t)M.stages[q] + LM.cb_off) & 7) L.dec[mi] = false;
+        bool want = (mi == 3 || mi == 4) && M.rows >= PAIR_TAB_MIN_ROWS;   // the heuristic
+        bool runs = tab::ok(LM, M.nstages, ng_of[mi]);
+        for (int q = 0; runs && q < M.nstages; q++)
+            if (((uintptr_t)M.stages[q] + LM.cb_off) & 7) runs = false;
+        // a profile entry for this geometry replaces the heuristic where its kernel can run
+        // (vq-model-gpu.cu:301-324); g_proj rides with q_k_v_proj and takes no entry
+        for (const spk_vqprof_entry &e : m->prof) {
+            if (mi == 1 || e.kind != 0 || e.dim != M.dim || e.nc != M.nc || e.rows != M.rows || e.cols != M.cols ||
+                e.v3 != M.v3)
+                continue;
+            if (e.variant == SPK_VARIANT_TABLE && !runs)
+                fprintf(stderr, "profile: gemv entry for %dx%d is not runnable here; heuristic kept\n", M.rows, M.cols);
+            else if (e.variant < 0 || e.variant > SPK_VARIANT_TABLE)
+                fprintf(stderr, "profile: gemv entry for %dx%d names variant %d; heuristic kept\n", M.rows, M.cols,
+                        e.variant);
+            else
+                want = e.variant == SPK_VARIANT_TABLE;
+            break;
+        }
+        L.dec[mi] = want && runs;
         if (L.dec[mi]) {
             const size_t pw = tab::bytes(LM);
             if (alloc(&L.tab_mem[mi], pw * M.nstages, "alloc vq table words")) return -1;
@@ -880,6 +898,48 @@ int spk_model_set_layer(spk_model *m, int layer, const spk_vq_matrix *qkv, const
     if (relay_layer(m, L)) return -1;
     L.set = true;
     return 0;
+}
+
+// Drop every captured graph: the next step (and verify batch) captures again.
+static void drop_graphs(spk_model *m) {
+    if (m->exec) cudaGraphExecDestroy(m->exec);
+    if (m->graph) cudaGraphDestroy(m->graph);
+    if (m->texec) cudaGraphExecDestroy(m->texec);
+    if (m->tgraph) cudaGraphDestroy(m->tgraph);
+    m->exec = nullptr;
+    m->graph = nullptr;
+    m->texec = nullptr;
+    m->tgraph = nullptr;
+    for (int k = 0; k <= ATT_MAX_TOK; k++) {
+        if (m->vexec[k]) cudaGraphExecDestroy(m->vexec[k]);
+        if (m->vgraph[k]) cudaGraphDestroy(m->vgraph[k]);
+        m->vexec[k] = nullptr;
+        m->vgraph[k] = nullptr;
+    }
+}
+
+int spk_model_use_profile(spk_model *m, const spk_vqprof *pf) {
+    if (!m) return set_error("use_profile: model is null");
+    m->prof.clear();
+    if (pf) {
+        if (pf->n < 0 || pf->n > SPK_VQPROF_MAX) return set_error("use_profile: %d entries (0..%d)", pf->n, SPK_VQPROF_MAX);
+        for (int i = 0; i < pf->n; i++)
+            if (pf->e[i].kind == 0) m->prof.push_back(pf->e[i]);
+    }
+    cudaError_t e = cudaStreamSynchronize(m->stream);   // no step in flight reads what is re-laid
+    if (e != cudaSuccess) return cuda_fail("use_profile: synchronize", e);
+    drop_graphs(m);
+    for (spk_model::Layer &L : m->layers)
+        if (L.set && relay_layer(m, L)) return -1;
+    return 0;
+}
+
+int spk_model_kernel_of(spk_model *m, int layer, int matrix) {
+    if (!m || layer < 0 || layer >= (int)m->layers.size() || matrix < 0 || matrix > 5)
+        return set_error("kernel_of: layer %d / matrix %d out of range", layer, matrix);
+    const spk_model::Layer &L = m->layers[layer];
+    if (!L.set) return set_error("kernel_of: layer %d is not set", layer);
+    return L.dec[matrix] ? SPK_VARIANT_TABLE : 3;
 }
 
 /* The tied embedding / LM head as Q8_0 blocks [vocab][hidden] and the final norm. */

@@ -115,6 +115,13 @@ _PROTOS = {
     "spk_q80_tile_scratch_bytes": ([], C.c_size_t),
     "spk_q80_tile_head": ([_vp, _i, _i, _i, _vp, _i, _vp, _f, _vp, _i, _vp, _vp, _vp], _i),
     "spk_bf16_gemm_pair": ([_vp, _vp, _i, _i, _i, _vp, _i, _vp, _i, _i, _vp], _i),
+    "spk_vqprof_fingerprint": ([_cp, C.POINTER(C.c_ulonglong)], _i),
+    "spk_vqprof_load": ([_cp, _vp], _i),
+    "spk_vqprof_find": ([_vp, _i, _i, _i, _i, _i, _i], _i),
+    "spk_vqprof_trust": ([_vp, C.c_ulonglong, _cp], _i),
+    "spk_vqprof_write": ([_cp, _vp], _i),
+    "spk_model_use_profile": ([_vp, _vp], _i),
+    "spk_model_kernel_of": ([_vp, _i, _i], _i),
 }
 
 

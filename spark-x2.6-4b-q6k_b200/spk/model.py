@@ -320,6 +320,19 @@ class DeviceModel:
                 return list(zip(names, [float(v) for v in buf[:n]]))
         raise SpkError(f"trace: {n} launches in a step, neither the fused nor the separate exchange layout")
 
+    def use_profile(self, profile) -> None:
+        """Apply a trusted VQPROF 1 profile (spk.vqprof.Profile) per matrix geometry, or None to
+        return to the kernel heuristic (spk_model_use_profile). The caller checks trust first
+        (spk.vqprof.trust, the reference runtime's gate, vq-model-gpu.cu:1094-1122)."""
+        check(lib().spk_model_use_profile(self.h, C.byref(profile) if profile is not None else None), "use_profile")
+
+    def kernel_of(self, layer: int, matrix: int) -> int:
+        """The decode step's kernel for a layer matrix (0 qkv .. 5 down): 4 table, 3 code-word."""
+        k = lib().spk_model_kernel_of(self.h, layer, matrix)
+        if k < 0:
+            raise SpkError(f"kernel_of: {lib().spk_last_error().decode()}")
+        return k
+
     def forward(self, token: int, pos: int, want_logits: bool = True):
         """Model::forward: returns (next_id, logits or None) through host buffers."""
         nxt = C.c_int()
