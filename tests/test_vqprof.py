@@ -157,3 +157,40 @@ def test_write_artifact_matches_manifest_format(tmp_path):
     if os.path.exists(REF):
         out = subprocess.run([REF, "fp", str(tmp_path)], check=True, capture_output=True, text=True).stdout.split()
         assert out == ["0", f"{P.fingerprint(str(tmp_path)):016x}"]
+
+
+def test_tuner_bookkeeping_with_stubbed_measurements(tmp_path, monkeypatch):
+    """spk.tune without a GPU: the measurement is stubbed, the rest is the tuner's own logic
+    (one entry per geometry in manifest order, the fastest passing kernel, no entry when
+    nothing passed, another artifact's profile kept unless forced)."""
+    from spk import formats as F
+    from spk import tune
+
+    bufs = {"a": F.random_rvq(32, 256, 4, 256, 2, seed=5), "b": F.random_rvq(64, 128, 4, 256, 2, seed=6),
+            "a2": F.random_rvq(32, 256, 4, 256, 2, seed=7), "c": F.random_rvq(16, 64, 4, 256, 1, seed=8)}
+    d = str(tmp_path)
+    P.write_artifact(d, bufs, 4, 256, 2)
+    seen = []
+
+    def fake(buf, iters, warmup, device):
+        c = F.parse_container(buf)
+        seen.append((c.rows, c.cols))
+        if c.rows == 16:
+            return []
+        return [{"variant": P.VARIANT_TABLE if c.rows == 32 else 3, "threads": 512, "us": 5.0, "gbs": 12.5, "rel": 0.0}]
+
+    monkeypatch.setattr(tune, "tune_geometry", fake)
+    monkeypatch.setattr(P, "device_name", lambda: "NVIDIA B200")
+    log = []
+    path = tune.tune(d, log=log.append)
+    assert seen == [(32, 256), (64, 128), (16, 64)]   # a2 shares a's geometry
+    p = P.load(path)
+    assert p.artifact == P.fingerprint(d) and p.gpu == b"NVIDIA B200" and p.n == 2
+    assert [(e.rows, e.cols, e.variant) for e in p.entries()] == [(32, 256, P.VARIANT_TABLE), (64, 128, 3)]
+    assert any("no kernel passed" in line for line in log)
+    other = P.new(P.fingerprint(d) ^ 1, "NVIDIA B200", "0")
+    P.write(path, other)
+    with pytest.raises(spk.SpkError, match="belongs to artifact"):
+        tune.tune(d, log=log.append)
+    tune.tune(d, force=True, log=log.append)
+    assert P.load(path).artifact == P.fingerprint(d)
