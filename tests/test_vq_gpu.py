@@ -55,6 +55,7 @@ GEOMS = [
     (37, 96, 4, 512, 2, False),         # DQVQ 9-bit -> generic
     (20, 64, 4, 256, 1, False),         # DQVQ 8-bit -> generic
     (17, 200, 4, 4096, 2, True),        # nidx_row 50: not whole 32-groups -> generic
+    (64, 16384, 4, 4096, 2, True),      # F=16, k-split 8: x wider than one staging batch
 ]
 
 
@@ -148,10 +149,11 @@ def test_vqg_dequant_bitexact(cuda, geom):
         assert np.array_equal(o.cpu().numpy().view(np.uint32), want[r].view(np.uint32))
 
 
-def test_spk_vq_gemv_rmsnorm_prologue(cuda):
+@pytest.mark.parametrize("rows,cols", [(2048, 2560), (64, 16384)])
+def test_spk_vq_gemv_rmsnorm_prologue(cuda, rows, cols):
+    """The RMSNorm prologue; 16384 columns take the staging loop for x wider than one batch."""
     import torch
 
-    rows, cols = 2048, 2560
     buf = F.random_rvq(rows, cols, 4, 4096, 2, seed=21, unit_gains=False)
     c = F.parse_container(buf)
     rng = np.random.default_rng(4)
