@@ -71,3 +71,45 @@ def test_noalloc_head_rejects_bad_arguments(cuda):
     y = torch.zeros(64, device=cuda)
     assert L.spk_q80_head_noalloc(w.data_ptr(), 64, 64, x.data_ptr(), None, 0.0, y.data_ptr(), None, None) == -1
     assert L.spk_q80_head_noalloc(w.data_ptr(), 64, 60, x.data_ptr(), None, 0.0, y.data_ptr(), None, None) == -1
+
+
+@pytest.mark.parametrize("rows,cols", [(131072, 2560), (4099, 64)], ids=["head-fast-path", "head-generic-path"])
+def test_noalloc_head_inside_a_graph_capture(cuda, rows, cols):
+    """Its stated use: called once eagerly, then inside a CUDA-graph capture on a caller
+    stream; two replays give the allocating head's logits and argmax."""
+    import torch
+
+    rng = np.random.default_rng(rows + 3 * cols)
+    blocks = F.quantize_q8_0(rng.normal(0, 0.02, (rows, cols)).astype(np.float32))
+    w = spk.dev_bytes(blocks, cuda)
+    x = torch.from_numpy(rng.normal(0, 1, cols).astype(np.float32)).to(cuda)
+    nw = torch.from_numpy(rng.normal(1, 0.1, cols).astype(np.float32)).to(cuda)
+    L = spk.lib()
+    ref_logits = torch.zeros(rows, device=cuda)
+    ref_arg = torch.full((1,), -1, dtype=torch.int32, device=cuda)
+    spk.check(L.spk_q80_head(w.data_ptr(), rows, cols, x.data_ptr(), nw.data_ptr(), 1e-6, ref_logits.data_ptr(),
+                             ref_arg.data_ptr(), None), "allocating head")
+    torch.cuda.synchronize()
+    want, want_arg = ref_logits.cpu().numpy(), int(ref_arg.item())
+
+    s = torch.cuda.Stream()
+    logits = torch.zeros(rows, device=cuda)
+    arg = torch.full((1,), -1, dtype=torch.int32, device=cuda)
+    call = lambda: spk.check(L.spk_q80_head_noalloc(w.data_ptr(), rows, cols, x.data_ptr(), nw.data_ptr(), 1e-6,
+                                                    logits.data_ptr(), arg.data_ptr(), s.cuda_stream), "no-alloc head")
+    with torch.cuda.stream(s):
+        call()   # eagerly first: the one-time set-up happens outside the capture
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        call()
+    for rep in range(2):
+        logits.zero_()
+        arg.fill_(-1)
+        torch.cuda.synchronize()
+        g.replay()
+        torch.cuda.synchronize()
+        spk.check(L.spk_check_device_error(), "device error")
+        assert rel(logits.cpu().numpy(), want) < TOL, rep
+        assert int(arg.item()) == want_arg, rep
+    del g
