@@ -259,6 +259,7 @@ typedef struct {
 } spk_vq_matrix;
 
 typedef struct spk_model spk_model;
+struct spk_vqprof;   /* a tuning profile, defined with its entry points below */
 
 /* Model::new (model.rs:294-320). stream: the cudaStream_t every launch goes to. */
 spk_model *spk_model_create(const spk_model_config *cfg, void *stream);
