@@ -49,3 +49,21 @@ def test_no_cpu_fallback_symbols():
     ours = {s for s in exported if s.startswith(("vqg_", "spk_", "orc_"))}
     assert not any(s.startswith("orc_") for s in ours)
     assert ours == set(declared_symbols())
+
+
+def test_header_compiles_clean_as_c_and_cpp(tmp_path):
+    """include/spk.h is the drop-in boundary for C and C++ callers: it compiles on its own
+    with warnings as errors in both languages, and a caller's pointers match its prototypes."""
+    import shutil
+    import subprocess
+
+    inc = os.path.join(ROOT, "include")
+    src = tmp_path / "use.c"
+    src.write_text('#include "spk.h"\n'
+                   "int use(spk_model *m, spk_vqprof *p) { return spk_model_use_profile(m, p); }\n"
+                   "int find(const spk_vqprof *p) { return spk_vqprof_find(p, 0, 4, 4096, 10240, 2560, 1); }\n")
+    for cc, lang in (("gcc", "c"), ("g++", "c++")):
+        if shutil.which(cc) is None:
+            pytest.skip(f"{cc} is not installed")
+        subprocess.run([cc, "-x", lang, "-std=" + ("c99" if lang == "c" else "c++17"), "-Wall", "-Wextra", "-Werror",
+                        "-c", "-I", inc, str(src), "-o", str(tmp_path / f"use_{lang}.o")], check=True)
