@@ -7,8 +7,8 @@ hashed twice), one of exactly 4096, one above, a comment line, a matrix line wit
 hashed), a line with five fields (not a matrix line for the runtime's reader) and an empty
 line. The profiles cover the reader: gemv and prefill entries with and without the trailing
 rate, an unknown directive, CRLF line ends, trailing spaces, a device name longer than the
-reader's buffer, a second entry for one geometry (the first one wins), and a file that is not
-version 1.
+reader's buffer, a second entry for one geometry (the first one wins), a file that is not
+version 1, more entries than the reader keeps and a line longer than its read buffer.
 
 Usage: python tests/golden/make_vqprof.py
 """
@@ -82,6 +82,18 @@ def main() -> None:
                       f"artifact {fp}\n"
                       "gpu NVIDIA B200\n"
                       "gemv 4 256 8 64 1 0 256 1.0\n",
+        # more entries than the reader keeps (512), and a line longer than its 512-byte buffer
+        # (the rest of that line is read as a line of its own)
+        "many.profile": "VQPROF 1\n"
+                        f"artifact {fp}\n"
+                        "gpu NVIDIA B200\n"
+                        "driver " + "d" * 80 + "\n"
+                        + "".join(f"gemv 4 4096 {32 * (i + 1)} 2560 1 {i % 5} 512 {i}.5\n" for i in range(520)),
+        "long.profile": "VQPROF 1\n"
+                        f"artifact {fp}\n"
+                        "gpu NVIDIA B200\n"
+                        "gemv 4 4096 64 2560 1 3 512" + " " * 600 + "gemv 4 4096 96 2560 1 4 512 7.0\n"
+                        "prefill 4 4096 64 2560 1 2 128 64\n",
     }
     expect = {"fingerprint": fp, "profiles": {}}
     for name, text in profiles.items():
